@@ -1,0 +1,286 @@
+"""Benchmark of the quantized flat-scan path on BASELINE config 2.
+
+Workload: TurboQuant int8, N=100,000 rows, d=768
+(P=1024), i.i.d. N(0,1) rows L2-normalised (seed 2), cosine, 1,000 queries
+issued one at a time, k=10, 4x oversample (F=40) re-ranked in exact fp32.
+A step is the 1,000 queries; each query is one scan launch.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+value  : queries/s with corpus and queries resident in HBM (device timed,
+         CUDA events on the launch stream, max over ranks).
+e2e    : queries/s through the public host API (AddonQuantIndex.search ->
+         bv_search): per query a pinned H2D of the query, the scan, a D2H of
+         the k results and a host synchronisation.
+L2     : the 102.8 MB corpus would fit in the 126 MB L2, so the index is
+         replicated (4 replicas, 411 MB) and query i scans replica i % 4: each
+         scan reads a corpus that 3 other scans (308 MB) evicted.
+N > 1  : one process per GPU, each serving its own replicas and query stream
+         (replicas only: config 2 does not shard), weak scaling.
+--impl reference: the reference's CPU path for this workload -- the WASM-SIMD
+         exact fp32 flat scan (src/fallback/kernel.wat + CpuIndex.query),
+         restated in C (oracle/), on all host threads, bounded query sample.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+N_ROWS, DIM, N_QUERIES, K, RERANK_FACTOR, SEED = 100_000, 768, 1000, 10, 4, 2
+METRIC = "queries/sec at fixed recall@10 (TurboQuant int8 flat scan, N=100k, d=768, k=10, F=40)"
+UNIT = "queries/s"
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def make_data(torch, device, seed, n, dim):
+    """Seeded counter-based (Philox) N(0,1) rows on the GPU, L2-normalised in f64."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    x = torch.randn((n, dim), generator=g, device=device, dtype=torch.float32)
+    x64 = x.double()
+    norm = x64.pow(2).sum(1, keepdim=True).sqrt()
+    return (x64 / norm).float().contiguous()
+
+
+class Clocks:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    def __init__(self, gpu_index: int):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={gpu_index}", f"--query-gpu={q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except (FileNotFoundError, OSError):
+            self.p = None
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        self.p.wait()
+        self.f.flush()
+        rows = [r.split(",") for r in open(self.f.name).read().strip().splitlines() if r.strip()]
+        os.unlink(self.f.name)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+                for nm, v in zip(names, r[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(nm)
+            except (ValueError, IndexError):
+                continue
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_reference_qps(corpus_np, queries_np, steps, warmup, per_step, threads):
+    """The reference CPU path (WASM-SIMD fp32 scan + topK), restated in C."""
+    from oracle import oracle as O
+
+    nq = queries_np.shape[0]
+    times = []
+    for s in range(warmup + steps):
+        sel = queries_np[(np.arange(per_step) + s * per_step) % nq]
+        t0 = time.perf_counter()
+        O.cpu_index_query_batch(corpus_np, DIM, sel, K, threads=threads)
+        dt = time.perf_counter() - t0
+        if s >= warmup:
+            times.append(dt)
+    return per_step * len(times) / sum(times), per_step
+
+
+def recall_at_10(torch, corpus, queries, got_rows):
+    exact = (queries.double() @ corpus.double().T).topk(K, dim=1).indices.cpu().numpy()
+    hit = 0
+    for i in range(exact.shape[0]):
+        hit += len(set(exact[i].tolist()) & set(got_rows[i].tolist()))
+    return hit / (exact.shape[0] * K)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--scoring", default="asym", choices=["asym", "int"])
+    ap.add_argument("--replicas", type=int, default=4)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    fetch = min(N_ROWS, max(K, K * RERANK_FACTOR))  # src/index.ts:414-417
+    config = {"workload": "BASELINE config 2: TurboQuant int8 flat, single-query scans",
+              "rows": N_ROWS, "dim": DIM, "padded_dim": 1024, "queries_per_step": N_QUERIES,
+              "k": K, "fetch": fetch, "metric": "cosine", "scoring": args.scoring,
+              "parallelism": f"replicas x{max(world, 1)}",
+              "l2": f"corpus replicated x{args.replicas} ({args.replicas * 102.8:.0f} MB > 126 MB L2), "
+                    "query i scans replica i % replicas"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            if dist:
+                dist.destroy_process_group()
+            return
+        corpus = make_data(torch, dev, SEED, N_ROWS, DIM)
+        queries = make_data(torch, dev, SEED + 1, N_QUERIES, DIM)
+        c_np, q_np = corpus.cpu().numpy(), queries.cpu().numpy()
+        threads = os.cpu_count() or 1
+        qps, per_step = cpu_reference_qps(c_np, q_np, args.steps, args.warmup, max(threads, 8), threads)
+        line = {"metric": METRIC, "value": qps, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": per_step / qps * 1e3, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+                "config": config,
+                "cpu_baseline": {"value": qps, "unit": UNIT, "cores": threads, "kind": "port",
+                                 "sample": f"{per_step} queries per step over the full 100k x 768 fp32 corpus "
+                                           "(WASM-SIMD scan restated in C, one query per thread)"},
+                "e2e": {"value": qps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        if dist:
+            dist.destroy_process_group()
+        return
+
+    from browservec_b200.index import AddonQuantIndex
+
+    corpus = make_data(torch, dev, SEED, N_ROWS, DIM)
+    queries = make_data(torch, dev, SEED + 1, N_QUERIES, DIM)
+    reps = []
+    for _ in range(args.replicas):
+        ix = AddonQuantIndex(DIM, bits=8, scoring=args.scoring, device=local)
+        torch.cuda.synchronize()
+        ix.append_device(corpus.data_ptr(), N_ROWS, torch.cuda.current_stream().cuda_stream)
+        reps.append(ix)
+    out_rows = torch.zeros((N_QUERIES, K), dtype=torch.int32, device=dev)
+    out_scores = torch.zeros((N_QUERIES, K), dtype=torch.float32, device=dev)
+    out_counts = torch.zeros((N_QUERIES,), dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+
+    def step():
+        for i in range(N_QUERIES):
+            reps[i % len(reps)].search_device(queries[i].data_ptr(), 1, K, fetch, True,
+                                              out_rows[i].data_ptr(), out_scores[i].data_ptr(),
+                                              out_counts[i:].data_ptr(), stream=sp)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clocks = Clocks(local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    launches = args.steps * N_QUERIES
+    qps = max(world, 1) * launches / (ms / 1e3)
+    kernel_ms = ms / launches
+    rec = recall_at_10(torch, corpus, queries, out_rows.cpu().numpy())
+
+    # roofline: algorithmic bytes of one scan launch
+    algo_bytes = N_ROWS * (1024 + 4) + fetch * DIM * 4 + DIM * 4
+    peak, peak_kind = peaks()
+    achieved = algo_bytes / (kernel_ms / 1e3) / 1e9
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "traffic": None,
+                "peak_kind": f"{peak_kind} (copy bandwidth, MEASURED_PEAKS.json hbm_gbs)",
+                "algorithmic_bytes_per_launch": algo_bytes}
+
+    # e2e through the host API (host buffers, H2D + D2H + sync per query)
+    e2e = None
+    if not args.no_e2e:
+        q_np = queries.cpu().numpy()
+        for i in range(min(64, N_QUERIES)):
+            reps[i % len(reps)].search_arrays(q_np[i:i + 1], K, fetch, True)
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        e2e_steps = max(1, min(args.steps, 3))
+        for _ in range(e2e_steps):
+            for i in range(N_QUERIES):
+                reps[i % len(reps)].search_arrays(q_np[i:i + 1], K, fetch, True)
+        wall = time.perf_counter() - t0
+        if dist:
+            t = torch.tensor([wall], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            wall = float(t.item())
+        out_words = 2 * K + 1 + 2 * fetch + 1
+        e2e = {"value": max(world, 1) * e2e_steps * N_QUERIES / wall, "unit": UNIT,
+               "h2d_bytes_per_step": N_QUERIES * DIM * 4, "d2h_bytes_per_step": N_QUERIES * out_words * 4,
+               "steps": e2e_steps, "timing": "host wall clock around synchronous bv_search calls"}
+
+    cpu = None
+    if rank == 0 and not args.no_cpu and world == 1:
+        threads = os.cpu_count() or 1
+        c_np, q_np = corpus.cpu().numpy(), queries.cpu().numpy()
+        cqps, per = cpu_reference_qps(c_np, q_np, 1, 0, max(threads, 8), threads)
+        cpu = {"value": cqps, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"{per} queries over the full 100k x 768 fp32 corpus, WASM-SIMD exact scan "
+                         "restated in C (src/fallback/kernel.wat), one query per thread"}
+
+    for ix in reps:
+        ix.destroy()
+    if rank == 0:
+        line = {"metric": METRIC, "value": qps, "unit": UNIT, "n_gpus": max(world, 1), "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "s8" if args.scoring == "int" else "f32xs8",
+                "data": "synthetic (seeded Philox N(0,1), L2-normalised)", "config": config,
+                "recall_at_10": rec, "kernel_ms": kernel_ms, "gpu_launches": launches,
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk}
+        print(json.dumps(line))
+    if dist:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,575 @@
+// bv_api.cu -- the C ABI (include/browservec.h): index lifetime, corpus
+// storage in HBM, the encoder and scan launches, and error reporting.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "../../include/browservec.h"
+#include "bv_internal.h"
+#include "bv_scan.cuh"
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return status;
+}
+
+constexpr const char* kLostMsg = "GPU device lost; re-create the store";  // quant.ts:183
+constexpr uint32_t kRowAlign = 2048;      // capacity granularity (>= any scan tile)
+constexpr uint32_t kMaxFetch = 1024;      // fused single-query path: F <= 1024
+constexpr uint32_t kMaxPadded = 8192;
+
+bool is_sticky(cudaError_t e) {
+  switch (e) {
+    case cudaErrorIllegalAddress:
+    case cudaErrorLaunchFailure:
+    case cudaErrorHardwareStackError:
+    case cudaErrorIllegalInstruction:
+    case cudaErrorMisalignedAddress:
+    case cudaErrorInvalidAddressSpace:
+    case cudaErrorInvalidPc:
+    case cudaErrorECCUncorrectable:
+    case cudaErrorLaunchTimeout:
+    case cudaErrorUnknown:
+      return true;
+    default:
+      return false;
+  }
+}
+
+// prng.ts:5-14 (mulberry32) -- uint32 arithmetic.
+uint32_t mulberry32_next(uint32_t* state) {
+  uint32_t a = *state + 0x6d2b79f5u;
+  *state = a;
+  uint32_t t = (a ^ (a >> 15)) * (1u | a);
+  t = (t + (t ^ (t >> 7)) * (61u | t)) ^ t;
+  return t ^ (t >> 14);
+}
+
+uint32_t pad_to_pow2(uint32_t n) {  // rotator.ts:39-43
+  uint32_t p = 4;
+  while (p < n) p <<= 1;
+  return p;
+}
+
+}  // namespace
+
+struct bv_index {
+  int device = 0;
+  uint32_t dim = 0, bits = 8, metric = 0, seed = 0, rounds = 2, scoring = 0, row_base = 0;
+  uint32_t P = 0, R = 0;
+  uint64_t rows = 0, cap_rows = 0;
+  uint8_t* d_codes = nullptr;
+  float* d_scales = nullptr;
+  float* d_orig = nullptr;
+  float* d_signs = nullptr;
+  // scratch of the scan: per-CTA candidate lists, last-CTA ticket, error flags
+  uint64_t* d_partials = nullptr;
+  size_t partials_cap = 0;
+  uint32_t* d_ticket = nullptr;
+  uint32_t* d_err = nullptr;
+  // staging for the host-pointer entry points
+  float* d_q = nullptr;
+  size_t q_cap = 0;
+  uint32_t* d_mask = nullptr;
+  size_t mask_cap = 0;
+  uint32_t* d_rows = nullptr;
+  size_t rows_cap = 0;
+  uint32_t* d_out = nullptr;  // out rows | scores | counts | cand rows | cand scores | cand counts
+  size_t out_cap = 0;
+  void* h_pin = nullptr;
+  size_t pin_cap = 0;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  int num_sms = 148;
+  int max_smem = 227 * 1024;
+  float last_ms = 0.0f;
+  uint32_t last_launches = 0;
+  bool lost = false;
+};
+
+namespace {
+
+int cuda_fail(bv_index* idx, cudaError_t e, const char* what) {
+  if (is_sticky(e)) {
+    if (idx) idx->lost = true;
+    return fail(BV_ERR_DEVICE_LOST, "%s", kLostMsg);
+  }
+  if (e == cudaErrorMemoryAllocation) return fail(BV_ERR_NOMEM, "%s: out of device memory", what);
+  return fail(BV_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define BV_CUDA(idx, call, what)                  \
+  do {                                            \
+    cudaError_t e_ = (call);                      \
+    if (e_ != cudaSuccess) return cuda_fail(idx, e_, what); \
+  } while (0)
+
+template <class T>
+int grow(bv_index* idx, T** p, size_t* cap, size_t need, const char* what) {
+  if (*cap >= need) return BV_OK;
+  if (*p) cudaFree(*p);
+  *p = nullptr;
+  *cap = 0;
+  size_t n = need < 64 ? 64 : need;
+  BV_CUDA(idx, cudaMalloc(reinterpret_cast<void**>(p), n * sizeof(T)), what);
+  *cap = n;
+  return BV_OK;
+}
+
+int grow_pinned(bv_index* idx, size_t bytes) {
+  if (idx->pin_cap >= bytes) return BV_OK;
+  if (idx->h_pin) cudaFreeHost(idx->h_pin);
+  idx->h_pin = nullptr;
+  idx->pin_cap = 0;
+  size_t n = bytes < 4096 ? 4096 : bytes;
+  BV_CUDA(idx, cudaMallocHost(&idx->h_pin, n), "pinned staging");
+  idx->pin_cap = n;
+  return BV_OK;
+}
+
+int ensure_capacity(bv_index* idx, uint64_t need_rows) {
+  if (need_rows <= idx->cap_rows) return BV_OK;
+  uint64_t cap = idx->cap_rows * 2;
+  if (cap < need_rows) cap = need_rows;
+  cap = (cap + kRowAlign - 1) / kRowAlign * kRowAlign;
+  uint8_t* codes = nullptr;
+  float* scales = nullptr;
+  float* orig = nullptr;
+  BV_CUDA(idx, cudaMalloc(&codes, cap * idx->R), "codes");
+  cudaError_t e = cudaMalloc(&scales, cap * sizeof(float));
+  if (e == cudaSuccess) e = cudaMalloc(&orig, cap * idx->dim * sizeof(float));
+  if (e != cudaSuccess) {
+    cudaFree(codes);
+    cudaFree(scales);
+    return cuda_fail(idx, e, "corpus");
+  }
+  BV_CUDA(idx, cudaMemsetAsync(codes, 0, cap * idx->R, idx->stream), "memset");
+  BV_CUDA(idx, cudaMemsetAsync(scales, 0, cap * sizeof(float), idx->stream), "memset");
+  if (idx->rows) {
+    BV_CUDA(idx, cudaMemcpyAsync(codes, idx->d_codes, idx->rows * idx->R, cudaMemcpyDeviceToDevice,
+                                 idx->stream), "copy");
+    BV_CUDA(idx, cudaMemcpyAsync(scales, idx->d_scales, idx->rows * sizeof(float),
+                                 cudaMemcpyDeviceToDevice, idx->stream), "copy");
+    BV_CUDA(idx, cudaMemcpyAsync(orig, idx->d_orig, idx->rows * idx->dim * sizeof(float),
+                                 cudaMemcpyDeviceToDevice, idx->stream), "copy");
+  }
+  BV_CUDA(idx, cudaStreamSynchronize(idx->stream), "grow");
+  cudaFree(idx->d_codes);
+  cudaFree(idx->d_scales);
+  cudaFree(idx->d_orig);
+  idx->d_codes = codes;
+  idx->d_scales = scales;
+  idx->d_orig = orig;
+  idx->cap_rows = cap;
+  return BV_OK;
+}
+
+struct Plan {
+  bv::ScanShape sh;
+  uint32_t tile_rows, tile_bytes, ntiles, stages, grid, F, Fp, cap;
+  size_t smem;
+};
+
+int plan_scan(bv_index* idx, uint32_t F, Plan* pl) {
+  if (!bv::scan_shape(static_cast<int>(idx->bits), idx->P, &pl->sh))
+    return fail(BV_ERR_UNSUPPORTED, "padded dimension %u is outside the scan's range", idx->P);
+  const uint32_t R = pl->sh.R;
+  uint32_t tr = 32768u / R;
+  if (tr > 2048u) tr = 2048u;
+  if (tr < pl->sh.rows_per_iter) tr = pl->sh.rows_per_iter;
+  pl->tile_rows = tr;
+  pl->tile_bytes = tr * R;
+  pl->ntiles = static_cast<uint32_t>((idx->rows + tr - 1) / tr);
+  pl->F = F;
+  uint32_t fp = 32;
+  while (fp < F) fp <<= 1;
+  pl->Fp = fp;
+  pl->cap = 2 * fp;
+  pl->stages = 0;
+  for (uint32_t st = 4; st >= 2; --st) {
+    bv::ScanSmem lay = bv::scan_smem_layout(pl->tile_bytes, tr, st, idx->P, pl->cap);
+    if (lay.total <= static_cast<uint32_t>(idx->max_smem)) {
+      pl->stages = st;
+      pl->smem = lay.total;
+      break;
+    }
+  }
+  if (!pl->stages) return fail(BV_ERR_UNSUPPORTED, "scan tile does not fit in shared memory");
+  pl->grid = pl->ntiles < static_cast<uint32_t>(idx->num_sms) ? pl->ntiles
+                                                              : static_cast<uint32_t>(idx->num_sms);
+  return BV_OK;
+}
+
+cudaError_t launch_scan(int bits, int mode, const bv::ScanShape& sh, const bv::ScanParams& p,
+                        unsigned grid, size_t smem, cudaStream_t s) {
+  if (bits == 8) return bv::launch_scan8(mode, sh, p, grid, smem, s);
+  if (bits == 4) return bv::launch_scan4(mode, sh, p, grid, smem, s);
+  return bv::launch_scan1(mode, sh, p, grid, smem, s);
+}
+
+// Validate a request; returns the effective F (0 on error, message set).
+int check_args(bv_index* idx, const bv_search_args* a, uint32_t* F_out) {
+  if (!idx || !a) return fail(BV_ERR_INVALID, "null index or args");
+  if (idx->lost) return fail(BV_ERR_DEVICE_LOST, "%s", kLostMsg);
+  if (a->nq && !a->queries) return fail(BV_ERR_INVALID, "queries is null");
+  if (a->k == 0) return fail(BV_ERR_INVALID, "k must be >= 1");
+  if (!a->out_rows || !a->out_scores || !a->out_counts)
+    return fail(BV_ERR_INVALID, "output pointers are required");
+  uint32_t F = a->fetch ? a->fetch : a->k;
+  if (F < a->k) F = a->k;
+  if (F > kMaxFetch)
+    return fail(BV_ERR_UNSUPPORTED, "fetch %u exceeds the single-query scan limit (%u)", F, kMaxFetch);
+  if (a->mask) {
+    const uint64_t words = (idx->rows + 31) / 32;
+    if (a->mask_words < words)  // scoreMask.ts:68-70
+      return fail(BV_ERR_INVALID, "mask has %llu words, need %llu for %llu rows",
+                  static_cast<unsigned long long>(a->mask_words),
+                  static_cast<unsigned long long>(words), static_cast<unsigned long long>(idx->rows));
+  }
+  *F_out = F;
+  return BV_OK;
+}
+
+// Enqueue every query of `a` (device pointers) on `s`.
+int enqueue_search(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStream_t s) {
+  Plan pl;
+  int rc = plan_scan(idx, F, &pl);
+  if (rc) return rc;
+  rc = grow(idx, &idx->d_partials, &idx->partials_cap, static_cast<size_t>(pl.grid) * pl.Fp, "scratch");
+  if (rc) return rc;
+  bv::ScanParams p;
+  memset(&p, 0, sizeof(p));
+  p.codes = idx->d_codes;
+  p.scales = idx->d_scales;
+  p.originals = idx->d_orig;
+  p.signs = idx->d_signs;
+  p.mask = a->mask;
+  p.nrows = idx->rows;
+  p.dim = idx->dim;
+  p.P = idx->P;
+  p.rounds = idx->rounds;
+  p.R = pl.sh.R;
+  p.tile_rows = pl.tile_rows;
+  p.tile_bytes = pl.tile_bytes;
+  p.ntiles = pl.ntiles;
+  p.stages = pl.stages;
+  p.F = pl.F;
+  p.Fp = pl.Fp;
+  p.cap = pl.cap;
+  p.k = a->k;
+  p.rerank = a->rerank ? 1 : 0;
+  p.row_base = idx->row_base;
+  p.partials = idx->d_partials;
+  p.ticket = idx->d_ticket;
+  p.err = idx->d_err;
+  for (uint32_t q = 0; q < a->nq; ++q) {
+    p.query = a->queries + static_cast<size_t>(q) * idx->dim;
+    p.out_rows = a->out_rows + static_cast<size_t>(q) * a->k;
+    p.out_scores = a->out_scores + static_cast<size_t>(q) * a->k;
+    p.out_count = a->out_counts + q;
+    p.cand_rows = a->cand_rows ? a->cand_rows + static_cast<size_t>(q) * F : nullptr;
+    p.cand_scores = a->cand_scores ? a->cand_scores + static_cast<size_t>(q) * F : nullptr;
+    p.cand_count = a->cand_counts ? a->cand_counts + q : nullptr;
+    if (p.cand_rows && (!p.cand_scores || !p.cand_count)) p.cand_rows = nullptr;
+    cudaError_t e = launch_scan(static_cast<int>(idx->bits), static_cast<int>(idx->scoring), pl.sh,
+                                p, pl.grid, pl.smem, s);
+    if (e == cudaErrorNotSupported)
+      return fail(BV_ERR_UNSUPPORTED, "no scan kernel for bits=%u scoring=%u P=%u", idx->bits,
+                  idx->scoring, idx->P);
+    if (e != cudaSuccess) return cuda_fail(idx, e, "scan launch");
+  }
+  idx->last_launches = a->nq;
+  return BV_OK;
+}
+
+int check_err_flag(bv_index* idx) {
+  uint32_t flag = 0;
+  BV_CUDA(idx, cudaMemcpy(&flag, idx->d_err, 4, cudaMemcpyDeviceToHost), "error flag");
+  if (flag) {
+    cudaMemset(idx->d_err, 0, 4);
+    return fail(BV_ERR_TIMEOUT, "scan kernel wait ran out of budget (flag 0x%x)", flag);
+  }
+  return BV_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* bv_last_error(void) { return g_err.c_str(); }
+
+int bv_create(const bv_config* cfg, bv_index** out) {
+  if (!cfg || !out) return fail(BV_ERR_INVALID, "null config or output");
+  *out = nullptr;
+  if (cfg->dim == 0) return fail(BV_ERR_INVALID, "dimension must be a positive integer, got 0");
+  if (cfg->bits != 8 && cfg->bits != 4 && cfg->bits != 1)
+    return fail(BV_ERR_INVALID, "quantBits %u not supported (ships 0, 1, 4, 8)", cfg->bits);
+  if (cfg->metric > BV_METRIC_DOT)  // index.ts:135-137
+    return fail(BV_ERR_INVALID,
+                "quantized mode supports metric cosine/dot only (l2 quantization is later work)");
+  if (cfg->scoring > BV_SCORE_HAMMING) return fail(BV_ERR_INVALID, "unknown scoring mode %u", cfg->scoring);
+  if (cfg->scoring == BV_SCORE_HAMMING && cfg->bits != 1)
+    return fail(BV_ERR_INVALID, "hamming scoring needs 1-bit codes");
+  const uint32_t P = pad_to_pow2(cfg->dim);
+  if (P > kMaxPadded) return fail(BV_ERR_UNSUPPORTED, "dimension %u pads beyond %u", cfg->dim, kMaxPadded);
+  if (cfg->bits == 4 && P % 8) return fail(BV_ERR_INVALID, "paddedDim must be a multiple of 8 for 4-bit");
+  if (cfg->bits == 1 && P % 32)
+    return fail(BV_ERR_INVALID, "paddedDim must be a multiple of 32 for 1-bit");
+  bv_index* idx = new bv_index();
+  idx->device = cfg->device;
+  idx->dim = cfg->dim;
+  idx->bits = cfg->bits;
+  idx->metric = cfg->metric;
+  idx->seed = cfg->seed;
+  idx->rounds = cfg->rounds;
+  idx->scoring = cfg->scoring;
+  idx->row_base = cfg->row_base;
+  idx->P = P;
+  idx->R = bv::code_row_bytes(static_cast<int>(cfg->bits), P);
+  auto bail = [&](int rc) {
+    bv_destroy(idx);
+    return rc;
+  };
+  cudaError_t e = cudaSetDevice(cfg->device);
+  if (e != cudaSuccess) return bail(cuda_fail(nullptr, e, "cudaSetDevice"));
+  cudaDeviceGetAttribute(&idx->num_sms, cudaDevAttrMultiProcessorCount, cfg->device);
+  cudaDeviceGetAttribute(&idx->max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, cfg->device);
+  if ((e = cudaStreamCreateWithFlags(&idx->stream, cudaStreamNonBlocking)) != cudaSuccess ||
+      (e = cudaEventCreate(&idx->ev0)) != cudaSuccess || (e = cudaEventCreate(&idx->ev1)) != cudaSuccess)
+    return bail(cuda_fail(nullptr, e, "stream"));
+  // rotator.ts:66-80: per round, signs from mulberry32((seed ^ 0x9e3779b9*(r+1)) >>> 0),
+  // pre-scaled by f32(+-1 * (1/sqrt(P) in f64)).
+  const size_t ns = static_cast<size_t>(P) * (cfg->rounds ? cfg->rounds : 1);
+  float* hs = new float[ns];
+  const double inv = 1.0 / std::sqrt(static_cast<double>(P));
+  for (uint32_t r = 0; r < cfg->rounds; ++r) {
+    uint32_t st = cfg->seed ^ (0x9e3779b9u * (r + 1u));
+    for (uint32_t i = 0; i < P; ++i) {
+      const double s = mulberry32_next(&st) < 0x80000000u ? -1.0 : 1.0;
+      hs[static_cast<size_t>(r) * P + i] = static_cast<float>(s * inv);
+    }
+  }
+  e = cudaMalloc(&idx->d_signs, ns * sizeof(float));
+  if (e == cudaSuccess) e = cudaMemcpy(idx->d_signs, hs, ns * sizeof(float), cudaMemcpyHostToDevice);
+  delete[] hs;
+  if (e == cudaSuccess) e = cudaMalloc(&idx->d_ticket, 16);
+  if (e == cudaSuccess) e = cudaMalloc(&idx->d_err, 16);
+  if (e == cudaSuccess) e = cudaMemset(idx->d_ticket, 0, 16);
+  if (e == cudaSuccess) e = cudaMemset(idx->d_err, 0, 16);
+  if (e != cudaSuccess) return bail(cuda_fail(nullptr, e, "index buffers"));
+  *out = idx;
+  return BV_OK;
+}
+
+int bv_destroy(bv_index* idx) {
+  if (!idx) return BV_OK;
+  if (idx->stream) cudaStreamSynchronize(idx->stream);
+  cudaFree(idx->d_codes);
+  cudaFree(idx->d_scales);
+  cudaFree(idx->d_orig);
+  cudaFree(idx->d_signs);
+  cudaFree(idx->d_partials);
+  cudaFree(idx->d_ticket);
+  cudaFree(idx->d_err);
+  cudaFree(idx->d_q);
+  cudaFree(idx->d_mask);
+  cudaFree(idx->d_rows);
+  cudaFree(idx->d_out);
+  if (idx->h_pin) cudaFreeHost(idx->h_pin);
+  if (idx->ev0) cudaEventDestroy(idx->ev0);
+  if (idx->ev1) cudaEventDestroy(idx->ev1);
+  if (idx->stream) cudaStreamDestroy(idx->stream);
+  delete idx;
+  return BV_OK;
+}
+
+int bv_size(const bv_index* idx, uint64_t* rows) {
+  if (!idx || !rows) return fail(BV_ERR_INVALID, "null argument");
+  *rows = idx->rows;
+  return BV_OK;
+}
+
+static int append_impl(bv_index* idx, const float* rows, uint64_t count, bool device, cudaStream_t s) {
+  if (!idx) return fail(BV_ERR_INVALID, "null index");
+  if (idx->lost) return fail(BV_ERR_DEVICE_LOST, "%s", kLostMsg);
+  if (count == 0) return BV_OK;
+  if (!rows) return fail(BV_ERR_INVALID, "rows is null");
+  if (idx->rows + count > 0xFFFFFFFEull)
+    return fail(BV_ERR_UNSUPPORTED, "a shard holds at most 2^32-2 rows");
+  BV_CUDA(idx, cudaSetDevice(idx->device), "cudaSetDevice");
+  if (s) BV_CUDA(idx, cudaStreamSynchronize(s), "sync");
+  int rc = ensure_capacity(idx, idx->rows + count);
+  if (rc) return rc;
+  float* dst = idx->d_orig + idx->rows * idx->dim;
+  const size_t bytes = count * idx->dim * sizeof(float);
+  BV_CUDA(idx, cudaMemcpyAsync(dst, rows, bytes, device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                               idx->stream), "append copy");
+  cudaError_t e = bv::launch_encode(static_cast<int>(idx->bits), dst, count, idx->dim, idx->P, idx->d_signs,
+                                    idx->rounds, idx->d_codes + idx->rows * idx->R,
+                                    idx->d_scales + idx->rows, idx->R, idx->stream);
+  if (e != cudaSuccess) return cuda_fail(idx, e, "encode");
+  BV_CUDA(idx, cudaStreamSynchronize(idx->stream), "encode");
+  idx->rows += count;
+  return BV_OK;
+}
+
+int bv_append(bv_index* idx, const float* rows, uint64_t count) {
+  return append_impl(idx, rows, count, false, nullptr);
+}
+
+int bv_append_device(bv_index* idx, const float* rows_dev, uint64_t count, void* stream) {
+  return append_impl(idx, rows_dev, count, true, static_cast<cudaStream_t>(stream));
+}
+
+int bv_search_async(bv_index* idx, const bv_search_args* a, void* stream) {
+  uint32_t F = 0;
+  int rc = check_args(idx, a, &F);
+  if (rc) return rc;
+  BV_CUDA(idx, cudaSetDevice(idx->device), "cudaSetDevice");
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : idx->stream;
+  if (idx->rows == 0 || a->nq == 0) {  // quant.ts:184: an empty index returns []
+    if (a->nq) BV_CUDA(idx, cudaMemsetAsync(a->out_counts, 0, a->nq * 4, s), "memset");
+    idx->last_launches = 0;
+    return BV_OK;
+  }
+  return enqueue_search(idx, a, F, s);
+}
+
+int bv_search(bv_index* idx, const bv_search_args* a) {
+  uint32_t F = 0;
+  int rc = check_args(idx, a, &F);
+  if (rc) return rc;
+  BV_CUDA(idx, cudaSetDevice(idx->device), "cudaSetDevice");
+  const uint32_t nq = a->nq;
+  if (idx->rows == 0 || nq == 0) {
+    for (uint32_t q = 0; q < nq; ++q) a->out_counts[q] = 0;
+    if (a->cand_counts)
+      for (uint32_t q = 0; q < nq; ++q) a->cand_counts[q] = 0;
+    idx->last_launches = 0;
+    return BV_OK;
+  }
+  const bool cand = a->cand_rows && a->cand_scores && a->cand_counts;
+  const size_t qn = static_cast<size_t>(nq) * idx->dim;
+  const size_t on = static_cast<size_t>(nq) * a->k;
+  const size_t cn = cand ? static_cast<size_t>(nq) * F : 0;
+  // device staging: [rows on | scores on | counts nq | cand rows cn | cand scores cn | cand counts nq]
+  const size_t out_words = 2 * on + nq + 2 * cn + (cand ? nq : 0);
+  if ((rc = grow(idx, &idx->d_q, &idx->q_cap, qn, "query staging"))) return rc;
+  if ((rc = grow(idx, &idx->d_out, &idx->out_cap, out_words, "output staging"))) return rc;
+  const size_t mw = a->mask ? (idx->rows + 31) / 32 : 0;
+  if (mw && (rc = grow(idx, &idx->d_mask, &idx->mask_cap, mw, "mask staging"))) return rc;
+  const size_t pin_bytes = (qn > out_words ? qn : out_words) * 4;
+  if ((rc = grow_pinned(idx, pin_bytes))) return rc;
+  memcpy(idx->h_pin, a->queries, qn * 4);
+  BV_CUDA(idx, cudaEventRecord(idx->ev0, idx->stream), "event");
+  BV_CUDA(idx, cudaMemcpyAsync(idx->d_q, idx->h_pin, qn * 4, cudaMemcpyHostToDevice, idx->stream), "H2D");
+  if (mw)
+    BV_CUDA(idx, cudaMemcpyAsync(idx->d_mask, a->mask, mw * 4, cudaMemcpyHostToDevice, idx->stream), "H2D");
+  bv_search_args d = *a;
+  d.queries = idx->d_q;
+  d.mask = mw ? idx->d_mask : nullptr;
+  d.mask_words = mw;
+  d.out_rows = idx->d_out;
+  d.out_scores = reinterpret_cast<float*>(idx->d_out + on);
+  d.out_counts = idx->d_out + 2 * on;
+  d.cand_rows = cand ? idx->d_out + 2 * on + nq : nullptr;
+  d.cand_scores = cand ? reinterpret_cast<float*>(idx->d_out + 2 * on + nq + cn) : nullptr;
+  d.cand_counts = cand ? idx->d_out + 2 * on + nq + 2 * cn : nullptr;
+  if ((rc = enqueue_search(idx, &d, F, idx->stream))) return rc;
+  BV_CUDA(idx, cudaMemcpyAsync(idx->h_pin, idx->d_out, out_words * 4, cudaMemcpyDeviceToHost, idx->stream),
+          "D2H");
+  BV_CUDA(idx, cudaEventRecord(idx->ev1, idx->stream), "event");
+  BV_CUDA(idx, cudaStreamSynchronize(idx->stream), "search");
+  cudaEventElapsedTime(&idx->last_ms, idx->ev0, idx->ev1);
+  if ((rc = check_err_flag(idx))) return rc;
+  const uint32_t* h = static_cast<const uint32_t*>(idx->h_pin);
+  memcpy(a->out_rows, h, on * 4);
+  memcpy(a->out_scores, h + on, on * 4);
+  memcpy(a->out_counts, h + 2 * on, nq * 4);
+  if (cand) {
+    memcpy(a->cand_rows, h + 2 * on + nq, cn * 4);
+    memcpy(a->cand_scores, h + 2 * on + nq + cn, cn * 4);
+    memcpy(a->cand_counts, h + 2 * on + nq + 2 * cn, nq * 4);
+  }
+  return BV_OK;
+}
+
+int bv_query_rows_exact(bv_index* idx, const float* query, const uint32_t* rows, uint32_t nrows,
+                        uint32_t k, uint32_t* out_rows, float* out_scores, uint32_t* out_count) {
+  if (!idx || !query || !out_rows || !out_scores || !out_count) return fail(BV_ERR_INVALID, "null argument");
+  if (idx->lost) return fail(BV_ERR_DEVICE_LOST, "%s", kLostMsg);
+  if (nrows > 4096) return fail(BV_ERR_INVALID, "exact row scan takes at most 4096 rows, got %u", nrows);
+  if (nrows && !rows) return fail(BV_ERR_INVALID, "rows is null");
+  for (uint32_t i = 0; i < nrows; ++i)
+    if (rows[i] >= idx->rows) return fail(BV_ERR_INVALID, "row %u out of range (%llu rows)", rows[i],
+                                          static_cast<unsigned long long>(idx->rows));
+  if (nrows == 0 || k == 0) {
+    *out_count = 0;
+    return BV_OK;
+  }
+  BV_CUDA(idx, cudaSetDevice(idx->device), "cudaSetDevice");
+  int rc;
+  if ((rc = grow(idx, &idx->d_q, &idx->q_cap, idx->dim, "query staging"))) return rc;
+  if ((rc = grow(idx, &idx->d_rows, &idx->rows_cap, nrows, "row staging"))) return rc;
+  if ((rc = grow(idx, &idx->d_out, &idx->out_cap, 2 * static_cast<size_t>(k) + 1, "output staging"))) return rc;
+  BV_CUDA(idx, cudaMemcpyAsync(idx->d_q, query, idx->dim * 4, cudaMemcpyHostToDevice, idx->stream), "H2D");
+  BV_CUDA(idx, cudaMemcpyAsync(idx->d_rows, rows, nrows * 4, cudaMemcpyHostToDevice, idx->stream), "H2D");
+  cudaError_t e = bv::launch_exact_rows(idx->d_orig, idx->dim, idx->d_q, idx->d_rows, nrows, k,
+                                        idx->row_base, idx->d_out, reinterpret_cast<float*>(idx->d_out + k),
+                                        idx->d_out + 2 * k, idx->stream);
+  if (e != cudaSuccess) return cuda_fail(idx, e, "exact scan");
+  uint32_t n = 0;
+  BV_CUDA(idx, cudaMemcpyAsync(&n, idx->d_out + 2 * k, 4, cudaMemcpyDeviceToHost, idx->stream), "D2H");
+  BV_CUDA(idx, cudaMemcpyAsync(out_rows, idx->d_out, k * 4, cudaMemcpyDeviceToHost, idx->stream), "D2H");
+  BV_CUDA(idx, cudaMemcpyAsync(out_scores, idx->d_out + k, k * 4, cudaMemcpyDeviceToHost, idx->stream), "D2H");
+  BV_CUDA(idx, cudaStreamSynchronize(idx->stream), "exact scan");
+  *out_count = n;
+  idx->last_launches = 1;
+  return BV_OK;
+}
+
+int bv_export_codes(const bv_index* idx, uint64_t row0, uint64_t count, uint32_t* words, float* scales) {
+  if (!idx) return fail(BV_ERR_INVALID, "null index");
+  if (row0 + count > idx->rows) return fail(BV_ERR_INVALID, "rows out of range");
+  bv_index* m = const_cast<bv_index*>(idx);
+  BV_CUDA(m, cudaSetDevice(idx->device), "cudaSetDevice");
+  if (words)
+    BV_CUDA(m, cudaMemcpy(words, idx->d_codes + row0 * idx->R, count * idx->R, cudaMemcpyDeviceToHost), "D2H");
+  if (scales)
+    BV_CUDA(m, cudaMemcpy(scales, idx->d_scales + row0, count * 4, cudaMemcpyDeviceToHost), "D2H");
+  return BV_OK;
+}
+
+int bv_get_stats(const bv_index* idx, bv_stats* out) {
+  if (!idx || !out) return fail(BV_ERR_INVALID, "null argument");
+  out->rows = idx->rows;
+  out->dim = idx->dim;
+  out->padded_dim = idx->P;
+  out->bits = idx->bits;
+  out->words_per_row = idx->R / 4;
+  out->chunks = 1;
+  out->last_query_gpu_ms = idx->last_ms;
+  out->device_bytes = idx->cap_rows * (idx->R + 4 + static_cast<uint64_t>(idx->dim) * 4);
+  return BV_OK;
+}
+
+int bv_launches_last_search(const bv_index* idx, uint32_t* launches) {
+  if (!idx || !launches) return fail(BV_ERR_INVALID, "null argument");
+  *launches = idx->last_launches;
+  return BV_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,432 @@
+"""Python host of the B200 quantized flat-scan path.
+
+``AddonQuantIndex`` is the index the reference's ``buildIndex`` would construct
+instead of ``QuantIndex`` (src/index.ts:134-140): it implements the
+``VectorIndex`` seam (src/index/flat.ts:30-40) plus the duck-typed extras
+``queryMasked``/``queryBatch``/``chunkCount``/``ingestMode`` that ``BrowserVec``
+probes, over the C ABI of libbvcuda.so.
+
+``BrowserVec`` mirrors the quantized branch of the reference's orchestration
+(src/index.ts): store bookkeeping, normalisation, the filter strategy
+(exact scan for <= 4096 matches, else an in-index mask), the fetch/re-rank
+rule and the id mapping.  The re-rank runs on the GPU inside the search call,
+so ``query_batch`` re-ranks as well (the reference's batched branch skips it,
+src/index.ts:495-516).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, field
+from typing import Any, Mapping, Sequence
+
+import numpy as np
+
+from . import _lib
+from .filter import FilterColumns, compile_filter, pack_mask
+
+DEFAULT_SEED = 0x9E3779B9          # src/index.ts:71
+FILTER_CPU_SCAN_MAX = 4096         # src/index.ts:76
+
+
+def default_rerank_factor(bits: int) -> int:
+    """src/index.ts:99-103"""
+    if bits == 1:
+        return 32
+    return 16 if bits == 4 else 4
+
+
+@dataclass
+class FlatHit:
+    row: int
+    score: float
+
+
+@dataclass
+class QueryResult:
+    id: str
+    score: float
+    metadata: Mapping[str, Any] | None = None
+
+
+def _ptr(a: np.ndarray | None):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+def normalize_rows(m: np.ndarray) -> np.ndarray:
+    """store.ts:209-217 for each row: f64 running sum of squares (sequential),
+    sqrt, f64 inverse, f32 store.  np.cumsum accumulates strictly in order."""
+    m = np.ascontiguousarray(m, dtype=np.float32)
+    x = m.astype(np.float64)
+    sums = np.cumsum(x * x, axis=1)[:, -1] if m.shape[1] else np.zeros(m.shape[0])
+    norm = np.sqrt(sums)
+    inv = np.where(norm > 0, 1.0 / np.where(norm > 0, norm, 1.0), 1.0)
+    out = (x * inv[:, None]).astype(np.float32)
+    return np.where((norm > 0)[:, None], out, m)
+
+
+class AddonQuantIndex:
+    """VectorIndex over libbvcuda (quantized flat scan on one GPU shard)."""
+
+    def __init__(self, dim: int, seed: int = DEFAULT_SEED, rounds: int = 2, bits: int = 8,
+                 scoring: str = "asym", device: int = 0, metric: str = "cosine", row_base: int = 0):
+        L = _lib.load()
+        if metric == "l2":
+            raise ValueError("quantized mode supports metric cosine/dot only (l2 quantization is later work)")
+        cfg = _lib.BvConfig(dim=dim, bits=bits, metric=_lib.METRIC_DOT if metric == "dot" else _lib.METRIC_COSINE,
+                            seed=seed & 0xFFFFFFFF, rounds=rounds, scoring=_lib.SCORING[scoring],
+                            device=device, row_base=row_base)
+        h = C.c_void_p()
+        _lib.check(L.bv_create(C.byref(cfg), C.byref(h)))
+        self._h = h
+        self._L = L
+        self.dim, self.bits, self.seed, self.rounds, self.scoring = dim, bits, seed, rounds, scoring
+        self.device = device
+        self.row_base = row_base
+
+    # ---- VectorIndex seam -------------------------------------------------
+    @property
+    def size(self) -> int:
+        n = C.c_uint64()
+        _lib.check(self._L.bv_size(self._h, C.byref(n)))
+        return int(n.value)
+
+    @property
+    def chunk_count(self) -> int:
+        return 1
+
+    @property
+    def ingest_mode(self) -> str:
+        return "gpu"
+
+    def append(self, data: np.ndarray, count: int) -> None:
+        """quant.ts:129-141 (the error message of quant.ts:130-132)."""
+        data = np.ascontiguousarray(data, dtype=np.float32).reshape(-1)
+        if data.size != count * self.dim:
+            raise ValueError(f"expected {count * self.dim} floats, got {data.size}")
+        _lib.check(self._L.bv_append(self._h, _ptr(data), count))
+
+    def append_device(self, ptr: int, count: int, stream: int = 0) -> None:
+        _lib.check(self._L.bv_append_device(self._h, C.c_void_p(ptr), count, C.c_void_p(stream)))
+
+    def query(self, q: np.ndarray, k: int) -> list[FlatHit]:
+        """quant.ts:165-167: approximate top-k by quantized score."""
+        return self.search(q[None, :], k, k, rerank=False)[0]
+
+    def query_masked(self, q: np.ndarray, k: int, mask_words: np.ndarray) -> list[FlatHit]:
+        """quant.ts:174-176"""
+        return self.search(q[None, :], k, k, rerank=False, mask=mask_words)[0]
+
+    def query_batch(self, packed: np.ndarray, n: int, k: int, fetch: int | None = None,
+                    rerank: bool = True, mask: np.ndarray | None = None) -> list[list[FlatHit]]:
+        return self.search(np.asarray(packed, np.float32).reshape(n, self.dim), k,
+                           fetch if fetch else k, rerank=rerank, mask=mask)
+
+    def search(self, qs: np.ndarray, k: int, fetch: int, rerank: bool = True,
+               mask: np.ndarray | None = None, with_candidates: bool = False):
+        """k results per query after (optional) exact re-rank of `fetch` candidates."""
+        qs = np.ascontiguousarray(qs, dtype=np.float32).reshape(-1, self.dim)
+        nq = qs.shape[0]
+        F = max(fetch, k)
+        out_rows = np.zeros((nq, k), np.uint32)
+        out_scores = np.zeros((nq, k), np.float32)
+        out_counts = np.zeros(nq, np.uint32)
+        cand = (np.zeros((nq, F), np.uint32), np.zeros((nq, F), np.float32), np.zeros(nq, np.uint32)) \
+            if with_candidates else (None, None, None)
+        m = None if mask is None else np.ascontiguousarray(mask, dtype=np.uint32)
+        if m is not None:
+            need = (self.size + 31) // 32
+            if m.size < need:  # scoreMask.ts:68-70
+                raise ValueError(f"mask has {m.size} words, need {need} for {self.size} rows")
+        args = _lib.BvSearchArgs(queries=_ptr(qs), nq=nq, k=k, fetch=F, rerank=int(rerank),
+                                 mask=_ptr(m), mask_words=0 if m is None else m.size,
+                                 out_rows=_ptr(out_rows), out_scores=_ptr(out_scores),
+                                 out_counts=_ptr(out_counts), cand_rows=_ptr(cand[0]),
+                                 cand_scores=_ptr(cand[1]), cand_counts=_ptr(cand[2]))
+        _lib.check(self._L.bv_search(self._h, C.byref(args)))
+        hits = [[FlatHit(int(out_rows[i, j]), float(out_scores[i, j])) for j in range(int(out_counts[i]))]
+                for i in range(nq)]
+        if with_candidates:
+            return hits, cand
+        return hits
+
+    def search_arrays(self, qs: np.ndarray, k: int, fetch: int, rerank: bool = True,
+                      mask: np.ndarray | None = None):
+        """Like search() but returns (rows[nq,k], scores[nq,k], counts[nq], cand_rows, cand_scores,
+        cand_counts) numpy arrays."""
+        qs = np.ascontiguousarray(qs, dtype=np.float32).reshape(-1, self.dim)
+        nq = qs.shape[0]
+        F = max(fetch, k)
+        o = [np.zeros((nq, k), np.uint32), np.zeros((nq, k), np.float32), np.zeros(nq, np.uint32),
+             np.zeros((nq, F), np.uint32), np.zeros((nq, F), np.float32), np.zeros(nq, np.uint32)]
+        m = None if mask is None else np.ascontiguousarray(mask, dtype=np.uint32)
+        args = _lib.BvSearchArgs(queries=_ptr(qs), nq=nq, k=k, fetch=F, rerank=int(rerank),
+                                 mask=_ptr(m), mask_words=0 if m is None else m.size,
+                                 out_rows=_ptr(o[0]), out_scores=_ptr(o[1]), out_counts=_ptr(o[2]),
+                                 cand_rows=_ptr(o[3]), cand_scores=_ptr(o[4]), cand_counts=_ptr(o[5]))
+        _lib.check(self._L.bv_search(self._h, C.byref(args)))
+        return tuple(o)
+
+    def search_device(self, q_ptr: int, nq: int, k: int, fetch: int, rerank: bool,
+                      out_rows_ptr: int, out_scores_ptr: int, out_counts_ptr: int,
+                      mask_ptr: int = 0, mask_words: int = 0, stream: int = 0) -> None:
+        """Device-pointer search enqueued on `stream` (no host synchronisation)."""
+        args = _lib.BvSearchArgs(queries=q_ptr, nq=nq, k=k, fetch=max(fetch, k), rerank=int(rerank),
+                                 mask=mask_ptr or None, mask_words=mask_words, out_rows=out_rows_ptr,
+                                 out_scores=out_scores_ptr, out_counts=out_counts_ptr)
+        _lib.check(self._L.bv_search_async(self._h, C.byref(args), C.c_void_p(stream)))
+
+    def query_rows_exact(self, q: np.ndarray, rows: np.ndarray, k: int) -> list[FlatHit]:
+        """index.ts:445-464 on the GPU (rows <= 4096)."""
+        q = np.ascontiguousarray(q, dtype=np.float32)
+        rows = np.ascontiguousarray(rows, dtype=np.uint32)
+        ro = np.zeros(max(k, 1), np.uint32)
+        so = np.zeros(max(k, 1), np.float32)
+        n = C.c_uint32()
+        _lib.check(self._L.bv_query_rows_exact(self._h, _ptr(q), _ptr(rows), rows.size, k, _ptr(ro),
+                                               _ptr(so), C.byref(n)))
+        return [FlatHit(int(ro[i]), float(so[i])) for i in range(n.value)]
+
+    def export_codes(self, row0: int = 0, count: int | None = None):
+        count = self.size - row0 if count is None else count
+        wpr = {8: 4, 4: 8, 1: 32}[self.bits]
+        P = 4
+        while P < self.dim:
+            P <<= 1
+        words = np.zeros((count, P // wpr), np.uint32)
+        scales = np.zeros(count, np.float32)
+        _lib.check(self._L.bv_export_codes(self._h, row0, count, _ptr(words), _ptr(scales)))
+        return words, scales
+
+    def stats(self) -> dict:
+        s = _lib.BvStats()
+        _lib.check(self._L.bv_get_stats(self._h, C.byref(s)))
+        return {f: getattr(s, f) for f, _ in s._fields_}
+
+    def last_launches(self) -> int:
+        n = C.c_uint32()
+        _lib.check(self._L.bv_launches_last_search(self._h, C.byref(n)))
+        return int(n.value)
+
+    def destroy(self) -> None:
+        if getattr(self, "_h", None):
+            self._L.bv_destroy(self._h)
+            self._h = None
+
+    def __del__(self):  # pragma: no cover - best effort
+        try:
+            self.destroy()
+        except Exception:
+            pass
+
+
+@dataclass
+class _Entry:
+    id: str
+    row: int
+    metadata: Mapping[str, Any] | None = None
+
+
+@dataclass
+class _Store:
+    """src/store/store.ts: id<->row map, tombstones, metadata columns."""
+
+    dimension: int
+    metric: str
+    normalize: bool
+    by_id: dict = field(default_factory=dict)
+    by_row: list = field(default_factory=list)
+    deleted: set = field(default_factory=set)
+    columns: FilterColumns = field(default_factory=FilterColumns)
+
+
+class BrowserVec:
+    """The quantized flat branch of src/index.ts over AddonQuantIndex."""
+
+    def __init__(self, dimension: int, metric: str = "cosine", normalize: bool | None = None,
+                 quant_bits: int = 8, quant: Mapping[str, Any] | None = None, scoring: str = "asym",
+                 device: int = 0):
+        if not isinstance(dimension, int) or dimension <= 0:
+            raise ValueError(f"dimension must be a positive integer, got {dimension}")
+        quant = dict(quant or {})
+        if quant_bits not in (1, 4, 8):
+            raise ValueError(f"quantBits {quant_bits} not supported on this path (1, 4, 8)")
+        self.store = _Store(dimension, metric, metric == "cosine" if normalize is None else normalize)
+        self.quant_bits = quant_bits
+        self.rerank_factor = int(quant.get("rerankFactor", default_rerank_factor(quant_bits)))
+        self.index = AddonQuantIndex(dimension, quant.get("seed", DEFAULT_SEED), quant.get("rounds", 2),
+                                     quant_bits, scoring, device, metric)
+        self.last_query_ms: float | None = None
+        self.last_query_gpu_ms: float | None = None
+
+    @classmethod
+    def create(cls, config: Mapping[str, Any]) -> "BrowserVec":
+        """BrowserVec.create (src/index.ts:232-263), quantized flat stores only."""
+        return cls(config["dimension"], config.get("metric", "cosine"), config.get("normalize"),
+                   config.get("quantBits", 8), config.get("quant"), config.get("scoring", "asym"),
+                   config.get("device", 0))
+
+    # ---- ingest -----------------------------------------------------------
+    def add_batch(self, records: Sequence[Mapping[str, Any]]) -> None:
+        """src/index.ts:293-305"""
+        if not records:
+            return
+        d = self.store.dimension
+        vecs = np.zeros((len(records), d), np.float32)
+        metas = []
+        for i, r in enumerate(records):
+            v = np.asarray(r["vector"], np.float32)
+            if v.size != d:
+                raise ValueError(f"vector dim {v.size} != store dim {d}")
+            if r["id"] in self.store.by_id:
+                raise ValueError(f"duplicate id: {r['id']}")
+            vecs[i] = v
+            row = len(self.store.by_row)
+            e = _Entry(r["id"], row, r.get("metadata"))
+            self.store.by_id[r["id"]] = e
+            self.store.by_row.append(e)
+            metas.append(r.get("metadata"))
+        if self.store.normalize:
+            vecs = normalize_rows(vecs)
+        self.store.columns.append(metas)
+        self.index.append(vecs, len(records))
+
+    def add(self, record: Mapping[str, Any]) -> None:
+        self.add_batch([record])
+
+    def add_arrays(self, vectors: np.ndarray, ids: Sequence[str] | None = None,
+                   columns: Mapping[str, np.ndarray] | None = None,
+                   dictionaries: Mapping[str, list] | None = None) -> None:
+        """Bulk ingest of prepared arrays (rows normalized like store.prepare)."""
+        vectors = np.ascontiguousarray(vectors, np.float32)
+        n = vectors.shape[0]
+        base = len(self.store.by_row)
+        for i in range(n):
+            rid = ids[i] if ids is not None else f"v{base + i}"
+            e = _Entry(rid, base + i, None)
+            self.store.by_id[rid] = e
+            self.store.by_row.append(e)
+        if self.store.normalize:
+            vectors = normalize_rows(vectors)
+        if columns:
+            self.store.columns.append_columns(n, columns, dictionaries)
+        else:
+            self.store.columns.append([None] * n)
+        self.index.append(vectors, n)
+
+    def delete(self, id: str) -> bool:
+        e = self.store.by_id.pop(id, None)
+        if e is None:
+            return False
+        self.store.deleted.add(e.row)
+        return True
+
+    @property
+    def count(self) -> int:
+        return len(self.store.by_id)
+
+    # ---- query ------------------------------------------------------------
+    def _prep_query(self, query) -> np.ndarray:
+        q = np.asarray(query, np.float32).reshape(-1).copy()
+        if q.size != self.store.dimension:
+            raise ValueError(f"query dim {q.size} != store dim {self.store.dimension}")
+        if self.store.normalize:
+            q = normalize_rows(q[None, :])[0]
+        return q
+
+    def _meta_of(self, row: int):
+        return self.store.by_row[row].metadata
+
+    def _filter_rows(self, flt, predicate) -> np.ndarray:
+        """Rows (not deleted) matching the filter: src/index.ts:372-386."""
+        rows_total = len(self.store.by_row)
+        try:
+            match = self.store.columns.match(flt)
+        except ValueError:
+            raise
+        if self.store.deleted:
+            match[np.fromiter(self.store.deleted, np.int64)] = False
+        return np.flatnonzero(match[:rows_total]).astype(np.uint32)
+
+    def query(self, query, k: int = 10, filter: Mapping[str, Any] | None = None,
+              rerank: bool | None = None) -> list[QueryResult]:
+        """src/index.ts:343-436 (quantized branch)."""
+        import time
+
+        q = self._prep_query(query)
+        predicate = compile_filter(filter) if filter else None
+        mask = None
+        if predicate is not None:
+            match_rows = self._filter_rows(filter, predicate)
+            if match_rows.size == 0:
+                return []
+            if match_rows.size <= FILTER_CPU_SCAN_MAX:
+                return self._query_rows_exact(q, match_rows, k)
+            bits = np.zeros(len(self.store.by_row), bool)
+            bits[match_rows] = True
+            mask = pack_mask(bits)
+        deleted = len(self.store.deleted)
+        total = self.index.size
+        k_eff = min(total, k) if mask is not None else min(total, k + deleted)
+        if k_eff <= 0:
+            return []
+        do_rerank = rerank if rerank is not None else self.rerank_factor > 1
+        fetch = min(total, max(k_eff, k_eff * self.rerank_factor)) if do_rerank else k_eff
+        t0 = time.perf_counter()
+        hits = self.index.search(q[None, :], k_eff, fetch, rerank=do_rerank, mask=mask)[0]
+        self.last_query_ms = (time.perf_counter() - t0) * 1e3
+        self.last_query_gpu_ms = min(self.index.stats()["last_query_gpu_ms"], self.last_query_ms)
+        return self._map_hits(hits, k, predicate)
+
+    def _map_hits(self, hits, k, predicate=None) -> list[QueryResult]:
+        out = []
+        for h in hits:
+            if self.store.deleted and h.row in self.store.deleted:
+                continue
+            e = self.store.by_row[h.row]
+            if predicate is not None and not predicate(e.metadata):
+                continue
+            out.append(QueryResult(e.id, h.score, e.metadata))
+            if len(out) == k:
+                break
+        return out
+
+    def _query_rows_exact(self, q, rows, k) -> list[QueryResult]:
+        """src/index.ts:445-464"""
+        hits = self.index.query_rows_exact(q, rows, k)
+        return [QueryResult(self.store.by_row[h.row].id, h.score, self.store.by_row[h.row].metadata)
+                for h in hits]
+
+    def query_batch(self, queries, k: int = 10, filter: Mapping[str, Any] | None = None,
+                    rerank: bool | None = None) -> list[list[QueryResult]]:
+        """src/index.ts:473-517, with the re-rank the batched reference branch lacks."""
+        queries = list(queries) if not isinstance(queries, np.ndarray) else queries
+        if len(queries) == 0:
+            return []
+        if filter:
+            return [self.query(q, k, filter, rerank) for q in queries]
+        qs = np.stack([self._prep_query(q) for q in queries])
+        deleted = len(self.store.deleted)
+        total = self.index.size
+        k_eff = min(total, k + deleted)
+        if k_eff <= 0:
+            return [[] for _ in range(qs.shape[0])]
+        do_rerank = rerank if rerank is not None else self.rerank_factor > 1
+        fetch = min(total, max(k_eff, k_eff * self.rerank_factor)) if do_rerank else k_eff
+        batch = self.index.search(qs, k_eff, fetch, rerank=do_rerank)
+        return [self._map_hits(h, k) for h in batch]
+
+    def stats(self) -> dict:
+        """src/index.ts:702-750 (fields this path produces)."""
+        s = {"count": self.count, "dimension": self.store.dimension, "metric": self.store.metric,
+             "device": "cuda", "quantBits": self.quant_bits}
+        if self.store.deleted:
+            s["deleted"] = len(self.store.deleted)
+        if self.last_query_ms is not None:
+            s["lastQueryMs"] = self.last_query_ms
+            s["lastQueryGpuMs"] = self.last_query_gpu_ms
+            s["lastQueryCpuMs"] = self.last_query_ms - (self.last_query_gpu_ms or 0.0)
+        s["ingest"] = self.index.ingest_mode
+        return s
+
+    def destroy(self) -> None:
+        self.index.destroy()

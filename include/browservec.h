@@ -1,0 +1,159 @@
+/*
+ * browservec.h -- C ABI of libbvcuda, the B200 (sm_100a) quantized flat-scan
+ * engine behind BrowserVec's VectorIndex seam.
+ *
+ * The reference (sharma-open-source/browservec, TypeScript) runs this path as
+ * WebGPU dispatches inside QuantIndex (src/index/quant.ts).  A host that
+ * binds this library (a Node N-API addon for the TypeScript host, ctypes for
+ * the Python host in browservec_b200/) swaps `new QuantIndex(...)` in
+ * buildIndex (src/index.ts:134-140) for an index object backed by these calls.
+ * Each entry point names the reference interface it replaces.
+ *
+ * Conventions: every function returns a bv_status (0 = OK); on failure
+ * bv_last_error() returns the message (thread-local), using the reference's
+ * wording where the reference has one.  Pointers are plain host or device
+ * addresses as documented per call; sizes are element counts.  Calls on one
+ * index must not run concurrently (the reference serializes them the same
+ * way: appends are awaited in order, src/index/flat.ts:32-35).
+ */
+#ifndef BROWSERVEC_H
+#define BROWSERVEC_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define BV_API __attribute__((visibility("default")))
+#else
+#define BV_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum bv_status {
+  BV_OK = 0,
+  BV_ERR_INVALID = 1,      /* bad argument (message says which) */
+  BV_ERR_UNSUPPORTED = 2,  /* valid request this build does not serve */
+  BV_ERR_CUDA = 3,         /* CUDA runtime error */
+  BV_ERR_DEVICE_LOST = 4,  /* sticky device error: 'GPU device lost; re-create the store' */
+  BV_ERR_TIMEOUT = 5,      /* a kernel wait ran out of budget and aborted */
+  BV_ERR_NOMEM = 6
+} bv_status;
+
+/* Scoring arithmetic of the quantized scan.
+ *  BV_SCORE_ASYM    fp32 rotated query x integer codes, the reference's own
+ *                   asymmetric kernels (distanceQ8.ts:56-66, distanceQ4.ts:44-62,
+ *                   distanceQ1.ts:44-66) in a fixed canonical order;
+ *  BV_SCORE_INT     int8-coded query (codec.ts:132-154 applied to the rotated
+ *                   query) x codes, exact integer dot: dp4a for int8/int4,
+ *                   bit-plane popc for 1-bit;
+ *  BV_SCORE_HAMMING 1-bit corpus only: sign-bit query, xor + popc. */
+typedef enum bv_scoring { BV_SCORE_ASYM = 0, BV_SCORE_INT = 1, BV_SCORE_HAMMING = 2 } bv_scoring;
+
+typedef enum bv_metric { BV_METRIC_COSINE = 0, BV_METRIC_DOT = 1 } bv_metric;
+
+/* BrowserVecConfig / QuantConfig subset that reaches the index
+ * (src/types.ts:9-128; buildIndex src/index.ts:105-142). */
+typedef struct bv_config {
+  uint32_t dim;           /* dimension (any positive int; padded to pow2 >= 4) */
+  uint32_t bits;          /* quantBits: 8, 4 or 1 */
+  uint32_t metric;        /* bv_metric; l2 is rejected like index.ts:135-137 */
+  uint32_t seed;          /* QuantConfig.seed, default 0x9e3779b9 (index.ts:71) */
+  uint32_t rounds;        /* QuantConfig.rounds, default 2 */
+  uint32_t scoring;       /* bv_scoring */
+  int32_t device;         /* CUDA device ordinal */
+  uint32_t row_base;      /* global row id of this shard's row 0 (row-sharded corpora) */
+} bv_config;
+
+typedef struct bv_index bv_index;
+
+/* Replaces `new QuantIndex(ctx, dim, seed, rounds, bits)` (src/index/quant.ts:43-88). */
+BV_API int bv_create(const bv_config* cfg, bv_index** out);
+
+/* Replaces QuantIndex.destroy (src/index/quant.ts:247-257). */
+BV_API int bv_destroy(bv_index* idx);
+
+/* Thread-local message of the last failed call. */
+BV_API const char* bv_last_error(void);
+
+/* QuantIndex.append (src/index/quant.ts:129-141): `rows` are `count` host
+ * fp32 vectors (count*dim floats), already prepared by Store.prepare
+ * (normalized for cosine, src/store/store.ts:163-170).  The library keeps the
+ * fp32 originals on the device for the exact re-rank and encodes the codes on
+ * the GPU with the reference encoder's arithmetic (src/quant/encode.ts:64-78). */
+BV_API int bv_append(bv_index* idx, const float* rows, uint64_t count);
+
+/* Same with device-resident rows, stream-ordered on `stream` (cudaStream_t). */
+BV_API int bv_append_device(bv_index* idx, const float* rows_dev, uint64_t count, void* stream);
+
+/* QuantIndex.size (src/index/quant.ts:90-92). */
+BV_API int bv_size(const bv_index* idx, uint64_t* rows);
+
+/* One search request: queries, k, the candidate pool and the optional mask.
+ * queries: nq*dim fp32 (normalized for cosine, src/index.ts:349).
+ * fetch:   F approximate candidates per query, min(total, max(k, k*rf))
+ *          (src/index.ts:414-417); 0 means k.
+ * rerank:  1 = exact fp32 re-rank of the F candidates (src/index.ts:583-594)
+ *          then top k; 0 = the approximate top k.
+ * mask:    optional 1 bit per row, bit r of mask[r>>5] set = row r passes
+ *          (src/index/scoreMask.ts:66-92); mask_words must cover the rows.
+ * Results per query q: out_rows/out_scores[q*k .. q*k+out_counts[q]), sorted
+ * by score descending, ties by lower row.  cand_* (optional) receive the F
+ * approximate candidates with their quantized scores. */
+typedef struct bv_search_args {
+  const float* queries;
+  uint32_t nq;
+  uint32_t k;
+  uint32_t fetch;
+  int32_t rerank;
+  const uint32_t* mask;
+  uint64_t mask_words;
+  uint32_t* out_rows;
+  float* out_scores;
+  uint32_t* out_counts;
+  uint32_t* cand_rows;
+  float* cand_scores;
+  uint32_t* cand_counts;
+} bv_search_args;
+
+/* QuantIndex.query / queryMasked (src/index/quant.ts:165-245) plus the
+ * re-rank BrowserVec.query applies (src/index.ts:414-419), and the batched
+ * form BrowserVec.queryBatch lacks for quantized stores (src/index.ts:473-481).
+ * All pointers are HOST memory; the call returns when results are written. */
+BV_API int bv_search(bv_index* idx, const bv_search_args* args);
+
+/* Same with DEVICE pointers, enqueued on `stream` (cudaStream_t, NULL = the
+ * index's own stream) without a host synchronisation. */
+BV_API int bv_search_async(bv_index* idx, const bv_search_args* args, void* stream);
+
+/* BrowserVec.queryRowsExact (src/index.ts:445-464): exact f64-accumulated dot
+ * over an explicit list of rows (host pointers), top k.  Used for filters that
+ * match at most FILTER_CPU_SCAN_MAX = 4096 rows (src/index.ts:76, :388). */
+BV_API int bv_query_rows_exact(bv_index* idx, const float* query, const uint32_t* rows, uint32_t nrows,
+                        uint32_t k, uint32_t* out_rows, float* out_scores, uint32_t* out_count);
+
+/* Copy `count` rows of codes (count*wordsPerRow u32) and scales to host
+ * memory, starting at row `row0` (for parity checks; the reference exposes
+ * the same data through BatchEncoder.encode, src/quant/encode.ts:64-78). */
+BV_API int bv_export_codes(const bv_index* idx, uint64_t row0, uint64_t count, uint32_t* words,
+                    float* scales);
+
+/* Stats the index contributes to BrowserVec.stats() (src/index.ts:702-750). */
+typedef struct bv_stats {
+  uint64_t rows;
+  uint32_t dim, padded_dim, bits, words_per_row;
+  uint32_t chunks;            /* chunkCount: shards held by this index (1) */
+  float last_query_gpu_ms;    /* device time of the last bv_search (lastQueryGpuMs) */
+  uint64_t device_bytes;      /* HBM held by codes, scales and originals */
+} bv_stats;
+BV_API int bv_get_stats(const bv_index* idx, bv_stats* out);
+
+/* Kernel launches made by the last bv_search / bv_search_async /
+ * bv_query_rows_exact on this index (the scan launches once per query). */
+BV_API int bv_launches_last_search(const bv_index* idx, uint32_t* launches);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
