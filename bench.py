@@ -193,8 +193,11 @@ def main():
     out_rows = torch.zeros((N_QUERIES, K), dtype=torch.int32, device=dev)
     out_scores = torch.zeros((N_QUERIES, K), dtype=torch.float32, device=dev)
     out_counts = torch.zeros((N_QUERIES,), dtype=torch.int32, device=dev)
-    stream = torch.cuda.current_stream()
+    # One explicit stream for every launch and both timing events (never the
+    # legacy default stream, whose handle 0 would select each index's own stream).
+    stream = torch.cuda.Stream(device=dev)
     sp = stream.cuda_stream
+    assert sp != 0
 
     def step():
         for i in range(N_QUERIES):
@@ -202,6 +205,7 @@ def main():
                                               out_rows[i].data_ptr(), out_scores[i].data_ptr(),
                                               out_counts[i:].data_ptr(), stream=sp)
 
+    torch.cuda.synchronize()
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()

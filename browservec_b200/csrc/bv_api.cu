@@ -11,6 +11,7 @@
 #include "../../include/browservec.h"
 #include "bv_internal.h"
 #include "bv_scan.cuh"
+#include "bv_tail.cuh"
 
 namespace {
 
@@ -29,7 +30,7 @@ int fail(int status, const char* fmt, ...) {
 constexpr const char* kLostMsg = "GPU device lost; re-create the store";  // quant.ts:183
 constexpr uint32_t kRowAlign = 2048;      // capacity granularity (>= any scan tile)
 constexpr uint32_t kMaxFetch = 1024;      // fused single-query path: F <= 1024
-constexpr uint32_t kMaxPadded = 8192;
+constexpr uint32_t kMaxPadded = 4096;
 
 bool is_sticky(cudaError_t e) {
   switch (e) {
@@ -97,6 +98,8 @@ struct bv_index {
   int max_smem = 227 * 1024;
   float last_ms = 0.0f;
   uint32_t last_launches = 0;
+  uint64_t* d_trace = nullptr;   // optional phase-timestamp buffer (caller-owned device memory)
+  uint64_t trace_cap = 0;
   bool lost = false;
 };
 
@@ -179,17 +182,20 @@ int ensure_capacity(bv_index* idx, uint64_t need_rows) {
 
 struct Plan {
   bv::ScanShape sh;
-  uint32_t tile_rows, tile_bytes, ntiles, stages, grid, F, Fp, cap;
+  uint32_t tile_rows, tile_bytes, ntiles, stages, grid, F, Fp, capc, check_tiles;
   size_t smem;
 };
 
 int plan_scan(bv_index* idx, uint32_t F, Plan* pl) {
-  if (!bv::scan_shape(static_cast<int>(idx->bits), idx->P, &pl->sh))
+  if (!bv::scan_shape(static_cast<int>(idx->bits), static_cast<int>(idx->scoring), idx->P, &pl->sh))
     return fail(BV_ERR_UNSUPPORTED, "padded dimension %u is outside the scan's range", idx->P);
   const uint32_t R = pl->sh.R;
+  // ~32 KB tiles of at least one iteration's rows, at most 64 KB and 2048 rows
   uint32_t tr = 32768u / R;
   if (tr > 2048u) tr = 2048u;
   if (tr < pl->sh.rows_per_iter) tr = pl->sh.rows_per_iter;
+  const uint32_t tr_max = 65536u / R > 0 ? 65536u / R : 1u;
+  if (tr > tr_max) tr = tr_max;
   pl->tile_rows = tr;
   pl->tile_bytes = tr * R;
   pl->ntiles = static_cast<uint32_t>((idx->rows + tr - 1) / tr);
@@ -197,10 +203,18 @@ int plan_scan(bv_index* idx, uint32_t F, Plan* pl) {
   uint32_t fp = 32;
   while (fp < F) fp <<= 1;
   pl->Fp = fp;
-  pl->cap = 2 * fp;
+  // candidate slots: room for 2*Fp plus a tile between checks, and for the
+  // 16 warp lists of the register merge (Fp <= 256)
+  uint32_t capc = 1024;
+  while (capc < 2 * fp + tr || (fp <= 256 && capc < 16 * fp)) capc <<= 1;
+  if (capc > static_cast<uint32_t>(bv::kSelMax * bv::kConsumerThreads))
+    return fail(BV_ERR_UNSUPPORTED, "candidate buffer for fetch %u does not fit", F);
+  pl->capc = capc;
+  pl->check_tiles = (capc - 2 * fp) / tr;
+  if (pl->check_tiles < 1) pl->check_tiles = 1;
   pl->stages = 0;
   for (uint32_t st = 4; st >= 2; --st) {
-    bv::ScanSmem lay = bv::scan_smem_layout(pl->tile_bytes, tr, st, idx->P, pl->cap);
+    bv::ScanSmem lay = bv::scan_smem_layout(pl->tile_bytes, tr, st, idx->P, idx->rounds, capc);
     if (lay.total <= static_cast<uint32_t>(idx->max_smem)) {
       pl->stages = st;
       pl->smem = lay.total;
@@ -208,16 +222,22 @@ int plan_scan(bv_index* idx, uint32_t F, Plan* pl) {
     }
   }
   if (!pl->stages) return fail(BV_ERR_UNSUPPORTED, "scan tile does not fit in shared memory");
-  pl->grid = pl->ntiles < static_cast<uint32_t>(idx->num_sms) ? pl->ntiles
-                                                              : static_cast<uint32_t>(idx->num_sms);
+  // One SM stays free for the previous query's merging CTA, so a following
+  // launch finds a whole grid's worth of SMs.
+  const uint32_t sms = idx->num_sms > 1 ? static_cast<uint32_t>(idx->num_sms) - 1u : 1u;
+  pl->grid = pl->ntiles < sms ? pl->ntiles : sms;
   return BV_OK;
 }
 
 cudaError_t launch_scan(int bits, int mode, const bv::ScanShape& sh, const bv::ScanParams& p,
                         unsigned grid, size_t smem, cudaStream_t s) {
-  if (bits == 8) return bv::launch_scan8(mode, sh, p, grid, smem, s);
-  if (bits == 4) return bv::launch_scan4(mode, sh, p, grid, smem, s);
-  return bv::launch_scan1(mode, sh, p, grid, smem, s);
+  if (bits == 8) return mode == 0 ? bv::launch_scan8_asym(sh, p, grid, smem, s)
+                                  : bv::launch_scan8_int(sh, p, grid, smem, s);
+  if (bits == 4) return mode == 0 ? bv::launch_scan4_asym(sh, p, grid, smem, s)
+                                  : bv::launch_scan4_int(sh, p, grid, smem, s);
+  if (mode == 0) return bv::launch_scan1_asym(sh, p, grid, smem, s);
+  if (mode == 1) return bv::launch_scan1_int(sh, p, grid, smem, s);
+  return bv::launch_scan1_hamming(sh, p, grid, smem, s);
 }
 
 // Validate a request; returns the effective F (0 on error, message set).
@@ -243,7 +263,9 @@ int check_args(bv_index* idx, const bv_search_args* a, uint32_t* F_out) {
   return BV_OK;
 }
 
-// Enqueue every query of `a` (device pointers) on `s`.
+// Enqueue every query of `a` (device pointers) on `s`: per query the scan
+// kernel (CTA candidate lists into scratch) then the tail kernel (merge +
+// exact re-rank + outputs), chained by programmatic dependent launch.
 int enqueue_search(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStream_t s) {
   Plan pl;
   int rc = plan_scan(idx, F, &pl);
@@ -254,7 +276,6 @@ int enqueue_search(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStrea
   memset(&p, 0, sizeof(p));
   p.codes = idx->d_codes;
   p.scales = idx->d_scales;
-  p.originals = idx->d_orig;
   p.signs = idx->d_signs;
   p.mask = a->mask;
   p.nrows = idx->rows;
@@ -268,30 +289,58 @@ int enqueue_search(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStrea
   p.stages = pl.stages;
   p.F = pl.F;
   p.Fp = pl.Fp;
-  p.cap = pl.cap;
-  p.k = a->k;
-  p.rerank = a->rerank ? 1 : 0;
-  p.row_base = idx->row_base;
+  p.capc = pl.capc;
+  p.check_tiles = pl.check_tiles;
   p.partials = idx->d_partials;
-  p.ticket = idx->d_ticket;
   p.err = idx->d_err;
+  const bool tracing = idx->d_trace && idx->trace_cap >= (static_cast<uint64_t>(pl.grid) + 1) * 8;
+  p.trace = tracing ? idx->d_trace : nullptr;
+
+  bv::TailParams t;
+  memset(&t, 0, sizeof(t));
+  t.partials = idx->d_partials;
+  t.G = pl.grid;
+  t.F = pl.F;
+  t.Fp = pl.Fp;
+  t.capc = pl.capc;
+  t.k = a->k;
+  t.rerank = a->rerank ? 1 : 0;
+  t.originals = idx->d_orig;
+  t.dim = idx->dim;
+  t.row_base = idx->row_base;
+  t.err = idx->d_err;
+  t.trace = tracing ? idx->d_trace + static_cast<size_t>(pl.grid) * 8 : nullptr;
+  // gathered-row staging: as many rows of stride dim+4 as fit beside the rest
+  const uint32_t row_bytes = (idx->dim + 4) * 4;
+  const uint32_t fixed = bv::tail_smem_layout(idx->dim, pl.capc, 0).total + 256;
+  uint32_t rows_bytes = static_cast<uint32_t>(idx->max_smem) > fixed ? static_cast<uint32_t>(idx->max_smem) - fixed : 0;
+  const uint32_t want = pl.F * row_bytes;
+  if (rows_bytes > want) rows_bytes = want;
+  rows_bytes = rows_bytes / row_bytes * row_bytes;
+  if (rows_bytes < row_bytes) return fail(BV_ERR_UNSUPPORTED, "re-rank row does not fit in shared memory");
+  t.rows_bytes = rows_bytes;
+  const size_t tail_smem = bv::tail_smem_layout(idx->dim, pl.capc, rows_bytes).total;
+
   for (uint32_t q = 0; q < a->nq; ++q) {
     p.query = a->queries + static_cast<size_t>(q) * idx->dim;
-    p.out_rows = a->out_rows + static_cast<size_t>(q) * a->k;
-    p.out_scores = a->out_scores + static_cast<size_t>(q) * a->k;
-    p.out_count = a->out_counts + q;
-    p.cand_rows = a->cand_rows ? a->cand_rows + static_cast<size_t>(q) * F : nullptr;
-    p.cand_scores = a->cand_scores ? a->cand_scores + static_cast<size_t>(q) * F : nullptr;
-    p.cand_count = a->cand_counts ? a->cand_counts + q : nullptr;
-    if (p.cand_rows && (!p.cand_scores || !p.cand_count)) p.cand_rows = nullptr;
     cudaError_t e = launch_scan(static_cast<int>(idx->bits), static_cast<int>(idx->scoring), pl.sh,
                                 p, pl.grid, pl.smem, s);
     if (e == cudaErrorNotSupported)
       return fail(BV_ERR_UNSUPPORTED, "no scan kernel for bits=%u scoring=%u P=%u", idx->bits,
                   idx->scoring, idx->P);
     if (e != cudaSuccess) return cuda_fail(idx, e, "scan launch");
+    t.query = p.query;
+    t.out_rows = a->out_rows + static_cast<size_t>(q) * a->k;
+    t.out_scores = a->out_scores + static_cast<size_t>(q) * a->k;
+    t.out_count = a->out_counts + q;
+    const bool cand = a->cand_rows && a->cand_scores && a->cand_counts;
+    t.cand_rows = cand ? a->cand_rows + static_cast<size_t>(q) * F : nullptr;
+    t.cand_scores = cand ? a->cand_scores + static_cast<size_t>(q) * F : nullptr;
+    t.cand_count = cand ? a->cand_counts + q : nullptr;
+    e = bv::launch_tail(t, tail_smem, s);
+    if (e != cudaSuccess) return cuda_fail(idx, e, "tail launch");
   }
-  idx->last_launches = a->nq;
+  idx->last_launches = 2 * a->nq;
   return BV_OK;
 }
 
@@ -563,6 +612,13 @@ int bv_get_stats(const bv_index* idx, bv_stats* out) {
   out->chunks = 1;
   out->last_query_gpu_ms = idx->last_ms;
   out->device_bytes = idx->cap_rows * (idx->R + 4 + static_cast<uint64_t>(idx->dim) * 4);
+  return BV_OK;
+}
+
+int bv_set_phase_trace(bv_index* idx, uint64_t* trace_dev, uint64_t capacity) {
+  if (!idx) return fail(BV_ERR_INVALID, "null index");
+  idx->d_trace = trace_dev;
+  idx->trace_cap = trace_dev ? capacity : 0;
   return BV_OK;
 }
 

@@ -92,8 +92,216 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, u
       : "memory");
 }
 
+// Same with an L2 cache policy (createpolicy), e.g. evict-first for data read
+// once, so a streamed corpus does not flush the L2 (kernel code, scratch).
+__device__ __forceinline__ void bulk_g2s_hint(void* dst_smem, const void* src_gmem, uint32_t bytes,
+                                              uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, "
+      "[%3], %4;" ::"r"(smem_addr(dst_smem)),
+      "l"(src_gmem), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Programmatic dependent launch: let the next kernel in the stream start, and
+// wait until the previous one has completed with its memory visible.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Packed fp32 pairs (sm_100 f32x2 arithmetic): two independent lanes per op.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t r, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+// ------------------------------------------- block-wide radix select
+constexpr int kSelBins = 2048;  // 11-bit digits
+constexpr int kSelScratch = 64;  // words of `sh` the select needs
+
+// Among `total` unique nonzero keys held in registers (v[0..nv) per thread,
+// zero slots ignored) by the NT threads of named barrier `bar`, find thr such
+// that exactly min(F, total) keys are >= thr.  The bits all keys share are
+// skipped (block max/min), then 11-bit digits MSB-first with plain
+// shared-memory histograms; usually one or two passes.  hist: kSelBins words;
+// sh: kSelScratch words.  Block-collective; all threads return the same thr.
+template <int MAXK, int NT>
+__device__ __forceinline__ uint64_t block_select_threshold(const uint64_t (&v)[MAXK], int nv,
+                                                           uint32_t F, uint32_t total,
+                                                           uint32_t* hist, uint32_t* sh, int tid,
+                                                           uint32_t bar) {
+  static_assert(NT % 32 == 0 && NT / 32 <= 16 && kSelBins == 4 * NT, "4 bins per thread");
+  if (total <= F) return 1ull;
+  const int lane = tid & 31, warp = tid >> 5;
+  // common leading bits: max and min of the nonzero keys
+  uint64_t mx = 0ull, mn = ~0ull;
+#pragma unroll
+  for (int i = 0; i < MAXK; ++i)
+    if (i < nv && v[i] != 0ull) {
+      mx = v[i] > mx ? v[i] : mx;
+      mn = v[i] < mn ? v[i] : mn;
+    }
+#pragma unroll
+  for (int off = 16; off; off >>= 1) {
+    const uint64_t a = __shfl_xor_sync(0xffffffffu, mx, off);
+    const uint64_t b = __shfl_xor_sync(0xffffffffu, mn, off);
+    mx = a > mx ? a : mx;
+    mn = b < mn ? b : mn;
+  }
+  uint64_t* sh64 = reinterpret_cast<uint64_t*>(sh);
+  if (lane == 0) {
+    sh64[2 * warp] = mx;
+    sh64[2 * warp + 1] = mn;
+  }
+  named_bar_sync(bar, NT);
+  mx = 0ull;
+  mn = ~0ull;
+#pragma unroll
+  for (int w = 0; w < NT / 32; ++w) {
+    mx = sh64[2 * w] > mx ? sh64[2 * w] : mx;
+    mn = sh64[2 * w + 1] < mn ? sh64[2 * w + 1] : mn;
+  }
+  named_bar_sync(bar, NT);  // sh is reused below
+  int top = 63 - __clzll(static_cast<long long>(mx ^ mn));  // highest differing bit (mx != mn)
+  uint64_t pmask = top >= 63 ? 0ull : ~((2ull << top) - 1ull);
+  uint64_t prefix = mx & pmask;
+  uint32_t need = F;
+  for (;;) {
+    const int width = top + 1 < 11 ? top + 1 : 11;
+    const int shift = top + 1 - width;
+    const uint32_t nb = 1u << width, dmask = nb - 1u;
+    for (int i = tid; i < kSelBins; i += NT) hist[i] = 0u;
+    named_bar_sync(bar, NT);
+    // plain shared atomics: warp aggregation with match_any costs ~1000 cycles
+    // per call on sm_100a, far more than the contention it saves
+#pragma unroll
+    for (int i = 0; i < MAXK; ++i) {
+      const bool act = i < nv && v[i] != 0ull && (v[i] & pmask) == prefix;
+      if (act) atomicAdd(&hist[static_cast<uint32_t>(v[i] >> shift) & dmask], 1u);
+    }
+    named_bar_sync(bar, NT);
+    // thread t owns bins nb-1-4t .. nb-4-4t (highest first)
+    uint32_t hb[4], s = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int b = static_cast<int>(nb) - 1 - 4 * tid - j;
+      hb[j] = b >= 0 ? hist[b] : 0u;
+      s += hb[j];
+    }
+    uint32_t x = s;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, x, off);
+      if (lane >= off) x += y;
+    }
+    if (lane == 31) sh[warp] = x;
+    named_bar_sync(bar, NT);
+    uint32_t run = x - s;
+    for (int w = 0; w < warp; ++w) run += sh[w];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (run < need && run + hb[j] >= need) {
+        sh[32] = static_cast<uint32_t>(static_cast<int>(nb) - 1 - 4 * tid - j);
+        sh[33] = run;
+        sh[34] = hb[j];
+      }
+      run += hb[j];
+    }
+    named_bar_sync(bar, NT);
+    const uint32_t d = sh[32], above = sh[33], hd = sh[34];
+    prefix |= static_cast<uint64_t>(d) << shift;
+    pmask |= static_cast<uint64_t>(dmask) << shift;
+    need -= above;
+    named_bar_sync(bar, NT);  // sh and hist are rewritten by the next pass
+    if (hd == need || shift == 0) break;
+    top = shift - 1;
+  }
+  return prefix;
+}
+
+// ------------------------------------------ warp register sort / merge
+// A warp list of n = 32*E keys lives in registers, striped: element i is
+// register i/32 of lane i%32.  Bitonic networks run on shuffles (cross-lane
+// strides) and register swaps (strides >= 32): no shared memory, no barrier.
+__device__ __forceinline__ uint64_t shfl_xor64(uint64_t v, int m) {
+  return __shfl_xor_sync(0xffffffffu, v, m);
+}
+
+// One compare-exchange stage of stride j inside bitonic blocks of `size`
+// (final order descending: the lower index keeps the max in a descending block).
+template <int E>
+__device__ __forceinline__ void wreg_stage(uint64_t (&v)[E], int size, int j, int lane) {
+  if (j >= 32) {
+    const int rj = j >> 5;
+#pragma unroll
+    for (int r = 0; r < E; ++r) {
+      const int r2 = r ^ rj;
+      if (r2 > r) {
+        const int i = lane + 32 * r;
+        const bool desc = (i & size) == 0;
+        const uint64_t x = v[r], y = v[r2];
+        const uint64_t hi = x > y ? x : y, lo = x > y ? y : x;
+        v[r] = desc ? hi : lo;
+        v[r2] = desc ? lo : hi;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int r = 0; r < E; ++r) {
+      const int i = lane + 32 * r;
+      const uint64_t x = v[r], y = shfl_xor64(x, j);
+      const bool lower = (lane & j) == 0;
+      const bool desc = (i & size) == 0;
+      const uint64_t hi = x > y ? x : y, lo = x > y ? y : x;
+      v[r] = (lower == desc) ? hi : lo;
+    }
+  }
+}
+
+// Sort the warp list descending (fully unrolled: the stage indices must be
+// compile-time so the register array never spills to local memory).
+template <int E>
+__device__ __forceinline__ void wreg_sort_desc(uint64_t (&v)[E], int lane) {
+#pragma unroll
+  for (int size = 2; size <= 32 * E; size <<= 1)
+#pragma unroll
+    for (int j = size >> 1; j > 0; j >>= 1) wreg_stage<E>(v, size, j, lane);
+}
+
+// a, b: descending warp lists.  a becomes the best 32*E keys of a U b, descending.
+template <int E>
+__device__ __forceinline__ void wreg_merge_top(uint64_t (&a)[E], const uint64_t (&b)[E], int lane) {
+  // c[i] = max(a[i], b[n-1-i]) is bitonic and holds the top n
+#pragma unroll
+  for (int r = 0; r < E; ++r) {
+    const uint64_t y = __shfl_sync(0xffffffffu, b[E - 1 - r], 31 - lane);
+    a[r] = a[r] > y ? a[r] : y;
+  }
+  constexpr int n = 32 * E;
+#pragma unroll
+  for (int j = n >> 1; j > 0; j >>= 1) wreg_stage<E>(a, 2 * n, j, lane);  // size 2n: all descending
 }
 
 // --------------------------------------------------- warp sort / merge

@@ -20,16 +20,26 @@ inline uint32_t code_row_bytes(int bits, uint32_t P) {
   return bits == 8 ? P : (bits == 4 ? P / 2 : P / 8);
 }
 
-inline bool scan_shape(int bits, uint32_t P, ScanShape* s) {
+// Lane layout of one scan: the asym mode uses the canonical layout (L = min(32,
+// C) lanes per row, the order the oracle defines); the integer modes, whose
+// sums are exact in any order, use at most 8 lanes per row and up to 8 chunks
+// per lane so fewer shuffles reduce each row.
+inline bool scan_shape(int bits, int mode, uint32_t P, ScanShape* s) {
   const uint32_t R = code_row_bytes(bits, P);
-  if (R < 4 || R > 8192) return false;
+  if (R < 4 || R > 4096) return false;
   s->R = R;
   s->CB = R < 16 ? static_cast<int>(R) : 16;
   const uint32_t C = R / static_cast<uint32_t>(s->CB);
-  s->L = C < 32 ? static_cast<int>(C) : 32;
-  s->CPL = static_cast<int>(C / static_cast<uint32_t>(s->L));
-  s->U = s->CPL == 1 ? 4 : (s->CPL == 2 ? 2 : 1);
-  s->rows_per_iter = 8u * (32u / static_cast<uint32_t>(s->L)) * static_cast<uint32_t>(s->U);
+  uint32_t L;
+  if (mode == 0) {
+    L = C < 32 ? C : 32;
+  } else {
+    L = C <= 8 ? C : (C <= 64 ? 8 : C / 8);
+  }
+  s->L = static_cast<int>(L);
+  s->CPL = static_cast<int>(C / L);
+  s->U = (mode == 0 || s->CPL < 4) ? 2 : 1;
+  s->rows_per_iter = 16u * (32u / L) * static_cast<uint32_t>(s->U);
   return true;
 }
 
@@ -37,12 +47,23 @@ cudaError_t launch_encode(int bits, const float* rows, uint64_t count, uint32_t 
                           const float* signs, uint32_t rounds, uint8_t* codes, float* scales,
                           uint32_t R, cudaStream_t stream);
 
-cudaError_t launch_scan8(int mode, const ScanShape& sh, const ScanParams& p, unsigned grid,
-                         size_t smem, cudaStream_t stream);
-cudaError_t launch_scan4(int mode, const ScanShape& sh, const ScanParams& p, unsigned grid,
-                         size_t smem, cudaStream_t stream);
-cudaError_t launch_scan1(int mode, const ScanShape& sh, const ScanParams& p, unsigned grid,
-                         size_t smem, cudaStream_t stream);
+cudaError_t launch_scan8_asym(const ScanShape& sh, const ScanParams& p, unsigned grid, size_t smem,
+                              cudaStream_t stream);
+cudaError_t launch_scan8_int(const ScanShape& sh, const ScanParams& p, unsigned grid, size_t smem,
+                             cudaStream_t stream);
+cudaError_t launch_scan4_asym(const ScanShape& sh, const ScanParams& p, unsigned grid, size_t smem,
+                              cudaStream_t stream);
+cudaError_t launch_scan4_int(const ScanShape& sh, const ScanParams& p, unsigned grid, size_t smem,
+                             cudaStream_t stream);
+cudaError_t launch_scan1_asym(const ScanShape& sh, const ScanParams& p, unsigned grid, size_t smem,
+                              cudaStream_t stream);
+cudaError_t launch_scan1_int(const ScanShape& sh, const ScanParams& p, unsigned grid, size_t smem,
+                             cudaStream_t stream);
+cudaError_t launch_scan1_hamming(const ScanShape& sh, const ScanParams& p, unsigned grid, size_t smem,
+                                 cudaStream_t stream);
+
+struct TailParams;
+cudaError_t launch_tail(const TailParams& p, size_t smem, cudaStream_t stream);
 
 cudaError_t launch_exact_rows(const float* originals, uint32_t dim, const float* query,
                               const uint32_t* rows, uint32_t nrows, uint32_t k, uint32_t row_base,

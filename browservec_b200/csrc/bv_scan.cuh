@@ -1,26 +1,31 @@
 // bv_scan.cuh -- the fused single-query quantized flat scan for sm_100a.
 //
-// One launch answers one query against one corpus shard:
-//   1. every CTA rotates the query itself (random-sign diagonal + FWHT, the
-//      operation order of rotator.ts:83-92; warp-shuffle stages for len < 32,
-//      shared-memory stages above) while its producer warp already streams
-//      code tiles with 1-D bulk copies (TMA engine) into a 2..4-stage ring;
-//   2. 8 consumer warps score the rows of each tile in the canonical lane
-//      order (asym: fmaf chains over exact integer codes, the restatement of
-//      distanceQ8.ts:56-66 / distanceQ4.ts:44-62 / distanceQ1.ts:44-66; int:
-//      dp4a / bit-plane popc over an int8-coded query; hamming: xor+popc),
-//      drop rows whose mask bit is clear (scoreMask.ts:66-92 and mask.ts:20-35:
-//      a masked row can never win a slot) and offer (score,row) keys to a
-//      per-warp top-F buffer;
-//   3. the warps' lists merge into one sorted CTA list in global scratch; the
-//      last CTA to finish (atomic ticket) merges all CTA lists (the device form
-//      of gpuTopk.ts:160-189), re-ranks the F candidates with the exact f64 dot
-//      of store.ts:114-130 over the fp32 originals and keeps the best k
-//      (index.ts:583-594), under the (score desc, row asc) order.
+// One launch scores one query against one corpus shard:
+//   1. the producer warp's first 1-D bulk copies (TMA engine) bring the query
+//      and the rotation signs into shared memory, then it streams code tiles
+//      into a 2..4-stage ring;
+//   2. meanwhile the 16 consumer warps rotate the query (random-sign diagonal
+//      + FWHT in the operation order of rotator.ts:83-92: warp-shuffle stages
+//      for len < 32, shared-memory stages above) and, for the integer modes,
+//      code it with the reference int8 codec (codec.ts:132-154);
+//   3. the consumers score every row of every tile in the canonical lane order
+//      (asym: exact integer codes x fp32 query in fmaf chains, two rows per
+//      f32x2 instruction -- the restatement of distanceQ8.ts:56-66,
+//      distanceQ4.ts:44-62, distanceQ1.ts:44-66; int: dp4a / bit-plane popc;
+//      hamming: xor + popc), drop rows whose mask bit is clear (a masked row
+//      can never win a slot, scoreMask.ts:66-92 + mask.ts:20-35) and append
+//      the (score,row) keys above the CTA threshold to a shared candidate
+//      buffer, compacted by block radix select when it fills;
+//   4. each CTA writes its best F keys (sorted when F <= 256) to global
+//      scratch; the tail kernel (bv_tail.cu) merges them and re-ranks.
+// Launches chain with programmatic dependent launch: a CTA lets the next
+// kernel start once its rows are scored, and waits for the previous kernel
+// (the previous query's tail) to finish before it writes the shared scratch.
 // Every wait is bounded; a timeout raises a flag in `err` instead of hanging.
 #pragma once
 
 #include <cstdint>
+#include <type_traits>
 
 #include "bv_device.cuh"
 
@@ -28,15 +33,16 @@ namespace bv {
 
 enum ScoreMode : int { kAsym = 0, kInt = 1, kHamming = 2 };
 
-constexpr int kConsumerWarps = 8;
+constexpr int kConsumerWarps = 16;
 constexpr int kScanThreads = (kConsumerWarps + 1) * 32;
-constexpr uint32_t kConsumerThreads = kConsumerWarps * 32;
-constexpr uint32_t kBarConsumers = 1;  // named barrier id for the consumer warps
+constexpr int kConsumerThreads = kConsumerWarps * 32;
+constexpr uint32_t kBarConsumers = 1;  // named barrier id of the consumer warps
+constexpr int kSelMax = 8;             // keys per consumer thread in a CTA selection
+constexpr int kMergeMax = 24;          // keys per consumer thread in the last-CTA merge
 
 struct ScanParams {
   const uint8_t* codes;      // rows x R bytes (capacity padded to whole tiles)
   const float* scales;       // one per row (padded like codes)
-  const float* originals;    // rows x dim fp32 (normalized, store.ts:163-170)
   const float* signs;        // rounds x P, pre-scaled (rotator.ts:66-80)
   const float* query;        // dim fp32, normalized by the host (store.ts:209-217)
   const uint32_t* mask;      // optional: bit r of mask[r>>5] = row r passes
@@ -47,30 +53,34 @@ struct ScanParams {
   uint32_t tile_bytes;       // tile_rows * R
   uint32_t ntiles;
   uint32_t stages;           // 2..4
-  uint32_t F, Fp, cap;       // fetch, pow2 pad (>= 32), per-warp buffer slots (2*Fp)
-  uint32_t k;
-  int rerank;
-  uint32_t row_base;         // global row of this shard's row 0
+  uint32_t F, Fp;            // fetch, pow2 >= max(F, 32)
+  uint32_t capc;             // CTA candidate buffer slots (pow2, <= kSelMax * 512, >= 2*Fp)
+  uint32_t check_tiles;      // tiles between candidate-buffer checks
   uint64_t* partials;        // gridDim.x x Fp keys
-  uint32_t* ticket;          // last-CTA ticket (self-resetting)
   uint32_t* err;             // error flags
-  uint32_t* out_rows;        // k
-  float* out_scores;         // k
-  uint32_t* out_count;       // 1
-  uint32_t* cand_rows;       // optional: F approximate candidates
-  float* cand_scores;
-  uint32_t* cand_count;
+  uint64_t* trace;           // optional: per-CTA phase timestamps (globaltimer ns)
 };
+
+// Phase timestamps: CTA b writes trace[b*8 + phase].
+enum : int { kTrEntry = 0, kTrRotated = 1, kTrScanned = 2, kTrCtaMerged = 3 };
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 // Shared-memory carve-up (host and device agree on it).
 struct ScanSmem {
-  uint32_t codes_off, scales_off, bars_off, rq_off, qb_off, bufs_off, misc_off, total;
+  uint32_t codes_off, scales_off, bars_off, q_off, signs_off, qb_off, cand_off, hist_off, misc_off,
+      total;
 };
 
 __host__ __device__ inline uint32_t align_up(uint32_t x, uint32_t a) { return (x + a - 1) / a * a; }
 
 __host__ __device__ inline ScanSmem scan_smem_layout(uint32_t tile_bytes, uint32_t tile_rows,
-                                                     uint32_t stages, uint32_t P, uint32_t cap) {
+                                                     uint32_t stages, uint32_t P, uint32_t rounds,
+                                                     uint32_t capc) {
   ScanSmem s;
   uint32_t o = 0;
   s.codes_off = o;
@@ -78,31 +88,38 @@ __host__ __device__ inline ScanSmem scan_smem_layout(uint32_t tile_bytes, uint32
   s.scales_off = o;
   o = align_up(o + stages * tile_rows * 4, 128);
   s.bars_off = o;
-  o = align_up(o + 2 * stages * 8, 16);
-  s.rq_off = o;
+  o = align_up(o + (2 * stages + 1) * 8, 16);
+  s.q_off = o;
   o = align_up(o + P * 4, 16);
+  s.signs_off = o;
+  o = align_up(o + rounds * P * 4, 16);
   s.qb_off = o;
   o = align_up(o + P, 16);
-  s.bufs_off = o;
-  o = align_up(o + kConsumerWarps * cap * 8, 16);
+  s.cand_off = o;
+  o = align_up(o + capc * 8, 16);
+  s.hist_off = o;
+  o = align_up(o + kSelBins * 4, 16);
   s.misc_off = o;
-  o = align_up(o + 64, 16);
+  o = align_up(o + 128 * 4, 16);
   s.total = o;
   return s;
 }
 
+// misc word slots
+enum : int { kMiscCount = 0, kMiscNc = 5, kMiscRed = 16, kMiscSel = 64 };
+
 // ------------------------------------------------------------ code -> value
-// int8 byte of word xb (= x ^ 0x80808080) as an exact float: the biased byte
-// u = b + 128 goes into a float's low mantissa (2^23 + u); subtract 2^23 + 128.
-__device__ __forceinline__ float s8_to_f32(uint32_t xb, int byte) {
-  uint32_t v = __byte_perm(xb, 0x4B00u, 0x5440u | static_cast<uint32_t>(byte));
-  return __fsub_rn(__uint_as_float(v), 8388736.0f);
+// int8 byte of word xb (= x ^ 0x80808080) as a biased float 2^23 + (b + 128):
+// PRMT places the byte in the low mantissa; subtracting 2^23 + 128 gives b.
+__device__ __forceinline__ float s8_biased(uint32_t xb, int byte) {
+  return __uint_as_float(__byte_perm(xb, 0x4B00u, 0x5440u | static_cast<uint32_t>(byte)));
 }
-// int4 nibble of word xn (= x ^ 0x88888888) as an exact float.
-__device__ __forceinline__ float s4_to_f32(uint32_t xn, int nib) {
-  uint32_t v = ((xn >> (4 * nib)) & 0xFu) | 0x4B000000u;
-  return __fsub_rn(__uint_as_float(v), 8388616.0f);
+// int4 nibble of word xn (= x ^ 0x88888888) as a biased float 2^23 + (n + 8).
+__device__ __forceinline__ float s4_biased(uint32_t xn, int nib) {
+  return __uint_as_float(((xn >> (4 * nib)) & 0xFu) | 0x4B000000u);
 }
+constexpr float kBias8 = 8388736.0f;  // 2^23 + 128
+constexpr float kBias4 = 8388616.0f;  // 2^23 + 8
 
 __device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
   int d;
@@ -136,47 +153,45 @@ __device__ __forceinline__ Chunk<W> lds_chunk(const uint8_t* p) {
 }
 
 // ----------------------------------------------------------- query prologue
-// Rotate the query into rq[0..P) (rotator.ts:83-92) with the 256 consumer
-// threads: pad, then per round a sign multiply and the FWHT stages in order
-// len = 1, 2, ..., P/2 (stages below 32 by warp shuffles).
-__device__ __forceinline__ void rotate_query(const ScanParams& p, float* rq, int ctid) {
-  const uint32_t P = p.P;
+// Rotate q[0..P) in place (rotator.ts:83-92): per round a sign multiply and
+// the FWHT stages len = 1, 2, ..., P/2 in order.  Consumer-collective.
+__device__ __forceinline__ void rotate_query(float* q, const float* signs, uint32_t P,
+                                             uint32_t rounds, int ctid) {
   const int lane = ctid & 31, warp = ctid >> 5;
-  for (uint32_t i = ctid; i < P; i += kConsumerThreads) rq[i] = i < p.dim ? p.query[i] : 0.0f;
-  named_bar_sync(kBarConsumers, kConsumerThreads);
-  for (uint32_t r = 0; r < p.rounds; ++r) {
-    const float* s = p.signs + static_cast<size_t>(r) * P;
+  for (uint32_t r = 0; r < rounds; ++r) {
+    const float* s = signs + static_cast<size_t>(r) * P;
     if (P >= 32) {
-      // sign multiply fused into the shuffle stages: each warp owns 32-element blocks
       for (uint32_t blk = warp; blk < P / 32; blk += kConsumerWarps) {
-        uint32_t i = blk * 32 + lane;
-        float x = __fmul_rn(rq[i], s[i]);
+        const uint32_t i = blk * 32 + lane;
+        float x = __fmul_rn(q[i], s[i]);
 #pragma unroll
         for (int len = 1; len < 32; len <<= 1) {
-          float y = __shfl_xor_sync(0xffffffffu, x, len);
+          const float y = __shfl_xor_sync(0xffffffffu, x, len);
           x = (lane & len) ? __fsub_rn(y, x) : __fadd_rn(x, y);
         }
-        rq[i] = x;
+        q[i] = x;
       }
       named_bar_sync(kBarConsumers, kConsumerThreads);
-      for (uint32_t len = 32; len < P; len <<= 1) {
+      for (uint32_t lg = 5; (1u << lg) < P; ++lg) {
+        const uint32_t len = 1u << lg;
         for (uint32_t b = ctid; b < P / 2; b += kConsumerThreads) {
-          uint32_t j = (b / len) * 2 * len + (b % len);
-          float x = rq[j], y = rq[j + len];
-          rq[j] = __fadd_rn(x, y);
-          rq[j + len] = __fsub_rn(x, y);
+          const uint32_t j = ((b >> lg) << (lg + 1)) | (b & (len - 1));
+          const float x = q[j], y = q[j + len];
+          q[j] = __fadd_rn(x, y);
+          q[j + len] = __fsub_rn(x, y);
         }
         named_bar_sync(kBarConsumers, kConsumerThreads);
       }
     } else {
-      for (uint32_t i = ctid; i < P; i += kConsumerThreads) rq[i] = __fmul_rn(rq[i], s[i]);
+      for (uint32_t i = ctid; i < P; i += kConsumerThreads) q[i] = __fmul_rn(q[i], s[i]);
       named_bar_sync(kBarConsumers, kConsumerThreads);
-      for (uint32_t len = 1; len < P; len <<= 1) {
+      for (uint32_t lg = 0; (1u << lg) < P; ++lg) {
+        const uint32_t len = 1u << lg;
         for (uint32_t b = ctid; b < P / 2; b += kConsumerThreads) {
-          uint32_t j = (b / len) * 2 * len + (b % len);
-          float x = rq[j], y = rq[j + len];
-          rq[j] = __fadd_rn(x, y);
-          rq[j + len] = __fsub_rn(x, y);
+          const uint32_t j = ((b >> lg) << (lg + 1)) | (b & (len - 1));
+          const float x = q[j], y = q[j + len];
+          q[j] = __fadd_rn(x, y);
+          q[j + len] = __fsub_rn(x, y);
         }
         named_bar_sync(kBarConsumers, kConsumerThreads);
       }
@@ -194,7 +209,7 @@ __device__ __forceinline__ double js_round(double x) {
 // int8 code of the rotated query with the corpus codec (codec.ts:132-154):
 // qb[i] in [-127,127]; returns the f32 scale (max |rq|, or 1).
 __device__ __forceinline__ float quantize_query8(const float* rq, int8_t* qb, uint32_t P, int ctid,
-                                                 float* red /* >= 8 floats */) {
+                                                 float* red /* >= 16 floats */) {
   float m = 0.0f;
   for (uint32_t i = ctid; i < P; i += kConsumerThreads) m = fmaxf(m, fabsf(rq[i]));
 #pragma unroll
@@ -216,9 +231,182 @@ __device__ __forceinline__ float quantize_query8(const float* rq, int8_t* qb, ui
   return scale;
 }
 
+// ------------------------------------------------------------- selection
+// Append the keys of lanes with `want` to cand (warp-aggregated reservation).
+__device__ __forceinline__ void append_keys(uint64_t* cand, uint32_t* count, uint64_t key, bool want,
+                                            int lane) {
+  const unsigned m = __ballot_sync(0xffffffffu, want);
+  if (m) {
+    const int leader = __ffs(m) - 1;
+    uint32_t pos = 0;
+    if (lane == leader) pos = atomicAdd(count, static_cast<uint32_t>(__popc(m)));
+    pos = __shfl_sync(0xffffffffu, pos, leader);
+    if (want) cand[pos + __popc(m & ((1u << lane) - 1u))] = key;
+  }
+}
+
+// Keep the best F of the keys held in v[] (zero = empty slot; `total` nonzero
+// keys across the consumers): radix select, then the survivors are written to
+// cand[0..min(total,F)).  Returns the kept count.  Consumer-collective; ends
+// with a barrier.  The caller must have finished reading cand into v[].
+template <int MAXK>
+__device__ __forceinline__ uint32_t keep_best(const uint64_t (&v)[MAXK], uint32_t total, uint32_t F,
+                                              uint64_t* cand, uint32_t* hist, uint32_t* misc,
+                                              int ctid) {
+  const uint64_t thr = block_select_threshold<MAXK, kConsumerThreads>(
+      v, MAXK, F, total, hist, misc + kMiscSel, ctid, kBarConsumers);
+  if (ctid == 0) misc[kMiscCount] = 0;
+  named_bar_sync(kBarConsumers, kConsumerThreads);
+  const int lane = ctid & 31;
+#pragma unroll
+  for (int i = 0; i < MAXK; ++i) append_keys(cand, &misc[kMiscCount], v[i], v[i] != 0ull && v[i] >= thr, lane);
+  named_bar_sync(kBarConsumers, kConsumerThreads);
+  return total < F ? total : F;
+}
+
+// Bitonic sort (descending) of n = 2^m keys in shared memory, consumer-collective.
+__device__ __forceinline__ void cta_sort_desc(uint64_t* a, uint32_t n, int ctid) {
+  for (uint32_t size = 2; size <= n; size <<= 1)
+    for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
+      for (uint32_t i = ctid; i < n; i += kConsumerThreads) {
+        const uint32_t j = i ^ stride;
+        if (j > i) {
+          const uint64_t x = a[i], y = a[j];
+          const bool desc = (i & size) == 0;
+          if (desc ? (x < y) : (x > y)) {
+            a[i] = y;
+            a[j] = x;
+          }
+        }
+      }
+      named_bar_sync(kBarConsumers, kConsumerThreads);
+    }
+}
+
+// ------------------------------------------------- fast top-F (F <= 256)
+// Warp-register sorts and merges: shuffles and register swaps, barriers only
+// between the levels of the cross-warp tree.
+
+// The CTA's best Fp keys, sorted descending, into cand[0..Fp): every warp
+// sorts a slice of Fp candidates in registers, then a 4-level tree of register
+// merges through shared memory.  Requires n <= 16 * Fp <= capc.
+template <int E>
+__device__ __forceinline__ void cta_best_sorted(uint64_t* cand, uint32_t n, int ctid) {
+  constexpr int Fp = 32 * E;
+  const int lane = ctid & 31, warp = ctid >> 5;
+  uint64_t v[E];
+#pragma unroll
+  for (int r = 0; r < E; ++r) {
+    const uint32_t idx = static_cast<uint32_t>(warp * Fp + lane + 32 * r);
+    v[r] = idx < n ? cand[idx] : 0ull;
+  }
+  wreg_sort_desc<E>(v, lane);
+  named_bar_sync(kBarConsumers, kConsumerThreads);  // every slice is in registers
+#pragma unroll 1
+  for (int step = 1; step < kConsumerWarps; step <<= 1) {
+    if ((warp % (2 * step)) == step) {
+#pragma unroll
+      for (int r = 0; r < E; ++r) cand[warp * Fp + lane + 32 * r] = v[r];
+    }
+    named_bar_sync(kBarConsumers, kConsumerThreads);
+    if ((warp % (2 * step)) == 0) {
+      uint64_t b[E];
+#pragma unroll
+      for (int r = 0; r < E; ++r) b[r] = cand[(warp + step) * Fp + lane + 32 * r];
+      wreg_merge_top<E>(v, b, lane);
+    }
+  }
+  if (warp == 0) {
+#pragma unroll
+    for (int r = 0; r < E; ++r) cand[lane + 32 * r] = v[r];
+  }
+  named_bar_sync(kBarConsumers, kConsumerThreads);
+}
+
+// Last CTA: merge the G sorted CTA lists (partials, Fp keys each) into
+// out[0..Fp), descending.  Warps merge strided lists in registers (the next
+// list loads while the current one merges), then the same 4-level tree
+// through `stage` (16 * Fp keys); out may alias stage.
+template <int E>
+__device__ __forceinline__ void merge_cta_lists(const uint64_t* partials, uint32_t G, uint64_t* stage,
+                                             int ctid) {
+  constexpr int Fp = 32 * E;
+  const int lane = ctid & 31, warp = ctid >> 5;
+  uint64_t v[E], nx[E];
+#pragma unroll
+  for (int r = 0; r < E; ++r) {
+    v[r] = 0ull;
+    nx[r] = static_cast<uint32_t>(warp) < G ? __ldcg(partials + static_cast<size_t>(warp) * Fp + lane + 32 * r) : 0ull;
+  }
+#pragma unroll 1
+  for (uint32_t l = warp; l < G; l += kConsumerWarps) {
+    uint64_t cur[E];
+#pragma unroll
+    for (int r = 0; r < E; ++r) cur[r] = nx[r];
+    const uint32_t ln = l + kConsumerWarps;
+#pragma unroll
+    for (int r = 0; r < E; ++r) nx[r] = ln < G ? __ldcg(partials + static_cast<size_t>(ln) * Fp + lane + 32 * r) : 0ull;
+    wreg_merge_top<E>(v, cur, lane);
+  }
+#pragma unroll 1
+  for (int step = 1; step < kConsumerWarps; step <<= 1) {
+    if ((warp % (2 * step)) == step) {
+#pragma unroll
+      for (int r = 0; r < E; ++r) stage[warp * Fp + lane + 32 * r] = v[r];
+    }
+    named_bar_sync(kBarConsumers, kConsumerThreads);
+    if ((warp % (2 * step)) == 0) {
+      uint64_t b[E];
+#pragma unroll
+      for (int r = 0; r < E; ++r) b[r] = stage[(warp + step) * Fp + lane + 32 * r];
+      wreg_merge_top<E>(v, b, lane);
+    }
+  }
+  named_bar_sync(kBarConsumers, kConsumerThreads);  // tree reads of stage are done
+  if (warp == 0) {
+#pragma unroll
+    for (int r = 0; r < E; ++r) stage[lane + 32 * r] = v[r];
+  }
+  named_bar_sync(kBarConsumers, kConsumerThreads);
+}
+
+// Warp 0 sorts a[0..32E) descending in place (the other warps return).
+template <int E>
+__device__ __forceinline__ void warp0_sort_smem(uint64_t* a, int ctid) {
+  if ((ctid >> 5) != 0) return;
+  const int lane = ctid & 31;
+  uint64_t v[E];
+#pragma unroll
+  for (int r = 0; r < E; ++r) v[r] = a[lane + 32 * r];
+  wreg_sort_desc<E>(v, lane);
+#pragma unroll
+  for (int r = 0; r < E; ++r) a[lane + 32 * r] = v[r];
+}
+
+__device__ __forceinline__ void cta_best_sorted_dispatch(uint32_t Fp, uint64_t* cand, uint32_t n, int ctid) {
+  if (Fp == 32) cta_best_sorted<1>(cand, n, ctid);
+  else if (Fp == 64) cta_best_sorted<2>(cand, n, ctid);
+  else if (Fp == 128) cta_best_sorted<4>(cand, n, ctid);
+  else cta_best_sorted<8>(cand, n, ctid);
+}
+__device__ __forceinline__ void merge_cta_lists_dispatch(uint32_t Fp, const uint64_t* partials, uint32_t G,
+                                                         uint64_t* stage, int ctid) {
+  if (Fp == 32) merge_cta_lists<1>(partials, G, stage, ctid);
+  else if (Fp == 64) merge_cta_lists<2>(partials, G, stage, ctid);
+  else if (Fp == 128) merge_cta_lists<4>(partials, G, stage, ctid);
+  else merge_cta_lists<8>(partials, G, stage, ctid);
+}
+__device__ __forceinline__ void warp0_sort_dispatch(uint32_t Fp, uint64_t* a, int ctid) {
+  if (Fp == 32) warp0_sort_smem<1>(a, ctid);
+  else if (Fp == 64) warp0_sort_smem<2>(a, ctid);
+  else if (Fp == 128) warp0_sort_smem<4>(a, ctid);
+  else warp0_sort_smem<8>(a, ctid);
+}
+
 // ------------------------------------------------------------------ kernel
 // BITS 8/4/1; MODE asym/int/hamming; CB chunk bytes (4, 8 or 16); L lanes per
-// row; CPL chunks per lane; U rows in flight per row-group.
+// row; CPL chunks per lane; U rows in flight per row-group (asym: even, two
+// rows per f32x2 accumulator).
 template <int BITS, int MODE, int CB, int L, int CPL, int U>
 struct ScanCfg {
   static constexpr int W = CB / 4;                                     // words per chunk
@@ -230,33 +418,43 @@ struct ScanCfg {
   // per-chunk integer query words: int8 W, int4 2W (even/odd), 1-bit 8W planes, hamming W
   static constexpr int QW = MODE == kInt ? (BITS == 8 ? W : (BITS == 4 ? 2 * W : 8 * W))
                                          : (MODE == kHamming ? W : 1);
+  static_assert(MODE != kAsym || (U % 2) == 0, "asym rows go in f32x2 pairs");
 };
 
 template <int BITS, int MODE, int CB, int L, int CPL, int U>
 __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams p) {
   using C = ScanCfg<BITS, MODE, CB, L, CPL, U>;
   extern __shared__ __align__(128) uint8_t smem[];
-  const ScanSmem lay = scan_smem_layout(p.tile_bytes, p.tile_rows, p.stages, p.P, p.cap);
+  const ScanSmem lay = scan_smem_layout(p.tile_bytes, p.tile_rows, p.stages, p.P, p.rounds, p.capc);
   uint8_t* s_codes = smem + lay.codes_off;
   float* s_scales = reinterpret_cast<float*>(smem + lay.scales_off);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + lay.bars_off);
   uint64_t* empty = full + p.stages;
-  float* rq = reinterpret_cast<float*>(smem + lay.rq_off);
+  uint64_t* qbar = empty + p.stages;  // query + signs landed
+  float* q = reinterpret_cast<float*>(smem + lay.q_off);  // query, rotated in place
+  float* s_signs = reinterpret_cast<float*>(smem + lay.signs_off);
   int8_t* qb = reinterpret_cast<int8_t*>(smem + lay.qb_off);
-  uint64_t* bufs = reinterpret_cast<uint64_t*>(smem + lay.bufs_off);
-  float* miscf = reinterpret_cast<float*>(smem + lay.misc_off);
-  uint32_t* miscu = reinterpret_cast<uint32_t*>(smem + lay.misc_off);
+  uint64_t* cand = reinterpret_cast<uint64_t*>(smem + lay.cand_off);
+  uint32_t* hist = reinterpret_cast<uint32_t*>(smem + lay.hist_off);
+  uint32_t* misc = reinterpret_cast<uint32_t*>(smem + lay.misc_off);
+  float* miscf = reinterpret_cast<float*>(misc);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (p.trace && threadIdx.x == 0) p.trace[blockIdx.x * 8 + kTrEntry] = globaltimer();
   const uint32_t t0 = static_cast<uint32_t>(static_cast<uint64_t>(blockIdx.x) * p.ntiles / gridDim.x);
   const uint32_t t1 =
       static_cast<uint32_t>(static_cast<uint64_t>(blockIdx.x + 1) * p.ntiles / gridDim.x);
+  // bulk part of the query copy: whole 16-byte blocks of a 16-byte aligned query
+  const uint32_t q_bulk =
+      (reinterpret_cast<uintptr_t>(p.query) & 15u) == 0 ? (p.dim * 4u) & ~15u : 0u;
 
   if (threadIdx.x == 0) {
     for (uint32_t s = 0; s < p.stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumerWarps);
     }
+    mbar_init(qbar, 1);
+    misc[kMiscCount] = 0;
     fence_mbar_init();
   }
   __syncthreads();
@@ -264,31 +462,43 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
   if (warp == kConsumerWarps) {
     // ---------------------------------------------------------- producer
     if (lane == 0) {
+      const uint32_t sbytes = p.rounds * p.P * 4u;
+      mbar_arrive_expect_tx(qbar, q_bulk + sbytes);
+      if (q_bulk) bulk_g2s(q, p.query, q_bulk, qbar);
+      if (sbytes) bulk_g2s(s_signs, p.signs, sbytes, qbar);
       const uint32_t bytes = p.tile_bytes + p.tile_rows * 4;
+      const uint64_t stream_policy = l2_policy_evict_first();  // codes are read once per query
       for (uint32_t t = t0, it = 0; t < t1; ++t, ++it) {
         const uint32_t s = it % p.stages, ph = (it / p.stages) & 1u;
         if (it >= p.stages && !mbar_wait_bounded(&empty[s], ph ^ 1u, p.err)) break;
         mbar_arrive_expect_tx(&full[s], bytes);
-        bulk_g2s(s_codes + static_cast<size_t>(s) * p.tile_bytes,
-                 p.codes + static_cast<size_t>(t) * p.tile_bytes, p.tile_bytes, &full[s]);
-        bulk_g2s(s_scales + static_cast<size_t>(s) * p.tile_rows,
-                 p.scales + static_cast<size_t>(t) * p.tile_rows, p.tile_rows * 4, &full[s]);
+        bulk_g2s_hint(s_codes + static_cast<size_t>(s) * p.tile_bytes,
+                      p.codes + static_cast<size_t>(t) * p.tile_bytes, p.tile_bytes, &full[s], stream_policy);
+        bulk_g2s_hint(s_scales + static_cast<size_t>(s) * p.tile_rows,
+                      p.scales + static_cast<size_t>(t) * p.tile_rows, p.tile_rows * 4, &full[s], stream_policy);
       }
     }
+    __syncwarp();
+    pdl_trigger();
   } else {
     // ---------------------------------------------------------- consumers
     const int ctid = threadIdx.x;
-    rotate_query(p, rq, ctid);
+    mbar_wait_bounded(qbar, 0, p.err);
+    for (uint32_t i = q_bulk / 4 + ctid; i < p.P; i += kConsumerThreads)
+      q[i] = i < p.dim ? p.query[i] : 0.0f;
+    named_bar_sync(kBarConsumers, kConsumerThreads);
+    rotate_query(q, s_signs, p.P, p.rounds, ctid);
     float qfac = 1.0f;
     if constexpr (MODE == kInt) {
-      float qscale = quantize_query8(rq, qb, p.P, ctid, miscf);
+      const float qscale = quantize_query8(q, qb, p.P, ctid, miscf + kMiscRed);
       qfac = __fmul_rn(qscale, kInv127);
     } else if constexpr (MODE == kHamming) {
       uint32_t* qbits = reinterpret_cast<uint32_t*>(qb);
       for (uint32_t blk = warp; blk < p.P / 32; blk += kConsumerWarps)
-        qbits[blk] = __ballot_sync(0xffffffffu, rq[blk * 32 + lane] >= 0.0f);
+        qbits[blk] = __ballot_sync(0xffffffffu, q[blk * 32 + lane] >= 0.0f);
     }
     named_bar_sync(kBarConsumers, kConsumerThreads);
+    if (p.trace && threadIdx.x == 0) p.trace[blockIdx.x * 8 + kTrRotated] = globaltimer();
 
     const int g = lane / L, sl = lane % L;
     // lane-resident query slices
@@ -300,7 +510,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
       const uint32_t e0 = static_cast<uint32_t>(sl + j * L) * C::EPC;  // first element of chunk
       if constexpr (C::kQReg) {
 #pragma unroll
-        for (int e = 0; e < C::EPC; ++e) qf[j][e] = rq[e0 + e];
+        for (int e = 0; e < C::EPC; ++e) qf[j][e] = q[e0 + e];
       } else if constexpr (MODE == kInt && BITS == 8) {
 #pragma unroll
         for (int w = 0; w < C::W; ++w) qw[j][w] = reinterpret_cast<const uint32_t*>(qb + e0)[w];
@@ -335,22 +545,18 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
     (void)qw;
     (void)qsum;
 
-    WarpTopF tf;
-    tf.init(bufs + static_cast<size_t>(warp) * p.cap, static_cast<int>(p.cap), static_cast<int>(p.F),
-            lane);
-
-    bool ok = true;
+    // candidate buffer: keys above thr are appended; checked every check_tiles
+    const uint32_t high = p.capc - p.check_tiles * p.tile_rows;
+    uint64_t thr = 0;
     for (uint32_t t = t0, it = 0; t < t1; ++t, ++it) {
       const uint32_t s = it % p.stages, ph = (it / p.stages) & 1u;
-      if (!mbar_wait_bounded(&full[s], ph, p.err)) {
-        ok = false;
-        break;
-      }
+      const bool landed = mbar_wait_bounded(&full[s], ph, p.err);
       const uint8_t* cb = s_codes + static_cast<size_t>(s) * p.tile_bytes;
       const float* sc = s_scales + static_cast<size_t>(s) * p.tile_rows;
       const uint64_t base = static_cast<uint64_t>(t) * p.tile_rows;
-      const uint32_t nvalid =
-          p.nrows - base < p.tile_rows ? static_cast<uint32_t>(p.nrows - base) : p.tile_rows;
+      const uint32_t nvalid = !landed ? 0u
+                              : (p.nrows - base < p.tile_rows ? static_cast<uint32_t>(p.nrows - base)
+                                                              : p.tile_rows);
 
       for (uint32_t rb = 0; rb < p.tile_rows; rb += C::RPI) {
         uint32_t rho[U];
@@ -358,15 +564,20 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
 #pragma unroll
         for (int u = 0; u < U; ++u) {
           rho[u] = rb + static_cast<uint32_t>(warp * (C::G * U) + u * C::G + g);
+          // a tile may hold fewer rows than one iteration covers (very wide rows):
+          // surplus lanes read row 0 and never offer a key
+          const uint32_t rr = rho[u] < p.tile_rows ? rho[u] : 0u;
 #pragma unroll
           for (int j = 0; j < CPL; ++j)
-            x[u][j] = lds_chunk<C::W>(cb + static_cast<size_t>(rho[u]) * p.R + (sl + j * L) * CB);
+            x[u][j] = lds_chunk<C::W>(cb + static_cast<size_t>(rr) * p.R + (sl + j * L) * CB);
         }
         float score[U];
         if constexpr (MODE == kAsym) {
-          float acc[U];
+          // rows (2v, 2v+1) share one f32x2 accumulator; each row keeps its own
+          // fmaf chain in the canonical element order.
+          uint64_t acc[U / 2];
 #pragma unroll
-          for (int u = 0; u < U; ++u) acc[u] = 0.0f;
+          for (int v = 0; v < U / 2; ++v) acc[v] = 0ull;
 #pragma unroll
           for (int j = 0; j < CPL; ++j) {
             const uint32_t e0 = static_cast<uint32_t>(sl + j * L) * C::EPC;
@@ -375,33 +586,49 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
               if constexpr (BITS == 8) {
 #pragma unroll
                 for (int b = 0; b < 4; ++b) {
-                  const float q = C::kQReg ? qf[C::kQReg ? j : 0][C::kQReg ? w * 4 + b : 0]
-                                           : rq[e0 + w * 4 + b];
+                  const float qv = C::kQReg ? qf[C::kQReg ? j : 0][C::kQReg ? w * 4 + b : 0]
+                                            : q[e0 + w * 4 + b];
+                  const uint64_t q2 = f2_pack(qv, qv);
 #pragma unroll
-                  for (int u = 0; u < U; ++u)
-                    acc[u] = __fmaf_rn(s8_to_f32(x[u][j].w[w] ^ 0x80808080u, b), q, acc[u]);
+                  for (int v = 0; v < U / 2; ++v) {
+                    const uint64_t val =
+                        f2_add(f2_pack(s8_biased(x[2 * v][j].w[w] ^ 0x80808080u, b),
+                                       s8_biased(x[2 * v + 1][j].w[w] ^ 0x80808080u, b)),
+                               f2_pack(-kBias8, -kBias8));
+                    acc[v] = f2_fma(val, q2, acc[v]);
+                  }
                 }
               } else if constexpr (BITS == 4) {
 #pragma unroll
                 for (int n = 0; n < 8; ++n) {
-                  const float q = C::kQReg ? qf[C::kQReg ? j : 0][C::kQReg ? w * 8 + n : 0]
-                                           : rq[e0 + w * 8 + n];
+                  const float qv = C::kQReg ? qf[C::kQReg ? j : 0][C::kQReg ? w * 8 + n : 0]
+                                            : q[e0 + w * 8 + n];
+                  const uint64_t q2 = f2_pack(qv, qv);
 #pragma unroll
-                  for (int u = 0; u < U; ++u)
-                    acc[u] = __fmaf_rn(s4_to_f32(x[u][j].w[w] ^ 0x88888888u, n), q, acc[u]);
+                  for (int v = 0; v < U / 2; ++v) {
+                    const uint64_t val =
+                        f2_add(f2_pack(s4_biased(x[2 * v][j].w[w] ^ 0x88888888u, n),
+                                       s4_biased(x[2 * v + 1][j].w[w] ^ 0x88888888u, n)),
+                               f2_pack(-kBias4, -kBias4));
+                    acc[v] = f2_fma(val, q2, acc[v]);
+                  }
                 }
               } else {
 #pragma unroll
                 for (int b4 = 0; b4 < 8; ++b4) {
-                  const float4 q4 = *reinterpret_cast<const float4*>(rq + e0 + w * 32 + b4 * 4);
+                  const float4 q4 = *reinterpret_cast<const float4*>(q + e0 + w * 32 + b4 * 4);
                   const float qv[4] = {q4.x, q4.y, q4.z, q4.w};
 #pragma unroll
                   for (int bb = 0; bb < 4; ++bb) {
                     const int b = b4 * 4 + bb;
+                    const uint32_t qbits = __float_as_uint(qv[bb]);
 #pragma unroll
-                    for (int u = 0; u < U; ++u) {
-                      const uint32_t flip = (~(x[u][j].w[w] << (31 - b))) & 0x80000000u;
-                      acc[u] = __fadd_rn(acc[u], __uint_as_float(__float_as_uint(qv[bb]) ^ flip));
+                    for (int v = 0; v < U / 2; ++v) {
+                      // fmaf(+-1, q, acc) == acc + (+-q) exactly
+                      const uint32_t f0 = (~(x[2 * v][j].w[w] << (31 - b))) & 0x80000000u;
+                      const uint32_t f1 = (~(x[2 * v + 1][j].w[w] << (31 - b))) & 0x80000000u;
+                      acc[v] = f2_add(acc[v], f2_pack(__uint_as_float(qbits ^ f0),
+                                                      __uint_as_float(qbits ^ f1)));
                     }
                   }
                 }
@@ -409,14 +636,20 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
             }
           }
 #pragma unroll
-          for (int u = 0; u < U; ++u) {
+          for (int v = 0; v < U / 2; ++v) {
+            float a0, a1;
+            f2_unpack(acc[v], a0, a1);
 #pragma unroll
-            for (int off = L / 2; off >= 1; off >>= 1)
-              acc[u] = __fadd_rn(acc[u], __shfl_xor_sync(0xffffffffu, acc[u], off));
-            const float scale = sc[rho[u]];
-            const float rowfac =
-                BITS == 8 ? __fmul_rn(scale, kInv127) : (BITS == 4 ? __fmul_rn(scale, kInv7) : scale);
-            score[u] = __fmul_rn(acc[u], rowfac);
+            for (int off = L / 2; off >= 1; off >>= 1) {
+              a0 = __fadd_rn(a0, __shfl_xor_sync(0xffffffffu, a0, off));
+              a1 = __fadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, off));
+            }
+            const float s0 = sc[rho[2 * v] < p.tile_rows ? rho[2 * v] : 0u],
+                        s1 = sc[rho[2 * v + 1] < p.tile_rows ? rho[2 * v + 1] : 0u];
+            const float f0 = BITS == 8 ? __fmul_rn(s0, kInv127) : (BITS == 4 ? __fmul_rn(s0, kInv7) : s0);
+            const float f1 = BITS == 8 ? __fmul_rn(s1, kInv127) : (BITS == 4 ? __fmul_rn(s1, kInv7) : s1);
+            score[2 * v] = __fmul_rn(a0, f0);
+            score[2 * v + 1] = __fmul_rn(a1, f1);
           }
         } else {
           int iacc[U];
@@ -452,10 +685,9 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
             if constexpr (MODE == kInt && BITS == 1) v = 2 * v - qsum;
 #pragma unroll
             for (int off = L / 2; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-            const float scale = sc[rho[u]];
+            const float scale = sc[rho[u] < p.tile_rows ? rho[u] : 0u];
             if constexpr (MODE == kHamming) {
-              const int idot = static_cast<int>(p.P) - 2 * v;
-              score[u] = __fmul_rn(__int2float_rn(idot), scale);
+              score[u] = __fmul_rn(__int2float_rn(static_cast<int>(p.P) - 2 * v), scale);
             } else {
               const float rowfac = BITS == 8 ? __fmul_rn(scale, kInv127)
                                              : (BITS == 4 ? __fmul_rn(scale, kInv7) : scale);
@@ -468,143 +700,77 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
           const uint64_t row = base + rho[u];
           bool valid = (sl == 0) && rho[u] < nvalid;
           if (valid && p.mask) valid = (p.mask[row >> 5] >> (row & 31)) & 1u;
-          tf.offer(make_key(score[u], static_cast<uint32_t>(row)), valid, lane);
+          const uint64_t key = make_key(score[u], static_cast<uint32_t>(row));
+          append_keys(cand, &misc[kMiscCount], key, valid && key > thr, lane);
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
-    }
-    (void)ok;
-    tf.finish(lane);
-
-    // ------------------------------------------------ CTA merge of warp lists
-    named_bar_sync(kBarConsumers, kConsumerThreads);
-    for (int step = 1; step < kConsumerWarps; step <<= 1) {
-      if ((warp % (2 * step)) == 0)
-        warp_merge_top(bufs + static_cast<size_t>(warp) * p.cap,
-                       bufs + static_cast<size_t>(warp + step) * p.cap, static_cast<int>(p.Fp), lane);
-      named_bar_sync(kBarConsumers, kConsumerThreads);
-    }
-    if (warp == 0) {
-      for (uint32_t i = lane; i < p.Fp; i += 32)
-        p.partials[static_cast<size_t>(blockIdx.x) * p.Fp + i] = i < p.F ? bufs[i] : 0ull;
-      __threadfence();
-    }
-  }
-
-  // ------------------------------------------------------ last-CTA ticket
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const uint32_t ticket = atomicAdd(p.ticket, 1u);
-    miscu[8] = (ticket == gridDim.x - 1) ? 1u : 0u;
-  }
-  __syncthreads();
-  if (miscu[8] == 0u) return;
-  __threadfence();
-  if (warp == kConsumerWarps) return;  // the producer warp sits out the merge
-
-  // ------------------------------------------------ global merge (last CTA)
-  {
-    WarpTopF tf;
-    tf.init(bufs + static_cast<size_t>(warp) * p.cap, static_cast<int>(p.cap), static_cast<int>(p.F),
-            lane);
-    const uint32_t nlists = gridDim.x;
-    for (uint32_t lb = 0; lb < nlists; lb += 32 * kConsumerWarps) {
-      const uint32_t li = lb + static_cast<uint32_t>(lane) * kConsumerWarps + warp;
-      bool active = li < nlists;
-      for (uint32_t r = 0; r < p.F; ++r) {
-        if (!__any_sync(0xffffffffu, active)) break;
-        uint64_t key = 0;
-        if (active) {
-          key = __ldcg(p.partials + static_cast<size_t>(li) * p.Fp + r);
-          if (key == 0 || key <= tf.thr) active = false;
-        }
-        tf.offer(key, active, lane);
-      }
-    }
-    tf.finish(lane);
-  }
-  named_bar_sync(kBarConsumers, kConsumerThreads);
-  for (int step = 1; step < kConsumerWarps; step <<= 1) {
-    if ((warp % (2 * step)) == 0)
-      warp_merge_top(bufs + static_cast<size_t>(warp) * p.cap,
-                     bufs + static_cast<size_t>(warp + step) * p.cap, static_cast<int>(p.Fp), lane);
-    named_bar_sync(kBarConsumers, kConsumerThreads);
-  }
-  uint64_t* top = bufs;  // best Fp keys of the shard, sorted descending
-  if (warp == 0) {
-    uint32_t nc = 0;
-    for (uint32_t i = lane; i < p.F; i += 32) nc += top[i] != 0ull ? 1u : 0u;
+      if ((it + 1) % p.check_tiles == 0 && t + 1 < t1) {
+        named_bar_sync(kBarConsumers, kConsumerThreads);
+        const uint32_t n = misc[kMiscCount];
+        if (n > high) {  // uniform: every consumer read the same count after the barrier
+          uint64_t v[kSelMax];
 #pragma unroll
-    for (int off = 16; off; off >>= 1) nc += __shfl_xor_sync(0xffffffffu, nc, off);
-    if (lane == 0) miscu[9] = nc;
-    if (p.cand_rows) {
-      for (uint32_t i = lane; i < nc; i += 32) {
-        p.cand_rows[i] = key_row(top[i]) + p.row_base;
-        p.cand_scores[i] = key_score(top[i]);
-      }
-      if (lane == 0) *p.cand_count = nc;
-    }
-  }
-  named_bar_sync(kBarConsumers, kConsumerThreads);
-  const uint32_t nc = miscu[9];
-  const int ctid = threadIdx.x;
-
-  if (p.rerank) {
-    // exact f64 dot (store.ts:114-130): 4 lanes per candidate hold a0..a3
-    uint64_t* ex = bufs + p.cap;  // second warp buffer: Fp exact keys
-    const uint32_t vec = p.dim & ~3u;
-    const uint32_t groups = kConsumerThreads / 4;
-    for (uint32_t c0 = 0; c0 < p.Fp; c0 += groups) {
-      const uint32_t c = c0 + static_cast<uint32_t>(ctid) / 4u;
-      const uint32_t j = static_cast<uint32_t>(ctid) & 3u;
-      const bool act = c < nc;
-      double a = 0.0;
-      uint32_t row = 0;
-      if (act) {
-        row = key_row(top[c]);
-        const float* xr = p.originals + static_cast<size_t>(row) * p.dim;
-#pragma unroll 8
-        for (uint32_t i = j; i < vec; i += 4)
-          a = __fma_rn(static_cast<double>(__ldg(xr + i)), static_cast<double>(__ldg(p.query + i)), a);
-      }
-      const int gl = lane & ~3;
-      const double a0 = __shfl_sync(0xffffffffu, a, gl + 0);
-      const double a1 = __shfl_sync(0xffffffffu, a, gl + 1);
-      const double a2 = __shfl_sync(0xffffffffu, a, gl + 2);
-      const double a3 = __shfl_sync(0xffffffffu, a, gl + 3);
-      if (c < p.Fp && j == 0) {
-        uint64_t kx = 0;
-        if (act) {
-          double sacc = __dadd_rn(__dadd_rn(__dadd_rn(a0, a1), a2), a3);
-          const float* xr = p.originals + static_cast<size_t>(row) * p.dim;
-          for (uint32_t i = vec; i < p.dim; ++i)
-            sacc = __fma_rn(static_cast<double>(xr[i]), static_cast<double>(p.query[i]), sacc);
-          kx = make_key(__double2float_rn(sacc), row);
+          for (int i = 0; i < kSelMax; ++i) {
+            const uint32_t idx = static_cast<uint32_t>(ctid) + static_cast<uint32_t>(i) * kConsumerThreads;
+            v[i] = idx < n ? cand[idx] : 0ull;
+          }
+          named_bar_sync(kBarConsumers, kConsumerThreads);
+          keep_best<kSelMax>(v, n, p.F, cand, hist, misc, ctid);
+          // the F-th best key is the smallest kept one; admit only keys above it
+          uint64_t lo = ~0ull;
+          for (uint32_t i = ctid; i < p.F; i += kConsumerThreads) lo = cand[i] < lo ? cand[i] : lo;
+#pragma unroll
+          for (int off = 16; off; off >>= 1) {
+            const uint64_t o = __shfl_xor_sync(0xffffffffu, lo, off);
+            lo = o < lo ? o : lo;
+          }
+          if (lane == 0) reinterpret_cast<uint64_t*>(miscf + kMiscRed)[warp] = lo;
+          named_bar_sync(kBarConsumers, kConsumerThreads);
+          uint64_t t2 = ~0ull;
+#pragma unroll
+          for (int w = 0; w < kConsumerWarps; ++w) {
+            const uint64_t o = reinterpret_cast<const uint64_t*>(miscf + kMiscRed)[w];
+            t2 = o < t2 ? o : t2;
+          }
+          thr = t2 - 1;  // keys > F-th best - 1, i.e. >= it (never re-admits the dropped ones)
+          named_bar_sync(kBarConsumers, kConsumerThreads);
         }
-        ex[c] = kx;
       }
     }
+    pdl_trigger();
     named_bar_sync(kBarConsumers, kConsumerThreads);
-    if (warp == 0) {
-      warp_sort_desc(ex, static_cast<int>(p.Fp), lane);
-      const uint32_t n = nc < p.k ? nc : p.k;
-      for (uint32_t i = lane; i < n; i += 32) {
-        p.out_rows[i] = key_row(ex[i]) + p.row_base;
-        p.out_scores[i] = key_score(ex[i]);
+    if (p.trace && threadIdx.x == 0) p.trace[blockIdx.x * 8 + kTrScanned] = globaltimer();
+
+    // ---------------------------------------------- best F of this CTA
+    uint32_t n = misc[kMiscCount];
+    if (n > (p.Fp <= 256u ? 16u * p.Fp : p.F)) {  // radix-compact to F first
+      uint64_t v[kSelMax];
+#pragma unroll
+      for (int i = 0; i < kSelMax; ++i) {
+        const uint32_t idx = static_cast<uint32_t>(ctid) + static_cast<uint32_t>(i) * kConsumerThreads;
+        v[i] = idx < n ? cand[idx] : 0ull;
       }
-      if (lane == 0) *p.out_count = n;
+      named_bar_sync(kBarConsumers, kConsumerThreads);
+      n = keep_best<kSelMax>(v, n, p.F, cand, hist, misc, ctid);
     }
-  } else if (warp == 0) {
-    const uint32_t n = nc < p.k ? nc : p.k;
-    for (uint32_t i = lane; i < n; i += 32) {
-      p.out_rows[i] = key_row(top[i]) + p.row_base;
-      p.out_scores[i] = key_score(top[i]);
+    if (p.Fp <= 256u) {
+      cta_best_sorted_dispatch(p.Fp, cand, n, ctid);
+      pdl_wait();  // the previous launch has finished with the shared scratch
+      for (uint32_t i = ctid; i < p.Fp; i += kConsumerThreads)
+        p.partials[static_cast<size_t>(blockIdx.x) * p.Fp + i] = i < p.F ? cand[i] : 0ull;
+    } else {
+      // wide F: unsorted best F (the last CTA re-selects them)
+      const uint32_t m = n < p.F ? n : p.F;
+      pdl_wait();
+      for (uint32_t i = ctid; i < p.Fp; i += kConsumerThreads)
+        p.partials[static_cast<size_t>(blockIdx.x) * p.Fp + i] = i < m ? cand[i] : 0ull;
     }
-    if (lane == 0) *p.out_count = n;
+    __threadfence();
+    if (p.trace && threadIdx.x == 0) p.trace[blockIdx.x * 8 + kTrCtaMerged] = globaltimer();
   }
-  if (ctid == 0) *p.ticket = 0u;  // ready for the next launch (stream-ordered)
+
 }
 
 }  // namespace bv

@@ -20,27 +20,53 @@ cudaError_t launch_one(const ScanParams& p, unsigned grid, size_t smem, cudaStre
     if (e != cudaSuccess) return e;
     opted = maxs;
   }
-  kern<<<grid, kScanThreads, smem, stream>>>(p);
-  return cudaGetLastError();
+  // Programmatic dependent launch: the kernel may start while the previous
+  // scan in the stream finishes its merge; it waits (griddepcontrol.wait)
+  // before touching the shared scratch.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kScanThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
 #define BV_TRY_SHAPE(BITS, MODE, CB_, L_, CPL_, U_)                                   \
   if (sh.CB == CB_ && sh.L == L_ && sh.CPL == CPL_ && sh.U == U_)                     \
     return launch_one<BITS, MODE, CB_, L_, CPL_, U_>(p, grid, smem, stream);
 
+// Shapes of small rows (R < 512 bytes): shared by every mode.
 #define BV_SHAPES_SMALL(BITS, MODE)                                                   \
-  BV_TRY_SHAPE(BITS, MODE, 4, 1, 1, 4)                                                \
-  BV_TRY_SHAPE(BITS, MODE, 8, 1, 1, 4)                                                \
-  BV_TRY_SHAPE(BITS, MODE, 16, 1, 1, 4)                                               \
-  BV_TRY_SHAPE(BITS, MODE, 16, 2, 1, 4)                                               \
-  BV_TRY_SHAPE(BITS, MODE, 16, 4, 1, 4)                                               \
-  BV_TRY_SHAPE(BITS, MODE, 16, 8, 1, 4)                                               \
-  BV_TRY_SHAPE(BITS, MODE, 16, 16, 1, 4)                                              \
-  BV_TRY_SHAPE(BITS, MODE, 16, 32, 1, 4)                                              \
-  BV_TRY_SHAPE(BITS, MODE, 16, 32, 2, 2)
+  BV_TRY_SHAPE(BITS, MODE, 4, 1, 1, 2)                                                \
+  BV_TRY_SHAPE(BITS, MODE, 8, 1, 1, 2)                                                \
+  BV_TRY_SHAPE(BITS, MODE, 16, 1, 1, 2)                                               \
+  BV_TRY_SHAPE(BITS, MODE, 16, 2, 1, 2)                                               \
+  BV_TRY_SHAPE(BITS, MODE, 16, 4, 1, 2)                                               \
+  BV_TRY_SHAPE(BITS, MODE, 16, 8, 1, 2)
 
-#define BV_SHAPES_LARGE(BITS, MODE)                                                   \
-  BV_TRY_SHAPE(BITS, MODE, 16, 32, 4, 1)                                              \
+// Canonical asym layouts of wider rows.
+#define BV_SHAPES_ASYM(BITS)                                                          \
+  BV_TRY_SHAPE(BITS, kAsym, 16, 16, 1, 2)                                             \
+  BV_TRY_SHAPE(BITS, kAsym, 16, 32, 1, 2)                                             \
+  BV_TRY_SHAPE(BITS, kAsym, 16, 32, 2, 2)
+
+#define BV_SHAPES_ASYM_WIDE(BITS)                                                     \
+  BV_TRY_SHAPE(BITS, kAsym, 16, 32, 4, 2)                                             \
+  BV_TRY_SHAPE(BITS, kAsym, 16, 32, 8, 2)
+
+// Integer-mode layouts of wider rows (<= 8 lanes per row up to 64 chunks).
+#define BV_SHAPES_INT(BITS, MODE)                                                     \
+  BV_TRY_SHAPE(BITS, MODE, 16, 8, 2, 2)                                               \
+  BV_TRY_SHAPE(BITS, MODE, 16, 8, 4, 1)                                               \
+  BV_TRY_SHAPE(BITS, MODE, 16, 8, 8, 1)
+
+#define BV_SHAPES_INT_WIDE(BITS, MODE)                                                \
+  BV_TRY_SHAPE(BITS, MODE, 16, 16, 8, 1)                                              \
   BV_TRY_SHAPE(BITS, MODE, 16, 32, 8, 1)
 
 }  // namespace bv

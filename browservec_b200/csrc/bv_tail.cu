@@ -1,0 +1,220 @@
+// bv_tail.cu -- the per-query tail: merge the CTA candidate lists of a scan
+// into the shard's best F (the device form of gpuTopk.ts:160-189), gather the
+// F candidate rows of the fp32 originals, re-rank them with the exact f64 dot
+// of store.ts:114-130 and write the best k (index.ts:583-594), all under the
+// (score desc, row asc) order.
+//
+// One CTA, launched right after its scan with programmatic dependent launch:
+// it lets the NEXT scan start at once (so the tail runs beside that scan on
+// the one SM the scan grid leaves free) and waits for its own scan to finish
+// before it reads the candidate lists.
+#include <cstdint>
+
+#include "bv_internal.h"
+#include "bv_scan.cuh"
+#include "bv_tail.cuh"
+
+namespace bv {
+
+__global__ void __launch_bounds__(kConsumerThreads, 1) tail_kernel(const TailParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const TailSmem lay = tail_smem_layout(p.dim, p.capc, p.rows_bytes);
+  uint64_t* cand = reinterpret_cast<uint64_t*>(smem + lay.cand_off);
+  uint32_t* hist = reinterpret_cast<uint32_t*>(smem + lay.hist_off);
+  uint32_t* misc = reinterpret_cast<uint32_t*>(smem + lay.misc_off);
+  float* q = reinterpret_cast<float*>(smem + lay.q_off);
+  float* rows_s = reinterpret_cast<float*>(smem + lay.rows_off);
+  uint64_t* gbar = reinterpret_cast<uint64_t*>(smem + lay.bar_off);
+  const int ctid = threadIdx.x, warp = ctid >> 5, lane = ctid & 31;
+
+  pdl_trigger();  // the next query's scan may launch now
+  if (p.trace && ctid == 0) p.trace[kTrTailEntry] = globaltimer();
+  if (ctid == 0) {
+    mbar_init(gbar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  // the normalized query (an input, ready before this kernel): gbar phase 0
+  const uint32_t q_bulk =
+      (reinterpret_cast<uintptr_t>(p.query) & 15u) == 0 ? (p.dim * 4u) & ~15u : 0u;
+  if (ctid == 0) {
+    mbar_arrive_expect_tx(gbar, p.rerank ? q_bulk : 0u);
+    if (p.rerank && q_bulk) bulk_g2s(q, p.query, q_bulk, gbar);
+  }
+  pdl_wait();  // this query's scan has completed: the CTA lists are visible
+  if (p.trace && ctid == 0) p.trace[kTrTailStart] = globaltimer();
+
+  // ---------------------------------------------- merge of the CTA lists
+  // Result: cand[0..Fp) = the shard's best keys, descending, zero padded;
+  // nc = how many of the first F are real.
+  uint32_t nc = 0;
+  if (p.Fp <= 256u) {
+    merge_cta_lists_dispatch(p.Fp, p.partials, p.G, cand, ctid);
+    if (warp == 0) {
+      uint32_t c = 0;
+      for (uint32_t i = lane; i < p.Fp; i += 32) {
+        if (i >= p.F) cand[i] = 0ull;
+        c += __popc(__ballot_sync(0xffffffffu, i < p.F && cand[i] != 0ull));
+      }
+      if (lane == 0) misc[kMiscNc] = c;
+    }
+    named_bar_sync(kBarConsumers, kConsumerThreads);
+    nc = misc[kMiscNc];
+  } else {
+    // wide F: cand[0..nc) holds the running best F; the lists stream in by chunks
+    const uint32_t total = p.G * p.Fp;
+    constexpr uint32_t kChunkSlots = kMergeMax - 2;  // 2 slots per thread carry cand (F <= 1024)
+    const uint32_t per_chunk = kChunkSlots * kConsumerThreads;
+    for (uint32_t c0 = 0; c0 < total; c0 += per_chunk) {
+      uint64_t v[kMergeMax];
+      uint32_t cnt = 0;
+#pragma unroll
+      for (int i = 0; i < static_cast<int>(kChunkSlots); ++i) {
+        const uint32_t idx = c0 + static_cast<uint32_t>(ctid) + static_cast<uint32_t>(i) * kConsumerThreads;
+        v[i] = idx < total ? __ldcg(p.partials + idx) : 0ull;
+        cnt += v[i] != 0ull ? 1u : 0u;
+      }
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const uint32_t idx = static_cast<uint32_t>(ctid) + static_cast<uint32_t>(i) * kConsumerThreads;
+        v[kChunkSlots + i] = idx < nc ? cand[idx] : 0ull;
+        cnt += v[kChunkSlots + i] != 0ull ? 1u : 0u;
+      }
+#pragma unroll
+      for (int off = 16; off; off >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, off);
+      if (lane == 0) misc[kMiscRed + warp] = cnt;
+      named_bar_sync(kBarConsumers, kConsumerThreads);
+      uint32_t tot = 0;
+#pragma unroll
+      for (int i = 0; i < kConsumerWarps; ++i) tot += misc[kMiscRed + i];
+      named_bar_sync(kBarConsumers, kConsumerThreads);
+      nc = keep_best<kMergeMax>(v, tot, p.F, cand, hist, misc, ctid);
+    }
+    for (uint32_t i = nc + static_cast<uint32_t>(ctid); i < p.Fp; i += kConsumerThreads) cand[i] = 0ull;
+    named_bar_sync(kBarConsumers, kConsumerThreads);
+    cta_sort_desc(cand, p.Fp, ctid);
+  }
+  if (p.trace && ctid == 0) p.trace[kTrTailMerged] = globaltimer();
+  if (p.cand_rows) {
+    for (uint32_t i = ctid; i < nc; i += kConsumerThreads) {
+      p.cand_rows[i] = key_row(cand[i]) + p.row_base;
+      p.cand_scores[i] = key_score(cand[i]);
+    }
+    if (ctid == 0) *p.cand_count = nc;
+  }
+
+  const uint32_t n = nc < p.k ? nc : p.k;
+  if (p.rerank) {
+    // Gather the candidate rows (row stride dim+4 floats: conflict-free for the
+    // 4-lane groups), then the exact f64 dot: lanes j = 0..3 of a group hold
+    // the four accumulators a0..a3 of Store.dotRow.
+    const uint32_t stride = p.dim + 4;
+    mbar_wait_bounded(gbar, 0, p.err);
+    for (uint32_t i = q_bulk / 4 + ctid; i < p.dim; i += kConsumerThreads) q[i] = p.query[i];
+    const bool bulk = (p.dim % 4u) == 0u && (reinterpret_cast<uintptr_t>(p.originals) & 15u) == 0u;
+    const uint32_t batch = p.rows_bytes / (stride * 4u);
+    uint64_t* ex = cand + p.Fp;  // exact keys (cand has capc >= 2*Fp slots)
+    uint32_t gph = 1;
+    named_bar_sync(kBarConsumers, kConsumerThreads);
+    for (uint32_t c0 = 0; c0 < nc; c0 += batch) {
+      const uint32_t nb = nc - c0 < batch ? nc - c0 : batch;
+      if (bulk) {
+        if (warp == 0) {
+          if (lane == 0) mbar_arrive_expect_tx(gbar, nb * p.dim * 4u);
+          __syncwarp();
+          for (uint32_t c = lane; c < nb; c += 32)
+            bulk_g2s(rows_s + static_cast<size_t>(c) * stride,
+                     p.originals + static_cast<size_t>(key_row(cand[c0 + c])) * p.dim, p.dim * 4u, gbar);
+        }
+        mbar_wait_bounded(gbar, gph, p.err);
+        gph ^= 1u;
+        if (p.trace && ctid == 0) p.trace[kTrTailGathered] = globaltimer();
+      } else {
+        for (uint32_t c = 0; c < nb; ++c) {
+          const float* src = p.originals + static_cast<size_t>(key_row(cand[c0 + c])) * p.dim;
+          for (uint32_t i = ctid; i < p.dim; i += kConsumerThreads)
+            rows_s[static_cast<size_t>(c) * stride + i] = src[i];
+        }
+      }
+      named_bar_sync(kBarConsumers, kConsumerThreads);
+      const uint32_t vec = p.dim & ~3u;
+      for (uint32_t cc = 0; cc < nb; cc += kConsumerThreads / 4) {
+        const uint32_t c = cc + static_cast<uint32_t>(ctid) / 4u;
+        const uint32_t j = static_cast<uint32_t>(ctid) & 3u;
+        const bool act = c < nb;
+        double a = 0.0;
+        const float* xr = rows_s + static_cast<size_t>(act ? c : 0) * stride;
+        if (act) {
+#pragma unroll 8
+          for (uint32_t i = j; i < vec; i += 4)
+            a = __fma_rn(static_cast<double>(xr[i]), static_cast<double>(q[i]), a);
+        }
+        const int gl = lane & ~3;
+        const double a0 = __shfl_sync(0xffffffffu, a, gl + 0);
+        const double a1 = __shfl_sync(0xffffffffu, a, gl + 1);
+        const double a2 = __shfl_sync(0xffffffffu, a, gl + 2);
+        const double a3 = __shfl_sync(0xffffffffu, a, gl + 3);
+        if (act && j == 0) {
+          double sacc = __dadd_rn(__dadd_rn(__dadd_rn(a0, a1), a2), a3);
+          for (uint32_t i = vec; i < p.dim; ++i)
+            sacc = __fma_rn(static_cast<double>(xr[i]), static_cast<double>(q[i]), sacc);
+          ex[c0 + c] = make_key(__double2float_rn(sacc), key_row(cand[c0 + c]));
+        }
+      }
+      named_bar_sync(kBarConsumers, kConsumerThreads);
+    }
+    for (uint32_t i = nc + static_cast<uint32_t>(ctid); i < p.Fp; i += kConsumerThreads) ex[i] = 0ull;
+    named_bar_sync(kBarConsumers, kConsumerThreads);
+    if (p.trace && ctid == 0) p.trace[kTrTailDotted] = globaltimer();
+    if (p.Fp <= 256u) {
+      warp0_sort_dispatch(p.Fp, ex, ctid);
+      if (warp == 0) {
+        __syncwarp();
+        for (uint32_t i = lane; i < n; i += 32) {
+          p.out_rows[i] = key_row(ex[i]) + p.row_base;
+          p.out_scores[i] = key_score(ex[i]);
+        }
+      }
+    } else {
+      cta_sort_desc(ex, p.Fp, ctid);
+      for (uint32_t i = ctid; i < n; i += kConsumerThreads) {
+        p.out_rows[i] = key_row(ex[i]) + p.row_base;
+        p.out_scores[i] = key_score(ex[i]);
+      }
+    }
+  } else {
+    for (uint32_t i = ctid; i < n; i += kConsumerThreads) {
+      p.out_rows[i] = key_row(cand[i]) + p.row_base;
+      p.out_scores[i] = key_score(cand[i]);
+    }
+  }
+  if (ctid == 0) {
+    *p.out_count = n;
+    if (p.trace) p.trace[kTrTailDone] = globaltimer();
+  }
+}
+
+cudaError_t launch_tail(const TailParams& p, size_t smem, cudaStream_t stream) {
+  static int opted = 0;
+  if (opted < static_cast<int>(smem)) {
+    int dev = 0, maxs = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&maxs, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaError_t e = cudaFuncSetAttribute(tail_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, maxs);
+    if (e != cudaSuccess) return e;
+    opted = maxs;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(kConsumerThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, tail_kernel, p);
+}
+
+}  // namespace bv

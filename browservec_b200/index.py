@@ -202,6 +202,10 @@ class AddonQuantIndex:
         _lib.check(self._L.bv_get_stats(self._h, C.byref(s)))
         return {f: getattr(s, f) for f, _ in s._fields_}
 
+    def set_phase_trace(self, ptr: int, capacity: int) -> None:
+        """Device buffer (u64) receiving per-phase timestamps of each scan launch."""
+        _lib.check(self._L.bv_set_phase_trace(self._h, C.c_void_p(ptr) if ptr else None, capacity))
+
     def last_launches(self) -> int:
         n = C.c_uint32()
         _lib.check(self._L.bv_launches_last_search(self._h, C.byref(n)))
