@@ -125,10 +125,12 @@ def recall_at_10(torch, corpus, queries, got_rows):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--scoring", default="asym", choices=["asym", "int"])
+    ap.add_argument("--scoring", default="int", choices=["asym", "int"])
+    ap.add_argument("--also", default="asym", choices=["asym", "int", "none"],
+                    help="second scoring mode timed and reported beside the headline")
     ap.add_argument("--replicas", type=int, default=4)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -184,12 +186,6 @@ def main():
 
     corpus = make_data(torch, dev, SEED, N_ROWS, DIM)
     queries = make_data(torch, dev, SEED + 1, N_QUERIES, DIM)
-    reps = []
-    for _ in range(args.replicas):
-        ix = AddonQuantIndex(DIM, bits=8, scoring=args.scoring, device=local)
-        torch.cuda.synchronize()
-        ix.append_device(corpus.data_ptr(), N_ROWS, torch.cuda.current_stream().cuda_stream)
-        reps.append(ix)
     out_rows = torch.zeros((N_QUERIES, K), dtype=torch.int32, device=dev)
     out_scores = torch.zeros((N_QUERIES, K), dtype=torch.float32, device=dev)
     out_counts = torch.zeros((N_QUERIES,), dtype=torch.int32, device=dev)
@@ -199,45 +195,64 @@ def main():
     sp = stream.cuda_stream
     assert sp != 0
 
-    def step():
+    def build(scoring):
+        reps = []
+        for _ in range(args.replicas):
+            ix = AddonQuantIndex(DIM, bits=8, scoring=scoring, device=local)
+            torch.cuda.synchronize()
+            ix.append_device(corpus.data_ptr(), N_ROWS, torch.cuda.current_stream().cuda_stream)
+            reps.append(ix)
+        torch.cuda.synchronize()
+        return reps
+
+    def step(reps):
         for i in range(N_QUERIES):
             reps[i % len(reps)].search_device(queries[i].data_ptr(), 1, K, fetch, True,
                                               out_rows[i].data_ptr(), out_scores[i].data_ptr(),
                                               out_counts[i:].data_ptr(), stream=sp)
 
-    torch.cuda.synchronize()
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    clocks = Clocks(local)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    e0.record(stream)
-    for _ in range(args.steps):
-        step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    clk = clocks.stop()
-    ms = e0.elapsed_time(e1)
-    if dist:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    launches = args.steps * N_QUERIES
-    qps = max(world, 1) * launches / (ms / 1e3)
-    kernel_ms = ms / launches
-    rec = recall_at_10(torch, corpus, queries, out_rows.cpu().numpy())
+    def timed(reps, clocks=False):
+        for _ in range(args.warmup):
+            step(reps)
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        clk = Clocks(local) if clocks else None
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            step(reps)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        clk_res = clk.stop() if clk else None
+        ms = e0.elapsed_time(e1)
+        if dist:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        rec = recall_at_10(torch, corpus, queries, out_rows.cpu().numpy())
+        return ms, rec, clk_res
 
-    # roofline: algorithmic bytes of one scan launch
+    reps = build(args.scoring)
+    ms, rec, clk = timed(reps, clocks=True)
+    launches = args.steps * N_QUERIES * reps[0].last_launches()
+    qps = max(world, 1) * args.steps * N_QUERIES / (ms / 1e3)
+    query_ms = ms / (args.steps * N_QUERIES)
+
+    # roofline: algorithmic bytes of one query (codes + scales + re-rank rows + query)
     algo_bytes = N_ROWS * (1024 + 4) + fetch * DIM * 4 + DIM * 4
     peak, peak_kind = peaks()
-    achieved = algo_bytes / (kernel_ms / 1e3) / 1e9
+    achieved = algo_bytes / (query_ms / 1e3) / 1e9
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "scan_c2_traffic.json")
+    if os.path.exists(tp):
+        traffic = json.load(open(tp)).get(args.scoring)
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                "frac": achieved / peak, "traffic": None,
+                "frac": achieved / peak, "traffic": traffic,
                 "peak_kind": f"{peak_kind} (copy bandwidth, MEASURED_PEAKS.json hbm_gbs)",
-                "algorithmic_bytes_per_launch": algo_bytes}
+                "algorithmic_bytes_per_launch": algo_bytes,
+                "duration": "per query: timed region / queries (scan + tail kernels, PDL-overlapped)"}
 
     # e2e through the host API (host buffers, H2D + D2H + sync per query)
     e2e = None
@@ -262,6 +277,17 @@ def main():
         e2e = {"value": max(world, 1) * e2e_steps * N_QUERIES / wall, "unit": UNIT,
                "h2d_bytes_per_step": N_QUERIES * DIM * 4, "d2h_bytes_per_step": N_QUERIES * out_words * 4,
                "steps": e2e_steps, "timing": "host wall clock around synchronous bv_search calls"}
+    for ix in reps:
+        ix.destroy()
+
+    also = None
+    if args.also != "none" and args.also != args.scoring:
+        reps2 = build(args.also)
+        ms2, rec2, _ = timed(reps2)
+        also = {"scoring": args.also, "value": max(world, 1) * args.steps * N_QUERIES / (ms2 / 1e3),
+                "unit": UNIT, "recall_at_10": rec2, "ms_per_step": ms2 / args.steps}
+        for ix in reps2:
+            ix.destroy()
 
     cpu = None
     if rank == 0 and not args.no_cpu and world == 1:
@@ -272,15 +298,13 @@ def main():
                "sample": f"{per} queries over the full 100k x 768 fp32 corpus, WASM-SIMD exact scan "
                          "restated in C (src/fallback/kernel.wat), one query per thread"}
 
-    for ix in reps:
-        ix.destroy()
     if rank == 0:
         line = {"metric": METRIC, "value": qps, "unit": UNIT, "n_gpus": max(world, 1), "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "s8" if args.scoring == "int" else "f32xs8",
                 "data": "synthetic (seeded Philox N(0,1), L2-normalised)", "config": config,
-                "recall_at_10": rec, "kernel_ms": kernel_ms, "gpu_launches": launches,
-                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk}
+                "recall_at_10": rec, "query_ms": query_ms, "gpu_launches": launches,
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk, "also": also}
         print(json.dumps(line))
     if dist:
         dist.destroy_process_group()

@@ -76,10 +76,11 @@ struct bv_index {
   float* d_scales = nullptr;
   float* d_orig = nullptr;
   float* d_signs = nullptr;
-  // scratch of the scan: per-CTA candidate lists, last-CTA ticket, error flags
+  // scratch of the scan: per-CTA candidate lists, tile counters, error flags
   uint64_t* d_partials = nullptr;
   size_t partials_cap = 0;
-  uint32_t* d_ticket = nullptr;
+  unsigned long long* d_tile_ctr = nullptr;  // 4 rotating dynamic-tile counters
+  uint32_t epoch = 0;                        // scan launches so far
   uint32_t* d_err = nullptr;
   // staging for the host-pointer entry points
   float* d_q = nullptr;
@@ -323,6 +324,8 @@ int enqueue_search(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStrea
 
   for (uint32_t q = 0; q < a->nq; ++q) {
     p.query = a->queries + static_cast<size_t>(q) * idx->dim;
+    p.epoch = ++idx->epoch;
+    p.tile_ctr = idx->d_tile_ctr + (p.epoch & 3u);
     cudaError_t e = launch_scan(static_cast<int>(idx->bits), static_cast<int>(idx->scoring), pl.sh,
                                 p, pl.grid, pl.smem, s);
     if (e == cudaErrorNotSupported)
@@ -414,9 +417,9 @@ int bv_create(const bv_config* cfg, bv_index** out) {
   e = cudaMalloc(&idx->d_signs, ns * sizeof(float));
   if (e == cudaSuccess) e = cudaMemcpy(idx->d_signs, hs, ns * sizeof(float), cudaMemcpyHostToDevice);
   delete[] hs;
-  if (e == cudaSuccess) e = cudaMalloc(&idx->d_ticket, 16);
+  if (e == cudaSuccess) e = cudaMalloc(&idx->d_tile_ctr, 4 * sizeof(unsigned long long));
   if (e == cudaSuccess) e = cudaMalloc(&idx->d_err, 16);
-  if (e == cudaSuccess) e = cudaMemset(idx->d_ticket, 0, 16);
+  if (e == cudaSuccess) e = cudaMemset(idx->d_tile_ctr, 0, 4 * sizeof(unsigned long long));
   if (e == cudaSuccess) e = cudaMemset(idx->d_err, 0, 16);
   if (e != cudaSuccess) return bail(cuda_fail(nullptr, e, "index buffers"));
   *out = idx;
@@ -431,7 +434,7 @@ int bv_destroy(bv_index* idx) {
   cudaFree(idx->d_orig);
   cudaFree(idx->d_signs);
   cudaFree(idx->d_partials);
-  cudaFree(idx->d_ticket);
+  cudaFree(idx->d_tile_ctr);
   cudaFree(idx->d_err);
   cudaFree(idx->d_q);
   cudaFree(idx->d_mask);

@@ -57,9 +57,34 @@ struct ScanParams {
   uint32_t capc;             // CTA candidate buffer slots (pow2, <= kSelMax * 512, >= 2*Fp)
   uint32_t check_tiles;      // tiles between candidate-buffer checks
   uint64_t* partials;        // gridDim.x x Fp keys
+  unsigned long long* tile_ctr;  // dynamic tile counter slot: (epoch << 32) | next tile
+  uint32_t epoch;            // launch number owning tile_ctr (slots rotate over 4 launches)
   uint32_t* err;             // error flags
   uint64_t* trace;           // optional: per-CTA phase timestamps (globaltimer ns)
 };
+
+// Next tile of this launch from the shared counter.  The slot still holds an
+// older launch's epoch until the first grab of this launch installs its own
+// (CAS), claiming tile 0; later grabs are plain atomic adds.
+__device__ __forceinline__ uint32_t grab_tile(unsigned long long* ctr, uint32_t epoch, uint32_t* err) {
+  unsigned long long prev = atomicAdd(ctr, 1ull);
+  if (static_cast<uint32_t>(prev >> 32) == epoch) return static_cast<uint32_t>(prev);
+  unsigned long long cur = prev + 1ull;
+  for (int i = 0; i < 4096; ++i) {
+    if (static_cast<uint32_t>(cur >> 32) == epoch) {
+      prev = atomicAdd(ctr, 1ull);
+      if (static_cast<uint32_t>(prev >> 32) == epoch) return static_cast<uint32_t>(prev);
+      cur = prev + 1ull;
+      continue;
+    }
+    const unsigned long long want = (static_cast<unsigned long long>(epoch) << 32) | 1ull;
+    const unsigned long long got = atomicCAS(ctr, cur, want);
+    if (got == cur) return 0u;
+    cur = got;
+  }
+  atomicOr(err, kErrBadLaunch);
+  return 0xFFFFFFFFu;
+}
 
 // Phase timestamps: CTA b writes trace[b*8 + phase].
 enum : int { kTrEntry = 0, kTrRotated = 1, kTrScanned = 2, kTrCtaMerged = 3 };
@@ -88,7 +113,7 @@ __host__ __device__ inline ScanSmem scan_smem_layout(uint32_t tile_bytes, uint32
   s.scales_off = o;
   o = align_up(o + stages * tile_rows * 4, 128);
   s.bars_off = o;
-  o = align_up(o + (2 * stages + 1) * 8, 16);
+  o = align_up(o + (2 * stages + 1) * 8 + stages * 4, 16);
   s.q_off = o;
   o = align_up(o + P * 4, 16);
   s.signs_off = o;
@@ -418,7 +443,6 @@ struct ScanCfg {
   // per-chunk integer query words: int8 W, int4 2W (even/odd), 1-bit 8W planes, hamming W
   static constexpr int QW = MODE == kInt ? (BITS == 8 ? W : (BITS == 4 ? 2 * W : 8 * W))
                                          : (MODE == kHamming ? W : 1);
-  static_assert(MODE != kAsym || (U % 2) == 0, "asym rows go in f32x2 pairs");
 };
 
 template <int BITS, int MODE, int CB, int L, int CPL, int U>
@@ -431,6 +455,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + lay.bars_off);
   uint64_t* empty = full + p.stages;
   uint64_t* qbar = empty + p.stages;  // query + signs landed
+  volatile uint32_t* tile_ids = reinterpret_cast<volatile uint32_t*>(qbar + 1);  // tile in each stage
   float* q = reinterpret_cast<float*>(smem + lay.q_off);  // query, rotated in place
   float* s_signs = reinterpret_cast<float*>(smem + lay.signs_off);
   int8_t* qb = reinterpret_cast<int8_t*>(smem + lay.qb_off);
@@ -441,9 +466,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (p.trace && threadIdx.x == 0) p.trace[blockIdx.x * 8 + kTrEntry] = globaltimer();
-  const uint32_t t0 = static_cast<uint32_t>(static_cast<uint64_t>(blockIdx.x) * p.ntiles / gridDim.x);
-  const uint32_t t1 =
-      static_cast<uint32_t>(static_cast<uint64_t>(blockIdx.x + 1) * p.ntiles / gridDim.x);
+  constexpr uint32_t kNoTile = 0xFFFFFFFFu;  // end-of-work marker in tile_ids
   // bulk part of the query copy: whole 16-byte blocks of a 16-byte aligned query
   const uint32_t q_bulk =
       (reinterpret_cast<uintptr_t>(p.query) & 15u) == 0 ? (p.dim * 4u) & ~15u : 0u;
@@ -468,14 +491,24 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
       if (sbytes) bulk_g2s(s_signs, p.signs, sbytes, qbar);
       const uint32_t bytes = p.tile_bytes + p.tile_rows * 4;
       const uint64_t stream_policy = l2_policy_evict_first();  // codes are read once per query
-      for (uint32_t t = t0, it = 0; t < t1; ++t, ++it) {
+      // tiles come from a shared counter, so faster SMs take more of them
+      uint32_t t = grab_tile(p.tile_ctr, p.epoch, p.err);
+      uint32_t it = 0;
+      for (;; ++it) {
         const uint32_t s = it % p.stages, ph = (it / p.stages) & 1u;
         if (it >= p.stages && !mbar_wait_bounded(&empty[s], ph ^ 1u, p.err)) break;
+        if (t >= p.ntiles) {  // no more work: an empty stage tells the consumers
+          tile_ids[s] = kNoTile;
+          mbar_arrive(&full[s]);
+          break;
+        }
+        tile_ids[s] = t;
         mbar_arrive_expect_tx(&full[s], bytes);
         bulk_g2s_hint(s_codes + static_cast<size_t>(s) * p.tile_bytes,
                       p.codes + static_cast<size_t>(t) * p.tile_bytes, p.tile_bytes, &full[s], stream_policy);
         bulk_g2s_hint(s_scales + static_cast<size_t>(s) * p.tile_rows,
                       p.scales + static_cast<size_t>(t) * p.tile_rows, p.tile_rows * 4, &full[s], stream_policy);
+        t = grab_tile(p.tile_ctr, p.epoch, p.err);
       }
     }
     __syncwarp();
@@ -502,7 +535,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
 
     const int g = lane / L, sl = lane % L;
     // lane-resident query slices
-    float qf[C::kQReg ? CPL : 1][C::kQReg ? C::EPC : 1];
+    uint64_t qf2[C::kQReg ? CPL : 1][C::kQReg ? C::EPC / 2 : 1];  // fp32 query pairs
     uint32_t qw[MODE == kAsym ? 1 : CPL][C::QW];
     int qsum = 0;
 #pragma unroll
@@ -510,7 +543,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
       const uint32_t e0 = static_cast<uint32_t>(sl + j * L) * C::EPC;  // first element of chunk
       if constexpr (C::kQReg) {
 #pragma unroll
-        for (int e = 0; e < C::EPC; ++e) qf[j][e] = q[e0 + e];
+        for (int e = 0; e < C::EPC / 2; ++e) qf2[j][e] = reinterpret_cast<const uint64_t*>(q + e0)[e];
       } else if constexpr (MODE == kInt && BITS == 8) {
 #pragma unroll
         for (int w = 0; w < C::W; ++w) qw[j][w] = reinterpret_cast<const uint32_t*>(qb + e0)[w];
@@ -541,22 +574,23 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
         for (int w = 0; w < C::W; ++w) qw[j][w] = reinterpret_cast<const uint32_t*>(qb)[e0 / 32 + w];
       }
     }
-    (void)qf;
+    (void)qf2;
     (void)qw;
     (void)qsum;
 
     // candidate buffer: keys above thr are appended; checked every check_tiles
     const uint32_t high = p.capc - p.check_tiles * p.tile_rows;
     uint64_t thr = 0;
-    for (uint32_t t = t0, it = 0; t < t1; ++t, ++it) {
+    for (uint32_t it = 0;; ++it) {
       const uint32_t s = it % p.stages, ph = (it / p.stages) & 1u;
       const bool landed = mbar_wait_bounded(&full[s], ph, p.err);
+      const uint32_t t = landed ? tile_ids[s] : kNoTile;
+      if (t == kNoTile) break;
       const uint8_t* cb = s_codes + static_cast<size_t>(s) * p.tile_bytes;
       const float* sc = s_scales + static_cast<size_t>(s) * p.tile_rows;
       const uint64_t base = static_cast<uint64_t>(t) * p.tile_rows;
-      const uint32_t nvalid = !landed ? 0u
-                              : (p.nrows - base < p.tile_rows ? static_cast<uint32_t>(p.nrows - base)
-                                                              : p.tile_rows);
+      const uint32_t nvalid =
+          p.nrows - base < p.tile_rows ? static_cast<uint32_t>(p.nrows - base) : p.tile_rows;
 
       for (uint32_t rb = 0; rb < p.tile_rows; rb += C::RPI) {
         uint32_t rho[U];
@@ -573,11 +607,12 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
         }
         float score[U];
         if constexpr (MODE == kAsym) {
-          // rows (2v, 2v+1) share one f32x2 accumulator; each row keeps its own
-          // fmaf chain in the canonical element order.
-          uint64_t acc[U / 2];
+          // per row one f32x2 accumulator {even, odd}: the lane's elements
+          // alternate between the two chains (canonical order), so one packed
+          // FMA takes an element pair of one row and a register pair of q.
+          uint64_t acc[U];
 #pragma unroll
-          for (int v = 0; v < U / 2; ++v) acc[v] = 0ull;
+          for (int u = 0; u < U; ++u) acc[u] = 0ull;
 #pragma unroll
           for (int j = 0; j < CPL; ++j) {
             const uint32_t e0 = static_cast<uint32_t>(sl + j * L) * C::EPC;
@@ -585,50 +620,45 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
             for (int w = 0; w < C::W; ++w) {
               if constexpr (BITS == 8) {
 #pragma unroll
-                for (int b = 0; b < 4; ++b) {
-                  const float qv = C::kQReg ? qf[C::kQReg ? j : 0][C::kQReg ? w * 4 + b : 0]
-                                            : q[e0 + w * 4 + b];
-                  const uint64_t q2 = f2_pack(qv, qv);
+                for (int bp = 0; bp < 4; bp += 2) {
+                  const uint64_t q2 = C::kQReg ? qf2[C::kQReg ? j : 0][C::kQReg ? (w * 4 + bp) / 2 : 0]
+                                               : *reinterpret_cast<const uint64_t*>(q + e0 + w * 4 + bp);
 #pragma unroll
-                  for (int v = 0; v < U / 2; ++v) {
-                    const uint64_t val =
-                        f2_add(f2_pack(s8_biased(x[2 * v][j].w[w] ^ 0x80808080u, b),
-                                       s8_biased(x[2 * v + 1][j].w[w] ^ 0x80808080u, b)),
-                               f2_pack(-kBias8, -kBias8));
-                    acc[v] = f2_fma(val, q2, acc[v]);
+                  for (int u = 0; u < U; ++u) {
+                    const uint32_t xb = x[u][j].w[w] ^ 0x80808080u;
+                    const uint64_t val = f2_add(f2_pack(s8_biased(xb, bp), s8_biased(xb, bp + 1)),
+                                                f2_pack(-kBias8, -kBias8));
+                    acc[u] = f2_fma(val, q2, acc[u]);
                   }
                 }
               } else if constexpr (BITS == 4) {
 #pragma unroll
-                for (int n = 0; n < 8; ++n) {
-                  const float qv = C::kQReg ? qf[C::kQReg ? j : 0][C::kQReg ? w * 8 + n : 0]
-                                            : q[e0 + w * 8 + n];
-                  const uint64_t q2 = f2_pack(qv, qv);
+                for (int np = 0; np < 8; np += 2) {
+                  const uint64_t q2 = C::kQReg ? qf2[C::kQReg ? j : 0][C::kQReg ? (w * 8 + np) / 2 : 0]
+                                               : *reinterpret_cast<const uint64_t*>(q + e0 + w * 8 + np);
 #pragma unroll
-                  for (int v = 0; v < U / 2; ++v) {
-                    const uint64_t val =
-                        f2_add(f2_pack(s4_biased(x[2 * v][j].w[w] ^ 0x88888888u, n),
-                                       s4_biased(x[2 * v + 1][j].w[w] ^ 0x88888888u, n)),
-                               f2_pack(-kBias4, -kBias4));
-                    acc[v] = f2_fma(val, q2, acc[v]);
+                  for (int u = 0; u < U; ++u) {
+                    const uint32_t xn = x[u][j].w[w] ^ 0x88888888u;
+                    const uint64_t val = f2_add(f2_pack(s4_biased(xn, np), s4_biased(xn, np + 1)),
+                                                f2_pack(-kBias4, -kBias4));
+                    acc[u] = f2_fma(val, q2, acc[u]);
                   }
                 }
               } else {
 #pragma unroll
                 for (int b4 = 0; b4 < 8; ++b4) {
-                  const float4 q4 = *reinterpret_cast<const float4*>(q + e0 + w * 32 + b4 * 4);
-                  const float qv[4] = {q4.x, q4.y, q4.z, q4.w};
+                  const uint4 q4 = *reinterpret_cast<const uint4*>(q + e0 + w * 32 + b4 * 4);
 #pragma unroll
-                  for (int bb = 0; bb < 4; ++bb) {
-                    const int b = b4 * 4 + bb;
-                    const uint32_t qbits = __float_as_uint(qv[bb]);
+                  for (int hp = 0; hp < 2; ++hp) {
+                    const int b = b4 * 4 + hp * 2;  // element pair (b, b+1) of word w
+                    const uint32_t qlo = hp ? q4.z : q4.x, qhi = hp ? q4.w : q4.y;
 #pragma unroll
-                    for (int v = 0; v < U / 2; ++v) {
-                      // fmaf(+-1, q, acc) == acc + (+-q) exactly
-                      const uint32_t f0 = (~(x[2 * v][j].w[w] << (31 - b))) & 0x80000000u;
-                      const uint32_t f1 = (~(x[2 * v + 1][j].w[w] << (31 - b))) & 0x80000000u;
-                      acc[v] = f2_add(acc[v], f2_pack(__uint_as_float(qbits ^ f0),
-                                                      __uint_as_float(qbits ^ f1)));
+                    for (int u = 0; u < U; ++u) {
+                      // fmaf(+-1, q, acc) == acc + (+-q) exactly: flip q's sign where the bit is 0
+                      const uint32_t xw = x[u][j].w[w];
+                      const uint32_t f0 = (~(xw << (31 - b))) & 0x80000000u;
+                      const uint32_t f1 = (~(xw << (30 - b))) & 0x80000000u;
+                      acc[u] = f2_add(acc[u], f2_pack(__uint_as_float(qlo ^ f0), __uint_as_float(qhi ^ f1)));
                     }
                   }
                 }
@@ -636,20 +666,15 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
             }
           }
 #pragma unroll
-          for (int v = 0; v < U / 2; ++v) {
-            float a0, a1;
-            f2_unpack(acc[v], a0, a1);
+          for (int u = 0; u < U; ++u) {
+            float ev, od;
+            f2_unpack(acc[u], ev, od);
+            float a = __fadd_rn(ev, od);
 #pragma unroll
-            for (int off = L / 2; off >= 1; off >>= 1) {
-              a0 = __fadd_rn(a0, __shfl_xor_sync(0xffffffffu, a0, off));
-              a1 = __fadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, off));
-            }
-            const float s0 = sc[rho[2 * v] < p.tile_rows ? rho[2 * v] : 0u],
-                        s1 = sc[rho[2 * v + 1] < p.tile_rows ? rho[2 * v + 1] : 0u];
-            const float f0 = BITS == 8 ? __fmul_rn(s0, kInv127) : (BITS == 4 ? __fmul_rn(s0, kInv7) : s0);
-            const float f1 = BITS == 8 ? __fmul_rn(s1, kInv127) : (BITS == 4 ? __fmul_rn(s1, kInv7) : s1);
-            score[2 * v] = __fmul_rn(a0, f0);
-            score[2 * v + 1] = __fmul_rn(a1, f1);
+            for (int off = L / 2; off >= 1; off >>= 1) a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, off));
+            const float sv = sc[rho[u] < p.tile_rows ? rho[u] : 0u];
+            const float f = BITS == 8 ? __fmul_rn(sv, kInv127) : (BITS == 4 ? __fmul_rn(sv, kInv7) : sv);
+            score[u] = __fmul_rn(a, f);
           }
         } else {
           int iacc[U];
@@ -706,7 +731,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
-      if ((it + 1) % p.check_tiles == 0 && t + 1 < t1) {
+      if ((it + 1) % p.check_tiles == 0) {
         named_bar_sync(kBarConsumers, kConsumerThreads);
         const uint32_t n = misc[kMiscCount];
         if (n > high) {  // uniform: every consumer read the same count after the barrier

@@ -256,13 +256,15 @@ static float score_asym(int bits, int P, const uint8_t *row, float scale, const 
   int epc = CB * epb;                             /* elements per chunk */
   float s[32] = {0};
   for (int l = 0; l < L; l++) {
-    float acc = 0.0f;
+    /* two sub-chains per lane: even and odd element positions in lane order */
+    float acc[2] = {0.0f, 0.0f};
+    int pos = 0;
     for (int c = l; c < C; c += L)
-      for (int j = 0; j < epc; j++) {
+      for (int j = 0; j < epc; j++, pos++) {
         int e = c * epc + j;
-        acc = fmaf((float)code_at(row, bits, e), rq[e], acc);
+        acc[pos & 1] = fmaf((float)code_at(row, bits, e), rq[e], acc[pos & 1]);
       }
-    s[l] = acc;
+    s[l] = acc[0] + acc[1];
   }
   for (int off = L / 2; off >= 1; off >>= 1) {
     float t[32];

@@ -21,9 +21,12 @@
  *   - inside a chunk the elements are taken in index order (byte order for
  *     int8, low nibble then high nibble for int4, bit 0..31 of each LE word
  *     for 1-bit);
- *   - asym mode: lane accumulator starts at +0.0f and does acc = fmaf(v, q, acc)
- *     per element, v the exact integer code (int8 b in [-127,127], int4 n in
- *     [-7,7], 1-bit +-1) and q the fp32 rotated query;
+ *   - asym mode: each lane keeps two accumulators, both starting at +0.0f;
+ *     the lane's elements, counted in the order above, go alternately to the
+ *     even and the odd accumulator, each acc = fmaf(v, q, acc) with v the exact
+ *     integer code (int8 b in [-127,127], int4 n in [-7,7], 1-bit +-1) and q
+ *     the fp32 rotated query; the lane sum is even + odd (the two chains run
+ *     as one packed f32x2 FMA on the GPU);
  *   - the L lane sums reduce with an xor butterfly: for off = L/2 .. 1,
  *     s[l] = s[l] + s[l ^ off]; the result is s[0];
  *   - the row factor is applied last: int8 acc * (scale * f32(1/127)),
