@@ -149,17 +149,18 @@ typedef struct bv_stats {
 } bv_stats;
 BV_API int bv_get_stats(const bv_index* idx, bv_stats* out);
 
-/* Per-phase device timestamps of every scan launch (the device-side
- * counterpart of the reference's queryTrace, src/engine/profile.ts:16-29).
- * trace_dev: caller-owned device buffer of `capacity` u64; each launch with
- * grid G writes globaltimer ns at trace[b*8 + {0 entry, 1 query rotated,
- * 2 rows scored, 3 CTA list written}] for CTA b and, for the last CTA,
- * trace[G*8 + {0 merge start, 1 global merge done, 2 outputs written}].
- * Needs capacity >= (G+1)*8 (G <= the SM count); NULL disables. */
+/* Per-phase device timestamps of every search (the device-side counterpart
+ * of the reference's queryTrace, src/engine/profile.ts:16-29).  trace_dev is a
+ * caller-owned device buffer of `capacity` u64; a search with scan grid G
+ * writes globaltimer ns at trace[b*8 + {0 entry, 1 query rotated, 2 rows
+ * scored, 3 CTA list written}] for scan CTA b, and the tail kernel writes
+ * trace[G*8 + {5 entry, 0 merge start, 1 merged, 3 rows gathered, 4 re-ranked,
+ * 2 done}].  Needs capacity >= (G+1)*8 (G < the SM count); NULL disables. */
 BV_API int bv_set_phase_trace(bv_index* idx, uint64_t* trace_dev, uint64_t capacity);
 
 /* Kernel launches made by the last bv_search / bv_search_async /
- * bv_query_rows_exact on this index (the scan launches once per query). */
+ * bv_query_rows_exact on this index (a search launches a scan and a tail
+ * kernel per query). */
 BV_API int bv_launches_last_search(const bv_index* idx, uint32_t* launches);
 
 #ifdef __cplusplus
