@@ -19,7 +19,7 @@ SCORING = {"asym": SCORE_ASYM, "int": SCORE_INT, "hamming": SCORE_HAMMING}
 # Every symbol include/browservec.h declares (checked by the CPU test suite).
 EXPORTS = ("bv_create", "bv_destroy", "bv_last_error", "bv_append", "bv_append_device", "bv_size",
            "bv_search", "bv_search_async", "bv_query_rows_exact", "bv_export_codes", "bv_get_stats",
-           "bv_launches_last_search", "bv_set_phase_trace")
+           "bv_launches_last_search", "bv_set_phase_trace", "bv_search_noalloc")
 
 
 class BvConfig(C.Structure):
@@ -75,6 +75,7 @@ def load(path: str = LIB_PATH):
         "bv_get_stats": (C.c_int, [P, C.POINTER(BvStats)]),
         "bv_launches_last_search": (C.c_int, [P, C.POINTER(C.c_uint32)]),
         "bv_set_phase_trace": (C.c_int, [P, P, C.c_uint64]),
+        "bv_search_noalloc": (C.c_int, [P, C.POINTER(BvSearchArgs), P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

@@ -6,6 +6,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "../../include/browservec.h"
@@ -632,3 +633,152 @@ int bv_launches_last_search(const bv_index* idx, uint32_t* launches) {
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------- no-alloc search
+// bv_search_noalloc: the same scan + tail launches as bv_search_async, but all
+// of their scratch lives in one fixed device array of this file instead of
+// buffers the index allocates on demand.  For hosts that must not allocate
+// device memory after start-up.
+namespace {
+
+constexpr uint32_t kNoAllocMaxCtas = 160;  // scan grid bound (one CTA per SM, minus one)
+constexpr uint32_t kNoAllocMaxFp = 256;    // candidate slots per CTA: fetch <= 256
+constexpr size_t kNoAllocKeys = static_cast<size_t>(kNoAllocMaxCtas) * kNoAllocMaxFp;
+constexpr size_t kNoAllocCtr = kNoAllocKeys;      // 4 rotating tile counters
+constexpr size_t kNoAllocErr = kNoAllocKeys + 4;  // kernel error word
+constexpr size_t kNoAllocWords = kNoAllocKeys + 5;
+
+struct NoAllocDevice {
+  bool ready = false;
+  unsigned long long* base = nullptr;  // device address of the scratch array
+  uint32_t epoch = 0;                  // tile-counter epochs used on this device
+};
+constexpr int kNoAllocMaxDevices = 64;
+NoAllocDevice g_noalloc_dev[kNoAllocMaxDevices];
+std::mutex g_noalloc_mu;
+
+}  // namespace
+
+// 320 KB per device, loaded with the library and held until the process exits.
+static __device__ __align__(256) unsigned long long g_noalloc_scratch[kNoAllocWords];
+
+extern "C" int bv_search_noalloc(bv_index* idx, const bv_search_args* a, void* stream) {
+  uint32_t F = 0;
+  int rc = check_args(idx, a, &F);
+  if (rc) return rc;
+  uint32_t fp = 32;
+  while (fp < F) fp <<= 1;
+  if (fp > kNoAllocMaxFp)
+    return fail(BV_ERR_INVALID,
+                "bv_search_noalloc: fetch %u is above its fixed scratch limit of %u candidates per query",
+                F, kNoAllocMaxFp);
+  if (idx->device < 0 || idx->device >= kNoAllocMaxDevices)
+    return fail(BV_ERR_INVALID, "bv_search_noalloc: device ordinal %d out of range", idx->device);
+  BV_CUDA(idx, cudaSetDevice(idx->device), "cudaSetDevice");
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : idx->stream;
+
+  // First call on a device: resolve the array's device address (host code only
+  // sees a stand-in symbol).  Later calls reuse it.
+  unsigned long long* base = nullptr;
+  uint32_t epoch0 = 0;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    NoAllocDevice& d = g_noalloc_dev[idx->device];
+    if (!d.ready) {
+      void* ptr = nullptr;
+      const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+      if (e != cudaSuccess) return cuda_fail(idx, e, "bv_search_noalloc: scratch address");
+      d.base = static_cast<unsigned long long*>(ptr);
+      d.ready = true;
+    }
+    base = d.base;
+    epoch0 = d.epoch;
+    d.epoch += a->nq;
+  }
+  if (idx->rows == 0 || a->nq == 0) {
+    if (a->nq) BV_CUDA(idx, cudaMemsetAsync(a->out_counts, 0, a->nq * 4, s), "memset");
+    BV_CUDA(idx, cudaStreamSynchronize(s), "sync");
+    idx->last_launches = 0;
+    return BV_OK;
+  }
+  Plan pl;
+  if ((rc = plan_scan(idx, F, &pl))) return rc;
+  if (pl.grid > kNoAllocMaxCtas)
+    return fail(BV_ERR_UNSUPPORTED, "bv_search_noalloc: scan grid %u above its scratch bound %u", pl.grid,
+                kNoAllocMaxCtas);
+  uint32_t* err = reinterpret_cast<uint32_t*>(base + kNoAllocErr);
+  BV_CUDA(idx, cudaMemsetAsync(err, 0, sizeof(unsigned long long), s), "clear error word");
+
+  bv::ScanParams p;
+  memset(&p, 0, sizeof(p));
+  p.codes = idx->d_codes;
+  p.scales = idx->d_scales;
+  p.signs = idx->d_signs;
+  p.mask = a->mask;
+  p.nrows = idx->rows;
+  p.dim = idx->dim;
+  p.P = idx->P;
+  p.rounds = idx->rounds;
+  p.R = pl.sh.R;
+  p.tile_rows = pl.tile_rows;
+  p.tile_bytes = pl.tile_bytes;
+  p.ntiles = pl.ntiles;
+  p.stages = pl.stages;
+  p.F = pl.F;
+  p.Fp = pl.Fp;
+  p.capc = pl.capc;
+  p.check_tiles = pl.check_tiles;
+  p.partials = reinterpret_cast<uint64_t*>(base);
+  p.err = err;
+
+  bv::TailParams t;
+  memset(&t, 0, sizeof(t));
+  t.partials = reinterpret_cast<const uint64_t*>(base);
+  t.G = pl.grid;
+  t.F = pl.F;
+  t.Fp = pl.Fp;
+  t.capc = pl.capc;
+  t.k = a->k;
+  t.rerank = a->rerank ? 1 : 0;
+  t.originals = idx->d_orig;
+  t.dim = idx->dim;
+  t.row_base = idx->row_base;
+  t.err = err;
+  const uint32_t row_bytes = (idx->dim + 4) * 4;
+  const uint32_t fixed = bv::tail_smem_layout(idx->dim, pl.capc, 0).total + 256;
+  uint32_t rows_bytes =
+      static_cast<uint32_t>(idx->max_smem) > fixed ? static_cast<uint32_t>(idx->max_smem) - fixed : 0;
+  if (rows_bytes > pl.F * row_bytes) rows_bytes = pl.F * row_bytes;
+  rows_bytes = rows_bytes / row_bytes * row_bytes;
+  if (rows_bytes < row_bytes) return fail(BV_ERR_UNSUPPORTED, "re-rank row does not fit in shared memory");
+  t.rows_bytes = rows_bytes;
+  const size_t tail_smem = bv::tail_smem_layout(idx->dim, pl.capc, rows_bytes).total;
+
+  for (uint32_t q = 0; q < a->nq; ++q) {
+    p.query = a->queries + static_cast<size_t>(q) * idx->dim;
+    p.epoch = epoch0 + q + 1;  // unique per device; the array starts zeroed (epoch 0)
+    p.tile_ctr = base + kNoAllocCtr + (p.epoch & 3u);
+    cudaError_t e = launch_scan(static_cast<int>(idx->bits), static_cast<int>(idx->scoring), pl.sh, p,
+                                pl.grid, pl.smem, s);
+    if (e == cudaErrorNotSupported)
+      return fail(BV_ERR_UNSUPPORTED, "no scan kernel for bits=%u scoring=%u P=%u", idx->bits, idx->scoring,
+                  idx->P);
+    if (e != cudaSuccess) return cuda_fail(idx, e, "scan launch");
+    t.query = p.query;
+    t.out_rows = a->out_rows + static_cast<size_t>(q) * a->k;
+    t.out_scores = a->out_scores + static_cast<size_t>(q) * a->k;
+    t.out_count = a->out_counts + q;
+    const bool cand = a->cand_rows && a->cand_scores && a->cand_counts;
+    t.cand_rows = cand ? a->cand_rows + static_cast<size_t>(q) * F : nullptr;
+    t.cand_scores = cand ? a->cand_scores + static_cast<size_t>(q) * F : nullptr;
+    t.cand_count = cand ? a->cand_counts + q : nullptr;
+    e = bv::launch_tail(t, tail_smem, s);
+    if (e != cudaSuccess) return cuda_fail(idx, e, "tail launch");
+  }
+  idx->last_launches = 2 * a->nq;
+  BV_CUDA(idx, cudaStreamSynchronize(s), "bv_search_noalloc");
+  uint32_t flag = 0;
+  BV_CUDA(idx, cudaMemcpy(&flag, err, sizeof(flag), cudaMemcpyDeviceToHost), "error word");
+  if (flag) return fail(BV_ERR_TIMEOUT, "scan kernel wait ran out of budget (flag 0x%x)", flag);
+  return BV_OK;
+}

@@ -163,6 +163,27 @@ BV_API int bv_set_phase_trace(bv_index* idx, uint64_t* trace_dev, uint64_t capac
  * kernel per query). */
 BV_API int bv_launches_last_search(const bv_index* idx, uint32_t* launches);
 
+/* bv_search_noalloc: bv_search_async for callers that may not allocate
+ * device memory once they are running -- hosts whose device memory is all
+ * reserved up front by their own pool, or that run under a memory budget where
+ * a cudaMalloc (and the device-wide synchronisation a cudaFree brings) is not
+ * allowed on the query path.  It has no counterpart in the reference.
+ *
+ * Same arguments and results as bv_search_async (DEVICE pointers, the caller
+ * owns queries and outputs), but all scratch of the scan and tail kernels lives
+ * in one fixed array inside this library: 160 x 256 candidate keys plus a few
+ * counters, about 320 KB on every GPU that loads the library, held until the
+ * process exits.  Limits: fetch = max(fetch, k) <= 256 (BV_ERR_INVALID above
+ * that) and a scan grid of at most 160 CTAs (BV_ERR_UNSUPPORTED otherwise).
+ * The first call on a device looks up the array's device address with that
+ * device current; make that first call before any stream capture.  Every call
+ * on a device shares the one array, so calls that overlap on the GPU (other
+ * streams, other threads, other indexes on the same device) race and corrupt
+ * each other's results: serialise them.  The call synchronises `stream`
+ * (NULL = the index's stream) before it returns, and reports a kernel wait
+ * that ran out of budget as BV_ERR_TIMEOUT. */
+BV_API int bv_search_noalloc(bv_index* idx, const bv_search_args* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
