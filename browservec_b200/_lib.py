@@ -19,7 +19,8 @@ SCORING = {"asym": SCORE_ASYM, "int": SCORE_INT, "hamming": SCORE_HAMMING}
 # Every symbol include/browservec.h declares (checked by the CPU test suite).
 EXPORTS = ("bv_create", "bv_destroy", "bv_last_error", "bv_append", "bv_append_device", "bv_size",
            "bv_search", "bv_search_async", "bv_query_rows_exact", "bv_export_codes", "bv_get_stats",
-           "bv_launches_last_search", "bv_set_phase_trace", "bv_search_noalloc")
+           "bv_launches_last_search", "bv_set_phase_trace", "bv_search_noalloc",
+           "bv_merge_shards")
 
 
 class BvConfig(C.Structure):
@@ -33,7 +34,7 @@ class BvSearchArgs(C.Structure):
                 ("fetch", C.c_uint32), ("rerank", C.c_int32), ("mask", C.c_void_p),
                 ("mask_words", C.c_uint64), ("out_rows", C.c_void_p), ("out_scores", C.c_void_p),
                 ("out_counts", C.c_void_p), ("cand_rows", C.c_void_p), ("cand_scores", C.c_void_p),
-                ("cand_counts", C.c_void_p)]
+                ("cand_counts", C.c_void_p), ("cand_exact", C.c_void_p)]
 
 
 class BvStats(C.Structure):
@@ -76,6 +77,7 @@ def load(path: str = LIB_PATH):
         "bv_launches_last_search": (C.c_int, [P, C.POINTER(C.c_uint32)]),
         "bv_set_phase_trace": (C.c_int, [P, P, C.c_uint64]),
         "bv_search_noalloc": (C.c_int, [P, C.POINTER(BvSearchArgs), P]),
+        "bv_merge_shards": (C.c_int, [P, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, P, P, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

@@ -250,6 +250,8 @@ int check_args(bv_index* idx, const bv_search_args* a, uint32_t* F_out) {
   if (a->k == 0) return fail(BV_ERR_INVALID, "k must be >= 1");
   if (!a->out_rows || !a->out_scores || !a->out_counts)
     return fail(BV_ERR_INVALID, "output pointers are required");
+  if (a->cand_exact && !(a->rerank && a->cand_rows && a->cand_scores && a->cand_counts))
+    return fail(BV_ERR_INVALID, "cand_exact needs rerank and the cand_* outputs");
   uint32_t F = a->fetch ? a->fetch : a->k;
   if (F < a->k) F = a->k;
   if (F > kMaxFetch)
@@ -341,6 +343,7 @@ int enqueue_search(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStrea
     t.cand_rows = cand ? a->cand_rows + static_cast<size_t>(q) * F : nullptr;
     t.cand_scores = cand ? a->cand_scores + static_cast<size_t>(q) * F : nullptr;
     t.cand_count = cand ? a->cand_counts + q : nullptr;
+    t.cand_exact = cand && a->cand_exact ? a->cand_exact + static_cast<size_t>(q) * F : nullptr;
     e = bv::launch_tail(t, tail_smem, s);
     if (e != cudaSuccess) return cuda_fail(idx, e, "tail launch");
   }
@@ -495,6 +498,7 @@ int bv_search_async(bv_index* idx, const bv_search_args* a, void* stream) {
   cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : idx->stream;
   if (idx->rows == 0 || a->nq == 0) {  // quant.ts:184: an empty index returns []
     if (a->nq) BV_CUDA(idx, cudaMemsetAsync(a->out_counts, 0, a->nq * 4, s), "memset");
+    if (a->nq && a->cand_counts) BV_CUDA(idx, cudaMemsetAsync(a->cand_counts, 0, a->nq * 4, s), "memset");
     idx->last_launches = 0;
     return BV_OK;
   }
@@ -518,8 +522,10 @@ int bv_search(bv_index* idx, const bv_search_args* a) {
   const size_t qn = static_cast<size_t>(nq) * idx->dim;
   const size_t on = static_cast<size_t>(nq) * a->k;
   const size_t cn = cand ? static_cast<size_t>(nq) * F : 0;
-  // device staging: [rows on | scores on | counts nq | cand rows cn | cand scores cn | cand counts nq]
-  const size_t out_words = 2 * on + nq + 2 * cn + (cand ? nq : 0);
+  const size_t xn = cand && a->cand_exact ? cn : 0;
+  // device staging: [rows on | scores on | counts nq | cand rows cn | cand scores cn | cand counts nq |
+  //                  cand exact xn]
+  const size_t out_words = 2 * on + nq + 2 * cn + (cand ? nq : 0) + xn;
   if ((rc = grow(idx, &idx->d_q, &idx->q_cap, qn, "query staging"))) return rc;
   if ((rc = grow(idx, &idx->d_out, &idx->out_cap, out_words, "output staging"))) return rc;
   const size_t mw = a->mask ? (idx->rows + 31) / 32 : 0;
@@ -541,6 +547,7 @@ int bv_search(bv_index* idx, const bv_search_args* a) {
   d.cand_rows = cand ? idx->d_out + 2 * on + nq : nullptr;
   d.cand_scores = cand ? reinterpret_cast<float*>(idx->d_out + 2 * on + nq + cn) : nullptr;
   d.cand_counts = cand ? idx->d_out + 2 * on + nq + 2 * cn : nullptr;
+  d.cand_exact = xn ? reinterpret_cast<float*>(idx->d_out + 2 * on + 2 * nq + 2 * cn) : nullptr;
   if ((rc = enqueue_search(idx, &d, F, idx->stream))) return rc;
   BV_CUDA(idx, cudaMemcpyAsync(idx->h_pin, idx->d_out, out_words * 4, cudaMemcpyDeviceToHost, idx->stream),
           "D2H");
@@ -556,6 +563,7 @@ int bv_search(bv_index* idx, const bv_search_args* a) {
     memcpy(a->cand_rows, h + 2 * on + nq, cn * 4);
     memcpy(a->cand_scores, h + 2 * on + nq + cn, cn * 4);
     memcpy(a->cand_counts, h + 2 * on + nq + 2 * cn, nq * 4);
+    if (xn) memcpy(a->cand_exact, h + 2 * on + 2 * nq + 2 * cn, xn * 4);
   }
   return BV_OK;
 }
@@ -633,6 +641,23 @@ int bv_launches_last_search(const bv_index* idx, uint32_t* launches) {
 }
 
 }  // extern "C"
+
+int bv_merge_shards(const uint32_t* gathered, uint32_t world, uint32_t nq, uint32_t fetch, uint32_t k,
+                    uint32_t* out_rows, float* out_scores, uint32_t* out_counts, void* stream) {
+  if (!gathered || !out_rows || !out_scores || !out_counts) return fail(BV_ERR_INVALID, "null argument");
+  if (world == 0 || world > bv::merge_max_world())
+    return fail(BV_ERR_INVALID, "world %u outside [1, %u]", world, bv::merge_max_world());
+  if (k == 0 || fetch < k) return fail(BV_ERR_INVALID, "need 1 <= k <= fetch (k=%u, fetch=%u)", k, fetch);
+  if (fetch > kMaxFetch) return fail(BV_ERR_UNSUPPORTED, "fetch %u exceeds %u", fetch, kMaxFetch);
+  if (nq == 0) return BV_OK;
+  const cudaError_t e = bv::launch_merge_shards(gathered, world, nq, fetch, k, out_rows, out_scores, out_counts,
+                                                static_cast<cudaStream_t>(stream));
+  if (e == cudaErrorInvalidValue)
+    return fail(BV_ERR_UNSUPPORTED, "merge of %u shards x %u candidates does not fit in shared memory", world,
+                fetch);
+  if (e != cudaSuccess) return cuda_fail(nullptr, e, "merge launch");
+  return BV_OK;
+}
 
 // ------------------------------------------------------- no-alloc search
 // bv_search_noalloc: the same scan + tail launches as bv_search_async, but all
@@ -772,6 +797,7 @@ extern "C" int bv_search_noalloc(bv_index* idx, const bv_search_args* a, void* s
     t.cand_rows = cand ? a->cand_rows + static_cast<size_t>(q) * F : nullptr;
     t.cand_scores = cand ? a->cand_scores + static_cast<size_t>(q) * F : nullptr;
     t.cand_count = cand ? a->cand_counts + q : nullptr;
+    t.cand_exact = cand && a->cand_exact ? a->cand_exact + static_cast<size_t>(q) * F : nullptr;
     e = bv::launch_tail(t, tail_smem, s);
     if (e != cudaSuccess) return cuda_fail(idx, e, "tail launch");
   }

@@ -70,4 +70,34 @@ cudaError_t launch_exact_rows(const float* originals, uint32_t dim, const float*
                               uint32_t* out_rows, float* out_scores, uint32_t* out_count,
                               cudaStream_t stream);
 
+// Raise `func`'s dynamic shared-memory limit on the CURRENT device to the
+// device's opt-in maximum (minus the kernel's static shared memory), once per
+// device: function attributes belong to a device's context.  `opted` is the
+// caller's per-kernel table of limits already set; cudaErrorInvalidValue when
+// `need` cannot fit.
+constexpr int kMaxDevices = 64;
+inline cudaError_t opt_in_smem(const void* func, size_t need, int* opted) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  if (opted[dev] >= static_cast<int>(need)) return cudaSuccess;
+  cudaFuncAttributes fa;
+  if ((e = cudaFuncGetAttributes(&fa, func)) != cudaSuccess) return e;
+  int maxs = 0;
+  if ((e = cudaDeviceGetAttribute(&maxs, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess) return e;
+  const int lim = maxs - static_cast<int>(fa.sharedSizeBytes);
+  if (static_cast<int>(need) > lim) return cudaErrorInvalidValue;
+  if ((e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, lim)) != cudaSuccess) return e;
+  opted[dev] = lim;
+  return cudaSuccess;
+}
+
+// bv_merge.cu: cross-shard merge of all-gathered shard records
+size_t merge_smem_bytes(uint32_t world, uint32_t F);
+uint32_t merge_max_world();
+cudaError_t launch_merge_shards(const uint32_t* gathered, uint32_t world, uint32_t nq, uint32_t F, uint32_t k,
+                                uint32_t* out_rows, float* out_scores, uint32_t* out_counts,
+                                cudaStream_t stream);
+
 }  // namespace bv

@@ -10,16 +10,10 @@ namespace bv {
 template <int BITS, int MODE, int CB, int L, int CPL, int U>
 cudaError_t launch_one(const ScanParams& p, unsigned grid, size_t smem, cudaStream_t stream) {
   auto kern = scan_kernel<BITS, MODE, CB, L, CPL, U>;
-  // Opt in to the device's full dynamic shared memory once per kernel.
-  static int opted = 0;
-  if (opted < static_cast<int>(smem)) {
-    int dev = 0, maxs = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&maxs, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, maxs);
-    if (e != cudaSuccess) return e;
-    opted = maxs;
-  }
+  // Opt in to the device's full dynamic shared memory once per kernel and device.
+  static int opted[kMaxDevices] = {};
+  const cudaError_t e = opt_in_smem(reinterpret_cast<const void*>(kern), smem, opted);
+  if (e != cudaSuccess) return e;
   // Programmatic dependent launch: the kernel may start while the previous
   // scan in the stream finishes its merge; it waits (griddepcontrol.wait)
   // before touching the shared scratch.

@@ -163,6 +163,8 @@ __global__ void __launch_bounds__(kConsumerThreads, 1) tail_kernel(const TailPar
       }
       named_bar_sync(kBarConsumers, kConsumerThreads);
     }
+    if (p.cand_exact)
+      for (uint32_t i = ctid; i < nc; i += kConsumerThreads) p.cand_exact[i] = key_score(ex[i]);
     for (uint32_t i = nc + static_cast<uint32_t>(ctid); i < p.Fp; i += kConsumerThreads) ex[i] = 0ull;
     named_bar_sync(kBarConsumers, kConsumerThreads);
     if (p.trace && ctid == 0) p.trace[kTrTailDotted] = globaltimer();
@@ -195,15 +197,9 @@ __global__ void __launch_bounds__(kConsumerThreads, 1) tail_kernel(const TailPar
 }
 
 cudaError_t launch_tail(const TailParams& p, size_t smem, cudaStream_t stream) {
-  static int opted = 0;
-  if (opted < static_cast<int>(smem)) {
-    int dev = 0, maxs = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&maxs, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    cudaError_t e = cudaFuncSetAttribute(tail_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, maxs);
-    if (e != cudaSuccess) return e;
-    opted = maxs;
-  }
+  static int opted[kMaxDevices] = {};
+  const cudaError_t e = opt_in_smem(reinterpret_cast<const void*>(tail_kernel), smem, opted);
+  if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(1);
   cfg.blockDim = dim3(kConsumerThreads);

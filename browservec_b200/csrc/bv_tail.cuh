@@ -21,6 +21,7 @@ struct TailParams {
   uint32_t* cand_rows;       // optional
   float* cand_scores;
   uint32_t* cand_count;
+  float* cand_exact;         // optional: exact scores of the candidates, candidate order
   uint64_t* trace;           // optional: trace[kTrTail*]
 };
 

@@ -1,0 +1,190 @@
+"""Row-sharded quantized search: one process per GPU, one all-gather per batch.
+
+The reference splits a large corpus into row chunks that one GPU scans in
+turn (``ChunkedCorpus``, src/engine/buffers.ts:92-214, driven by
+QuantIndex.search, src/index/quant.ts:194-245).  Here the chunks become
+per-GPU shards: rank r of W holds the contiguous global rows
+``shard_bounds(n, W, r)`` (codes, scales and fp32 originals), scans them for
+every query, re-ranks its local best F exactly, and writes one shard record
+per batch.  A single ``all_gather_into_tensor`` (NCCL over NVLink) gives every
+rank all W records, and ``bv_merge_shards`` rebuilds the answer a single
+store would give: the global best F by approximate score, then the best k of
+those by exact score.
+
+Record layout (u32 words, one per rank, ``record_words(nq, F)`` long):
+``[rows nq*F | approx nq*F | exact nq*F | counts nq]`` -- rows are global.
+
+The CUDA engine is the only engine shipped; tests substitute their own
+``engine`` object to exercise the distributed plumbing on CPU ranks.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from contextlib import nullcontext
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _lib
+from .index import DEFAULT_SEED, AddonQuantIndex
+
+
+def shard_bounds(n: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous split of n rows over world ranks; the first n % world ranks
+    take one extra row."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside world {world}")
+    base, extra = divmod(n, world)
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
+
+
+def record_words(nq: int, fetch: int) -> int:
+    return 3 * nq * fetch + nq
+
+
+@dataclass
+class RecordViews:
+    """Views of one shard record (a 1-D int32 tensor or ndarray)."""
+    rows: object
+    approx: object
+    exact: object
+    counts: object
+
+
+def record_views(rec, nq: int, fetch: int) -> RecordViews:
+    plane = nq * fetch
+    return RecordViews(rows=rec[:plane], approx=rec[plane:2 * plane], exact=rec[2 * plane:3 * plane],
+                       counts=rec[3 * plane:3 * plane + nq])
+
+
+class CudaShardEngine:
+    """The shard-local work on this rank's GPU: bv_search_async into the
+    record, bv_merge_shards over the gathered records."""
+
+    def __init__(self, dim: int, bits: int, scoring: str, seed: int, rounds: int, metric: str,
+                 device: int, row_base: int):
+        import torch
+
+        self.torch = torch
+        self.device = torch.device("cuda", device)
+        self.index = AddonQuantIndex(dim, seed=seed, rounds=rounds, bits=bits, scoring=scoring,
+                                     device=device, metric=metric, row_base=row_base)
+        self.L = _lib.load()
+
+    @property
+    def size(self) -> int:
+        return self.index.size
+
+    def append(self, rows) -> None:
+        """rows: a float32 CUDA tensor (n, dim) on this rank's device, or a host array."""
+        torch = self.torch
+        if isinstance(rows, torch.Tensor) and rows.is_cuda:
+            rows = rows.contiguous()
+            self.index.append_device(rows.data_ptr(), rows.shape[0],
+                                     torch.cuda.current_stream(self.device).cuda_stream)
+            torch.cuda.current_stream(self.device).synchronize()
+        else:
+            a = np.ascontiguousarray(rows, dtype=np.float32)
+            self.index.append(a, a.shape[0])
+
+    def new_record(self, nq: int, fetch: int):
+        return self.torch.empty(record_words(nq, fetch), dtype=self.torch.int32, device=self.device)
+
+    def search_record(self, q, k: int, fetch: int, rec, stream: int) -> None:
+        nq = q.shape[0]
+        v = record_views(rec, nq, fetch)
+        if not hasattr(self, "_scratch") or self._scratch.numel() < nq * (2 * k + 1):
+            self._scratch = self.torch.empty(nq * (2 * k + 1), dtype=self.torch.int32, device=self.device)
+        s = self._scratch
+        args = _lib.BvSearchArgs(queries=q.data_ptr(), nq=nq, k=k, fetch=fetch, rerank=1, mask=None,
+                                 mask_words=0, out_rows=s.data_ptr(), out_scores=s[nq * k:].data_ptr(),
+                                 out_counts=s[2 * nq * k:].data_ptr(), cand_rows=v.rows.data_ptr(),
+                                 cand_scores=v.approx.data_ptr(), cand_counts=v.counts.data_ptr(),
+                                 cand_exact=v.exact.data_ptr())
+        _lib.check(self.L.bv_search_async(self.index._h, C.byref(args), C.c_void_p(stream)))
+
+    def merge(self, gathered, world: int, nq: int, k: int, fetch: int, stream: int):
+        torch = self.torch
+        rows = torch.empty((nq, k), dtype=torch.int32, device=self.device)
+        scores = torch.empty((nq, k), dtype=torch.float32, device=self.device)
+        counts = torch.empty(nq, dtype=torch.int32, device=self.device)
+        _lib.check(self.L.bv_merge_shards(C.c_void_p(gathered.data_ptr()), world, nq, fetch, k,
+                                          C.c_void_p(rows.data_ptr()), C.c_void_p(scores.data_ptr()),
+                                          C.c_void_p(counts.data_ptr()), C.c_void_p(stream)))
+        return rows, scores, counts
+
+    def destroy(self) -> None:
+        self.index.destroy()
+
+
+class ShardedIndex:
+    """Quantized flat index whose rows are split across the ranks of a
+    torch.distributed process group (NCCL, one process per GPU).
+
+    Every rank constructs it with the same arguments and the planned corpus
+    size ``n_total``; rank r then holds global rows ``shard_bounds(n_total,
+    W, r)``.  ``load`` takes each rank's slice (host array or a CUDA tensor of
+    just this rank's rows); ``search`` is collective: every rank calls it with
+    the same queries and receives the merged global answer.
+    """
+
+    def __init__(self, dim: int, n_total: int, bits: int = 8, scoring: str = "asym",
+                 seed: int = DEFAULT_SEED, rounds: int = 2, metric: str = "cosine", group=None,
+                 device: int | None = None, engine=None):
+        import torch
+        import torch.distributed as dist
+
+        if not dist.is_initialized():
+            raise RuntimeError("ShardedIndex needs an initialised torch.distributed process group")
+        self.torch, self.dist, self.group = torch, dist, group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.dim, self.n_total = dim, n_total
+        self.lo, self.hi = shard_bounds(n_total, self.world, self.rank)
+        if engine is None:
+            if device is None:
+                device = torch.cuda.current_device()
+            engine = CudaShardEngine(dim, bits, scoring, seed, rounds, metric, device, self.lo)
+            self._stream = torch.cuda.Stream(device=engine.device)
+        else:
+            self._stream = None
+        self.engine = engine
+
+    @property
+    def local_rows(self) -> int:
+        return self.hi - self.lo
+
+    def load(self, rows, global_rows: bool = False) -> None:
+        """Append this rank's rows: ``rows`` is either the full corpus
+        (``global_rows=True``, sliced here) or exactly this rank's slice."""
+        part = rows[self.lo:self.hi] if global_rows else rows
+        if part.shape[0] != self.local_rows:
+            raise ValueError(f"rank {self.rank} expects {self.local_rows} rows, got {part.shape[0]}")
+        if self.engine.size != 0:
+            raise RuntimeError("shard already loaded")
+        self.engine.append(part)
+
+    def search(self, q, k: int, fetch: int):
+        """Collective search of nq queries (a (nq, dim) float32 tensor on this
+        rank's device, normalised for cosine).  Returns (rows, scores, counts)
+        tensors of shape (nq, k), (nq, k), (nq,) with global rows."""
+        torch = self.torch
+        fetch = max(fetch, k)
+        nq = q.shape[0]
+        if self._stream is not None:
+            self._stream.wait_stream(torch.cuda.current_stream(self.engine.device))
+        ctx = torch.cuda.stream(self._stream) if self._stream is not None else nullcontext()
+        with ctx:
+            sid = self._stream.cuda_stream if self._stream is not None else 0
+            rec = self.engine.new_record(nq, fetch)
+            self.engine.search_record(q, k, fetch, rec, sid)
+            gathered = torch.empty(self.world * rec.numel(), dtype=rec.dtype, device=rec.device)
+            self.dist.all_gather_into_tensor(gathered, rec, group=self.group)
+            out = self.engine.merge(gathered, self.world, nq, k, fetch, sid)
+        if self._stream is not None:
+            torch.cuda.current_stream(self.engine.device).wait_stream(self._stream)
+        return out
+
+    def destroy(self) -> None:
+        self.engine.destroy()

@@ -100,7 +100,9 @@ BV_API int bv_size(const bv_index* idx, uint64_t* rows);
  *          (src/index/scoreMask.ts:66-92); mask_words must cover the rows.
  * Results per query q: out_rows/out_scores[q*k .. q*k+out_counts[q]), sorted
  * by score descending, ties by lower row.  cand_* (optional) receive the F
- * approximate candidates with their quantized scores. */
+ * approximate candidates with their quantized scores; cand_exact (optional,
+ * needs rerank and cand_*) their exact re-rank scores in the same order, the
+ * per-shard record a row-sharded search all-gathers (bv_merge_shards). */
 typedef struct bv_search_args {
   const float* queries;
   uint32_t nq;
@@ -115,6 +117,7 @@ typedef struct bv_search_args {
   uint32_t* cand_rows;
   float* cand_scores;
   uint32_t* cand_counts;
+  float* cand_exact;
 } bv_search_args;
 
 /* QuantIndex.query / queryMasked (src/index/quant.ts:165-245) plus the
@@ -162,6 +165,22 @@ BV_API int bv_set_phase_trace(bv_index* idx, uint64_t* trace_dev, uint64_t capac
  * bv_query_rows_exact on this index (a search launches a scan and a tail
  * kernel per query). */
 BV_API int bv_launches_last_search(const bv_index* idx, uint32_t* launches);
+
+/* Cross-shard merge of a row-sharded search (DEVICE pointers, enqueued on
+ * `stream`).  The corpus is split into W contiguous row ranges, one per GPU;
+ * each shard runs bv_search_async with cand_rows/cand_scores/cand_exact/
+ * cand_counts pointing into one record of 3*nq*fetch + nq u32 words laid out
+ * [rows nq*fetch | approx scores nq*fetch | exact scores nq*fetch | counts nq]
+ * (rows global: the index's row_base added), and the W records are
+ * all-gathered in rank order into `gathered`.  Writes per query the best k by
+ * exact score among the global best `fetch` by approximate score -- what one
+ * index over all rows returns.  This replaces the chunk loop and partial merge
+ * of QuantIndex.search (src/index/quant.ts:194-245, mergePartials in
+ * src/index/gpuTopk.ts:160-189) followed by the re-rank's topK
+ * (src/index.ts:583-594).  W <= 64; W*fetch*12 + fetch*8 bytes must fit in
+ * shared memory (W = 8 takes fetch up to 1024). */
+BV_API int bv_merge_shards(const uint32_t* gathered, uint32_t world, uint32_t nq, uint32_t fetch, uint32_t k,
+                           uint32_t* out_rows, float* out_scores, uint32_t* out_counts, void* stream);
 
 /* bv_search_noalloc: bv_search_async for callers that may not allocate
  * device memory once they are running -- hosts whose device memory is all

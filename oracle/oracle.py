@@ -346,3 +346,38 @@ def cpu_index_query_batch(data, dim: int, qs, k: int, threads: int = 0):
     so = np.zeros((nq, k), np.float32)
     lib().bvo_cpu_index_query_batch(_p(data), rows, dim, _p(qs), nq, k, threads, _p(ro), _p(so))
     return ro, so
+
+
+def keys(scores, rows) -> np.ndarray:
+    """Vectorised bvo_key: orderable(score) << 32 | ~row (score desc, row asc
+    when sorted descending); -0.0 counts as +0.0."""
+    s = _f32(scores).copy()
+    s[s == 0] = 0.0
+    u = s.view(np.uint32).astype(np.uint64)
+    neg = (u & 0x80000000) != 0
+    u = np.where(neg, (~u) & 0xFFFFFFFF, u | 0x80000000)
+    return (u << np.uint64(32)) | ((~_u32(rows)).astype(np.uint64) & np.uint64(0xFFFFFFFF))
+
+
+def shard_record(shard: "Corpus", row_base: int, q, k: int, fetch: int, mode: int = MODE_ASYM):
+    """One shard's contribution to a row-sharded search: its best `fetch`
+    candidates by approximate score (quant.ts:194-245 per chunk) with global
+    rows and their exact re-rank scores (store.ts:114-130)."""
+    q = _f32(q)
+    _, _, cr, cs = shard.query(q, k, fetch, mode)
+    exact = np.array([np.float32(dot_row(shard.originals[r], q)) for r in cr], np.float32)
+    return cr.astype(np.uint32) + np.uint32(row_base), cs.astype(np.float32), exact
+
+
+def merge_shard_records(records, fetch: int, k: int):
+    """Global best `fetch` by approximate key over all shard records, then the
+    best k by exact key (gpuTopk.ts:160-189 mergePartials, index.ts:583-594),
+    canonical order.  records: [(rows, approx, exact), ...]."""
+    rows = np.concatenate([r[0] for r in records]).astype(np.uint32)
+    approx = np.concatenate([r[1] for r in records]).astype(np.float32)
+    exact = np.concatenate([r[2] for r in records]).astype(np.float32)
+    ka = keys(approx, rows)
+    sel = np.argsort(ka)[::-1][:fetch]
+    ke = keys(exact[sel], rows[sel])
+    best = sel[np.argsort(ke)[::-1][:k]]
+    return rows[best], exact[best].copy()

@@ -1,0 +1,102 @@
+"""Row-sharded search on one GPU: W shard indexes (row_base = their first
+global row) write shard records through bv_search_async, the records are
+concatenated in rank order (what the all-gather produces) and bv_merge_shards
+must return exactly what one index over all rows returns -- rows bit-exact,
+scores bit-identical -- and what the oracle's merge returns.
+"""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _rows(n, d, seed):
+    rng = np.random.default_rng(seed)
+    return O.normalize_rows(rng.standard_normal((n, d)).astype(np.float32))
+
+
+@pytest.mark.parametrize("bits,scoring,world,n,d,k,fetch", [
+    (8, "asym", 2, 20000, 384, 10, 40),
+    (8, "int", 3, 9001, 768, 10, 40),
+    (4, "asym", 8, 30000, 384, 10, 80),
+    (4, "int", 4, 12345, 128, 10, 80),
+    (1, "hamming", 8, 40000, 768, 100, 1000),
+    (1, "asym", 3, 5000, 256, 10, 320),
+    (8, "asym", 4, 3, 64, 2, 8),  # fewer rows than shards: one shard is empty
+])
+def test_merge_equals_single_index(bits, scoring, world, n, d, k, fetch):
+    import torch
+
+    from browservec_b200.index import AddonQuantIndex
+    from browservec_b200.sharded import CudaShardEngine, record_words, shard_bounds
+
+    x = _rows(n, d, bits * 13 + world)
+    nq = 5
+    qs = _rows(nq, d, 77)
+    engines, single = [], None
+    try:
+        for r in range(world):
+            lo, hi = shard_bounds(n, world, r)
+            e = CudaShardEngine(d, bits, scoring, O.DEFAULT_SEED, 2, "cosine", 0, lo)
+            if hi > lo:
+                e.append(x[lo:hi])
+            engines.append(e)
+        single = AddonQuantIndex(d, bits=bits, scoring=scoring)
+        single.append(x, n)
+        want_rows, want_scores, want_counts, *_ = single.search_arrays(qs, k, fetch)
+
+        stream = torch.cuda.Stream()
+        q = torch.from_numpy(qs).cuda()
+        torch.cuda.synchronize()
+        recs = []
+        with torch.cuda.stream(stream):
+            for e in engines:
+                rec = e.new_record(nq, fetch)
+                e.search_record(q, k, fetch, rec, stream.cuda_stream)
+                recs.append(rec)
+            gathered = torch.cat(recs)
+            rows, scores, counts = engines[0].merge(gathered, world, nq, k, fetch, stream.cuda_stream)
+        stream.synchronize()
+        rows, scores, counts = rows.cpu().numpy(), scores.cpu().numpy(), counts.cpu().numpy()
+        assert gathered.numel() == world * record_words(nq, fetch)
+
+        g = gathered.cpu().numpy().reshape(world, -1)
+        for i in range(nq):
+            c = int(counts[i])
+            assert c == int(want_counts[i]) == min(k, n)
+            assert np.array_equal(rows[i, :c].view(np.uint32), want_rows[i, :c].astype(np.uint32)), i
+            assert np.array_equal(scores[i, :c].view(np.uint32), want_scores[i, :c].view(np.uint32)), i
+            recs_np = []
+            for w in range(world):
+                plane = nq * fetch
+                cnt = int(g[w, 3 * plane + i])
+                sl = slice(i * fetch, i * fetch + cnt)
+                recs_np.append((g[w, :plane][sl].view(np.uint32), g[w, plane:2 * plane][sl].view(np.float32),
+                                g[w, 2 * plane:3 * plane][sl].view(np.float32)))
+            orow, oscore = O.merge_shard_records(recs_np, fetch, k)
+            assert np.array_equal(orow, rows[i, :c].view(np.uint32))
+            assert np.array_equal(oscore.view(np.uint32), scores[i, :c].view(np.uint32))
+    finally:
+        for e in engines:
+            e.destroy()
+        if single is not None:
+            single.destroy()
+
+
+def test_merge_rejects_bad_arguments():
+    import torch
+
+    from browservec_b200 import _lib
+    from browservec_b200.sharded import CudaShardEngine
+
+    e = CudaShardEngine(64, 8, "asym", O.DEFAULT_SEED, 2, "cosine", 0, 0)
+    try:
+        g = torch.zeros(1024, dtype=torch.int32, device="cuda")
+        with pytest.raises(_lib.BvError, match="k <= fetch"):
+            e.merge(g, 2, 1, 10, 5, 0)
+        with pytest.raises(_lib.BvError, match="world 65"):
+            e.merge(g, 65, 1, 1, 5, 0)
+    finally:
+        e.destroy()
