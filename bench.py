@@ -122,6 +122,200 @@ def recall_at_10(torch, corpus, queries, got_rows):
     return hit / (exact.shape[0] * K)
 
 
+# Row-sharded configurations: rows split over the ranks,
+# one all-gather of shard records per step, merged on every rank.
+SHARDED = {
+    "c3": dict(bits=4, n=1_000_000, dim=384, kind="mixture", seed=3, nq=10_000, metric="dot", k=10, rf=8,
+               scoring="int", workload="BASELINE config 3: TurboQuant int4, queryBatch of 10,000, row-sharded"),
+    "c4": dict(bits=1, n=10_000_000, dim=768, kind="mixture", seed=4, nq=1000, metric="cosine", k=100, rf=10,
+               scoring="hamming", workload="BASELINE config 4: 1-bit codes, Hamming prefilter, queryBatch of "
+                                           "1,000, row-sharded"),
+    "c5": dict(bits=8, n=50_000_000, dim=128, kind="iid", seed=5, nq=4096, metric="cosine", k=10, rf=4,
+               scoring="int", workload="BASELINE config 5: TurboQuant int8, queryBatch of 4,096, row-sharded "
+                                       "(metadata filter not applied yet)"),
+}
+
+
+def _init_dist(torch):
+    """One process per GPU over NCCL; a one-rank group when not under torchrun."""
+    import socket
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world == 1 and "MASTER_PORT" not in os.environ:
+        with socket.socket() as s:
+            s.bind(("127.0.0.1", 0))
+            os.environ["MASTER_PORT"] = str(s.getsockname()[1])
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("RANK", "0")
+        os.environ.setdefault("WORLD_SIZE", "1")
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    return dist, world, rank, local
+
+
+def _exact_top10(torch, dist, x, lo, qs, chunk=1 << 20):
+    """Global exact fp32 top-10 (rows) of qs over the sharded corpus."""
+    best_v = torch.full((qs.shape[0], 10), -float("inf"), device=qs.device)
+    best_r = torch.zeros((qs.shape[0], 10), dtype=torch.int64, device=qs.device)
+    for a in range(0, x.shape[0], chunk):
+        s = qs @ x[a:a + chunk].T
+        v, r = s.topk(min(10, s.shape[1]), dim=1)
+        v = torch.cat([best_v, v], 1)
+        r = torch.cat([best_r, r + lo + a], 1)
+        best_v, i = v.topk(10, dim=1)
+        best_r = r.gather(1, i)
+    world = dist.get_world_size()
+    gv = [torch.empty_like(best_v) for _ in range(world)]
+    gr = [torch.empty_like(best_r) for _ in range(world)]
+    dist.all_gather(gv, best_v)
+    dist.all_gather(gr, best_r)
+    v, r = torch.cat(gv, 1), torch.cat(gr, 1)
+    _, i = v.topk(10, dim=1)
+    return r.gather(1, i).cpu().numpy()
+
+
+def _cpu_sample_qps(torch, dev, cfg, threads, sample_rows, sample_queries):
+    """The reference CPU path (WASM-SIMD exact fp32 scan + topK, restated in C)
+    over the first `sample_rows` rows, scaled to the full corpus (a flat scan's
+    time is linear in the rows)."""
+    from browservec_b200 import datagen
+    from oracle import oracle as O
+
+    xs = datagen.rows(torch, dev, cfg["kind"], cfg["seed"], 0, sample_rows, cfg["dim"]).cpu().numpy()
+    qs = datagen.rows(torch, dev, cfg["kind"], cfg["seed"], 0, sample_queries, cfg["dim"],
+                      stream=datagen.STREAM_QUERIES).cpu().numpy()
+    O.cpu_index_query_batch(xs, cfg["dim"], qs[:threads], cfg["k"], threads=threads)  # warm
+    t0 = time.perf_counter()
+    O.cpu_index_query_batch(xs, cfg["dim"], qs, cfg["k"], threads=threads)
+    dt = time.perf_counter() - t0
+    return sample_queries / dt * (sample_rows / cfg["n"]), dt
+
+
+def run_sharded(args, name):
+    import torch
+
+    from browservec_b200 import datagen
+    from browservec_b200.sharded import ShardedIndex, shard_bounds
+
+    cfg = SHARDED[name]
+    dist, world, rank, local = _init_dist(torch)
+    dev = torch.device("cuda", local)
+    n, dim, nq, k = cfg["n"], cfg["dim"], cfg["nq"], cfg["k"]
+    fetch = min(n, max(k, k * cfg["rf"]))  # src/index.ts:414-417
+    lo, hi = shard_bounds(n, world, rank)
+    R = {8: 1, 4: 2, 1: 8}[cfg["bits"]]
+    P = 1 << (dim - 1).bit_length()
+    config = {"workload": cfg["workload"], "rows": n, "dim": dim, "padded_dim": P, "bits": cfg["bits"],
+              "queries_per_step": nq, "k": k, "fetch": fetch, "metric": cfg["metric"], "scoring": cfg["scoring"],
+              "parallelism": f"row shards x{world} + NCCL all-gather merge", "data_kind": cfg["kind"],
+              "l2": f"each query scans {(hi - lo) * (P // R + 4) / 1e6:.0f} MB of codes per GPU"
+                    + (" (> 126 MB L2)" if (hi - lo) * (P // R + 4) > 126e6 else " (L2-resident shard)"),
+              "search": "per query one scan + one tail launch, then one merge launch per step"}
+    threads = os.cpu_count() or 1
+    if args.impl == "reference":
+        if rank == 0:
+            srows = min(n, 1_000_000 if dim >= 384 else 2_000_000)
+            qps, dt = _cpu_sample_qps(torch, dev, cfg, threads, srows, max(threads, 16))
+            line = {"metric": METRIC_SHARDED, "value": qps, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                    "warmup": args.warmup, "ms_per_step": nq / qps * 1e3, "higher_is_better": True,
+                    "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                    "impl": "reference", "config": config,
+                    "cpu_baseline": {"value": qps, "unit": UNIT, "cores": threads, "kind": "port",
+                                     "sample": f"{max(threads, 16)} queries over the first {srows} rows, "
+                                               f"scaled to {n} rows (WASM-SIMD exact scan restated in C)"},
+                    "e2e": {"value": qps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            print(json.dumps(line))
+        dist.destroy_process_group()
+        return
+
+    x = datagen.rows(torch, dev, cfg["kind"], cfg["seed"], lo, hi, dim)
+    idx = ShardedIndex(dim, n, bits=cfg["bits"], scoring=cfg["scoring"], metric=cfg["metric"], device=local)
+    idx.load(x)
+    qs = datagen.rows(torch, dev, cfg["kind"], cfg["seed"], 0, nq, dim, stream=datagen.STREAM_QUERIES)
+    torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        rows, scores, counts = idx.search(qs, k, fetch)
+    torch.cuda.synchronize()
+    dist.barrier()
+    clk = Clocks(local)
+    cur = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(cur)
+    for _ in range(args.steps):
+        rows, scores, counts = idx.search(qs, k, fetch)
+    e1.record(cur)
+    torch.cuda.synchronize()
+    clk_res = clk.stop()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    qps = args.steps * nq / (ms / 1e3)
+
+    ns = min(nq, 100)
+    truth = _exact_top10(torch, dist, x, lo, qs[:ns])
+    got = rows[:ns, :10].cpu().numpy()
+    rec = sum(len(set(truth[i].tolist()) & set(got[i].tolist())) for i in range(ns)) / (ns * 10)
+
+    # per-GPU roofline of the scan: codes + scales of the shard, the re-rank rows, the query
+    query_ms = ms / (args.steps * nq)
+    algo_bytes = (hi - lo) * (P // R + 4) + fetch * dim * 4 + dim * 4
+    peak, peak_kind = peaks()
+    achieved = algo_bytes / (query_ms / 1e3) / 1e9
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "traffic": None, "peak_kind": f"{peak_kind} (copy bandwidth, MEASURED_PEAKS.json hbm_gbs)",
+                "algorithmic_bytes_per_launch": algo_bytes,
+                "duration": "per query per GPU: timed region / queries (scan + tail, all-gather and merge "
+                            "amortised)"}
+
+    # e2e: host queries (pinned) -> device, search, results back to the host, every step
+    q_host = qs.cpu().pin_memory()
+    e2e_steps = max(1, min(args.steps, 3))
+    torch.cuda.synchronize()
+    dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        qd = q_host.to(dev, non_blocking=True)
+        r_, s_, c_ = idx.search(qd, k, fetch)
+        r_, s_, c_ = r_.cpu(), s_.cpu(), c_.cpu()
+    wall = time.perf_counter() - t0
+    t = torch.tensor([wall], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    wall = float(t.item())
+    e2e = {"value": e2e_steps * nq / wall, "unit": UNIT, "h2d_bytes_per_step": nq * dim * 4,
+           "d2h_bytes_per_step": nq * (2 * k + 1) * 4, "steps": e2e_steps,
+           "timing": "host wall clock, max over ranks"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        srows = min(n, 1_000_000 if dim >= 384 else 2_000_000)
+        cqps, _ = _cpu_sample_qps(torch, dev, cfg, threads, srows, max(threads, 16))
+        cpu = {"value": cqps, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"{max(threads, 16)} queries over the first {srows} rows, scaled to {n} rows "
+                         "(WASM-SIMD exact scan restated in C, one query per thread)"}
+    if rank == 0:
+        line = {"metric": METRIC_SHARDED, "value": qps, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": {"int": "s8", "hamming": "b1"}.get(
+                    cfg["scoring"], "f32xs8"),
+                "data": f"synthetic (seeded Philox, {cfg['kind']}, L2-normalised)", "config": config,
+                "recall_at_10": rec, "recall_sample": ns, "query_ms": query_ms,
+                "gpu_launches": args.steps * (2 * nq + 1), "roofline": roofline, "cpu_baseline": cpu,
+                "e2e": e2e, "clocks": clk_res}
+        print(json.dumps(line))
+    idx.destroy()
+    dist.destroy_process_group()
+
+
+METRIC_SHARDED = "queries/sec at fixed recall@10 (row-sharded quantized flat scan)"
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -134,7 +328,10 @@ def main():
     ap.add_argument("--replicas", type=int, default=4)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--config", default="c2", choices=["c2", *SHARDED])
     args = ap.parse_args()
+    if args.config != "c2":
+        return run_sharded(args, args.config)
 
     import torch
 

@@ -20,7 +20,7 @@ SCORING = {"asym": SCORE_ASYM, "int": SCORE_INT, "hamming": SCORE_HAMMING}
 EXPORTS = ("bv_create", "bv_destroy", "bv_last_error", "bv_append", "bv_append_device", "bv_size",
            "bv_search", "bv_search_async", "bv_query_rows_exact", "bv_export_codes", "bv_get_stats",
            "bv_launches_last_search", "bv_set_phase_trace", "bv_search_noalloc",
-           "bv_merge_shards")
+           "bv_merge_shards", "bv_search_batch")
 
 
 class BvConfig(C.Structure):
@@ -78,6 +78,7 @@ def load(path: str = LIB_PATH):
         "bv_set_phase_trace": (C.c_int, [P, P, C.c_uint64]),
         "bv_search_noalloc": (C.c_int, [P, C.POINTER(BvSearchArgs), P]),
         "bv_merge_shards": (C.c_int, [P, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, P, P, P, P]),
+        "bv_search_batch": (C.c_int, [P, C.POINTER(BvSearchArgs), P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

@@ -13,6 +13,7 @@
 #include "bv_internal.h"
 #include "bv_scan.cuh"
 #include "bv_tail.cuh"
+#include "bv_batch.cuh"
 
 namespace {
 
@@ -30,6 +31,7 @@ int fail(int status, const char* fmt, ...) {
 
 constexpr const char* kLostMsg = "GPU device lost; re-create the store";  // quant.ts:183
 constexpr uint32_t kRowAlign = 2048;      // capacity granularity (>= any scan tile)
+constexpr uint32_t kBatchMinQueries = 64;  // bv_search batches at least this many on the tensor cores
 constexpr uint32_t kMaxFetch = 1024;      // fused single-query path: F <= 1024
 constexpr uint32_t kMaxPadded = 4096;
 
@@ -103,6 +105,28 @@ struct bv_index {
   uint64_t* d_trace = nullptr;   // optional phase-timestamp buffer (caller-owned device memory)
   uint64_t trace_cap = 0;
   bool lost = false;
+  // batched search: the codes as swizzled int8 MMA tiles (built lazily, for
+  // rows [0, mma_rows)), per-row score factors, per-tile factor maxima
+  int8_t* d_ctiles = nullptr;
+  size_t ctiles_cap = 0;  // bytes
+  float* d_rowfac = nullptr;
+  size_t rowfac_cap = 0;
+  float* d_tmax = nullptr;
+  size_t tmax_cap = 0;
+  uint64_t mma_rows = 0;
+  // batched search scratch
+  int8_t* d_qtiles = nullptr;
+  size_t qtiles_cap = 0;
+  float* d_qfac = nullptr;
+  size_t qfac_cap = 0;
+  uint64_t* d_thr = nullptr;
+  size_t thr_cap = 0;
+  uint32_t* d_bcnt = nullptr;  // candidate counts, then their backup
+  size_t bcnt_cap = 0;
+  uint64_t* d_bcand = nullptr;
+  size_t bcand_cap = 0;
+  uint32_t* d_overflow = nullptr;
+  uint32_t last_rounds = 0;
 };
 
 namespace {
@@ -444,6 +468,15 @@ int bv_destroy(bv_index* idx) {
   cudaFree(idx->d_mask);
   cudaFree(idx->d_rows);
   cudaFree(idx->d_out);
+  cudaFree(idx->d_ctiles);
+  cudaFree(idx->d_rowfac);
+  cudaFree(idx->d_tmax);
+  cudaFree(idx->d_qtiles);
+  cudaFree(idx->d_qfac);
+  cudaFree(idx->d_thr);
+  cudaFree(idx->d_bcnt);
+  cudaFree(idx->d_bcand);
+  cudaFree(idx->d_overflow);
   if (idx->h_pin) cudaFreeHost(idx->h_pin);
   if (idx->ev0) cudaEventDestroy(idx->ev0);
   if (idx->ev1) cudaEventDestroy(idx->ev1);
@@ -548,7 +581,12 @@ int bv_search(bv_index* idx, const bv_search_args* a) {
   d.cand_scores = cand ? reinterpret_cast<float*>(idx->d_out + 2 * on + nq + cn) : nullptr;
   d.cand_counts = cand ? idx->d_out + 2 * on + nq + 2 * cn : nullptr;
   d.cand_exact = xn ? reinterpret_cast<float*>(idx->d_out + 2 * on + 2 * nq + 2 * cn) : nullptr;
-  if ((rc = enqueue_search(idx, &d, F, idx->stream))) return rc;
+  if (idx->scoring != BV_SCORE_ASYM && nq >= kBatchMinQueries) {
+    // a batch on the tensor cores: the same results as the per-query scans
+    if ((rc = bv_search_batch(idx, &d, idx->stream))) return rc;
+  } else if ((rc = enqueue_search(idx, &d, F, idx->stream))) {
+    return rc;
+  }
   BV_CUDA(idx, cudaMemcpyAsync(idx->h_pin, idx->d_out, out_words * 4, cudaMemcpyDeviceToHost, idx->stream),
           "D2H");
   BV_CUDA(idx, cudaEventRecord(idx->ev1, idx->stream), "event");
@@ -657,6 +695,256 @@ int bv_merge_shards(const uint32_t* gathered, uint32_t world, uint32_t nq, uint3
                 fetch);
   if (e != cudaSuccess) return cuda_fail(nullptr, e, "merge launch");
   return BV_OK;
+}
+
+// ------------------------------------------------------- batched search
+namespace {
+
+// Grow a device buffer to `need` elements keeping its first `keep` elements.
+template <class T>
+int grow_keep(bv_index* idx, T** p, size_t* cap, size_t need, size_t keep, cudaStream_t s, const char* what) {
+  if (*cap >= need) return BV_OK;
+  size_t n = *cap ? *cap : 1;
+  while (n < need) n *= 2;
+  T* q = nullptr;
+  cudaError_t e = cudaMalloc(&q, n * sizeof(T));
+  if (e != cudaSuccess) return cuda_fail(idx, e, what);
+  if (keep && *p) {
+    e = cudaMemcpyAsync(q, *p, keep * sizeof(T), cudaMemcpyDeviceToDevice, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) {
+      cudaFree(q);
+      return cuda_fail(idx, e, what);
+    }
+  }
+  cudaFree(*p);
+  *p = q;
+  *cap = n;
+  return BV_OK;
+}
+
+// Bring the MMA tiles up to date with the appended rows.
+int ensure_mma(bv_index* idx, cudaStream_t s) {
+  if (idx->mma_rows >= idx->rows) return BV_OK;
+  const uint32_t KB = (idx->P + bv::kKBlock - 1) / bv::kKBlock;
+  const size_t tiles = (idx->rows + bv::kBRowTile - 1) / bv::kBRowTile;
+  const size_t kept_tiles = (idx->mma_rows + bv::kBRowTile - 1) / bv::kBRowTile;
+  int rc;
+  if ((rc = grow_keep(idx, &idx->d_ctiles, &idx->ctiles_cap, tiles * KB * bv::kBRowTileBytes,
+                      kept_tiles * KB * bv::kBRowTileBytes, s, "batch tiles")))
+    return rc;
+  if ((rc = grow_keep(idx, &idx->d_rowfac, &idx->rowfac_cap, tiles * bv::kBRowTile, idx->mma_rows, s,
+                      "batch factors")))
+    return rc;
+  if ((rc = grow_keep(idx, &idx->d_tmax, &idx->tmax_cap, tiles, kept_tiles, s, "batch factors"))) return rc;
+  bv::ExpandParams ep;
+  ep.codes = idx->d_codes;
+  ep.scales = idx->d_scales;
+  ep.R = idx->R;
+  ep.P = idx->P;
+  ep.KB = KB;
+  ep.bits = idx->bits;
+  ep.row0 = static_cast<uint32_t>(idx->mma_rows);
+  ep.row1 = static_cast<uint32_t>(idx->rows);
+  ep.nrows = static_cast<uint32_t>(idx->rows);
+  ep.ctiles = idx->d_ctiles;
+  ep.rowfac = idx->d_rowfac;
+  ep.tmax = idx->d_tmax;
+  const cudaError_t e = bv::launch_expand(ep, s);
+  if (e != cudaSuccess) return cuda_fail(idx, e, "batch expand");
+  idx->mma_rows = idx->rows;
+  return BV_OK;
+}
+
+}  // namespace
+
+int bv_search_batch(bv_index* idx, const bv_search_args* a, void* stream) {
+  uint32_t F = 0;
+  int rc = check_args(idx, a, &F);
+  if (rc) return rc;
+  if (idx->scoring == BV_SCORE_ASYM)
+    return fail(BV_ERR_UNSUPPORTED, "the batched search scores with the integer modes (int, hamming), "
+                                    "not asym");
+  if (idx->rows > 0xFFFFFF00ull) return fail(BV_ERR_UNSUPPORTED, "batched search takes < 2^32 rows");
+  BV_CUDA(idx, cudaSetDevice(idx->device), "cudaSetDevice");
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : idx->stream;
+  const uint32_t nq = a->nq;
+  if (idx->rows == 0 || nq == 0) {
+    if (nq) BV_CUDA(idx, cudaMemsetAsync(a->out_counts, 0, nq * 4, s), "memset");
+    if (nq && a->cand_counts) BV_CUDA(idx, cudaMemsetAsync(a->cand_counts, 0, nq * 4, s), "memset");
+    BV_CUDA(idx, cudaStreamSynchronize(s), "sync");
+    idx->last_launches = 0;
+    return BV_OK;
+  }
+  if ((rc = ensure_mma(idx, s))) return rc;
+  uint32_t Fp = 32;
+  while (Fp < F) Fp <<= 1;
+  const uint32_t cap = Fp * 16 > 4096 ? Fp * 16 : 4096;  // <= 16384 (F <= 1024)
+  const uint32_t KB = (idx->P + bv::kKBlock - 1) / bv::kKBlock;
+  const uint32_t nqt = (nq + bv::kBQTile - 1) / bv::kBQTile;
+  const uint32_t T = static_cast<uint32_t>((idx->rows + bv::kBRowTile - 1) / bv::kBRowTile);
+  if ((rc = grow(idx, &idx->d_qtiles, &idx->qtiles_cap, static_cast<size_t>(nqt) * KB * bv::kBQTileBytes,
+                 "batch queries")))
+    return rc;
+  if ((rc = grow(idx, &idx->d_qfac, &idx->qfac_cap, nq, "batch queries"))) return rc;
+  if ((rc = grow(idx, &idx->d_thr, &idx->thr_cap, nq, "batch thresholds"))) return rc;
+  if ((rc = grow(idx, &idx->d_bcnt, &idx->bcnt_cap, 2 * static_cast<size_t>(nq), "batch counts"))) return rc;
+  if ((rc = grow(idx, &idx->d_bcand, &idx->bcand_cap, static_cast<size_t>(nq) * cap, "batch candidates")))
+    return rc;
+  if (!idx->d_overflow) BV_CUDA(idx, cudaMalloc(&idx->d_overflow, 8), "batch flag");
+
+  bv::PrepParams pp;
+  pp.queries = a->queries;
+  pp.signs = idx->d_signs;
+  pp.nq = nq;
+  pp.dim = idx->dim;
+  pp.P = idx->P;
+  pp.KB = KB;
+  pp.rounds = idx->rounds;
+  pp.hamming = idx->scoring == BV_SCORE_HAMMING && idx->bits == 1 ? 1 : 0;
+  pp.qtiles = idx->d_qtiles;
+  pp.qfac = idx->d_qfac;
+  pp.thr = idx->d_thr;
+  pp.cnt = idx->d_bcnt;
+
+  bv::GemmParams g;
+  g.ctiles = idx->d_ctiles;
+  g.qtiles = idx->d_qtiles;
+  g.rowfac = idx->d_rowfac;
+  g.tmax = idx->d_tmax;
+  g.mask = a->mask;
+  g.nrows = static_cast<uint32_t>(idx->rows);
+  g.nq = nq;
+  g.KB = KB;
+  g.nqt = nqt;
+  g.thr = idx->d_thr;
+  g.qfac = idx->d_qfac;
+  g.cand = idx->d_bcand;
+  g.cap = cap;
+  g.cnt = idx->d_bcnt;
+  g.overflow = idx->d_overflow;
+  g.err = idx->d_err;
+
+  bv::SelectParams sp;
+  sp.cand = idx->d_bcand;
+  sp.cap = cap;
+  sp.F = F;
+  sp.Fp = Fp;
+  sp.nq = nq;
+  sp.cnt = idx->d_bcnt;
+  sp.thr = idx->d_thr;
+
+  uint32_t launches = 0;
+  auto gemm = [&](uint32_t rt0, uint32_t rt1) -> int {
+    g.rt0 = rt0;
+    g.rt1 = rt1;
+    const uint64_t tiles = static_cast<uint64_t>(rt1 - rt0) * nqt;
+    const uint32_t grid = static_cast<uint32_t>(tiles < static_cast<uint64_t>(idx->num_sms) ? tiles : idx->num_sms);
+    const cudaError_t e = bv::launch_gemm(g, grid, s);
+    if (e != cudaSuccess) return cuda_fail(idx, e, "batch gemm");
+    ++launches;
+    return BV_OK;
+  };
+  auto select = [&]() -> int {
+    const cudaError_t e = bv::launch_select(sp, s);
+    if (e != cudaSuccess) return cuda_fail(idx, e, "batch select");
+    ++launches;
+    return BV_OK;
+  };
+  // Round sizes in row tiles: the first takes cap rows (every row is a
+  // candidate); later ones grow so that about (cap - F) / 2 rows are expected
+  // to beat the threshold of the rows already seen.
+  const uint32_t first = cap / bv::kBRowTile;
+  auto next_size = [&](uint32_t seen_tiles) -> uint32_t {
+    const double grow = static_cast<double>(cap - F) / (2.0 * F);
+    double m = static_cast<double>(seen_tiles) * grow;
+    return m < 1.0 ? 1u : (m > 4.0e9 ? 0xFFFFFFFFu : static_cast<uint32_t>(m));
+  };
+
+  BV_CUDA(idx, cudaMemsetAsync(idx->d_overflow, 0, 4, s), "batch flag");
+  cudaError_t e = bv::launch_prep(pp, s);
+  if (e != cudaSuccess) return cuda_fail(idx, e, "batch prep");
+  launches = 1;
+  uint32_t nrounds = 0;
+  for (uint32_t rt = 0; rt < T;) {
+    const uint32_t m = rt == 0 ? first : next_size(rt);
+    const uint32_t rt1 = T - rt < m ? T : rt + m;
+    if ((rc = gemm(rt, rt1)) || (rc = select())) return rc;
+    ++nrounds;
+    rt = rt1;
+  }
+  uint32_t flag = 0;
+  BV_CUDA(idx, cudaMemcpyAsync(&flag, idx->d_overflow, 4, cudaMemcpyDeviceToHost, s), "batch flag");
+  BV_CUDA(idx, cudaStreamSynchronize(s), "batch search");
+  if (flag) {
+    // A buffer overflowed (rows that arrive in increasing score order, for
+    // instance): redo the batch round by round, halving a round that
+    // overflows; a round of one tile (256 rows) cannot overflow (cap >= F + 256).
+    e = bv::launch_prep(pp, s);
+    if (e != cudaSuccess) return cuda_fail(idx, e, "batch prep");
+    launches += 1;
+    uint32_t m = first;
+    for (uint32_t rt = 0; rt < T;) {
+      const uint32_t rt1 = T - rt < m ? T : rt + m;
+      BV_CUDA(idx, cudaMemcpyAsync(idx->d_bcnt + nq, idx->d_bcnt, nq * 4, cudaMemcpyDeviceToDevice, s), "backup");
+      BV_CUDA(idx, cudaMemsetAsync(idx->d_overflow, 0, 4, s), "batch flag");
+      if ((rc = gemm(rt, rt1))) return rc;
+      BV_CUDA(idx, cudaMemcpyAsync(&flag, idx->d_overflow, 4, cudaMemcpyDeviceToHost, s), "batch flag");
+      BV_CUDA(idx, cudaStreamSynchronize(s), "batch search");
+      if (flag) {
+        // the round's appends are discarded (the lists' first entries and the
+        // thresholds are untouched by the GEMM) and the round is repeated smaller
+        if (rt1 - rt == 1) return fail(BV_ERR_CUDA, "batch candidate buffer overflow on a single tile");
+        BV_CUDA(idx, cudaMemcpyAsync(idx->d_bcnt, idx->d_bcnt + nq, nq * 4, cudaMemcpyDeviceToDevice, s),
+                "restore");
+        m = (rt1 - rt) / 2;
+        continue;
+      }
+      if ((rc = select())) return rc;
+      ++nrounds;
+      rt = rt1;
+      m = m < 0x7FFFFFFFu ? 2 * m : m;
+    }
+  }
+  // exact re-rank of each query's best F and the outputs: one tail CTA per query
+  bv::TailParams t;
+  memset(&t, 0, sizeof(t));
+  t.partials = idx->d_bcand;
+  t.partials_stride = cap;
+  t.G = 1;
+  t.F = F;
+  t.Fp = Fp;
+  t.capc = Fp <= 256 ? (16 * Fp > 1024 ? 16 * Fp : 1024) : (2 * Fp > 1024 ? 2 * Fp : 1024);
+  t.k = a->k;
+  t.rerank = a->rerank ? 1 : 0;
+  t.query = a->queries;
+  t.originals = idx->d_orig;
+  t.dim = idx->dim;
+  t.row_base = idx->row_base;
+  t.err = idx->d_err;
+  t.out_rows = a->out_rows;
+  t.out_scores = a->out_scores;
+  t.out_count = a->out_counts;
+  const bool cand = a->cand_rows && a->cand_scores && a->cand_counts;
+  t.cand_rows = cand ? a->cand_rows : nullptr;
+  t.cand_scores = cand ? a->cand_scores : nullptr;
+  t.cand_count = cand ? a->cand_counts : nullptr;
+  t.cand_exact = cand ? a->cand_exact : nullptr;
+  const uint32_t row_bytes = (idx->dim + 4) * 4;
+  const uint32_t fixed = bv::tail_smem_layout(idx->dim, t.capc, 0).total + 256;
+  uint32_t rows_bytes =
+      static_cast<uint32_t>(idx->max_smem) > fixed ? static_cast<uint32_t>(idx->max_smem) - fixed : 0;
+  if (rows_bytes > F * row_bytes) rows_bytes = F * row_bytes;
+  rows_bytes = rows_bytes / row_bytes * row_bytes;
+  if (rows_bytes < row_bytes) return fail(BV_ERR_UNSUPPORTED, "re-rank row does not fit in shared memory");
+  t.rows_bytes = rows_bytes;
+  e = bv::launch_tail_grid(t, nq, bv::tail_smem_layout(idx->dim, t.capc, rows_bytes).total, s);
+  if (e != cudaSuccess) return cuda_fail(idx, e, "batch tail");
+  launches += 1;
+  BV_CUDA(idx, cudaStreamSynchronize(s), "batch search");
+  idx->last_launches = launches;
+  idx->last_rounds = nrounds;
+  return check_err_flag(idx);
 }
 
 // ------------------------------------------------------- no-alloc search

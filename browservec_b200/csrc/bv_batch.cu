@@ -1,0 +1,453 @@
+// bv_batch.cu -- kernels of the batched tensor-core search (see bv_batch.cuh).
+//
+//   expand_kernel  codes -> swizzled int8 row tiles + per-row score factor
+//                  (the layout the MMA reads; built once per appended row)
+//   prep_kernel    per query: rotation (rotator.ts:83-92), int8 codec
+//                  (codec.ts:132-154) or signs, swizzled query tiles
+//   gemm_kernel    persistent; warp-specialised: one producer warp (bulk
+//                  copies), one MMA warp (tcgen05.mma kind::i8, accumulators
+//                  double-buffered in TMEM), four epilogue warps (tcgen05.ld,
+//                  threshold filter, candidate append)
+//   select_kernel  per query: keep the best F candidates, sorted, and set the
+//                  threshold for the next round
+#include <climits>
+#include <cstdint>
+
+#include "bv_batch.cuh"
+#include "bv_device.cuh"
+#include "bv_internal.h"
+#include "bv_scan.cuh"
+
+namespace bv {
+
+namespace {
+
+// ------------------------------------------------------------- tcgen05
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// D[tmem] (+)= A[smem desc] x B[smem desc]^T, int8 x int8 -> int32.
+__device__ __forceinline__ void mma_i8(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+// Arrive on `bar` once every tcgen05.mma this thread issued so far completes.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_addr(bar))
+               : "memory");
+}
+// 32 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
+        "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]),
+        "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]),
+        "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory operand descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 bytes apart (SBO), Blackwell descriptor version 1.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(1) << 16) |
+         (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
+         (static_cast<uint64_t>(2) << 61);
+}
+// Instruction descriptor: s32 accumulator, s8 x s8, both K-major, M=128, N=256.
+constexpr uint32_t kIdescI8 = (2u << 4) | (1u << 7) | (1u << 10) | ((kBRowTile >> 3) << 17) |
+                              ((kBQTile >> 4) << 24);
+
+constexpr int kEpiWarps = 4;
+constexpr int kProdWarp = kEpiWarps, kMmaWarp = kEpiWarps + 1;
+constexpr int kGemmThreads = (kEpiWarps + 2) * 32;
+constexpr int kGemmStages = 4;
+constexpr uint32_t kStageBytes = kBQTileBytes + kBRowTileBytes;
+constexpr uint32_t kTmemCols = 2 * kBRowTile;  // two accumulator buffers
+
+struct GemmSmem {
+  uint32_t bars_off, total;
+};
+__host__ __device__ inline GemmSmem gemm_smem_layout() {
+  GemmSmem s;
+  s.bars_off = kGemmStages * kStageBytes;
+  // full[S], empty[S], tfull[2], tempty[2], done, then the TMEM address word
+  s.total = s.bars_off + (2 * kGemmStages + 5) * 8 + 16;
+  return s;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------- expand
+// One CTA per row tile, one thread per row: the row's int8 codes (int4
+// sign-extended, 1-bit as +-1, zero beyond P) into the tile's K blocks.
+template <int BITS>
+__global__ void __launch_bounds__(kBRowTile) expand_kernel(const ExpandParams p) {
+  const uint32_t rt = p.row0 / kBRowTile + blockIdx.x;
+  const uint32_t rr = threadIdx.x;
+  const uint32_t row = rt * kBRowTile + rr;
+  __shared__ float red[kBRowTile / 32];
+  if (row >= p.row0 && row < p.row1) {
+    const uint8_t* src = p.codes + static_cast<size_t>(row) * p.R;
+    float f = p.scales[row];
+    f = BITS == 8 ? __fmul_rn(f, kInv127) : (BITS == 4 ? __fmul_rn(f, kInv7) : f);
+    p.rowfac[row] = f;
+    for (uint32_t kb = 0; kb < p.KB; ++kb) {
+      int8_t* dst = p.ctiles + (static_cast<size_t>(rt) * p.KB + kb) * kBRowTileBytes;
+      for (uint32_t c = 0; c < 8; ++c) {
+        alignas(16) int8_t b[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const uint32_t e = kb * kKBlock + c * 16 + j;
+          int v = 0;
+          if (e < p.P) {
+            if constexpr (BITS == 8) {
+              v = static_cast<int8_t>(src[e]);
+            } else if constexpr (BITS == 4) {
+              const int n = (src[e >> 1] >> ((e & 1u) * 4u)) & 0xF;
+              v = n > 7 ? n - 16 : n;
+            } else {
+              v = ((src[e >> 3] >> (e & 7u)) & 1u) ? 1 : -1;
+            }
+          }
+          b[j] = static_cast<int8_t>(v);
+        }
+        *reinterpret_cast<uint4*>(dst + sw128_offset(rr, c * 16)) = *reinterpret_cast<const uint4*>(b);
+      }
+    }
+  } else if (row >= p.nrows) {
+    // rows past the end of the index are zeroed so the MMA reads defined
+    // values; rows before row0 were expanded earlier and keep their bytes
+    for (uint32_t kb = 0; kb < p.KB; ++kb) {
+      int8_t* dst = p.ctiles + (static_cast<size_t>(rt) * p.KB + kb) * kBRowTileBytes;
+      for (uint32_t c = 0; c < 8; ++c)
+        *reinterpret_cast<uint4*>(dst + sw128_offset(rr, c * 16)) = make_uint4(0, 0, 0, 0);
+    }
+  }
+  // tile maximum of the row factors over all rows present (rows before row0
+  // were written by an earlier expansion)
+  __syncthreads();
+  float m = 0.0f;
+  if (row < p.nrows) m = p.rowfac[row];
+#pragma unroll
+  for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+  if ((rr & 31u) == 0) red[rr >> 5] = m;
+  __syncthreads();
+  if (rr == 0) {
+    float t = 0.0f;
+    for (int w = 0; w < static_cast<int>(kBRowTile / 32); ++w) t = fmaxf(t, red[w]);
+    p.tmax[rt] = t;
+  }
+}
+
+// ------------------------------------------------------------- prep
+// One CTA (kConsumerThreads) per query.
+__global__ void __launch_bounds__(kConsumerThreads, 1) prep_kernel(const PrepParams p) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  float* q = reinterpret_cast<float*>(smem);                  // P
+  int8_t* qb = reinterpret_cast<int8_t*>(q + p.P);            // KB*128
+  float* red = reinterpret_cast<float*>(qb + p.KB * kKBlock);  // 16
+  const int ctid = threadIdx.x;
+  const uint32_t qi = blockIdx.x;
+  const float* src = p.queries + static_cast<size_t>(qi) * p.dim;
+  for (uint32_t i = ctid; i < p.P; i += kConsumerThreads) q[i] = i < p.dim ? src[i] : 0.0f;
+  named_bar_sync(kBarConsumers, kConsumerThreads);
+  rotate_query(q, p.signs, p.P, p.rounds, ctid);
+  float qfac = 1.0f;
+  if (p.hamming) {
+    for (uint32_t i = ctid; i < p.KB * kKBlock; i += kConsumerThreads)
+      qb[i] = i < p.P ? (q[i] >= 0.0f ? 1 : -1) : 0;
+  } else {
+    const float qscale = quantize_query8(q, qb, p.P, ctid, red);
+    for (uint32_t i = p.P + ctid; i < p.KB * kKBlock; i += kConsumerThreads) qb[i] = 0;
+    qfac = __fmul_rn(qscale, kInv127);
+  }
+  named_bar_sync(kBarConsumers, kConsumerThreads);
+  const uint32_t qt = qi / kBQTile, qr = qi % kBQTile;
+  for (uint32_t c = ctid; c < p.KB * 8; c += kConsumerThreads) {
+    const uint32_t kb = c / 8, cc = c % 8;
+    int8_t* dst = p.qtiles + (static_cast<size_t>(qt) * p.KB + kb) * kBQTileBytes;
+    *reinterpret_cast<uint4*>(dst + sw128_offset(qr, cc * 16)) =
+        *reinterpret_cast<const uint4*>(qb + kb * kKBlock + cc * 16);
+  }
+  if (ctid == 0) {
+    p.qfac[qi] = qfac;
+    p.thr[qi] = 0ull;
+    p.cnt[qi] = 0u;
+  }
+}
+
+// ------------------------------------------------------------- gemm
+__global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte aligned base for the swizzled operand tiles
+  const uint32_t raw = smem_addr(smem_raw);
+  uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  const GemmSmem lay = gemm_smem_layout();
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + lay.bars_off);
+  uint64_t* empty = full + kGemmStages;
+  uint64_t* tfull = empty + kGemmStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* done = tempty + 2;
+  uint32_t* tmem_word = reinterpret_cast<uint32_t*>(done + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kGemmStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], kEpiWarps);
+    }
+    mbar_init(done, 1);
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(tmem_word, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_word;
+
+  const uint32_t ntiles = (p.rt1 - p.rt0) * p.nqt;
+  const uint32_t KB = p.KB;
+
+  if (warp == kProdWarp) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (uint32_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        const uint32_t rt = p.rt0 + t / p.nqt, qt = t % p.nqt;
+        for (uint32_t kb = 0; kb < KB; ++kb, ++it) {
+          const uint32_t s = it % kGemmStages, ph = (it / kGemmStages) & 1u;
+          if (it >= kGemmStages && !mbar_wait_bounded(&empty[s], ph ^ 1u, p.err)) {
+            ok = false;
+            break;
+          }
+          uint8_t* a = smem + s * kStageBytes;
+          uint8_t* b = a + kBQTileBytes;
+          mbar_arrive_expect_tx(&full[s], kStageBytes);
+          bulk_g2s(a, p.qtiles + (static_cast<size_t>(qt) * KB + kb) * kBQTileBytes, kBQTileBytes, &full[s]);
+          bulk_g2s(b, p.ctiles + (static_cast<size_t>(rt) * KB + kb) * kBRowTileBytes, kBRowTileBytes,
+                   &full[s]);
+        }
+      }
+      // copies still in flight land before the CTA may exit
+      for (uint32_t j = it > kGemmStages ? it - kGemmStages : 0; j < it; ++j)
+        mbar_wait_bounded(&full[j % kGemmStages], (j / kGemmStages) & 1u, p.err);
+    }
+  } else if (warp == kMmaWarp) {
+    if (lane == 0) {
+      uint32_t it = 0, tc = 0;
+      bool ok = true;
+      for (uint32_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++tc) {
+        const uint32_t buf = tc & 1u, use = tc >> 1;
+        if (use > 0 && !mbar_wait_bounded(&tempty[buf], (use - 1u) & 1u, p.err)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + buf * kBRowTile;
+        for (uint32_t kb = 0; kb < KB; ++kb, ++it) {
+          const uint32_t s = it % kGemmStages, ph = (it / kGemmStages) & 1u;
+          if (!mbar_wait_bounded(&full[s], ph, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = smem_addr(smem + s * kStageBytes);
+          const uint64_t ad = sw128_desc(a), bd = sw128_desc(a + kBQTileBytes);
+#pragma unroll
+          for (uint32_t j = 0; j < kKBlock / 32; ++j)  // K = 32 bytes per instruction
+            mma_i8(d, ad + 2u * j, bd + 2u * j, kIdescI8, (kb | j) != 0u ? 1u : 0u);
+          mma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+        }
+        if (ok) mma_commit(&tfull[buf]);
+      }
+      // every MMA issued has completed before TMEM is released
+      mma_commit(done);
+      mbar_wait_bounded(done, 0, p.err);
+    }
+  } else {
+    // ------------------------------------------------------ epilogue
+    const uint32_t lane_base = static_cast<uint32_t>(warp) * 32u;
+    uint32_t tc = 0;
+    for (uint32_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++tc) {
+      const uint32_t rt = p.rt0 + t / p.nqt, qt = t % p.nqt;
+      const uint32_t buf = tc & 1u, use = tc >> 1;
+      const bool ready = mbar_wait_bounded(&tfull[buf], use & 1u, p.err);
+      if (!__all_sync(0xffffffffu, ready)) break;  // tcgen05.ld below is warp-collective
+      tc_fence_after();
+      const uint32_t qi = qt * kBQTile + lane_base + static_cast<uint32_t>(lane);
+      const bool qvalid = qi < p.nq;
+      uint64_t thr = 0ull;
+      float qf = 0.0f;
+      int bound = INT_MIN;
+      if (qvalid) {
+        thr = p.thr[qi];
+        qf = p.qfac[qi];
+        const float tm = p.tmax[rt];
+        if (thr != 0ull) {
+          const float ts = key_score(thr);
+          const double den = static_cast<double>(tm) * static_cast<double>(qf);
+          if (ts > 0.0f && den > 0.0) {
+            // score >= ts needs idot >= ts / (tmax * qfac) up to three f32 roundings
+            const double b = floor(static_cast<double>(ts) / den * (1.0 - 0x1p-20));
+            bound = b >= 2147483647.0 ? INT_MAX : static_cast<int>(b);
+          }
+        }
+      }
+      uint64_t* cq = p.cand + static_cast<size_t>(qvalid ? qi : 0) * p.cap;
+      for (uint32_t c0 = 0; c0 < kBRowTile; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem + ((lane_base) << 16) + buf * kBRowTile + c0, v);
+        tmem_ld_wait();
+        const uint32_t rbase = rt * kBRowTile + c0;
+        uint32_t valid = rbase >= p.nrows ? 0u : (p.nrows - rbase >= 32u ? 0xFFFFFFFFu : ((1u << (p.nrows - rbase)) - 1u));
+        if (p.mask && valid) valid &= p.mask[rbase >> 5];
+        uint32_t m = 0;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) m |= (static_cast<int>(v[j]) >= bound ? 1u : 0u) << j;
+        m &= valid;
+        if (!qvalid) m = 0;
+        if (m) {
+          uint32_t pass = 0;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if ((m >> j) & 1u) {
+              const uint32_t row = rbase + static_cast<uint32_t>(j);
+              const float sc = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(v[j])), p.rowfac[row]), qf);
+              if (make_key(sc, row) > thr) pass |= 1u << j;
+            }
+          if (pass) {
+            const uint32_t n = __popc(pass);
+            const uint32_t base = atomicAdd(p.cnt + qi, n);
+            if (base + n > p.cap) atomicOr(p.overflow, 1u);
+            uint32_t w = base;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if ((pass >> j) & 1u) {
+                const uint32_t row = rbase + static_cast<uint32_t>(j);
+                const float sc =
+                    __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(v[j])), p.rowfac[row]), qf);
+                if (w < p.cap) cq[w] = make_key(sc, row);
+                ++w;
+              }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------- select
+// One CTA per query: the best F of the query's candidates, sorted descending
+// into cand[0..Fp) (zero padded); thr = the F-th best key once F exist.
+template <int MAXK>
+__global__ void __launch_bounds__(kConsumerThreads, 1) select_kernel(const SelectParams p) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  uint64_t* kept = reinterpret_cast<uint64_t*>(smem);          // Fp
+  uint32_t* hist = reinterpret_cast<uint32_t*>(kept + p.Fp);   // kSelBins
+  uint32_t* misc = hist + kSelBins;                            // 128
+  const int ctid = threadIdx.x;
+  const uint32_t qi = blockIdx.x;
+  uint64_t* c = p.cand + static_cast<size_t>(qi) * p.cap;
+  uint32_t total = p.cnt[qi];
+  total = total < p.cap ? total : p.cap;
+  uint64_t v[MAXK];
+#pragma unroll
+  for (int i = 0; i < MAXK; ++i) {
+    const uint32_t idx = static_cast<uint32_t>(ctid) + static_cast<uint32_t>(i) * kConsumerThreads;
+    v[i] = idx < total ? c[idx] : 0ull;
+  }
+  for (uint32_t i = ctid; i < p.Fp; i += kConsumerThreads) kept[i] = 0ull;
+  named_bar_sync(kBarConsumers, kConsumerThreads);
+  const uint32_t n = keep_best<MAXK>(v, total, p.F, kept, hist, misc, ctid);
+  cta_sort_desc(kept, p.Fp, ctid);
+  for (uint32_t i = ctid; i < p.Fp; i += kConsumerThreads) c[i] = kept[i];
+  if (ctid == 0) {
+    p.cnt[qi] = n;
+    p.thr[qi] = n >= p.F ? kept[p.F - 1] : 0ull;
+  }
+}
+
+// ------------------------------------------------------------- launchers
+uint32_t batch_gemm_smem() { return gemm_smem_layout().total + 1024; }
+
+cudaError_t launch_expand(const ExpandParams& p, cudaStream_t s) {
+  if (p.row1 <= p.row0) return cudaSuccess;
+  const uint32_t t0 = p.row0 / kBRowTile, t1 = (p.row1 + kBRowTile - 1) / kBRowTile;
+  const dim3 grid(t1 - t0);
+  if (p.bits == 8) expand_kernel<8><<<grid, kBRowTile, 0, s>>>(p);
+  else if (p.bits == 4) expand_kernel<4><<<grid, kBRowTile, 0, s>>>(p);
+  else expand_kernel<1><<<grid, kBRowTile, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prep(const PrepParams& p, cudaStream_t s) {
+  const size_t smem = static_cast<size_t>(p.P) * 4 + p.KB * kKBlock + 64;
+  static int opted[kMaxDevices] = {};
+  cudaError_t e = opt_in_smem(reinterpret_cast<const void*>(prep_kernel), smem, opted);
+  if (e != cudaSuccess) return e;
+  prep_kernel<<<p.nq, kConsumerThreads, smem, s>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemm(const GemmParams& p, uint32_t grid, cudaStream_t s) {
+  const size_t smem = batch_gemm_smem();
+  static int opted[kMaxDevices] = {};
+  cudaError_t e = opt_in_smem(reinterpret_cast<const void*>(gemm_kernel), smem, opted);
+  if (e != cudaSuccess) return e;
+  gemm_kernel<<<grid, kGemmThreads, smem, s>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_select(const SelectParams& p, cudaStream_t s) {
+  const size_t smem = static_cast<size_t>(p.Fp) * 8 + kSelBins * 4 + 128 * 4;
+  const uint32_t maxk = (p.cap + kConsumerThreads - 1) / kConsumerThreads;
+  auto go = [&](auto kern) -> cudaError_t {
+    static int opted[kMaxDevices] = {};
+    cudaError_t e = opt_in_smem(reinterpret_cast<const void*>(kern), smem, opted);
+    if (e != cudaSuccess) return e;
+    kern<<<p.nq, kConsumerThreads, smem, s>>>(p);
+    return cudaGetLastError();
+  };
+  if (maxk <= 8) return go(select_kernel<8>);
+  if (maxk <= 16) return go(select_kernel<16>);
+  if (maxk <= 32) return go(select_kernel<32>);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace bv

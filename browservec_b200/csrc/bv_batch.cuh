@@ -1,0 +1,87 @@
+// bv_batch.cuh -- the batched search path: many queries against one shard on
+// the tensor cores (tcgen05.mma kind::i8), for the integer scorings.
+//
+// A batch of B queries is scored as one int8 contraction S = Q x C^T with
+// exact int32 accumulators: Q holds the queries' int8 codes (int mode: the
+// corpus int8 codec applied to the rotated query; hamming: +-1 from the
+// rotated query's signs), C the corpus codes widened to int8 (int4 nibbles
+// sign-extended, 1-bit codes as +-1).  Every integer dot is exact, so the
+// scores ((f32(idot) * rowfac) * qfac) are bit-identical to the single-query
+// integer scans.
+//
+// Both operands live in HBM pre-arranged as the shared-memory image of a
+// 128-byte-swizzled, K-major UMMA operand: a tile of T rows x 128 bytes of K
+// is T*128 contiguous bytes, row r at r*128, its 16-byte chunk c stored at
+// chunk c ^ (r & 7).  One 1-D bulk copy moves a tile into shared memory
+// unchanged (the swizzle is a function of the shared-memory address, so the
+// destination is 1024-byte aligned).
+//
+// Top-F selection runs in rounds over growing row ranges: the GEMM epilogue
+// appends the keys that beat each query's current F-th best key to a
+// per-query buffer, then a per-query select keeps the best F and raises the
+// threshold for the next round.  A buffer that would overflow is flagged and
+// the host repeats the batch with rounds small enough that it cannot.
+#pragma once
+
+#include <cstdint>
+
+namespace bv {
+
+constexpr uint32_t kBRowTile = 256;  // corpus rows per MMA tile (UMMA N)
+constexpr uint32_t kBQTile = 128;    // queries per MMA tile (UMMA M)
+constexpr uint32_t kKBlock = 128;    // bytes of K per stage: one swizzle atom row
+constexpr uint32_t kBRowTileBytes = kBRowTile * kKBlock;  // 32 KB
+constexpr uint32_t kBQTileBytes = kBQTile * kKBlock;      // 16 KB
+
+// Byte offset of (row r, byte k) inside one swizzled tile of 128-byte rows.
+__host__ __device__ inline uint32_t sw128_offset(uint32_t r, uint32_t k) {
+  return r * 128u + ((((k >> 4) ^ (r & 7u)) & 7u) << 4) + (k & 15u);
+}
+
+struct ExpandParams {
+  const uint8_t* codes;  // rows x R packed codes
+  const float* scales;   // rows
+  uint32_t R, P, KB, bits;
+  uint32_t row0, row1;   // rows to expand
+  uint32_t nrows;        // rows in the index (for the tile maxima)
+  int8_t* ctiles;        // [row tile][KB] swizzled 256 x 128 int8 tiles
+  float* rowfac;         // per-row score factor
+  float* tmax;           // per-row-tile maximum of rowfac
+};
+
+struct PrepParams {
+  const float* queries;  // nq x dim (normalized for cosine)
+  const float* signs;    // rounds x P
+  uint32_t nq, dim, P, KB, rounds;
+  int hamming;           // 1: +-1 query from signs; 0: int8 codec
+  int8_t* qtiles;        // [query tile][KB] swizzled 128 x 128 int8 tiles
+  float* qfac;           // per-query factor (qscale / 127, or 1)
+  uint64_t* thr;         // per-query threshold key (0 = none yet)
+  uint32_t* cnt;         // per-query candidate count
+};
+
+struct GemmParams {
+  const int8_t* ctiles;
+  const int8_t* qtiles;
+  const float* rowfac;
+  const float* tmax;
+  const uint32_t* mask;  // optional, 1 bit per row
+  uint32_t nrows, nq, KB, nqt;
+  uint32_t rt0, rt1;     // row tiles of this round
+  const uint64_t* thr;
+  const float* qfac;
+  uint64_t* cand;        // nq x cap keys
+  uint32_t cap;
+  uint32_t* cnt;
+  uint32_t* overflow;    // set when a buffer would overflow
+  uint32_t* err;
+};
+
+struct SelectParams {
+  uint64_t* cand;        // nq x cap
+  uint32_t cap, F, Fp, nq;
+  uint32_t* cnt;
+  uint64_t* thr;
+};
+
+}  // namespace bv

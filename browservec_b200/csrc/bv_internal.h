@@ -93,6 +93,21 @@ inline cudaError_t opt_in_smem(const void* func, size_t need, int* opted) {
   return cudaSuccess;
 }
 
+// bv_tail.cu: one tail CTA per query of a batch
+struct TailParams;
+cudaError_t launch_tail_grid(const TailParams& p, uint32_t nq, size_t smem, cudaStream_t stream);
+
+// bv_batch.cu: batched tensor-core search
+struct ExpandParams;
+struct PrepParams;
+struct GemmParams;
+struct SelectParams;
+uint32_t batch_gemm_smem();
+cudaError_t launch_expand(const ExpandParams& p, cudaStream_t s);
+cudaError_t launch_prep(const PrepParams& p, cudaStream_t s);
+cudaError_t launch_gemm(const GemmParams& p, uint32_t grid, cudaStream_t s);
+cudaError_t launch_select(const SelectParams& p, cudaStream_t s);
+
 // bv_merge.cu: cross-shard merge of all-gathered shard records
 size_t merge_smem_bytes(uint32_t world, uint32_t F);
 uint32_t merge_max_world();

@@ -18,6 +18,18 @@ namespace bv {
 
 __global__ void __launch_bounds__(kConsumerThreads, 1) tail_kernel(const TailParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
+  // CTA b of a batched launch serves query b: its own partials, query and outputs
+  const size_t b = blockIdx.x;
+  const uint64_t* const partials = p.partials + b * p.partials_stride;
+  const float* const query = p.query + b * p.dim;
+  uint32_t* const out_rows = p.out_rows + b * p.k;
+  float* const out_scores = p.out_scores + b * p.k;
+  uint32_t* const out_count = p.out_count + b;
+  uint32_t* const cand_rows = p.cand_rows ? p.cand_rows + b * p.F : nullptr;
+  float* const cand_scores = p.cand_scores ? p.cand_scores + b * p.F : nullptr;
+  uint32_t* const cand_count = p.cand_count ? p.cand_count + b : nullptr;
+  float* const cand_exact = p.cand_exact ? p.cand_exact + b * p.F : nullptr;
+  uint64_t* const trace = b == 0 ? p.trace : nullptr;
   const TailSmem lay = tail_smem_layout(p.dim, p.capc, p.rows_bytes);
   uint64_t* cand = reinterpret_cast<uint64_t*>(smem + lay.cand_off);
   uint32_t* hist = reinterpret_cast<uint32_t*>(smem + lay.hist_off);
@@ -28,7 +40,7 @@ __global__ void __launch_bounds__(kConsumerThreads, 1) tail_kernel(const TailPar
   const int ctid = threadIdx.x, warp = ctid >> 5, lane = ctid & 31;
 
   pdl_trigger();  // the next query's scan may launch now
-  if (p.trace && ctid == 0) p.trace[kTrTailEntry] = globaltimer();
+  if (trace && ctid == 0) trace[kTrTailEntry] = globaltimer();
   if (ctid == 0) {
     mbar_init(gbar, 1);
     fence_mbar_init();
@@ -36,20 +48,20 @@ __global__ void __launch_bounds__(kConsumerThreads, 1) tail_kernel(const TailPar
   __syncthreads();
   // the normalized query (an input, ready before this kernel): gbar phase 0
   const uint32_t q_bulk =
-      (reinterpret_cast<uintptr_t>(p.query) & 15u) == 0 ? (p.dim * 4u) & ~15u : 0u;
+      (reinterpret_cast<uintptr_t>(query) & 15u) == 0 ? (p.dim * 4u) & ~15u : 0u;
   if (ctid == 0) {
     mbar_arrive_expect_tx(gbar, p.rerank ? q_bulk : 0u);
-    if (p.rerank && q_bulk) bulk_g2s(q, p.query, q_bulk, gbar);
+    if (p.rerank && q_bulk) bulk_g2s(q, query, q_bulk, gbar);
   }
   pdl_wait();  // this query's scan has completed: the CTA lists are visible
-  if (p.trace && ctid == 0) p.trace[kTrTailStart] = globaltimer();
+  if (trace && ctid == 0) trace[kTrTailStart] = globaltimer();
 
   // ---------------------------------------------- merge of the CTA lists
   // Result: cand[0..Fp) = the shard's best keys, descending, zero padded;
   // nc = how many of the first F are real.
   uint32_t nc = 0;
   if (p.Fp <= 256u) {
-    merge_cta_lists_dispatch(p.Fp, p.partials, p.G, cand, ctid);
+    merge_cta_lists_dispatch(p.Fp, partials, p.G, cand, ctid);
     if (warp == 0) {
       uint32_t c = 0;
       for (uint32_t i = lane; i < p.Fp; i += 32) {
@@ -71,7 +83,7 @@ __global__ void __launch_bounds__(kConsumerThreads, 1) tail_kernel(const TailPar
 #pragma unroll
       for (int i = 0; i < static_cast<int>(kChunkSlots); ++i) {
         const uint32_t idx = c0 + static_cast<uint32_t>(ctid) + static_cast<uint32_t>(i) * kConsumerThreads;
-        v[i] = idx < total ? __ldcg(p.partials + idx) : 0ull;
+        v[i] = idx < total ? __ldcg(partials + idx) : 0ull;
         cnt += v[i] != 0ull ? 1u : 0u;
       }
 #pragma unroll
@@ -94,13 +106,13 @@ __global__ void __launch_bounds__(kConsumerThreads, 1) tail_kernel(const TailPar
     named_bar_sync(kBarConsumers, kConsumerThreads);
     cta_sort_desc(cand, p.Fp, ctid);
   }
-  if (p.trace && ctid == 0) p.trace[kTrTailMerged] = globaltimer();
-  if (p.cand_rows) {
+  if (trace && ctid == 0) trace[kTrTailMerged] = globaltimer();
+  if (cand_rows) {
     for (uint32_t i = ctid; i < nc; i += kConsumerThreads) {
-      p.cand_rows[i] = key_row(cand[i]) + p.row_base;
-      p.cand_scores[i] = key_score(cand[i]);
+      cand_rows[i] = key_row(cand[i]) + p.row_base;
+      cand_scores[i] = key_score(cand[i]);
     }
-    if (ctid == 0) *p.cand_count = nc;
+    if (ctid == 0) *cand_count = nc;
   }
 
   const uint32_t n = nc < p.k ? nc : p.k;
@@ -110,7 +122,7 @@ __global__ void __launch_bounds__(kConsumerThreads, 1) tail_kernel(const TailPar
     // the four accumulators a0..a3 of Store.dotRow.
     const uint32_t stride = p.dim + 4;
     mbar_wait_bounded(gbar, 0, p.err);
-    for (uint32_t i = q_bulk / 4 + ctid; i < p.dim; i += kConsumerThreads) q[i] = p.query[i];
+    for (uint32_t i = q_bulk / 4 + ctid; i < p.dim; i += kConsumerThreads) q[i] = query[i];
     const bool bulk = (p.dim % 4u) == 0u && (reinterpret_cast<uintptr_t>(p.originals) & 15u) == 0u;
     const uint32_t batch = p.rows_bytes / (stride * 4u);
     uint64_t* ex = cand + p.Fp;  // exact keys (cand has capc >= 2*Fp slots)
@@ -128,7 +140,7 @@ __global__ void __launch_bounds__(kConsumerThreads, 1) tail_kernel(const TailPar
         }
         mbar_wait_bounded(gbar, gph, p.err);
         gph ^= 1u;
-        if (p.trace && ctid == 0) p.trace[kTrTailGathered] = globaltimer();
+        if (trace && ctid == 0) trace[kTrTailGathered] = globaltimer();
       } else {
         for (uint32_t c = 0; c < nb; ++c) {
           const float* src = p.originals + static_cast<size_t>(key_row(cand[c0 + c])) * p.dim;
@@ -163,37 +175,45 @@ __global__ void __launch_bounds__(kConsumerThreads, 1) tail_kernel(const TailPar
       }
       named_bar_sync(kBarConsumers, kConsumerThreads);
     }
-    if (p.cand_exact)
-      for (uint32_t i = ctid; i < nc; i += kConsumerThreads) p.cand_exact[i] = key_score(ex[i]);
+    if (cand_exact)
+      for (uint32_t i = ctid; i < nc; i += kConsumerThreads) cand_exact[i] = key_score(ex[i]);
     for (uint32_t i = nc + static_cast<uint32_t>(ctid); i < p.Fp; i += kConsumerThreads) ex[i] = 0ull;
     named_bar_sync(kBarConsumers, kConsumerThreads);
-    if (p.trace && ctid == 0) p.trace[kTrTailDotted] = globaltimer();
+    if (trace && ctid == 0) trace[kTrTailDotted] = globaltimer();
     if (p.Fp <= 256u) {
       warp0_sort_dispatch(p.Fp, ex, ctid);
       if (warp == 0) {
         __syncwarp();
         for (uint32_t i = lane; i < n; i += 32) {
-          p.out_rows[i] = key_row(ex[i]) + p.row_base;
-          p.out_scores[i] = key_score(ex[i]);
+          out_rows[i] = key_row(ex[i]) + p.row_base;
+          out_scores[i] = key_score(ex[i]);
         }
       }
     } else {
       cta_sort_desc(ex, p.Fp, ctid);
       for (uint32_t i = ctid; i < n; i += kConsumerThreads) {
-        p.out_rows[i] = key_row(ex[i]) + p.row_base;
-        p.out_scores[i] = key_score(ex[i]);
+        out_rows[i] = key_row(ex[i]) + p.row_base;
+        out_scores[i] = key_score(ex[i]);
       }
     }
   } else {
     for (uint32_t i = ctid; i < n; i += kConsumerThreads) {
-      p.out_rows[i] = key_row(cand[i]) + p.row_base;
-      p.out_scores[i] = key_score(cand[i]);
+      out_rows[i] = key_row(cand[i]) + p.row_base;
+      out_scores[i] = key_score(cand[i]);
     }
   }
   if (ctid == 0) {
-    *p.out_count = n;
-    if (p.trace) p.trace[kTrTailDone] = globaltimer();
+    *out_count = n;
+    if (trace) trace[kTrTailDone] = globaltimer();
   }
+}
+
+cudaError_t launch_tail_grid(const TailParams& p, uint32_t nq, size_t smem, cudaStream_t stream) {
+  static int opted[kMaxDevices] = {};
+  const cudaError_t e = opt_in_smem(reinterpret_cast<const void*>(tail_kernel), smem, opted);
+  if (e != cudaSuccess) return e;
+  tail_kernel<<<nq, kConsumerThreads, smem, stream>>>(p);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_tail(const TailParams& p, size_t smem, cudaStream_t stream) {

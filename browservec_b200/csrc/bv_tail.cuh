@@ -23,6 +23,9 @@ struct TailParams {
   uint32_t* cand_count;
   float* cand_exact;         // optional: exact scores of the candidates, candidate order
   uint64_t* trace;           // optional: trace[kTrTail*]
+  // grid of queries (batched search): CTA b serves query b, its partials at
+  // partials + b * partials_stride; 0 for the one-CTA launch of a scan
+  uint32_t partials_stride;
 };
 
 // Tail timestamps (globaltimer ns) in the trace record given to the tail.

@@ -175,6 +175,33 @@ class AddonQuantIndex:
                                  out_scores=out_scores_ptr, out_counts=out_counts_ptr)
         _lib.check(self._L.bv_search_async(self._h, C.byref(args), C.c_void_p(stream)))
 
+    def search_device_cand(self, q_ptr: int, nq: int, k: int, fetch: int, rerank: bool,
+                           out_rows_ptr: int, out_scores_ptr: int, out_counts_ptr: int,
+                           mask_ptr: int = 0, mask_words: int = 0, stream: int = 0,
+                           cand_rows_ptr: int = 0, cand_scores_ptr: int = 0, cand_counts_ptr: int = 0,
+                           cand_exact_ptr: int = 0) -> None:
+        """search_device with the candidate outputs (per-query scans)."""
+        args = _lib.BvSearchArgs(queries=q_ptr, nq=nq, k=k, fetch=max(fetch, k), rerank=int(rerank),
+                                 mask=mask_ptr or None, mask_words=mask_words, out_rows=out_rows_ptr,
+                                 out_scores=out_scores_ptr, out_counts=out_counts_ptr,
+                                 cand_rows=cand_rows_ptr or None, cand_scores=cand_scores_ptr or None,
+                                 cand_counts=cand_counts_ptr or None, cand_exact=cand_exact_ptr or None)
+        _lib.check(self._L.bv_search_async(self._h, C.byref(args), C.c_void_p(stream)))
+
+    def search_batch_device(self, q_ptr: int, nq: int, k: int, fetch: int, rerank: bool,
+                            out_rows_ptr: int, out_scores_ptr: int, out_counts_ptr: int,
+                            mask_ptr: int = 0, mask_words: int = 0, stream: int = 0,
+                            cand_rows_ptr: int = 0, cand_scores_ptr: int = 0, cand_counts_ptr: int = 0,
+                            cand_exact_ptr: int = 0) -> None:
+        """Batched search on the tensor cores (integer scorings), device
+        pointers; returns once `stream` has finished the batch."""
+        args = _lib.BvSearchArgs(queries=q_ptr, nq=nq, k=k, fetch=max(fetch, k), rerank=int(rerank),
+                                 mask=mask_ptr or None, mask_words=mask_words, out_rows=out_rows_ptr,
+                                 out_scores=out_scores_ptr, out_counts=out_counts_ptr,
+                                 cand_rows=cand_rows_ptr or None, cand_scores=cand_scores_ptr or None,
+                                 cand_counts=cand_counts_ptr or None, cand_exact=cand_exact_ptr or None)
+        _lib.check(self._L.bv_search_batch(self._h, C.byref(args), C.c_void_p(stream)))
+
     def query_rows_exact(self, q: np.ndarray, rows: np.ndarray, k: int) -> list[FlatHit]:
         """index.ts:445-464 on the GPU (rows <= 4096)."""
         q = np.ascontiguousarray(q, dtype=np.float32)

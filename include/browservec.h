@@ -166,6 +166,19 @@ BV_API int bv_set_phase_trace(bv_index* idx, uint64_t* trace_dev, uint64_t capac
  * kernel per query). */
 BV_API int bv_launches_last_search(const bv_index* idx, uint32_t* launches);
 
+/* Batched search on the tensor cores: the same request and results as
+ * bv_search_async (DEVICE pointers; results identical to it, bit for bit) for
+ * an index created with the integer scorings (BV_SCORE_INT, or
+ * BV_SCORE_HAMMING with bits = 1).  The batch is scored as one int8
+ * contraction (tcgen05.mma kind::i8) of the queries' int8 codes with the
+ * corpus codes widened to int8; the best F per query are selected in rounds
+ * and re-ranked exactly.  This is the batched query path the reference runs
+ * as a per-query loop (BrowserVec.queryBatch, src/index.ts:473-517, over
+ * QuantIndex.search, src/index/quant.ts:178-245).  The first batched search
+ * after an append widens the new rows' codes (rows x paddedDim bytes more
+ * device memory).  Synchronises `stream` before returning. */
+BV_API int bv_search_batch(bv_index* idx, const bv_search_args* args, void* stream);
+
 /* Cross-shard merge of a row-sharded search (DEVICE pointers, enqueued on
  * `stream`).  The corpus is split into W contiguous row ranges, one per GPU;
  * each shard runs bv_search_async with cand_rows/cand_scores/cand_exact/
