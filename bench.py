@@ -50,6 +50,13 @@ def peaks():
     return 6650.0, "fallback"
 
 
+def tensor_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return float(json.load(open(p))["bf16_tflops"])
+    return 1590.0
+
+
 def make_data(torch, device, seed, n, dim):
     """Seeded counter-based (Philox) N(0,1) rows on the GPU, L2-normalised in f64."""
     g = torch.Generator(device=device)
@@ -128,8 +135,8 @@ SHARDED = {
     "c3": dict(bits=4, n=1_000_000, dim=384, kind="mixture", seed=3, nq=10_000, metric="dot", k=10, rf=8,
                scoring="int", workload="BASELINE config 3: TurboQuant int4, queryBatch of 10,000, row-sharded"),
     "c4": dict(bits=1, n=10_000_000, dim=768, kind="mixture", seed=4, nq=1000, metric="cosine", k=100, rf=10,
-               scoring="hamming", workload="BASELINE config 4: 1-bit codes, Hamming prefilter, queryBatch of "
-                                           "1,000, row-sharded"),
+               scoring="int", workload="BASELINE config 4: 1-bit codes (int8 query x +-1 codes, the popc-equivalent "
+                                       "integer dot), queryBatch of 1,000, row-sharded"),
     "c5": dict(bits=8, n=50_000_000, dim=128, kind="iid", seed=5, nq=4096, metric="cosine", k=10, rf=4,
                scoring="int", workload="BASELINE config 5: TurboQuant int8, queryBatch of 4,096, row-sharded "
                                        "(metadata filter not applied yet)"),
@@ -233,8 +240,15 @@ def run_sharded(args, name):
         dist.destroy_process_group()
         return
 
+    scoring = args.sharded_scoring or cfg["scoring"]
+    batched = scoring != "asym" and not args.per_query
+    config["scoring"] = scoring
+    config["search"] = ("batched: prep + rounds of (tcgen05 kind::i8 GEMM + select) + one re-rank tail "
+                        "per query, then one merge" if batched else
+                        "per query one scan + one tail launch, then one merge launch per step")
     x = datagen.rows(torch, dev, cfg["kind"], cfg["seed"], lo, hi, dim)
-    idx = ShardedIndex(dim, n, bits=cfg["bits"], scoring=cfg["scoring"], metric=cfg["metric"], device=local)
+    idx = ShardedIndex(dim, n, bits=cfg["bits"], scoring=scoring, metric=cfg["metric"], device=local,
+                       batched=batched)
     idx.load(x)
     qs = datagen.rows(torch, dev, cfg["kind"], cfg["seed"], 0, nq, dim, stream=datagen.STREAM_QUERIES)
     torch.cuda.synchronize()
@@ -257,22 +271,37 @@ def run_sharded(args, name):
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
     qps = args.steps * nq / (ms / 1e3)
+    launches_per_step = idx.engine.index.last_launches()
 
     ns = min(nq, 100)
     truth = _exact_top10(torch, dist, x, lo, qs[:ns])
     got = rows[:ns, :10].cpu().numpy()
     rec = sum(len(set(truth[i].tolist()) & set(got[i].tolist())) for i in range(ns)) / (ns * 10)
 
-    # per-GPU roofline of the scan: codes + scales of the shard, the re-rank rows, the query
     query_ms = ms / (args.steps * nq)
-    algo_bytes = (hi - lo) * (P // R + 4) + fetch * dim * 4 + dim * 4
-    peak, peak_kind = peaks()
-    achieved = algo_bytes / (query_ms / 1e3) / 1e9
-    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                "traffic": None, "peak_kind": f"{peak_kind} (copy bandwidth, MEASURED_PEAKS.json hbm_gbs)",
-                "algorithmic_bytes_per_launch": algo_bytes,
-                "duration": "per query per GPU: timed region / queries (scan + tail, all-gather and merge "
-                            "amortised)"}
+    if batched:
+        # per-GPU roofline of the contraction: 2 * queries * shard rows * paddedDim int8 ops per step
+        ops = 2.0 * nq * (hi - lo) * P
+        tops = ops / (ms / args.steps / 1e3) / 1e12
+        peak = 2.0 * tensor_peak()
+        roofline = {"bound": "tensor", "achieved": tops, "peak": peak, "unit": "TOP/s (int8)",
+                    "frac": tops / peak, "traffic": None,
+                    "peak_kind": "int8 dense = 2 x the measured bf16 burst (MEASURED_PEAKS.json bf16_tflops); "
+                                 "no int8 figure is measured",
+                    "algorithmic_ops_per_step": ops,
+                    "duration": "per step per GPU: prep + GEMM/select rounds + re-rank tails + all-gather + "
+                                "merge"}
+    else:
+        # per-GPU roofline of the scan: codes + scales of the shard, the re-rank rows, the query
+        algo_bytes = (hi - lo) * (P // R + 4) + fetch * dim * 4 + dim * 4
+        peak, peak_kind = peaks()
+        achieved = algo_bytes / (query_ms / 1e3) / 1e9
+        roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                    "frac": achieved / peak, "traffic": None,
+                    "peak_kind": f"{peak_kind} (copy bandwidth, MEASURED_PEAKS.json hbm_gbs)",
+                    "algorithmic_bytes_per_launch": algo_bytes,
+                    "duration": "per query per GPU: timed region / queries (scan + tail, all-gather and "
+                                "merge amortised)"}
 
     # e2e: host queries (pinned) -> device, search, results back to the host, every step
     q_host = qs.cpu().pin_memory()
@@ -306,7 +335,7 @@ def run_sharded(args, name):
                     cfg["scoring"], "f32xs8"),
                 "data": f"synthetic (seeded Philox, {cfg['kind']}, L2-normalised)", "config": config,
                 "recall_at_10": rec, "recall_sample": ns, "query_ms": query_ms,
-                "gpu_launches": args.steps * (2 * nq + 1), "roofline": roofline, "cpu_baseline": cpu,
+                "gpu_launches": args.steps * (launches_per_step + 1), "roofline": roofline, "cpu_baseline": cpu,
                 "e2e": e2e, "clocks": clk_res}
         print(json.dumps(line))
     idx.destroy()
@@ -329,6 +358,10 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--config", default="c2", choices=["c2", *SHARDED])
+    ap.add_argument("--sharded-scoring", default=None, choices=["asym", "int", "hamming"],
+                    help="scoring of a sharded config (default: the config's)")
+    ap.add_argument("--per-query", action="store_true",
+                    help="sharded configs: per-query scans instead of the batched tensor-core path")
     args = ap.parse_args()
     if args.config != "c2":
         return run_sharded(args, args.config)

@@ -87,12 +87,16 @@ constexpr int kGemmStages = 4;
 constexpr uint32_t kStageBytes = kBQTileBytes + kBRowTileBytes;
 constexpr uint32_t kTmemCols = 2 * kBRowTile;  // two accumulator buffers
 
+constexpr uint32_t kSlotWords = 36;  // per epilogue thread: 32 accumulators, padded for STS.128
+
 struct GemmSmem {
-  uint32_t bars_off, total;
+  uint32_t slots_off, rowfac_off, bars_off, total;
 };
 __host__ __device__ inline GemmSmem gemm_smem_layout() {
   GemmSmem s;
-  s.bars_off = kGemmStages * kStageBytes;
+  s.slots_off = kGemmStages * kStageBytes;
+  s.rowfac_off = s.slots_off + kEpiWarps * 32 * kSlotWords * 4;  // per epilogue warp: the tile's row factors
+  s.bars_off = s.rowfac_off + kEpiWarps * kBRowTile * 4;
   // full[S], empty[S], tfull[2], tempty[2], done, then the TMEM address word
   s.total = s.bars_off + (2 * kGemmStages + 5) * 8 + 16;
   return s;
@@ -295,67 +299,80 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const GemmParams 
     // ------------------------------------------------------ epilogue
     const uint32_t lane_base = static_cast<uint32_t>(warp) * 32u;
     uint32_t tc = 0;
+    float* rf_s = reinterpret_cast<float*>(smem + lay.rowfac_off) + warp * kBRowTile;
     for (uint32_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++tc) {
       const uint32_t rt = p.rt0 + t / p.nqt, qt = t % p.nqt;
       const uint32_t buf = tc & 1u, use = tc >> 1;
+      const uint32_t qi = qt * kBQTile + lane_base + static_cast<uint32_t>(lane);
+      const bool qvalid = qi < p.nq;
+      // the tile's inputs are loaded before the accumulator wait, so their
+      // latency hides behind the MMA
+      const uint64_t thr = qvalid ? p.thr[qi] : 0ull;
+      const float qf = qvalid ? p.qfac[qi] : 0.0f;
+      const float tm = p.tmax[rt];
+      float rf[kBRowTile / 32];
+#pragma unroll
+      for (int i = 0; i < static_cast<int>(kBRowTile / 32); ++i) {
+        const uint32_t row = rt * kBRowTile + static_cast<uint32_t>(lane + 32 * i);
+        rf[i] = row < p.nrows ? p.rowfac[row] : 0.0f;
+      }
+      const uint32_t mrow = rt * kBRowTile + static_cast<uint32_t>(lane) * 32u;
+      const uint32_t mword = (p.mask && lane < static_cast<int>(kBRowTile / 32) && mrow < p.nrows)
+                                 ? p.mask[mrow >> 5] : 0xFFFFFFFFu;
       const bool ready = mbar_wait_bounded(&tfull[buf], use & 1u, p.err);
       if (!__all_sync(0xffffffffu, ready)) break;  // tcgen05.ld below is warp-collective
       tc_fence_after();
-      const uint32_t qi = qt * kBQTile + lane_base + static_cast<uint32_t>(lane);
-      const bool qvalid = qi < p.nq;
-      uint64_t thr = 0ull;
-      float qf = 0.0f;
+#pragma unroll
+      for (int i = 0; i < static_cast<int>(kBRowTile / 32); ++i) rf_s[lane + 32 * i] = rf[i];
+      __syncwarp();
       int bound = INT_MIN;
-      if (qvalid) {
-        thr = p.thr[qi];
-        qf = p.qfac[qi];
-        const float tm = p.tmax[rt];
-        if (thr != 0ull) {
-          const float ts = key_score(thr);
-          const double den = static_cast<double>(tm) * static_cast<double>(qf);
-          if (ts > 0.0f && den > 0.0) {
-            // score >= ts needs idot >= ts / (tmax * qfac) up to three f32 roundings
-            const double b = floor(static_cast<double>(ts) / den * (1.0 - 0x1p-20));
-            bound = b >= 2147483647.0 ? INT_MAX : static_cast<int>(b);
-          }
+      if (qvalid && thr != 0ull) {
+        const float ts = key_score(thr);
+        const double den = static_cast<double>(tm) * static_cast<double>(qf);
+        if (ts > 0.0f && den > 0.0) {
+          // score >= ts needs idot >= ts / (tmax * qfac) up to three f32 roundings
+          const double b = floor(static_cast<double>(ts) / den * (1.0 - 0x1p-20));
+          bound = b >= 2147483647.0 ? INT_MAX : static_cast<int>(b);
         }
       }
       uint64_t* cq = p.cand + static_cast<size_t>(qvalid ? qi : 0) * p.cap;
+      uint32_t* slot = reinterpret_cast<uint32_t*>(smem + lay.slots_off) + threadIdx.x * kSlotWords;
       for (uint32_t c0 = 0; c0 < kBRowTile; c0 += 32) {
         uint32_t v[32];
         tmem_ld32(tmem + ((lane_base) << 16) + buf * kBRowTile + c0, v);
         tmem_ld_wait();
         const uint32_t rbase = rt * kBRowTile + c0;
         uint32_t valid = rbase >= p.nrows ? 0u : (p.nrows - rbase >= 32u ? 0xFFFFFFFFu : ((1u << (p.nrows - rbase)) - 1u));
-        if (p.mask && valid) valid &= p.mask[rbase >> 5];
+        valid &= __shfl_sync(0xffffffffu, mword, static_cast<int>(c0 >> 5));
         uint32_t m = 0;
 #pragma unroll
         for (int j = 0; j < 32; ++j) m |= (static_cast<int>(v[j]) >= bound ? 1u : 0u) << j;
         m &= valid;
         if (!qvalid) m = 0;
         if (m) {
-          uint32_t pass = 0;
+          // this lane's 32 accumulators go to its own shared-memory slot, and
+          // only the columns that passed the prefilter are scored exactly
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if ((m >> j) & 1u) {
-              const uint32_t row = rbase + static_cast<uint32_t>(j);
-              const float sc = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(v[j])), p.rowfac[row]), qf);
-              if (make_key(sc, row) > thr) pass |= 1u << j;
-            }
+          for (int i = 0; i < 8; ++i)
+            reinterpret_cast<uint4*>(slot)[i] = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          uint32_t pass = 0;
+          for (uint32_t mm = m; mm; mm &= mm - 1u) {
+            const uint32_t j = __ffs(mm) - 1u;
+            const uint32_t row = rbase + j;
+            const float sc = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(slot[j])), rf_s[c0 + j]), qf);
+            if (make_key(sc, row) > thr) pass |= 1u << j;
+          }
           if (pass) {
             const uint32_t n = __popc(pass);
             const uint32_t base = atomicAdd(p.cnt + qi, n);
             if (base + n > p.cap) atomicOr(p.overflow, 1u);
             uint32_t w = base;
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if ((pass >> j) & 1u) {
-                const uint32_t row = rbase + static_cast<uint32_t>(j);
-                const float sc =
-                    __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(v[j])), p.rowfac[row]), qf);
-                if (w < p.cap) cq[w] = make_key(sc, row);
-                ++w;
-              }
+            for (uint32_t mm = pass; mm; mm &= mm - 1u, ++w) {
+              const uint32_t j = __ffs(mm) - 1u;
+              const uint32_t row = rbase + j;
+              const float sc = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(slot[j])), rf_s[c0 + j]), qf);
+              if (w < p.cap) cq[w] = make_key(sc, row);
+            }
           }
         }
       }

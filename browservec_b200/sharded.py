@@ -63,10 +63,13 @@ class CudaShardEngine:
     record, bv_merge_shards over the gathered records."""
 
     def __init__(self, dim: int, bits: int, scoring: str, seed: int, rounds: int, metric: str,
-                 device: int, row_base: int):
+                 device: int, row_base: int, batched: bool | None = None):
         import torch
 
         self.torch = torch
+        # integer scorings serve a batch on the tensor cores (bv_search_batch);
+        # asym scores per query (bv_search_async)
+        self.batched = scoring != "asym" if batched is None else batched
         self.device = torch.device("cuda", device)
         self.index = AddonQuantIndex(dim, seed=seed, rounds=rounds, bits=bits, scoring=scoring,
                                      device=device, metric=metric, row_base=row_base)
@@ -102,7 +105,8 @@ class CudaShardEngine:
                                  out_counts=s[2 * nq * k:].data_ptr(), cand_rows=v.rows.data_ptr(),
                                  cand_scores=v.approx.data_ptr(), cand_counts=v.counts.data_ptr(),
                                  cand_exact=v.exact.data_ptr())
-        _lib.check(self.L.bv_search_async(self.index._h, C.byref(args), C.c_void_p(stream)))
+        fn = self.L.bv_search_batch if self.batched else self.L.bv_search_async
+        _lib.check(fn(self.index._h, C.byref(args), C.c_void_p(stream)))
 
     def merge(self, gathered, world: int, nq: int, k: int, fetch: int, stream: int):
         torch = self.torch
@@ -131,7 +135,7 @@ class ShardedIndex:
 
     def __init__(self, dim: int, n_total: int, bits: int = 8, scoring: str = "asym",
                  seed: int = DEFAULT_SEED, rounds: int = 2, metric: str = "cosine", group=None,
-                 device: int | None = None, engine=None):
+                 device: int | None = None, engine=None, batched: bool | None = None):
         import torch
         import torch.distributed as dist
 
@@ -145,7 +149,7 @@ class ShardedIndex:
         if engine is None:
             if device is None:
                 device = torch.cuda.current_device()
-            engine = CudaShardEngine(dim, bits, scoring, seed, rounds, metric, device, self.lo)
+            engine = CudaShardEngine(dim, bits, scoring, seed, rounds, metric, device, self.lo, batched)
             self._stream = torch.cuda.Stream(device=engine.device)
         else:
             self._stream = None
