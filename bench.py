@@ -138,8 +138,9 @@ SHARDED = {
                scoring="int", workload="BASELINE config 4: 1-bit codes (int8 query x +-1 codes, the popc-equivalent "
                                        "integer dot), queryBatch of 1,000, row-sharded"),
     "c5": dict(bits=8, n=50_000_000, dim=128, kind="iid", seed=5, nq=4096, metric="cosine", k=10, rf=4,
-               scoring="int", workload="BASELINE config 5: TurboQuant int8, queryBatch of 4,096, row-sharded "
-                                       "(metadata filter not applied yet)"),
+               scoring="int", filter=True,
+               workload="BASELINE config 5: TurboQuant int8, queryBatch of 4,096, metadata filter "
+                        "{lang: <most common>, year: {$gte: 2020}} as a device predicate + score mask, row-sharded"),
 }
 
 
@@ -165,12 +166,15 @@ def _init_dist(torch):
     return dist, world, rank, local
 
 
-def _exact_top10(torch, dist, x, lo, qs, chunk=1 << 20):
-    """Global exact fp32 top-10 (rows) of qs over the sharded corpus."""
+def _exact_top10(torch, dist, x, lo, qs, chunk=1 << 20, keep=None):
+    """Global exact fp32 top-10 (rows) of qs over the sharded corpus (rows
+    with keep False excluded)."""
     best_v = torch.full((qs.shape[0], 10), -float("inf"), device=qs.device)
     best_r = torch.zeros((qs.shape[0], 10), dtype=torch.int64, device=qs.device)
     for a in range(0, x.shape[0], chunk):
         s = qs @ x[a:a + chunk].T
+        if keep is not None:
+            s[:, ~keep[a:a + chunk]] = -float("inf")
         v, r = s.topk(min(10, s.shape[1]), dim=1)
         v = torch.cat([best_v, v], 1)
         r = torch.cat([best_r, r + lo + a], 1)
@@ -186,14 +190,36 @@ def _exact_top10(torch, dist, x, lo, qs, chunk=1 << 20):
     return r.gather(1, i).cpu().numpy()
 
 
+def _c5_keep(torch, dev, cfg, lo, hi):
+    """Config-5 metadata of rows [lo, hi) as device columns, and the filter."""
+    from browservec_b200 import datagen
+    from browservec_b200.filter import DeviceColumns
+
+    year, lang = datagen.metadata(torch, dev, cfg["seed"], lo, hi)
+    dc = DeviceColumns(dev)
+    dc.set_number_column("year", year)
+    dc.set_string_column("lang", lang, [f"lang{i}" for i in range(8)])
+    return dc, {"lang": "lang0", "year": {"$gte": 2020}}
+
+
+def _unpack(torch, words, n):
+    bits = (words.view(-1, 1) >> torch.arange(32, device=words.device, dtype=torch.int32)) & 1
+    return bits.reshape(-1)[:n].bool()
+
+
 def _cpu_sample_qps(torch, dev, cfg, threads, sample_rows, sample_queries):
     """The reference CPU path (WASM-SIMD exact fp32 scan + topK, restated in C)
     over the first `sample_rows` rows, scaled to the full corpus (a flat scan's
-    time is linear in the rows)."""
+    time is linear in the rows).  With a filter the scan covers the sample's
+    rows that pass it, scaled by the kept fraction."""
     from browservec_b200 import datagen
     from oracle import oracle as O
 
-    xs = datagen.rows(torch, dev, cfg["kind"], cfg["seed"], 0, sample_rows, cfg["dim"]).cpu().numpy()
+    xs = datagen.rows(torch, dev, cfg["kind"], cfg["seed"], 0, sample_rows, cfg["dim"])
+    if cfg.get("filter"):
+        dc, flt = _c5_keep(torch, dev, cfg, 0, sample_rows)
+        xs = xs[_unpack(torch, dc.mask(flt), sample_rows)]
+    xs = xs.cpu().numpy()
     qs = datagen.rows(torch, dev, cfg["kind"], cfg["seed"], 0, sample_queries, cfg["dim"],
                       stream=datagen.STREAM_QUERIES).cpu().numpy()
     O.cpu_index_query_batch(xs, cfg["dim"], qs[:threads], cfg["k"], threads=threads)  # warm
@@ -251,10 +277,17 @@ def run_sharded(args, name):
                        batched=batched)
     idx.load(x)
     qs = datagen.rows(torch, dev, cfg["kind"], cfg["seed"], 0, nq, dim, stream=datagen.STREAM_QUERIES)
+    dc, flt = _c5_keep(torch, dev, cfg, lo, hi) if cfg.get("filter") else (None, None)
+    if dc is not None:
+        config["filter"] = "device predicate (bv_filter_mask) evaluated every step, kept rows compacted"
     torch.cuda.synchronize()
 
+    def search(qq):
+        # the filter's mask is rebuilt every step from the shard's device columns
+        return idx.search(qq, k, fetch, dc.mask(flt) if dc is not None else None)
+
     for _ in range(args.warmup):
-        rows, scores, counts = idx.search(qs, k, fetch)
+        rows, scores, counts = search(qs)
     torch.cuda.synchronize()
     dist.barrier()
     clk = Clocks(local)
@@ -262,7 +295,7 @@ def run_sharded(args, name):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(cur)
     for _ in range(args.steps):
-        rows, scores, counts = idx.search(qs, k, fetch)
+        rows, scores, counts = search(qs)
     e1.record(cur)
     torch.cuda.synchronize()
     clk_res = clk.stop()
@@ -274,14 +307,16 @@ def run_sharded(args, name):
     launches_per_step = idx.engine.index.last_launches()
 
     ns = min(nq, 100)
-    truth = _exact_top10(torch, dist, x, lo, qs[:ns])
+    keep = _unpack(torch, dc.mask(flt), hi - lo) if dc is not None else None
+    kept_local = int(keep.sum().item()) if keep is not None else hi - lo
+    truth = _exact_top10(torch, dist, x, lo, qs[:ns], keep=keep)
     got = rows[:ns, :10].cpu().numpy()
     rec = sum(len(set(truth[i].tolist()) & set(got[i].tolist())) for i in range(ns)) / (ns * 10)
 
     query_ms = ms / (args.steps * nq)
     if batched:
         # per-GPU roofline of the contraction: 2 * queries * shard rows * paddedDim int8 ops per step
-        ops = 2.0 * nq * (hi - lo) * P
+        ops = 2.0 * nq * kept_local * P  # rows the filter keeps are the rows contracted
         tops = ops / (ms / args.steps / 1e3) / 1e12
         peak = 2.0 * tensor_peak()
         roofline = {"bound": "tensor", "achieved": tops, "peak": peak, "unit": "TOP/s (int8)",
@@ -311,7 +346,7 @@ def run_sharded(args, name):
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
         qd = q_host.to(dev, non_blocking=True)
-        r_, s_, c_ = idx.search(qd, k, fetch)
+        r_, s_, c_ = search(qd)
         r_, s_, c_ = r_.cpu(), s_.cpu(), c_.cpu()
     wall = time.perf_counter() - t0
     t = torch.tensor([wall], device=dev, dtype=torch.float64)

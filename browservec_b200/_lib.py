@@ -20,7 +20,7 @@ SCORING = {"asym": SCORE_ASYM, "int": SCORE_INT, "hamming": SCORE_HAMMING}
 EXPORTS = ("bv_create", "bv_destroy", "bv_last_error", "bv_append", "bv_append_device", "bv_size",
            "bv_search", "bv_search_async", "bv_query_rows_exact", "bv_export_codes", "bv_get_stats",
            "bv_launches_last_search", "bv_set_phase_trace", "bv_search_noalloc",
-           "bv_merge_shards", "bv_search_batch")
+           "bv_merge_shards", "bv_search_batch", "bv_filter_mask")
 
 
 class BvConfig(C.Structure):
@@ -41,6 +41,25 @@ class BvStats(C.Structure):
     _fields_ = [("rows", C.c_uint64), ("dim", C.c_uint32), ("padded_dim", C.c_uint32),
                 ("bits", C.c_uint32), ("words_per_row", C.c_uint32), ("chunks", C.c_uint32),
                 ("last_query_gpu_ms", C.c_float), ("device_bytes", C.c_uint64)]
+
+
+class BvColumn(C.Structure):
+    _fields_ = [("tag", C.c_void_p), ("num", C.c_void_p), ("code", C.c_void_p)]
+
+
+FILTER_MAX_TERMS = 16
+FILTER_MAX_IN = 16
+TAG_MISSING, TAG_NULL, TAG_BOOL, TAG_NUMBER, TAG_STRING = range(5)
+OP_CODES = {"$eq": 0, "$ne": 1, "$in": 2, "$gt": 3, "$gte": 4, "$lt": 5, "$lte": 6}
+
+
+class BvValue(C.Structure):
+    _fields_ = [("tag", C.c_uint32), ("code", C.c_int32), ("num", C.c_double)]
+
+
+class BvFilterTerm(C.Structure):
+    _fields_ = [("column", C.c_uint32), ("op", C.c_uint32), ("nvals", C.c_uint32),
+                ("vals", BvValue * FILTER_MAX_IN)]
 
 
 class BvError(RuntimeError):
@@ -79,6 +98,8 @@ def load(path: str = LIB_PATH):
         "bv_search_noalloc": (C.c_int, [P, C.POINTER(BvSearchArgs), P]),
         "bv_merge_shards": (C.c_int, [P, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, P, P, P, P]),
         "bv_search_batch": (C.c_int, [P, C.POINTER(BvSearchArgs), P]),
+        "bv_filter_mask": (C.c_int, [C.POINTER(BvColumn), C.c_uint32, C.POINTER(BvFilterTerm), C.c_uint32,
+                                     C.c_uint64, P, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

@@ -2,6 +2,7 @@
 // storage in HBM, the encoder and scan launches, and error reporting.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -107,13 +108,23 @@ struct bv_index {
   bool lost = false;
   // batched search: the codes as swizzled int8 MMA tiles (built lazily, for
   // rows [0, mma_rows)), per-row score factors, per-tile factor maxima
+  // (positions: each appended block of rows in ascending score-factor order)
   int8_t* d_ctiles = nullptr;
   size_t ctiles_cap = 0;  // bytes
-  float* d_rowfac = nullptr;
-  size_t rowfac_cap = 0;
+  float* d_posfac = nullptr;
+  size_t posfac_cap = 0;
+  uint32_t* d_posrow = nullptr;
+  size_t posrow_cap = 0;
   float* d_tmax = nullptr;
   size_t tmax_cap = 0;
   uint64_t mma_rows = 0;
+  // row-order sort scratch (factor keys, row ids, radix-sort temporary)
+  float* d_sfac = nullptr;  // 2 x n
+  size_t sfac_cap = 0;
+  uint32_t* d_sids = nullptr;  // 2 x n
+  size_t sids_cap = 0;
+  uint8_t* d_stmp = nullptr;
+  size_t stmp_cap = 0;
   // batched search scratch
   int8_t* d_qtiles = nullptr;
   size_t qtiles_cap = 0;
@@ -127,6 +138,22 @@ struct bv_index {
   size_t bcand_cap = 0;
   uint32_t* d_overflow = nullptr;
   uint32_t last_rounds = 0;
+  // filtered batches: the kept rows gathered into their own tiles
+  uint32_t* d_cwoff = nullptr;  // per mask word: kept rows before it (within its scan block)
+  size_t cwoff_cap = 0;
+  uint32_t* d_cbsum = nullptr;  // per scan block, then the total
+  size_t cbsum_cap = 0;
+  uint32_t* d_cmap = nullptr;   // compacted row -> row
+  size_t cmap_cap = 0;
+  int8_t* d_cctiles = nullptr;
+  size_t cctiles_cap = 0;
+  float* d_cposfac = nullptr;
+  size_t cposfac_cap = 0;
+  uint32_t* d_cposrow = nullptr;
+  size_t cposrow_cap = 0;
+  float* d_ctmax = nullptr;
+  size_t ctmax_cap = 0;
+  uint32_t last_kept = 0;
 };
 
 namespace {
@@ -469,14 +496,25 @@ int bv_destroy(bv_index* idx) {
   cudaFree(idx->d_rows);
   cudaFree(idx->d_out);
   cudaFree(idx->d_ctiles);
-  cudaFree(idx->d_rowfac);
+  cudaFree(idx->d_posfac);
+  cudaFree(idx->d_posrow);
   cudaFree(idx->d_tmax);
+  cudaFree(idx->d_sfac);
+  cudaFree(idx->d_sids);
+  cudaFree(idx->d_stmp);
   cudaFree(idx->d_qtiles);
   cudaFree(idx->d_qfac);
   cudaFree(idx->d_thr);
   cudaFree(idx->d_bcnt);
   cudaFree(idx->d_bcand);
   cudaFree(idx->d_overflow);
+  cudaFree(idx->d_cwoff);
+  cudaFree(idx->d_cbsum);
+  cudaFree(idx->d_cmap);
+  cudaFree(idx->d_cctiles);
+  cudaFree(idx->d_cposfac);
+  cudaFree(idx->d_cposrow);
+  cudaFree(idx->d_ctmax);
   if (idx->h_pin) cudaFreeHost(idx->h_pin);
   if (idx->ev0) cudaEventDestroy(idx->ev0);
   if (idx->ev1) cudaEventDestroy(idx->ev1);
@@ -723,7 +761,66 @@ int grow_keep(bv_index* idx, T** p, size_t* cap, size_t need, size_t keep, cudaS
   return BV_OK;
 }
 
-// Bring the MMA tiles up to date with the appended rows.
+uint64_t gcd_u64(uint64_t a, uint64_t b) {
+  while (b) {
+    const uint64_t t = a % b;
+    a = b;
+    b = t;
+  }
+  return a;
+}
+
+// Inverse of g modulo K (gcd(g, K) = 1).
+uint32_t inv_mod(uint32_t g, uint32_t K) {
+  int64_t t = 0, nt = 1, r = K, nr = g;
+  while (nr) {
+    const int64_t q = r / nr;
+    const int64_t a = t - q * nt;
+    t = nt;
+    nt = a;
+    const int64_t b = r - q * nr;
+    r = nr;
+    nr = b;
+  }
+  return static_cast<uint32_t>(t < 0 ? t + K : t);
+}
+
+// Rows for positions [pos0, pos0 + n): `rows` (or row0 + i when null) in
+// ascending order of their score factor, tiles scattered (scatter_tiles_kernel);
+// the result is idx->d_sids + n.
+int sort_rows_by_factor(bv_index* idx, const uint32_t* rows, uint32_t row0, uint32_t n, uint32_t pos0,
+                        cudaStream_t s) {
+  int rc;
+  if ((rc = grow(idx, &idx->d_sfac, &idx->sfac_cap, 2 * static_cast<size_t>(n), "sort scratch"))) return rc;
+  if ((rc = grow(idx, &idx->d_sids, &idx->sids_cap, 2 * static_cast<size_t>(n), "sort scratch"))) return rc;
+  size_t tmp = 0;
+  cudaError_t e = bv::launch_sort_rows(nullptr, &tmp, idx->d_sfac + n, idx->d_sfac, idx->d_sids + n, idx->d_sids,
+                                       n, s);
+  if (e != cudaSuccess) return cuda_fail(idx, e, "sort size");
+  if ((rc = grow(idx, &idx->d_stmp, &idx->stmp_cap, tmp + 16, "sort scratch"))) return rc;
+  e = bv::launch_factor(idx->bits, idx->d_scales, rows, row0, n, idx->d_sfac + n, idx->d_sids + n, s);
+  if (e == cudaSuccess) {
+    size_t cap = idx->stmp_cap;
+    e = bv::launch_sort_rows(idx->d_stmp, &cap, idx->d_sfac + n, idx->d_sfac, idx->d_sids + n, idx->d_sids, n, s);
+  }
+  if (e == cudaSuccess) {
+    const uint32_t head = static_cast<uint32_t>(
+        std::min<uint64_t>(n, (bv::kBRowTile - pos0 % bv::kBRowTile) % bv::kBRowTile));
+    const uint32_t K = (n - head) / bv::kBRowTile;
+    uint32_t g = 1, ginv = 1;
+    if (K > 1) {
+      g = static_cast<uint32_t>(static_cast<double>(K) * 0.381966) | 1u;
+      while (gcd_u64(g, K) != 1) ++g;
+      ginv = inv_mod(g % K, K);
+    }
+    e = bv::launch_scatter_tiles(idx->d_sids, idx->d_sids + n, n, head, K > 1 ? K : 1, ginv, s);
+  }
+  if (e != cudaSuccess) return cuda_fail(idx, e, "sort");
+  return BV_OK;
+}
+
+// Bring the MMA tiles up to date with the appended rows: the new block of
+// rows, sorted by factor, fills positions [mma_rows, rows).
 int ensure_mma(bv_index* idx, cudaStream_t s) {
   if (idx->mma_rows >= idx->rows) return BV_OK;
   const uint32_t KB = (idx->P + bv::kKBlock - 1) / bv::kKBlock;
@@ -733,10 +830,17 @@ int ensure_mma(bv_index* idx, cudaStream_t s) {
   if ((rc = grow_keep(idx, &idx->d_ctiles, &idx->ctiles_cap, tiles * KB * bv::kBRowTileBytes,
                       kept_tiles * KB * bv::kBRowTileBytes, s, "batch tiles")))
     return rc;
-  if ((rc = grow_keep(idx, &idx->d_rowfac, &idx->rowfac_cap, tiles * bv::kBRowTile, idx->mma_rows, s,
+  if ((rc = grow_keep(idx, &idx->d_posfac, &idx->posfac_cap, tiles * bv::kBRowTile, idx->mma_rows, s,
                       "batch factors")))
     return rc;
+  if ((rc = grow_keep(idx, &idx->d_posrow, &idx->posrow_cap, tiles * bv::kBRowTile, idx->mma_rows, s,
+                      "batch rows")))
+    return rc;
   if ((rc = grow_keep(idx, &idx->d_tmax, &idx->tmax_cap, tiles, kept_tiles, s, "batch factors"))) return rc;
+  const uint32_t n = static_cast<uint32_t>(idx->rows - idx->mma_rows);
+  if ((rc = sort_rows_by_factor(idx, nullptr, static_cast<uint32_t>(idx->mma_rows), n,
+                                static_cast<uint32_t>(idx->mma_rows), s)))
+    return rc;
   bv::ExpandParams ep;
   ep.codes = idx->d_codes;
   ep.scales = idx->d_scales;
@@ -744,11 +848,13 @@ int ensure_mma(bv_index* idx, cudaStream_t s) {
   ep.P = idx->P;
   ep.KB = KB;
   ep.bits = idx->bits;
-  ep.row0 = static_cast<uint32_t>(idx->mma_rows);
-  ep.row1 = static_cast<uint32_t>(idx->rows);
-  ep.nrows = static_cast<uint32_t>(idx->rows);
-  ep.ctiles = idx->d_ctiles;
-  ep.rowfac = idx->d_rowfac;
+  ep.rows = idx->d_sids + n;
+  ep.pos0 = static_cast<uint32_t>(idx->mma_rows);
+  ep.count = n;
+  ep.total = static_cast<uint32_t>(idx->rows);
+  ep.tiles = idx->d_ctiles;
+  ep.posfac = idx->d_posfac;
+  ep.posrow = idx->d_posrow;
   ep.tmax = idx->d_tmax;
   const cudaError_t e = bv::launch_expand(ep, s);
   if (e != cudaSuccess) return cuda_fail(idx, e, "batch expand");
@@ -765,7 +871,7 @@ int bv_search_batch(bv_index* idx, const bv_search_args* a, void* stream) {
   if (idx->scoring == BV_SCORE_ASYM)
     return fail(BV_ERR_UNSUPPORTED, "the batched search scores with the integer modes (int, hamming), "
                                     "not asym");
-  if (idx->rows > 0xFFFFFF00ull) return fail(BV_ERR_UNSUPPORTED, "batched search takes < 2^32 rows");
+  if (idx->rows >= 0x7FFFFF00ull) return fail(BV_ERR_UNSUPPORTED, "batched search takes < 2^31 rows per index");
   BV_CUDA(idx, cudaSetDevice(idx->device), "cudaSetDevice");
   cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : idx->stream;
   const uint32_t nq = a->nq;
@@ -782,7 +888,59 @@ int bv_search_batch(bv_index* idx, const bv_search_args* a, void* stream) {
   const uint32_t cap = Fp * 16 > 4096 ? Fp * 16 : 4096;  // <= 16384 (F <= 1024)
   const uint32_t KB = (idx->P + bv::kKBlock - 1) / bv::kKBlock;
   const uint32_t nqt = (nq + bv::kBQTile - 1) / bv::kBQTile;
-  const uint32_t T = static_cast<uint32_t>((idx->rows + bv::kBRowTile - 1) / bv::kBRowTile);
+  // A mask that keeps at most half the rows: contract only the kept rows,
+  // gathered into their own tiles (their order, hence the tie rule, is kept).
+  bool compact = false;
+  uint32_t kept = static_cast<uint32_t>(idx->rows);
+  if (a->mask) {
+    const uint64_t words = (idx->rows + 31) / 32;
+    const uint64_t nb = (words + bv::compact_block_words() - 1) / bv::compact_block_words();
+    if ((rc = grow(idx, &idx->d_cwoff, &idx->cwoff_cap, words, "filter scratch"))) return rc;
+    if ((rc = grow(idx, &idx->d_cbsum, &idx->cbsum_cap, nb + 1, "filter scratch"))) return rc;
+    cudaError_t e = bv::launch_mask_count(a->mask, idx->rows, idx->d_cwoff, idx->d_cbsum, idx->d_cbsum + nb, s);
+    if (e != cudaSuccess) return cuda_fail(idx, e, "filter count");
+    BV_CUDA(idx, cudaMemcpyAsync(&kept, idx->d_cbsum + nb, 4, cudaMemcpyDeviceToHost, s), "filter count");
+    BV_CUDA(idx, cudaStreamSynchronize(s), "filter count");
+    compact = static_cast<uint64_t>(kept) * 2 <= idx->rows;
+    if (compact && kept > 0) {
+      const size_t ct = (kept + bv::kBRowTile - 1) / bv::kBRowTile;
+      if ((rc = grow(idx, &idx->d_cmap, &idx->cmap_cap, kept, "filter rows"))) return rc;
+      if ((rc = grow(idx, &idx->d_cctiles, &idx->cctiles_cap, ct * KB * bv::kBRowTileBytes, "filter tiles")))
+        return rc;
+      if ((rc = grow(idx, &idx->d_cposfac, &idx->cposfac_cap, ct * bv::kBRowTile, "filter tiles"))) return rc;
+      if ((rc = grow(idx, &idx->d_cposrow, &idx->cposrow_cap, ct * bv::kBRowTile, "filter tiles"))) return rc;
+      if ((rc = grow(idx, &idx->d_ctmax, &idx->ctmax_cap, ct, "filter tiles"))) return rc;
+      e = bv::launch_row_map(a->mask, idx->rows, idx->d_cwoff, idx->d_cbsum, idx->d_cmap, s);
+      if (e != cudaSuccess) return cuda_fail(idx, e, "filter rows");
+      if ((rc = sort_rows_by_factor(idx, idx->d_cmap, 0, kept, 0, s))) return rc;
+      bv::ExpandParams ep;
+      ep.codes = idx->d_codes;
+      ep.scales = idx->d_scales;
+      ep.R = idx->R;
+      ep.P = idx->P;
+      ep.KB = KB;
+      ep.bits = idx->bits;
+      ep.rows = idx->d_sids + kept;
+      ep.pos0 = 0;
+      ep.count = kept;
+      ep.total = kept;
+      ep.tiles = idx->d_cctiles;
+      ep.posfac = idx->d_cposfac;
+      ep.posrow = idx->d_cposrow;
+      ep.tmax = idx->d_ctmax;
+      e = bv::launch_expand(ep, s);
+      if (e != cudaSuccess) return cuda_fail(idx, e, "filter compaction");
+    }
+  }
+  idx->last_kept = kept;
+  if (a->mask && kept == 0) {  // nothing passes the filter
+    BV_CUDA(idx, cudaMemsetAsync(a->out_counts, 0, nq * 4, s), "memset");
+    if (a->cand_counts) BV_CUDA(idx, cudaMemsetAsync(a->cand_counts, 0, nq * 4, s), "memset");
+    BV_CUDA(idx, cudaStreamSynchronize(s), "sync");
+    idx->last_launches = 3;
+    return BV_OK;
+  }
+  const uint32_t T = static_cast<uint32_t>(((compact ? kept : idx->rows) + bv::kBRowTile - 1) / bv::kBRowTile);
   if ((rc = grow(idx, &idx->d_qtiles, &idx->qtiles_cap, static_cast<size_t>(nqt) * KB * bv::kBQTileBytes,
                  "batch queries")))
     return rc;
@@ -808,12 +966,13 @@ int bv_search_batch(bv_index* idx, const bv_search_args* a, void* stream) {
   pp.cnt = idx->d_bcnt;
 
   bv::GemmParams g;
-  g.ctiles = idx->d_ctiles;
+  g.ctiles = compact ? idx->d_cctiles : idx->d_ctiles;
   g.qtiles = idx->d_qtiles;
-  g.rowfac = idx->d_rowfac;
-  g.tmax = idx->d_tmax;
-  g.mask = a->mask;
-  g.nrows = static_cast<uint32_t>(idx->rows);
+  g.posfac = compact ? idx->d_cposfac : idx->d_posfac;
+  g.posrow = compact ? idx->d_cposrow : idx->d_posrow;
+  g.tmax = compact ? idx->d_ctmax : idx->d_tmax;
+  g.mask = compact ? nullptr : a->mask;
+  g.npos = compact ? kept : static_cast<uint32_t>(idx->rows);
   g.nq = nq;
   g.KB = KB;
   g.nqt = nqt;
@@ -945,6 +1104,37 @@ int bv_search_batch(bv_index* idx, const bv_search_args* a, void* stream) {
   idx->last_launches = launches;
   idx->last_rounds = nrounds;
   return check_err_flag(idx);
+}
+
+int bv_filter_mask(const bv_column* cols, uint32_t ncols, const bv_filter_term* terms, uint32_t nterms,
+                   uint64_t rows, const uint32_t* live, uint32_t* mask_out, void* stream) {
+  if ((ncols && !cols) || (nterms && !terms) || !mask_out) return fail(BV_ERR_INVALID, "null argument");
+  if (ncols > BV_FILTER_MAX_TERMS || nterms > BV_FILTER_MAX_TERMS)
+    return fail(BV_ERR_UNSUPPORTED, "a filter takes at most %d columns and %d terms", BV_FILTER_MAX_TERMS,
+                BV_FILTER_MAX_TERMS);
+  for (uint32_t i = 0; i < nterms; ++i) {
+    const bv_filter_term& t = terms[i];
+    if (t.column >= ncols) return fail(BV_ERR_INVALID, "filter term %u: column %u out of range", i, t.column);
+    if (t.op > BV_OP_LTE) return fail(BV_ERR_INVALID, "filter term %u: unknown operator %u", i, t.op);
+    const uint32_t nv = t.op == BV_OP_IN ? t.nvals : 1u;
+    if (nv > BV_FILTER_MAX_IN || (t.op != BV_OP_IN && t.nvals != 1))
+      return fail(BV_ERR_INVALID, "filter term %u: %u values", i, t.nvals);
+    const bv_column& c = cols[t.column];
+    if (!c.tag) return fail(BV_ERR_INVALID, "filter term %u: column without tags", i);
+    for (uint32_t v = 0; v < nv; ++v) {
+      const uint32_t tag = t.vals[v].tag;
+      if (tag > BV_TAG_STRING) return fail(BV_ERR_INVALID, "filter term %u: bad value tag %u", i, tag);
+      if (t.op >= BV_OP_GT && tag != BV_TAG_NUMBER)
+        return fail(BV_ERR_INVALID, "filter term %u: range operator expects a number", i);
+      if ((tag == BV_TAG_NUMBER || tag == BV_TAG_BOOL) && !c.num)
+        return fail(BV_ERR_INVALID, "filter term %u: column has no numbers", i);
+      if (tag == BV_TAG_STRING && !c.code) return fail(BV_ERR_INVALID, "filter term %u: column has no strings", i);
+    }
+  }
+  const cudaError_t e =
+      bv::launch_filter(cols, ncols, terms, nterms, rows, live, mask_out, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(nullptr, e, "filter");
+  return BV_OK;
 }
 
 // ------------------------------------------------------- no-alloc search

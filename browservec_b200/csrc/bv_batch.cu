@@ -13,6 +13,8 @@
 #include <climits>
 #include <cstdint>
 
+#include <cub/device/device_radix_sort.cuh>
+
 #include "bv_batch.cuh"
 #include "bv_device.cuh"
 #include "bv_internal.h"
@@ -68,6 +70,18 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
       : "memory");
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// The wait, tied to the registers it makes valid so no use of them can be
+// scheduled above it.
+__device__ __forceinline__ void tmem_ld_wait_regs(uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.wait::ld.sync.aligned;"
+      : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+        "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15]),
+        "+r"(v[16]), "+r"(v[17]), "+r"(v[18]), "+r"(v[19]), "+r"(v[20]), "+r"(v[21]), "+r"(v[22]), "+r"(v[23]),
+        "+r"(v[24]), "+r"(v[25]), "+r"(v[26]), "+r"(v[27]), "+r"(v[28]), "+r"(v[29]), "+r"(v[30]), "+r"(v[31])
+      :
+      : "memory");
+}
 
 // Shared-memory operand descriptor: K-major, 128-byte swizzle, 8-row groups
 // 1024 bytes apart (SBO), Blackwell descriptor version 1.
@@ -80,23 +94,35 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
 constexpr uint32_t kIdescI8 = (2u << 4) | (1u << 7) | (1u << 10) | ((kBRowTile >> 3) << 17) |
                               ((kBQTile >> 4) << 24);
 
-constexpr int kEpiWarps = 4;
+// Epilogue: groups of four warps (one per TMEM lane quarter); group g drains
+// the accumulator buffer g, so with two groups two tiles drain at once and
+// each warp has two tiles' time to hide its latencies.
+#ifndef BV_EPI_GROUPS
+#define BV_EPI_GROUPS 2
+#endif
+#ifndef BV_GEMM_STAGES
+#define BV_GEMM_STAGES 3
+#endif
+constexpr int kEpiGroups = BV_EPI_GROUPS;
+constexpr int kEpiWarps = 4 * kEpiGroups;
 constexpr int kProdWarp = kEpiWarps, kMmaWarp = kEpiWarps + 1;
 constexpr int kGemmThreads = (kEpiWarps + 2) * 32;
-constexpr int kGemmStages = 4;
+constexpr int kGemmStages = BV_GEMM_STAGES;
+static_assert(kEpiGroups == 1 || kEpiGroups == 2, "one group per accumulator buffer at most");
 constexpr uint32_t kStageBytes = kBQTileBytes + kBRowTileBytes;
 constexpr uint32_t kTmemCols = 2 * kBRowTile;  // two accumulator buffers
 
 constexpr uint32_t kSlotWords = 36;  // per epilogue thread: 32 accumulators, padded for STS.128
 
 struct GemmSmem {
-  uint32_t slots_off, rowfac_off, bars_off, total;
+  uint32_t slots_off, rowfac_off, rowid_off, bars_off, total;
 };
 __host__ __device__ inline GemmSmem gemm_smem_layout() {
   GemmSmem s;
   s.slots_off = kGemmStages * kStageBytes;
-  s.rowfac_off = s.slots_off + kEpiWarps * 32 * kSlotWords * 4;  // per epilogue warp: the tile's row factors
-  s.bars_off = s.rowfac_off + kEpiWarps * kBRowTile * 4;
+  s.rowfac_off = s.slots_off + kEpiWarps * 32 * kSlotWords * 4;  // per epilogue warp: the tile's factors
+  s.rowid_off = s.rowfac_off + kEpiWarps * kBRowTile * 4;        // ... and the tile's rows
+  s.bars_off = s.rowid_off + kEpiWarps * kBRowTile * 4;
   // full[S], empty[S], tfull[2], tempty[2], done, then the TMEM address word
   s.total = s.bars_off + (2 * kGemmStages + 5) * 8 + 16;
   return s;
@@ -105,21 +131,58 @@ __host__ __device__ inline GemmSmem gemm_smem_layout() {
 }  // namespace
 
 // ------------------------------------------------------------- expand
-// One CTA per row tile, one thread per row: the row's int8 codes (int4
-// sign-extended, 1-bit as +-1, zero beyond P) into the tile's K blocks.
+// Score factor of a row (the row half of the integer-mode score).
+template <int BITS>
+__device__ __forceinline__ float row_factor(float scale) {
+  return BITS == 8 ? __fmul_rn(scale, kInv127) : (BITS == 4 ? __fmul_rn(scale, kInv7) : scale);
+}
+
+// Sort input for a block of rows: factor keys and row ids (rows[i] if given,
+// else row0 + i).
+template <int BITS>
+__global__ void __launch_bounds__(256) factor_kernel(const float* scales, const uint32_t* rows, uint32_t row0,
+                                                     uint32_t n, float* fac, uint32_t* ids) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint32_t r = rows ? rows[i] : row0 + i;
+  fac[i] = row_factor<BITS>(scales[r]);
+  ids[i] = r;
+}
+
+// Tiles of one sorted block in a scattered order: after the `head` positions
+// that complete an earlier block's last tile, the K full tiles of sorted rows
+// are placed with tile t holding sorted chunk (t * ginv) mod K (a
+// multiplicative permutation); a trailing partial tile stays last.  Every tile
+// keeps rows of nearly equal factor, and any range of tiles -- one round of a
+// batched search -- samples the whole range of factors.
+__global__ void __launch_bounds__(256) scatter_tiles_kernel(const uint32_t* in, uint32_t* out, uint32_t count,
+                                                            uint32_t head, uint32_t K, uint32_t ginv) {
+  const uint32_t j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= count) return;
+  uint32_t src = j;
+  if (j >= head) {
+    const uint32_t q = j - head, t = q / kBRowTile, off = q % kBRowTile;
+    if (t < K) src = head + static_cast<uint32_t>(static_cast<uint64_t>(t) * ginv % K) * kBRowTile + off;
+  }
+  out[j] = in[src];
+}
+
+// One CTA per tile, one thread per position: the position's row as int8
+// codes (int4 sign-extended, 1-bit as +-1, zero beyond P) into the tile's K
+// blocks, then the tile maximum of the factors of the positions in use.
 template <int BITS>
 __global__ void __launch_bounds__(kBRowTile) expand_kernel(const ExpandParams p) {
-  const uint32_t rt = p.row0 / kBRowTile + blockIdx.x;
-  const uint32_t rr = threadIdx.x;
-  const uint32_t row = rt * kBRowTile + rr;
+  const uint32_t tile = p.pos0 / kBRowTile + blockIdx.x;
+  const uint32_t tp = threadIdx.x;
+  const uint32_t pos = tile * kBRowTile + tp;
   __shared__ float red[kBRowTile / 32];
-  if (row >= p.row0 && row < p.row1) {
+  if (pos >= p.pos0 && pos < p.pos0 + p.count) {
+    const uint32_t row = p.rows[pos - p.pos0];
     const uint8_t* src = p.codes + static_cast<size_t>(row) * p.R;
-    float f = p.scales[row];
-    f = BITS == 8 ? __fmul_rn(f, kInv127) : (BITS == 4 ? __fmul_rn(f, kInv7) : f);
-    p.rowfac[row] = f;
+    p.posfac[pos] = row_factor<BITS>(p.scales[row]);
+    p.posrow[pos] = row;
     for (uint32_t kb = 0; kb < p.KB; ++kb) {
-      int8_t* dst = p.ctiles + (static_cast<size_t>(rt) * p.KB + kb) * kBRowTileBytes;
+      int8_t* dst = p.tiles + (static_cast<size_t>(tile) * p.KB + kb) * kBRowTileBytes;
       for (uint32_t c = 0; c < 8; ++c) {
         alignas(16) int8_t b[16];
 #pragma unroll
@@ -138,31 +201,29 @@ __global__ void __launch_bounds__(kBRowTile) expand_kernel(const ExpandParams p)
           }
           b[j] = static_cast<int8_t>(v);
         }
-        *reinterpret_cast<uint4*>(dst + sw128_offset(rr, c * 16)) = *reinterpret_cast<const uint4*>(b);
+        *reinterpret_cast<uint4*>(dst + sw128_offset(tp, c * 16)) = *reinterpret_cast<const uint4*>(b);
       }
     }
-  } else if (row >= p.nrows) {
-    // rows past the end of the index are zeroed so the MMA reads defined
-    // values; rows before row0 were expanded earlier and keep their bytes
+  } else if (pos >= p.total) {
+    // positions past the end are zeroed so the MMA reads defined values;
+    // positions before pos0 were written by an earlier expansion
+    p.posfac[pos] = 0.0f;
     for (uint32_t kb = 0; kb < p.KB; ++kb) {
-      int8_t* dst = p.ctiles + (static_cast<size_t>(rt) * p.KB + kb) * kBRowTileBytes;
+      int8_t* dst = p.tiles + (static_cast<size_t>(tile) * p.KB + kb) * kBRowTileBytes;
       for (uint32_t c = 0; c < 8; ++c)
-        *reinterpret_cast<uint4*>(dst + sw128_offset(rr, c * 16)) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(dst + sw128_offset(tp, c * 16)) = make_uint4(0, 0, 0, 0);
     }
   }
-  // tile maximum of the row factors over all rows present (rows before row0
-  // were written by an earlier expansion)
   __syncthreads();
-  float m = 0.0f;
-  if (row < p.nrows) m = p.rowfac[row];
+  float m = pos < p.total ? p.posfac[pos] : 0.0f;
 #pragma unroll
   for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-  if ((rr & 31u) == 0) red[rr >> 5] = m;
+  if ((tp & 31u) == 0) red[tp >> 5] = m;
   __syncthreads();
-  if (rr == 0) {
+  if (tp == 0) {
     float t = 0.0f;
     for (int w = 0; w < static_cast<int>(kBRowTile / 32); ++w) t = fmaxf(t, red[w]);
-    p.tmax[rt] = t;
+    p.tmax[tile] = t;
   }
 }
 
@@ -225,7 +286,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const GemmParams 
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], kEpiWarps);
+      mbar_init(&tempty[b], 4);  // the four warps of the group draining buffer b
     }
     mbar_init(done, 1);
     fence_mbar_init();
@@ -297,10 +358,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const GemmParams 
     }
   } else {
     // ------------------------------------------------------ epilogue
-    const uint32_t lane_base = static_cast<uint32_t>(warp) * 32u;
-    uint32_t tc = 0;
+    const uint32_t grp = static_cast<uint32_t>(warp) / 4u;
+    const uint32_t lane_base = static_cast<uint32_t>(warp % 4) * 32u;
     float* rf_s = reinterpret_cast<float*>(smem + lay.rowfac_off) + warp * kBRowTile;
-    for (uint32_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++tc) {
+    uint32_t* rid_s = reinterpret_cast<uint32_t*>(smem + lay.rowid_off) + warp * kBRowTile;
+    // this CTA's tiles in order are tc = 0, 1, 2, ...; group g takes tc = g mod groups
+    uint32_t tc = grp;
+    for (uint32_t t = blockIdx.x + grp * gridDim.x; t < ntiles; t += kEpiGroups * gridDim.x, tc += kEpiGroups) {
       const uint32_t rt = p.rt0 + t / p.nqt, qt = t % p.nqt;
       const uint32_t buf = tc & 1u, use = tc >> 1;
       const uint32_t qi = qt * kBQTile + lane_base + static_cast<uint32_t>(lane);
@@ -311,44 +375,55 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const GemmParams 
       const float qf = qvalid ? p.qfac[qi] : 0.0f;
       const float tm = p.tmax[rt];
       float rf[kBRowTile / 32];
+      uint32_t rid[kBRowTile / 32];
 #pragma unroll
       for (int i = 0; i < static_cast<int>(kBRowTile / 32); ++i) {
-        const uint32_t row = rt * kBRowTile + static_cast<uint32_t>(lane + 32 * i);
-        rf[i] = row < p.nrows ? p.rowfac[row] : 0.0f;
+        const uint32_t pos = rt * kBRowTile + static_cast<uint32_t>(lane + 32 * i);
+        rf[i] = pos < p.npos ? p.posfac[pos] : 0.0f;
+        rid[i] = pos < p.npos ? p.posrow[pos] : 0u;
       }
-      const uint32_t mrow = rt * kBRowTile + static_cast<uint32_t>(lane) * 32u;
-      const uint32_t mword = (p.mask && lane < static_cast<int>(kBRowTile / 32) && mrow < p.nrows)
-                                 ? p.mask[mrow >> 5] : 0xFFFFFFFFu;
       const bool ready = mbar_wait_bounded(&tfull[buf], use & 1u, p.err);
       if (!__all_sync(0xffffffffu, ready)) break;  // tcgen05.ld below is warp-collective
       tc_fence_after();
 #pragma unroll
-      for (int i = 0; i < static_cast<int>(kBRowTile / 32); ++i) rf_s[lane + 32 * i] = rf[i];
+      for (int i = 0; i < static_cast<int>(kBRowTile / 32); ++i) {
+        rf_s[lane + 32 * i] = rf[i];
+        rid_s[lane + 32 * i] = rid[i];
+      }
       __syncwarp();
       int bound = INT_MIN;
       if (qvalid && thr != 0ull) {
         const float ts = key_score(thr);
-        const double den = static_cast<double>(tm) * static_cast<double>(qf);
-        if (ts > 0.0f && den > 0.0) {
-          // score >= ts needs idot >= ts / (tmax * qfac) up to three f32 roundings
-          const double b = floor(static_cast<double>(ts) / den * (1.0 - 0x1p-20));
-          bound = b >= 2147483647.0 ? INT_MAX : static_cast<int>(b);
+        const float den = __fmul_rn(tm, qf);
+        if (ts > 0.0f && den > 0.0f) {
+          // score = ((f32(idot) * rowfac) * qfac) >= ts needs idot >= ts / (tmax * qfac)
+          // up to five f32 roundings (three in the score, two here): a 2^-16
+          // margin keeps the bound below every idot that can pass
+          const float b = floorf(__fmul_rn(__fdiv_rn(ts, den), 1.0f - 0x1p-16f));
+          bound = b >= 2147483520.0f ? INT_MAX : static_cast<int>(b);
         }
       }
       uint64_t* cq = p.cand + static_cast<size_t>(qvalid ? qi : 0) * p.cap;
       uint32_t* slot = reinterpret_cast<uint32_t*>(smem + lay.slots_off) + threadIdx.x * kSlotWords;
-      for (uint32_t c0 = 0; c0 < kBRowTile; c0 += 32) {
-        uint32_t v[32];
-        tmem_ld32(tmem + ((lane_base) << 16) + buf * kBRowTile + c0, v);
-        tmem_ld_wait();
-        const uint32_t rbase = rt * kBRowTile + c0;
-        uint32_t valid = rbase >= p.nrows ? 0u : (p.nrows - rbase >= 32u ? 0xFFFFFFFFu : ((1u << (p.nrows - rbase)) - 1u));
-        valid &= __shfl_sync(0xffffffffu, mword, static_cast<int>(c0 >> 5));
+      // Columns [c0, c0 + 32) of this lane's accumulator row, in registers:
+      // prefilter, then exact scores of the hits only.
+      auto chunk = [&](const uint32_t (&v)[32], uint32_t c0) {
+        // the common case is a chunk with no hit: one 3-input max tree decides it
+        int mx[11];
+#pragma unroll
+        for (int i = 0; i < 10; ++i)
+          mx[i] = __vimax3_s32(static_cast<int>(v[3 * i]), static_cast<int>(v[3 * i + 1]), static_cast<int>(v[3 * i + 2]));
+        mx[10] = max(static_cast<int>(v[30]), static_cast<int>(v[31]));
+        const int top = __vimax3_s32(__vimax3_s32(mx[0], mx[1], mx[2]), __vimax3_s32(mx[3], mx[4], mx[5]),
+                                     __vimax3_s32(__vimax3_s32(mx[6], mx[7], mx[8]), mx[9], mx[10]));
+        if (!qvalid || top < bound) return;
+        const uint32_t pbase = rt * kBRowTile + c0;
+        const uint32_t valid =
+            pbase >= p.npos ? 0u : (p.npos - pbase >= 32u ? 0xFFFFFFFFu : ((1u << (p.npos - pbase)) - 1u));
         uint32_t m = 0;
 #pragma unroll
         for (int j = 0; j < 32; ++j) m |= (static_cast<int>(v[j]) >= bound ? 1u : 0u) << j;
         m &= valid;
-        if (!qvalid) m = 0;
         if (m) {
           // this lane's 32 accumulators go to its own shared-memory slot, and
           // only the columns that passed the prefilter are scored exactly
@@ -358,7 +433,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const GemmParams 
           uint32_t pass = 0;
           for (uint32_t mm = m; mm; mm &= mm - 1u) {
             const uint32_t j = __ffs(mm) - 1u;
-            const uint32_t row = rbase + j;
+            const uint32_t row = rid_s[c0 + j];
+            if (p.mask && !((p.mask[row >> 5] >> (row & 31u)) & 1u)) continue;
             const float sc = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(slot[j])), rf_s[c0 + j]), qf);
             if (make_key(sc, row) > thr) pass |= 1u << j;
           }
@@ -369,12 +445,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const GemmParams 
             uint32_t w = base;
             for (uint32_t mm = pass; mm; mm &= mm - 1u, ++w) {
               const uint32_t j = __ffs(mm) - 1u;
-              const uint32_t row = rbase + j;
+              const uint32_t row = rid_s[c0 + j];
               const float sc = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(slot[j])), rf_s[c0 + j]), qf);
               if (w < p.cap) cq[w] = make_key(sc, row);
             }
           }
         }
+      };
+      // two register sets: the next 32 columns load while these are scored
+      const uint32_t taddr = tmem + (lane_base << 16) + buf * kBRowTile;
+      uint32_t va[32], vb[32];
+      tmem_ld32(taddr, va);
+      tmem_ld_wait_regs(va);
+#pragma unroll 1
+      for (uint32_t c0 = 0; c0 < kBRowTile; c0 += 64) {
+        tmem_ld32(taddr + c0 + 32, vb);
+        chunk(va, c0);
+        __syncwarp();
+        tmem_ld_wait_regs(vb);
+        if (c0 + 64 < kBRowTile) tmem_ld32(taddr + c0 + 64, va);
+        chunk(vb, c0 + 32);
+        __syncwarp();
+        if (c0 + 64 < kBRowTile) tmem_ld_wait_regs(va);
       }
       tc_fence_before();
       __syncwarp();
@@ -420,17 +512,158 @@ __global__ void __launch_bounds__(kConsumerThreads, 1) select_kernel(const Selec
   }
 }
 
+// ------------------------------------------------------------- compaction
+// A filtered batch contracts only the rows its mask keeps: the kept rows'
+// tiles are gathered into a dense corpus (row c of it = the c-th kept row, in
+// row order, so ordering by c is ordering by row) and the candidates' rows
+// are mapped back before the re-rank.
+constexpr uint32_t kScanWords = 1024;  // mask words per scan block
+
+// Per block: exclusive prefix of the popcounts of its mask words, and the block total.
+// Mask word w with the bits of rows past the end cleared.
+__device__ __forceinline__ uint32_t mask_word(const uint32_t* mask, uint64_t w, uint64_t rows) {
+  uint32_t m = mask[w];
+  const uint64_t end = (w + 1) * 32u;
+  if (end > rows) m &= (1u << static_cast<uint32_t>(rows - w * 32u)) - 1u;
+  return m;
+}
+
+__global__ void __launch_bounds__(kScanWords) mask_scan_kernel(const uint32_t* mask, uint64_t rows, uint64_t words,
+                                                               uint32_t* word_off, uint32_t* block_sum) {
+  __shared__ uint32_t warp_tot[32];
+  const uint64_t w = static_cast<uint64_t>(blockIdx.x) * kScanWords + threadIdx.x;
+  const uint32_t c = w < words ? __popc(mask_word(mask, w, rows)) : 0u;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t x = c;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, x, off);
+    if (lane >= off) x += y;
+  }
+  if (lane == 31) warp_tot[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t t = warp_tot[lane];
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, t, off);
+      if (lane >= off) t += y;
+    }
+    warp_tot[lane] = t;  // inclusive over warps
+  }
+  __syncthreads();
+  const uint32_t before = (warp ? warp_tot[warp - 1] : 0u) + x - c;
+  if (w < words) word_off[w] = before;
+  if (threadIdx.x == kScanWords - 1) block_sum[blockIdx.x] = warp_tot[31];
+}
+
+// Exclusive prefix of the block totals (one CTA, any count), and the grand total.
+__global__ void __launch_bounds__(1024) block_scan_kernel(uint32_t* block_sum, uint32_t nblocks, uint32_t* total) {
+  __shared__ uint32_t warp_tot[32];
+  __shared__ uint32_t carry;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (uint32_t b0 = 0; b0 < nblocks; b0 += 1024) {
+    const uint32_t b = b0 + threadIdx.x;
+    const uint32_t c = b < nblocks ? block_sum[b] : 0u;
+    uint32_t x = c;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, x, off);
+      if (lane >= off) x += y;
+    }
+    if (lane == 31) warp_tot[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+      uint32_t t = warp_tot[lane];
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, t, off);
+        if (lane >= off) t += y;
+      }
+      warp_tot[lane] = t;
+    }
+    __syncthreads();
+    const uint32_t before = carry + (warp ? warp_tot[warp - 1] : 0u) + x - c;
+    if (b < nblocks) block_sum[b] = before;
+    __syncthreads();
+    if (threadIdx.x == 0) carry += warp_tot[31];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *total = carry;
+}
+
+// map[c] = the c-th kept row.
+__global__ void __launch_bounds__(256) row_map_kernel(const uint32_t* mask, uint64_t rows, uint64_t words,
+                                                      const uint32_t* word_off, const uint32_t* block_sum,
+                                                      uint32_t* map) {
+  const uint64_t w = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (w >= words) return;
+  uint32_t m = mask_word(mask, w, rows);
+  uint32_t o = word_off[w] + block_sum[w / kScanWords];
+  while (m) {
+    const uint32_t b = __ffs(m) - 1u;
+    m &= m - 1u;
+    map[o++] = static_cast<uint32_t>(w * 32u + b);
+  }
+}
+
 // ------------------------------------------------------------- launchers
 uint32_t batch_gemm_smem() { return gemm_smem_layout().total + 1024; }
 
+cudaError_t launch_mask_count(const uint32_t* mask, uint64_t rows, uint32_t* word_off, uint32_t* block_sum,
+                              uint32_t* count, cudaStream_t s) {
+  const uint64_t words = (rows + 31) / 32;
+  const uint32_t nb = static_cast<uint32_t>((words + kScanWords - 1) / kScanWords);
+  mask_scan_kernel<<<nb, kScanWords, 0, s>>>(mask, rows, words, word_off, block_sum);
+  block_scan_kernel<<<1, 1024, 0, s>>>(block_sum, nb, count);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_row_map(const uint32_t* mask, uint64_t rows, const uint32_t* word_off, const uint32_t* block_sum,
+                           uint32_t* map, cudaStream_t s) {
+  const uint64_t words = (rows + 31) / 32;
+  row_map_kernel<<<static_cast<unsigned>((words + 255) / 256), 256, 0, s>>>(mask, rows, words, word_off, block_sum,
+                                                                            map);
+  return cudaGetLastError();
+}
+
+uint32_t compact_block_words() { return kScanWords; }
+
 cudaError_t launch_expand(const ExpandParams& p, cudaStream_t s) {
-  if (p.row1 <= p.row0) return cudaSuccess;
-  const uint32_t t0 = p.row0 / kBRowTile, t1 = (p.row1 + kBRowTile - 1) / kBRowTile;
+  if (p.count == 0) return cudaSuccess;
+  const uint32_t t0 = p.pos0 / kBRowTile, t1 = (p.pos0 + p.count + kBRowTile - 1) / kBRowTile;
   const dim3 grid(t1 - t0);
   if (p.bits == 8) expand_kernel<8><<<grid, kBRowTile, 0, s>>>(p);
   else if (p.bits == 4) expand_kernel<4><<<grid, kBRowTile, 0, s>>>(p);
   else expand_kernel<1><<<grid, kBRowTile, 0, s>>>(p);
   return cudaGetLastError();
+}
+
+cudaError_t launch_factor(uint32_t bits, const float* scales, const uint32_t* rows, uint32_t row0, uint32_t n,
+                          float* fac, uint32_t* ids, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  const unsigned grid = (n + 255) / 256;
+  if (bits == 8) factor_kernel<8><<<grid, 256, 0, s>>>(scales, rows, row0, n, fac, ids);
+  else if (bits == 4) factor_kernel<4><<<grid, 256, 0, s>>>(scales, rows, row0, n, fac, ids);
+  else factor_kernel<1><<<grid, 256, 0, s>>>(scales, rows, row0, n, fac, ids);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_scatter_tiles(const uint32_t* in, uint32_t* out, uint32_t count, uint32_t head, uint32_t K,
+                                 uint32_t ginv, cudaStream_t s) {
+  if (count == 0) return cudaSuccess;
+  scatter_tiles_kernel<<<(count + 255) / 256, 256, 0, s>>>(in, out, count, head, K, ginv);
+  return cudaGetLastError();
+}
+
+// Rows ordered by ascending factor (a radix sort of the factor keys carrying
+// the row ids); tmp == nullptr only sizes the temporary storage.
+cudaError_t launch_sort_rows(void* tmp, size_t* tmp_bytes, const float* fac_in, float* fac_out,
+                             const uint32_t* ids_in, uint32_t* ids_out, uint32_t n, cudaStream_t s) {
+  return cub::DeviceRadixSort::SortPairs(tmp, *tmp_bytes, fac_in, fac_out, ids_in, ids_out, static_cast<int>(n), 0,
+                                         32, s);
 }
 
 cudaError_t launch_prep(const PrepParams& p, cudaStream_t s) {

@@ -38,15 +38,21 @@ __host__ __device__ inline uint32_t sw128_offset(uint32_t r, uint32_t k) {
   return r * 128u + ((((k >> 4) ^ (r & 7u)) & 7u) << 4) + (k & 15u);
 }
 
+// Tile positions hold rows in ascending order of their score factor, so the
+// rows of one tile have nearly equal factors and the tile's maximum factor
+// gives a tight integer prefilter.  posrow keeps each position's row for the
+// candidate keys (the tie rule orders by row, not position).
 struct ExpandParams {
   const uint8_t* codes;  // rows x R packed codes
   const float* scales;   // rows
   uint32_t R, P, KB, bits;
-  uint32_t row0, row1;   // rows to expand
-  uint32_t nrows;        // rows in the index (for the tile maxima)
-  int8_t* ctiles;        // [row tile][KB] swizzled 256 x 128 int8 tiles
-  float* rowfac;         // per-row score factor
-  float* tmax;           // per-row-tile maximum of rowfac
+  const uint32_t* rows;  // position pos0 + i holds row rows[i]
+  uint32_t pos0, count;  // positions written
+  uint32_t total;        // positions in use; positions past it are zeroed
+  int8_t* tiles;         // [tile][KB] swizzled 256 x 128 int8 tiles
+  float* posfac;         // per position: score factor
+  uint32_t* posrow;      // per position: row
+  float* tmax;           // per tile: maximum factor
 };
 
 struct PrepParams {
@@ -63,10 +69,11 @@ struct PrepParams {
 struct GemmParams {
   const int8_t* ctiles;
   const int8_t* qtiles;
-  const float* rowfac;
+  const float* posfac;
+  const uint32_t* posrow;
   const float* tmax;
-  const uint32_t* mask;  // optional, 1 bit per row
-  uint32_t nrows, nq, KB, nqt;
+  const uint32_t* mask;  // optional, 1 bit per row (not position)
+  uint32_t npos, nq, KB, nqt;
   uint32_t rt0, rt1;     // row tiles of this round
   const uint64_t* thr;
   const float* qfac;

@@ -4,6 +4,8 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include "../../include/browservec.h"
+
 namespace bv {
 
 struct ScanParams;
@@ -107,6 +109,20 @@ cudaError_t launch_expand(const ExpandParams& p, cudaStream_t s);
 cudaError_t launch_prep(const PrepParams& p, cudaStream_t s);
 cudaError_t launch_gemm(const GemmParams& p, uint32_t grid, cudaStream_t s);
 cudaError_t launch_select(const SelectParams& p, cudaStream_t s);
+uint32_t compact_block_words();
+cudaError_t launch_mask_count(const uint32_t* mask, uint64_t rows, uint32_t* word_off, uint32_t* block_sum,
+                              uint32_t* count, cudaStream_t s);
+cudaError_t launch_row_map(const uint32_t* mask, uint64_t rows, const uint32_t* word_off, const uint32_t* block_sum,
+                           uint32_t* map, cudaStream_t s);
+cudaError_t launch_factor(uint32_t bits, const float* scales, const uint32_t* rows, uint32_t row0, uint32_t n,
+                          float* fac, uint32_t* ids, cudaStream_t s);
+cudaError_t launch_scatter_tiles(const uint32_t* in, uint32_t* out, uint32_t count, uint32_t head, uint32_t K,
+                                 uint32_t ginv, cudaStream_t s);
+cudaError_t launch_sort_rows(void* tmp, size_t* tmp_bytes, const float* fac_in, float* fac_out,
+                             const uint32_t* ids_in, uint32_t* ids_out, uint32_t n, cudaStream_t s);
+// bv_filter.cu
+cudaError_t launch_filter(const bv_column* cols, uint32_t ncols, const bv_filter_term* terms, uint32_t nterms,
+                          uint64_t rows, const uint32_t* live, uint32_t* mask, cudaStream_t s);
 
 // bv_merge.cu: cross-shard merge of all-gathered shard records
 size_t merge_smem_bytes(uint32_t world, uint32_t F);

@@ -11,6 +11,7 @@ JavaScript equality is strict (===): a bool never equals a number, ``None``
 """
 from __future__ import annotations
 
+import ctypes as C
 from typing import Any, Callable, Mapping
 
 import numpy as np
@@ -233,3 +234,125 @@ def pack_mask(bits: np.ndarray) -> np.ndarray:
     b = np.zeros(words * 32, np.uint8)
     b[:n] = bits
     return np.packbits(b, bitorder="little").view(np.uint32).copy()
+
+
+class DeviceColumns:
+    """Metadata columns on the GPU, evaluated by the library's predicate kernel
+    (bv_filter_mask): per field a type tag (uint8, FilterColumns.T_*), the
+    value as f64 (numbers, booleans as 0/1) and string dictionary codes."""
+
+    def __init__(self, device):
+        import torch
+
+        self.torch = torch
+        self.device = device
+        self.n = 0
+        self.fields: dict[str, dict] = {}
+
+    @classmethod
+    def from_host(cls, fc: FilterColumns, device) -> "DeviceColumns":
+        import torch
+
+        dc = cls(device)
+        dc.n = fc.n
+        for field, c in fc.cols.items():
+            dc.fields[field] = {
+                "tag": torch.from_numpy(np.ascontiguousarray(c["tag"], np.uint8)).to(device),
+                "num": torch.from_numpy(np.ascontiguousarray(c["num"], np.float64)).to(device),
+                "code": torch.from_numpy(np.ascontiguousarray(c["code"], np.int64).astype(np.int32)).to(device),
+                "dict": dict(c["dict"]),
+            }
+        return dc
+
+    def set_number_column(self, field: str, values) -> None:
+        """A field every row holds as a number (values: a device tensor)."""
+        torch = self.torch
+        v = values.to(self.device, torch.float64).contiguous()
+        self.n = v.numel()
+        self.fields[field] = {"tag": torch.full((self.n,), FilterColumns.T_NUM, dtype=torch.uint8, device=self.device),
+                              "num": v, "code": None, "dict": {}}
+
+    def set_string_column(self, field: str, codes, dictionary: list) -> None:
+        """A field every row holds as a string: codes (device tensor) index `dictionary`."""
+        torch = self.torch
+        c = codes.to(self.device, torch.int32).contiguous()
+        self.n = c.numel()
+        self.fields[field] = {"tag": torch.full((self.n,), FilterColumns.T_STR, dtype=torch.uint8, device=self.device),
+                              "num": None, "code": c, "dict": {w: i for i, w in enumerate(dictionary)}}
+
+    def _value(self, field: str, v) -> "_lib.BvValue":
+        from . import _lib
+
+        if v is None:
+            return _lib.BvValue(tag=_lib.TAG_NULL, code=-1, num=0.0)
+        if isinstance(v, bool):
+            return _lib.BvValue(tag=_lib.TAG_BOOL, code=-1, num=1.0 if v else 0.0)
+        if _is_number(v):
+            return _lib.BvValue(tag=_lib.TAG_NUMBER, code=-1, num=float(v))
+        if isinstance(v, str):
+            return _lib.BvValue(tag=_lib.TAG_STRING, code=self.fields[field]["dict"].get(v, -1), num=0.0)
+        return _lib.BvValue(tag=_lib.TAG_MISSING + 99, code=-1, num=0.0)  # objects never match
+
+    def compile(self, flt: Mapping[str, Any]):
+        """The reference filter as device terms.  Returns (columns, terms,
+        always_false); raises the reference's errors (filter.ts:49-66)."""
+        from . import _lib
+
+        names, terms, never = [], [], False
+        for field, cond in flt.items():
+            ops = cond.items() if _is_ops(cond) else [("$eq", cond)]
+            for op, arg in ops:
+                if op not in OPS:
+                    raise ValueError(f'filter: unknown operator "{op}" on field "{field}"')
+                if op == "$in" and not isinstance(arg, (list, tuple)):
+                    raise ValueError(f'filter: $in on "{field}" expects an array, got {_js_typeof(arg)}')
+                if op in ("$gt", "$gte", "$lt", "$lte") and not _is_number(arg):
+                    raise ValueError(f'filter: {op} on "{field}" expects a number, got {_js_typeof(arg)}')
+                if field not in self.fields:  # no row has the field: only $ne holds
+                    never |= op != "$ne"
+                    continue
+                vals = list(arg) if op == "$in" else [arg]
+                if op == "$in" and not vals:
+                    never = True
+                    continue
+                if len(vals) > _lib.FILTER_MAX_IN:
+                    raise ValueError(f"filter: $in on \"{field}\" takes at most {_lib.FILTER_MAX_IN} values here")
+                bad = [v for v in vals if not (v is None or isinstance(v, (bool, int, float, str)))]
+                if bad:  # objects and arrays never equal a stored value
+                    if op == "$ne":
+                        continue
+                    vals = [v for v in vals if v not in bad]
+                    if not vals:
+                        never = True
+                        continue
+                if field not in names:
+                    names.append(field)
+                t = _lib.BvFilterTerm(column=names.index(field), op=_lib.OP_CODES[op], nvals=len(vals))
+                for i, v in enumerate(vals):
+                    t.vals[i] = self._value(field, v)
+                terms.append(t)
+        if len(terms) > _lib.FILTER_MAX_TERMS or len(names) > _lib.FILTER_MAX_TERMS:
+            raise ValueError(f"filter: at most {_lib.FILTER_MAX_TERMS} operator terms here")
+        cols = (_lib.BvColumn * max(1, len(names)))()
+        for i, f in enumerate(names):
+            c = self.fields[f]
+            cols[i] = _lib.BvColumn(tag=c["tag"].data_ptr(), num=None if c["num"] is None else c["num"].data_ptr(),
+                                    code=None if c["code"] is None else c["code"].data_ptr())
+        arr = (_lib.BvFilterTerm * max(1, len(terms)))(*terms)
+        return cols, len(names), arr, len(terms), never
+
+    def mask(self, flt: Mapping[str, Any], live=None, stream: int = 0):
+        """uint32 mask words (a device tensor) of the rows the filter keeps."""
+        from . import _lib
+
+        torch = self.torch
+        words = max((self.n + 31) // 32, 1)
+        out = torch.zeros(words, dtype=torch.int32, device=self.device)
+        cols, ncols, terms, nterms, never = self.compile(flt)
+        if never or self.n == 0:
+            return out
+        L = _lib.load()
+        _lib.check(L.bv_filter_mask(cols, ncols, terms, nterms, self.n,
+                                    C.c_void_p(live.data_ptr()) if live is not None else None,
+                                    C.c_void_p(out.data_ptr()), C.c_void_p(stream)))
+        return out

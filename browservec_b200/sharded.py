@@ -94,14 +94,16 @@ class CudaShardEngine:
     def new_record(self, nq: int, fetch: int):
         return self.torch.empty(record_words(nq, fetch), dtype=self.torch.int32, device=self.device)
 
-    def search_record(self, q, k: int, fetch: int, rec, stream: int) -> None:
+    def search_record(self, q, k: int, fetch: int, rec, stream: int, mask=None) -> None:
         nq = q.shape[0]
         v = record_views(rec, nq, fetch)
         if not hasattr(self, "_scratch") or self._scratch.numel() < nq * (2 * k + 1):
             self._scratch = self.torch.empty(nq * (2 * k + 1), dtype=self.torch.int32, device=self.device)
         s = self._scratch
-        args = _lib.BvSearchArgs(queries=q.data_ptr(), nq=nq, k=k, fetch=fetch, rerank=1, mask=None,
-                                 mask_words=0, out_rows=s.data_ptr(), out_scores=s[nq * k:].data_ptr(),
+        args = _lib.BvSearchArgs(queries=q.data_ptr(), nq=nq, k=k, fetch=fetch, rerank=1,
+                                 mask=None if mask is None else mask.data_ptr(),
+                                 mask_words=0 if mask is None else mask.numel(),
+                                 out_rows=s.data_ptr(), out_scores=s[nq * k:].data_ptr(),
                                  out_counts=s[2 * nq * k:].data_ptr(), cand_rows=v.rows.data_ptr(),
                                  cand_scores=v.approx.data_ptr(), cand_counts=v.counts.data_ptr(),
                                  cand_exact=v.exact.data_ptr())
@@ -169,10 +171,12 @@ class ShardedIndex:
             raise RuntimeError("shard already loaded")
         self.engine.append(part)
 
-    def search(self, q, k: int, fetch: int):
+    def search(self, q, k: int, fetch: int, mask=None):
         """Collective search of nq queries (a (nq, dim) float32 tensor on this
-        rank's device, normalised for cosine).  Returns (rows, scores, counts)
-        tensors of shape (nq, k), (nq, k), (nq,) with global rows."""
+        rank's device, normalised for cosine).  `mask` (optional): this rank's
+        score mask, uint32 words over its local rows (e.g. DeviceColumns.mask
+        of its shard's metadata).  Returns (rows, scores, counts) tensors of
+        shape (nq, k), (nq, k), (nq,) with global rows."""
         torch = self.torch
         fetch = max(fetch, k)
         nq = q.shape[0]
@@ -182,7 +186,7 @@ class ShardedIndex:
         with ctx:
             sid = self._stream.cuda_stream if self._stream is not None else 0
             rec = self.engine.new_record(nq, fetch)
-            self.engine.search_record(q, k, fetch, rec, sid)
+            self.engine.search_record(q, k, fetch, rec, sid, mask)
             gathered = torch.empty(self.world * rec.numel(), dtype=rec.dtype, device=rec.device)
             self.dist.all_gather_into_tensor(gathered, rec, group=self.group)
             out = self.engine.merge(gathered, self.world, nq, k, fetch, sid)

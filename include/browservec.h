@@ -195,6 +195,44 @@ BV_API int bv_search_batch(bv_index* idx, const bv_search_args* args, void* stre
 BV_API int bv_merge_shards(const uint32_t* gathered, uint32_t world, uint32_t nq, uint32_t fetch, uint32_t k,
                            uint32_t* out_rows, float* out_scores, uint32_t* out_counts, void* stream);
 
+/* ---------------------------------------------------------- metadata filter
+ * The per-row metadata predicate of a filtered query (compileFilter,
+ * src/store/filter.ts:18-85, applied row by row at src/index.ts:372-395),
+ * evaluated on the GPU over device columns.  One column per metadata field:
+ * a type tag per row, the value as a JS number (f64; booleans as 0/1), and
+ * for strings a dictionary code.  A filter is an AND of terms, one per
+ * (field, operator) pair, with strict JS equality: $eq/$in match when tag and
+ * value both match, $ne matches everything $eq does not (missing fields
+ * included), range operators match numbers only. */
+typedef enum bv_tag { BV_TAG_MISSING = 0, BV_TAG_NULL = 1, BV_TAG_BOOL = 2, BV_TAG_NUMBER = 3,
+                      BV_TAG_STRING = 4 } bv_tag;
+typedef enum bv_op { BV_OP_EQ = 0, BV_OP_NE = 1, BV_OP_IN = 2, BV_OP_GT = 3, BV_OP_GTE = 4, BV_OP_LT = 5,
+                     BV_OP_LTE = 6 } bv_op;
+typedef struct bv_column {
+  const uint8_t* tag;   /* rows: bv_tag */
+  const double* num;    /* rows: number / bool value (read where tag is NUMBER or BOOL) */
+  const int32_t* code;  /* rows: string dictionary code (read where tag is STRING); may be NULL */
+} bv_column;
+#define BV_FILTER_MAX_TERMS 16
+#define BV_FILTER_MAX_IN 16
+typedef struct bv_value {
+  uint32_t tag;         /* bv_tag of the argument */
+  int32_t code;         /* string argument: dictionary code (-1: absent from the column) */
+  double num;           /* number / bool argument */
+} bv_value;
+typedef struct bv_filter_term {
+  uint32_t column;      /* index into the columns */
+  uint32_t op;          /* bv_op */
+  uint32_t nvals;       /* 1, or the $in list length (<= BV_FILTER_MAX_IN) */
+  bv_value vals[BV_FILTER_MAX_IN];
+} bv_filter_term;
+/* Writes ceil(rows/32) mask words (bit r of word r/32 set = row r matches),
+ * ANDed with `live` (optional, same layout: tombstoned rows cleared,
+ * src/index.ts:378-383).  Columns and masks are DEVICE pointers; terms are
+ * host memory.  Enqueued on `stream`. */
+BV_API int bv_filter_mask(const bv_column* cols, uint32_t ncols, const bv_filter_term* terms, uint32_t nterms,
+                          uint64_t rows, const uint32_t* live, uint32_t* mask_out, void* stream);
+
 /* bv_search_noalloc: bv_search_async for callers that may not allocate
  * device memory once they are running -- hosts whose device memory is all
  * reserved up front by their own pool, or that run under a memory budget where

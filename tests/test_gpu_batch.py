@@ -93,54 +93,60 @@ def test_batch_matches_per_query(bits, scoring, n, d, nq, k, fetch):
         idx.destroy()
 
 
-def test_batch_mask():
+@pytest.mark.parametrize("keep_frac", [0.1, 0.6, 0.0, 0.0005])
+def test_batch_mask(keep_frac):
+    """A mask keeping at most half the rows is served by compacting the kept
+    rows into their own tiles; above half the GEMM masks in its epilogue.
+    Bits past the last row are set on purpose: they must be ignored."""
     import torch
 
     from browservec_b200.index import AddonQuantIndex
 
-    n, d, nq, k, fetch = 9000, 128, 100, 10, 40
+    n, d, nq, k, fetch = 9001, 128, 100, 10, 40
     x = _rows(n, d, 3)
     rng = np.random.default_rng(4)
-    keep = rng.random(n) < 0.1
-    mask = np.packbits(np.concatenate([keep, np.zeros((-n) % 32, bool)]), bitorder="little").view(np.uint32)
+    keep = rng.random(n) < keep_frac
+    mask = np.packbits(np.concatenate([keep, np.ones((-n) % 32, bool)]), bitorder="little").view(np.uint32)
     idx = AddonQuantIndex(d, bits=8, scoring="int")
     try:
         idx.append(x, n)
         q = torch.from_numpy(_rows(nq, d, 5)).cuda()
         got = _run(idx, "batch", q, k, fetch, mask)
         _compare(got, _run(idx, "single", q, k, fetch, mask), nq, k, fetch)
-        assert all(keep[r] for r in got[0][:, :k].ravel().tolist())
+        assert int(got[2].min()) == min(k, int(keep.sum()))
+        for i in range(nq):
+            assert all(keep[r] for r in got[0][i, :int(got[2][i])].tolist())
     finally:
         idx.destroy()
 
 
 def test_batch_overflow_fallback():
-    """Rows ordered by increasing similarity to every query: each round beats
-    the previous threshold with nearly all its rows, the candidate buffers
-    overflow and the batch is redone round by round."""
+    """Rows along one direction with a growing norm (a raw index, not
+    normalised): the score factor and the score both grow with the row, so the
+    first round -- tiles scattered over the factor order -- misses the best
+    rows, the next round's candidates overflow their buffers and the batch is
+    redone round by round.  The result must not change."""
     import torch
 
-    from browservec_b200 import _lib
     from browservec_b200.index import AddonQuantIndex
 
-    n, d, nq, k, fetch = 60000, 64, 8, 10, 40
+    n, d, nq, k, fetch = 300_000, 64, 8, 10, 40
     rng = np.random.default_rng(9)
-    base = rng.standard_normal(d)
-    base /= np.linalg.norm(base)
-    noise = rng.standard_normal((n, d)) * 0.02
-    t = np.linspace(0.05, 1.0, n)[:, None]
-    x = O.normalize_rows((t * base + (1 - t) * rng.standard_normal(d) + noise).astype(np.float32))
-    qs = O.normalize_rows((base + 0.01 * rng.standard_normal((nq, d))).astype(np.float32))
-    idx = AddonQuantIndex(d, bits=8, scoring="int")
+    u = rng.standard_normal(d).astype(np.float64)
+    u /= np.linalg.norm(u)
+    x = (np.linspace(1.0, 2.0, n)[:, None] * u[None, :]).astype(np.float32)
+    qs = O.normalize_rows((u + 0.01 * rng.standard_normal((nq, d))).astype(np.float32))
+    idx = AddonQuantIndex(d, bits=8, scoring="int", metric="dot")
     try:
         idx.append(x, n)
         q = torch.from_numpy(qs).cuda()
         got = _run(idx, "batch", q, k, fetch)
         launches = idx.last_launches()
         _compare(got, _run(idx, "single", q, k, fetch), nq, k, fetch)
+        assert got[0][0, 0] == n - 1  # the largest row scores highest
         # fast path: prep + (gemm + select) per round + tail; the fallback adds more
         T = (n + 255) // 256
-        rounds, seen, m = 0, 0, 16
+        rounds, seen = 0, 0
         grow = (4096 - fetch) / (2.0 * fetch)
         while seen < T:
             size = 16 if seen == 0 else max(1, int(seen * grow))

@@ -78,7 +78,7 @@ class OracleShardEngine:
     def new_record(self, nq, fetch):
         return torch.zeros(record_words(nq, fetch), dtype=torch.int32)
 
-    def search_record(self, q, k, fetch, rec, stream):
+    def search_record(self, q, k, fetch, rec, stream, mask=None):
         nq = q.shape[0]
         v = record_views(rec.numpy(), nq, fetch)
         for i in range(nq):
