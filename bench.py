@@ -39,6 +39,25 @@ sys.path.insert(0, ROOT)
 
 N_ROWS, DIM, N_QUERIES, K, RERANK_FACTOR, SEED = 100_000, 768, 1000, 10, 4, 2
 METRIC = "queries/sec at fixed recall@10 (TurboQuant int8 flat scan, N=100k, d=768, k=10, F=40)"
+BITS, WORKLOAD = 8, "BASELINE config 2: TurboQuant int8 flat, single-query scans"
+# Single-query configurations: queries issued one at a time against one index
+# (replicated round-robin so that every scan reads a corpus evicted from L2).
+SINGLE = {
+    "c2": dict(n=100_000, dim=768, nq=1000, k=10, rf=4, seed=2, bits=8, metric=METRIC,
+               workload="BASELINE config 2: TurboQuant int8 flat, single-query scans"),
+    "c1": dict(n=20_000, dim=384, nq=100, k=10, rf=1, seed=0, bits=0,
+               metric="queries/sec at recall@10 = 1.0 (exact fp32 flat cosine scan, N=20k, d=384, k=10)",
+               workload="BASELINE config 1: exact fp32 flat scan (the reference CPU path's WASM-SIMD f32 "
+                        "arithmetic), single-query scans"),
+}
+
+
+def _use_single(name):
+    """Point the single-query flow at configuration `name`."""
+    global N_ROWS, DIM, N_QUERIES, K, RERANK_FACTOR, SEED, METRIC, BITS, WORKLOAD
+    c = SINGLE[name]
+    N_ROWS, DIM, N_QUERIES, K, RERANK_FACTOR, SEED = c["n"], c["dim"], c["nq"], c["k"], c["rf"], c["seed"]
+    METRIC, BITS, WORKLOAD = c["metric"], c["bits"], c["workload"]
 UNIT = "queries/s"
 
 
@@ -392,14 +411,19 @@ def main():
     ap.add_argument("--replicas", type=int, default=4)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--config", default="c2", choices=["c2", *SHARDED])
+    ap.add_argument("--config", default="c2", choices=[*SINGLE, *SHARDED])
     ap.add_argument("--sharded-scoring", default=None, choices=["asym", "int", "hamming"],
                     help="scoring of a sharded config (default: the config's)")
     ap.add_argument("--per-query", action="store_true",
                     help="sharded configs: per-query scans instead of the batched tensor-core path")
     args = ap.parse_args()
-    if args.config != "c2":
+    if args.config in SHARDED:
         return run_sharded(args, args.config)
+    _use_single(args.config)
+    if BITS == 0:  # the exact index has one scoring
+        args.scoring, args.also = "asym", "none"
+    corpus_mb = N_ROWS * (DIM * 4 if BITS == 0 else (1 << (DIM - 1).bit_length()) + 4) / 1e6
+    args.replicas = max(args.replicas, int(130.0 / corpus_mb) + 1)
 
     import torch
 
@@ -417,11 +441,11 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     fetch = min(N_ROWS, max(K, K * RERANK_FACTOR))  # src/index.ts:414-417
-    config = {"workload": "BASELINE config 2: TurboQuant int8 flat, single-query scans",
-              "rows": N_ROWS, "dim": DIM, "padded_dim": 1024, "queries_per_step": N_QUERIES,
-              "k": K, "fetch": fetch, "metric": "cosine", "scoring": args.scoring,
+    config = {"workload": WORKLOAD, "rows": N_ROWS, "dim": DIM, "bits": BITS,
+              "padded_dim": 1 << (DIM - 1).bit_length(), "queries_per_step": N_QUERIES,
+              "k": K, "fetch": fetch, "metric": "cosine", "scoring": args.scoring if BITS else "exact fp32",
               "parallelism": f"replicas x{max(world, 1)}",
-              "l2": f"corpus replicated x{args.replicas} ({args.replicas * 102.8:.0f} MB > 126 MB L2), "
+              "l2": f"corpus replicated x{args.replicas} ({args.replicas * corpus_mb:.0f} MB > 126 MB L2), "
                     "query i scans replica i % replicas"}
 
     if args.impl == "reference":
@@ -439,7 +463,7 @@ def main():
                 "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
                 "config": config,
                 "cpu_baseline": {"value": qps, "unit": UNIT, "cores": threads, "kind": "port",
-                                 "sample": f"{per_step} queries per step over the full 100k x 768 fp32 corpus "
+                                 "sample": f"{per_step} queries per step over the full {N_ROWS} x {DIM} fp32 corpus "
                                            "(WASM-SIMD scan restated in C, one query per thread)"},
                 "e2e": {"value": qps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line))
@@ -463,7 +487,7 @@ def main():
     def build(scoring):
         reps = []
         for _ in range(args.replicas):
-            ix = AddonQuantIndex(DIM, bits=8, scoring=scoring, device=local)
+            ix = AddonQuantIndex(DIM, bits=BITS, scoring=scoring, device=local)
             torch.cuda.synchronize()
             ix.append_device(corpus.data_ptr(), N_ROWS, torch.cuda.current_stream().cuda_stream)
             reps.append(ix)
@@ -506,12 +530,15 @@ def main():
     query_ms = ms / (args.steps * N_QUERIES)
 
     # roofline: algorithmic bytes of one query (codes + scales + re-rank rows + query)
-    algo_bytes = N_ROWS * (1024 + 4) + fetch * DIM * 4 + DIM * 4
+    if BITS == 0:
+        algo_bytes = N_ROWS * DIM * 4 + DIM * 4
+    else:
+        algo_bytes = N_ROWS * ((1 << (DIM - 1).bit_length()) * BITS // 8 + 4) + fetch * DIM * 4 + DIM * 4
     peak, peak_kind = peaks()
     achieved = algo_bytes / (query_ms / 1e3) / 1e9
     traffic = None
     tp = os.path.join(ROOT, "profiles", "scan_c2_traffic.json")
-    if os.path.exists(tp):
+    if os.path.exists(tp) and BITS == 8 and N_ROWS == 100_000:
         traffic = json.load(open(tp)).get(args.scoring)
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "traffic": traffic,
@@ -560,13 +587,13 @@ def main():
         c_np, q_np = corpus.cpu().numpy(), queries.cpu().numpy()
         cqps, per = cpu_reference_qps(c_np, q_np, 1, 0, max(threads, 8), threads)
         cpu = {"value": cqps, "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"{per} queries over the full 100k x 768 fp32 corpus, WASM-SIMD exact scan "
+               "sample": f"{per} queries over the full {N_ROWS} x {DIM} fp32 corpus, WASM-SIMD exact scan "
                          "restated in C (src/fallback/kernel.wat), one query per thread"}
 
     if rank == 0:
         line = {"metric": METRIC, "value": qps, "unit": UNIT, "n_gpus": max(world, 1), "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "s8" if args.scoring == "int" else "f32xs8",
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32" if BITS == 0 else ("s8" if args.scoring == "int" else "f32xs8"),
                 "data": "synthetic (seeded Philox N(0,1), L2-normalised)", "config": config,
                 "recall_at_10": rec, "query_ms": query_ms, "gpu_launches": launches,
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk, "also": also}

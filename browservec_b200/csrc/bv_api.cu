@@ -204,7 +204,7 @@ int ensure_capacity(bv_index* idx, uint64_t need_rows) {
   uint8_t* codes = nullptr;
   float* scales = nullptr;
   float* orig = nullptr;
-  BV_CUDA(idx, cudaMalloc(&codes, cap * idx->R), "codes");
+  BV_CUDA(idx, cudaMalloc(&codes, idx->R ? cap * idx->R : 16), "codes");
   cudaError_t e = cudaMalloc(&scales, cap * sizeof(float));
   if (e == cudaSuccess) e = cudaMalloc(&orig, cap * idx->dim * sizeof(float));
   if (e != cudaSuccess) {
@@ -321,7 +321,51 @@ int check_args(bv_index* idx, const bv_search_args* a, uint32_t* F_out) {
 // Enqueue every query of `a` (device pointers) on `s`: per query the scan
 // kernel (CTA candidate lists into scratch) then the tail kernel (merge +
 // exact re-rank + outputs), chained by programmatic dependent launch.
+// Exact fp32 index: per query the flat scan (CTA top lists, WASM-SIMD f32
+// arithmetic) then the tail (merge into the top k; re-rank off).
+int enqueue_flat(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStream_t s) {
+  uint32_t Fp = 32;
+  while (Fp < F) Fp <<= 1;
+  const uint32_t G = (static_cast<uint32_t>(idx->rows) + bv::flat_rows_per_cta() - 1) / bv::flat_rows_per_cta();
+  int rc = grow(idx, &idx->d_partials, &idx->partials_cap, static_cast<size_t>(G) * Fp, "scratch");
+  if (rc) return rc;
+  bv::TailParams t;
+  memset(&t, 0, sizeof(t));
+  t.partials = idx->d_partials;
+  t.G = G;
+  t.F = F;
+  t.Fp = Fp;
+  t.capc = Fp <= 256 ? (16 * Fp > 1024 ? 16 * Fp : 1024) : (2 * Fp > 1024 ? 2 * Fp : 1024);
+  t.k = a->k;
+  t.rerank = 0;
+  t.originals = idx->d_orig;
+  t.dim = idx->dim;
+  t.row_base = idx->row_base;
+  t.err = idx->d_err;
+  t.rows_bytes = 0;
+  const size_t tail_smem = bv::tail_smem_layout(idx->dim, t.capc, 0).total;
+  for (uint32_t q = 0; q < a->nq; ++q) {
+    const float* query = a->queries + static_cast<size_t>(q) * idx->dim;
+    cudaError_t e = bv::launch_flat(idx->d_orig, query, a->mask, static_cast<uint32_t>(idx->rows), idx->dim, Fp,
+                                    idx->d_partials, s);
+    if (e != cudaSuccess) return cuda_fail(idx, e, "flat launch");
+    t.query = query;
+    t.out_rows = a->out_rows + static_cast<size_t>(q) * a->k;
+    t.out_scores = a->out_scores + static_cast<size_t>(q) * a->k;
+    t.out_count = a->out_counts + q;
+    const bool cand = a->cand_rows && a->cand_scores && a->cand_counts;
+    t.cand_rows = cand ? a->cand_rows + static_cast<size_t>(q) * F : nullptr;
+    t.cand_scores = cand ? a->cand_scores + static_cast<size_t>(q) * F : nullptr;
+    t.cand_count = cand ? a->cand_counts + q : nullptr;
+    e = bv::launch_tail(t, tail_smem, s);
+    if (e != cudaSuccess) return cuda_fail(idx, e, "tail launch");
+  }
+  idx->last_launches = 2 * a->nq;
+  return BV_OK;
+}
+
 int enqueue_search(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStream_t s) {
+  if (idx->bits == 0) return enqueue_flat(idx, a, F, s);
   Plan pl;
   int rc = plan_scan(idx, F, &pl);
   if (rc) return rc;
@@ -422,12 +466,14 @@ int bv_create(const bv_config* cfg, bv_index** out) {
   if (!cfg || !out) return fail(BV_ERR_INVALID, "null config or output");
   *out = nullptr;
   if (cfg->dim == 0) return fail(BV_ERR_INVALID, "dimension must be a positive integer, got 0");
-  if (cfg->bits != 8 && cfg->bits != 4 && cfg->bits != 1)
+  if (cfg->bits != 8 && cfg->bits != 4 && cfg->bits != 1 && cfg->bits != 0)
     return fail(BV_ERR_INVALID, "quantBits %u not supported (ships 0, 1, 4, 8)", cfg->bits);
   if (cfg->metric > BV_METRIC_DOT)  // index.ts:135-137
     return fail(BV_ERR_INVALID,
                 "quantized mode supports metric cosine/dot only (l2 quantization is later work)");
   if (cfg->scoring > BV_SCORE_HAMMING) return fail(BV_ERR_INVALID, "unknown scoring mode %u", cfg->scoring);
+  if (cfg->bits == 0 && cfg->scoring != BV_SCORE_ASYM)
+    return fail(BV_ERR_INVALID, "the exact fp32 index (bits 0) has no quantized scoring");
   if (cfg->scoring == BV_SCORE_HAMMING && cfg->bits != 1)
     return fail(BV_ERR_INVALID, "hamming scoring needs 1-bit codes");
   const uint32_t P = pad_to_pow2(cfg->dim);
@@ -445,7 +491,7 @@ int bv_create(const bv_config* cfg, bv_index** out) {
   idx->scoring = cfg->scoring;
   idx->row_base = cfg->row_base;
   idx->P = P;
-  idx->R = bv::code_row_bytes(static_cast<int>(cfg->bits), P);
+  idx->R = cfg->bits ? bv::code_row_bytes(static_cast<int>(cfg->bits), P) : 0;  // bits 0: originals only
   auto bail = [&](int rc) {
     bv_destroy(idx);
     return rc;
@@ -544,10 +590,12 @@ static int append_impl(bv_index* idx, const float* rows, uint64_t count, bool de
   const size_t bytes = count * idx->dim * sizeof(float);
   BV_CUDA(idx, cudaMemcpyAsync(dst, rows, bytes, device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
                                idx->stream), "append copy");
-  cudaError_t e = bv::launch_encode(static_cast<int>(idx->bits), dst, count, idx->dim, idx->P, idx->d_signs,
-                                    idx->rounds, idx->d_codes + idx->rows * idx->R,
-                                    idx->d_scales + idx->rows, idx->R, idx->stream);
-  if (e != cudaSuccess) return cuda_fail(idx, e, "encode");
+  if (idx->bits) {  // the exact fp32 index keeps the originals only
+    cudaError_t e = bv::launch_encode(static_cast<int>(idx->bits), dst, count, idx->dim, idx->P, idx->d_signs,
+                                      idx->rounds, idx->d_codes + idx->rows * idx->R,
+                                      idx->d_scales + idx->rows, idx->R, idx->stream);
+    if (e != cudaSuccess) return cuda_fail(idx, e, "encode");
+  }
   BV_CUDA(idx, cudaStreamSynchronize(idx->stream), "encode");
   idx->rows += count;
   return BV_OK;
@@ -868,7 +916,7 @@ int bv_search_batch(bv_index* idx, const bv_search_args* a, void* stream) {
   uint32_t F = 0;
   int rc = check_args(idx, a, &F);
   if (rc) return rc;
-  if (idx->scoring == BV_SCORE_ASYM)
+  if (idx->scoring == BV_SCORE_ASYM || idx->bits == 0)
     return fail(BV_ERR_UNSUPPORTED, "the batched search scores with the integer modes (int, hamming), "
                                     "not asym");
   if (idx->rows >= 0x7FFFFF00ull) return fail(BV_ERR_UNSUPPORTED, "batched search takes < 2^31 rows per index");

@@ -95,6 +95,11 @@ inline cudaError_t opt_in_smem(const void* func, size_t need, int* opted) {
   return cudaSuccess;
 }
 
+// bv_flat.cu: exact fp32 flat scan (bits = 0)
+uint32_t flat_rows_per_cta();
+cudaError_t launch_flat(const float* rows, const float* query, const uint32_t* mask, uint32_t nrows, uint32_t dim,
+                        uint32_t Fp, uint64_t* partials, cudaStream_t stream);
+
 // bv_tail.cu: one tail CTA per query of a batch
 struct TailParams;
 cudaError_t launch_tail_grid(const TailParams& p, uint32_t nq, size_t smem, cudaStream_t stream);

@@ -29,7 +29,9 @@ FILTER_CPU_SCAN_MAX = 4096         # src/index.ts:76
 
 
 def default_rerank_factor(bits: int) -> int:
-    """src/index.ts:99-103"""
+    """src/index.ts:99-103 (bits 0: the exact fp32 index needs no re-rank)."""
+    if bits == 0:
+        return 1
     if bits == 1:
         return 32
     return 16 if bits == 4 else 4
@@ -271,7 +273,10 @@ class _Store:
 
 
 class BrowserVec:
-    """The quantized flat branch of src/index.ts over AddonQuantIndex."""
+    """The flat branches of src/index.ts over AddonQuantIndex: quantBits 1/4/8
+    (the quantized scan, QuantIndex) and 0 (the exact fp32 scan, FlatIndex,
+    src/index/flat.ts:132-211, scored with the WASM-SIMD f32 arithmetic of the
+    reference's CPU path)."""
 
     def __init__(self, dimension: int, metric: str = "cosine", normalize: bool | None = None,
                  quant_bits: int = 8, quant: Mapping[str, Any] | None = None, scoring: str = "asym",
@@ -279,8 +284,10 @@ class BrowserVec:
         if not isinstance(dimension, int) or dimension <= 0:
             raise ValueError(f"dimension must be a positive integer, got {dimension}")
         quant = dict(quant or {})
-        if quant_bits not in (1, 4, 8):
-            raise ValueError(f"quantBits {quant_bits} not supported on this path (1, 4, 8)")
+        if quant_bits not in (0, 1, 4, 8):
+            raise ValueError(f"quantBits {quant_bits} not supported (ships 0, 1, 4, 8)")
+        if quant_bits == 0:
+            scoring = "asym"  # exact scores: no quantized scoring mode applies
         self.store = _Store(dimension, metric, metric == "cosine" if normalize is None else normalize)
         self.quant_bits = quant_bits
         self.rerank_factor = int(quant.get("rerankFactor", default_rerank_factor(quant_bits)))
