@@ -254,7 +254,11 @@ def run_sharded(args, name):
     from browservec_b200 import datagen
     from browservec_b200.sharded import ShardedIndex, shard_bounds
 
-    cfg = SHARDED[name]
+    cfg = dict(SHARDED[name])
+    if args.rows:  # a smaller case of the same configuration (for ncu captures)
+        cfg["n"] = args.rows
+    if args.queries:
+        cfg["nq"] = args.queries
     dist, world, rank, local = _init_dist(torch)
     dev = torch.device("cuda", local)
     n, dim, nq, k = cfg["n"], cfg["dim"], cfg["nq"], cfg["k"]
@@ -414,6 +418,8 @@ def main():
     ap.add_argument("--config", default="c2", choices=[*SINGLE, *SHARDED])
     ap.add_argument("--sharded-scoring", default=None, choices=["asym", "int", "hamming"],
                     help="scoring of a sharded config (default: the config's)")
+    ap.add_argument("--rows", type=int, default=0, help="sharded configs: corpus rows (default: the config's)")
+    ap.add_argument("--queries", type=int, default=0, help="sharded configs: batch size (default: the config's)")
     ap.add_argument("--per-query", action="store_true",
                     help="sharded configs: per-query scans instead of the batched tensor-core path")
     args = ap.parse_args()
