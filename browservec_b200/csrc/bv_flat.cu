@@ -38,6 +38,7 @@ __global__ void __launch_bounds__(kConsumerThreads, 1) flat_kernel(const FlatPar
   uint64_t* cand = reinterpret_cast<uint64_t*>(smem);            // max(16 * Fp, 128) keys
   float* q = reinterpret_cast<float*>(cand + (p.Fp <= 256u ? 16u * p.Fp : p.Fp));
   const int ctid = threadIdx.x;
+  pdl_trigger();  // the tail (then the next query's scan) may be scheduled now
   for (uint32_t i = ctid; i < p.dim; i += kConsumerThreads) q[i] = p.query[i];
   for (uint32_t i = ctid; i < (p.Fp <= 256u ? 16u * p.Fp : p.Fp); i += kConsumerThreads) cand[i] = 0ull;
   __syncthreads();
@@ -61,7 +62,6 @@ __global__ void __launch_bounds__(kConsumerThreads, 1) flat_kernel(const FlatPar
     if (keep && p.mask) keep = (p.mask[row >> 5] >> (row & 31u)) & 1u;
     cand[local] = keep ? make_key(sum, row) : 0ull;
   }
-  pdl_trigger();  // the next kernel in the stream may start its prologue
   __syncthreads();
   if (p.Fp <= 256u) {
     cta_best_sorted_dispatch(p.Fp, cand, kFlatRows, ctid);

@@ -481,6 +481,13 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
     fence_mbar_init();
   }
   __syncthreads();
+  // Programmatic dependent launch, triggered at once: the next kernel in the
+  // stream (this query's tail, which then lets the next query's scan launch)
+  // may be scheduled now, so an SM this scan's CTA leaves is taken by the next
+  // query's CTA without waiting for the slowest CTA of this one.  Nothing the
+  // next kernels write is read here, and the shared scratch is written only
+  // after griddepcontrol.wait below.
+  pdl_trigger();
 
   if (warp == kConsumerWarps) {
     // ---------------------------------------------------------- producer
@@ -512,7 +519,6 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
       }
     }
     __syncwarp();
-    pdl_trigger();
   } else {
     // ---------------------------------------------------------- consumers
     const int ctid = threadIdx.x;
@@ -764,7 +770,6 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
         }
       }
     }
-    pdl_trigger();
     named_bar_sync(kBarConsumers, kConsumerThreads);
     if (p.trace && threadIdx.x == 0) p.trace[blockIdx.x * 8 + kTrScanned] = globaltimer();
 
