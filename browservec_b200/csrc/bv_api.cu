@@ -32,6 +32,13 @@ int fail(int status, const char* fmt, ...) {
 
 constexpr const char* kLostMsg = "GPU device lost; re-create the store";  // quant.ts:183
 constexpr uint32_t kRowAlign = 2048;      // capacity granularity (>= any scan tile)
+// Per-query scratch of the single-query searches (the scan CTAs' candidate
+// lists, tile counters) is a ring of kRing slots: consecutive queries never
+// share one, so a scan never waits for an earlier query's tail; each wrap of
+// the ring waits for all earlier work of the stream (an event), so a slot is
+// reused only after the tail that read it has finished.
+constexpr uint32_t kRing = 64;
+constexpr size_t kRingMaxBytes = 256u << 20;
 constexpr uint32_t kBatchMinQueries = 64;  // bv_search batches at least this many on the tensor cores
 constexpr uint32_t kMaxFetch = 1024;      // fused single-query path: F <= 1024
 constexpr uint32_t kMaxPadded = 4096;
@@ -83,7 +90,10 @@ struct bv_index {
   // scratch of the scan: per-CTA candidate lists, tile counters, error flags
   uint64_t* d_partials = nullptr;
   size_t partials_cap = 0;
-  unsigned long long* d_tile_ctr = nullptr;  // 4 rotating dynamic-tile counters
+  unsigned long long* d_tile_ctr = nullptr;  // kRing rotating dynamic-tile counters
+  size_t partials_slot = 0;                  // keys per query in the partials ring
+  uint32_t ring = 0;                         // slots of the partials ring
+  cudaEvent_t ev_ring = nullptr;             // all work before a ring wrap
   uint32_t epoch = 0;                        // scan launches so far
   uint32_t* d_err = nullptr;
   // staging for the host-pointer entry points
@@ -275,9 +285,10 @@ int plan_scan(bv_index* idx, uint32_t F, Plan* pl) {
     }
   }
   if (!pl->stages) return fail(BV_ERR_UNSUPPORTED, "scan tile does not fit in shared memory");
-  // One SM stays free for the previous query's merging CTA, so a following
-  // launch finds a whole grid's worth of SMs.
-  const uint32_t sms = idx->num_sms > 1 ? static_cast<uint32_t>(idx->num_sms) - 1u : 1u;
+  // Two SMs stay free for the tail kernels (one query's merge and re-rank can
+  // still run while the next query's finishes), so a following scan finds a
+  // whole grid's worth of SMs.
+  const uint32_t sms = idx->num_sms > 2 ? static_cast<uint32_t>(idx->num_sms) - 2u : 1u;
   pl->grid = pl->ntiles < sms ? pl->ntiles : sms;
   return BV_OK;
 }
@@ -318,16 +329,39 @@ int check_args(bv_index* idx, const bv_search_args* a, uint32_t* F_out) {
   return BV_OK;
 }
 
-// Enqueue every query of `a` (device pointers) on `s`: per query the scan
-// kernel (CTA candidate lists into scratch) then the tail kernel (merge +
-// exact re-rank + outputs), chained by programmatic dependent launch.
+// Size the partials ring for `keys` candidate keys per query (keeping earlier
+// slots is not needed: a resize happens between searches).
+int ring_prepare(bv_index* idx, size_t keys) {
+  uint32_t r = kRing;
+  while (r > 2 && static_cast<size_t>(r) * keys * 8 > kRingMaxBytes) r >>= 1;
+  if (idx->partials_slot != keys || idx->ring != r) {
+    // a new geometry: earlier queries' slots must be out of use before reuse
+    BV_CUDA(idx, cudaDeviceSynchronize(), "ring resize");
+    idx->partials_slot = keys;
+    idx->ring = r;
+  }
+  return grow(idx, &idx->d_partials, &idx->partials_cap, static_cast<size_t>(r) * keys, "scratch");
+}
+
+// The next query's slot; at a wrap the stream first waits for all its earlier
+// work (every tail that read the slots being reused).
+int ring_next(bv_index* idx, cudaStream_t s, uint32_t* epoch, uint32_t* slot) {
+  *epoch = ++idx->epoch;
+  *slot = *epoch % idx->ring;
+  if (*slot == 0) {
+    BV_CUDA(idx, cudaEventRecord(idx->ev_ring, s), "ring event");
+    BV_CUDA(idx, cudaStreamWaitEvent(s, idx->ev_ring, 0), "ring wait");
+  }
+  return BV_OK;
+}
+
 // Exact fp32 index: per query the flat scan (CTA top lists, WASM-SIMD f32
 // arithmetic) then the tail (merge into the top k; re-rank off).
 int enqueue_flat(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStream_t s) {
   uint32_t Fp = 32;
   while (Fp < F) Fp <<= 1;
   const uint32_t G = (static_cast<uint32_t>(idx->rows) + bv::flat_rows_per_cta() - 1) / bv::flat_rows_per_cta();
-  int rc = grow(idx, &idx->d_partials, &idx->partials_cap, static_cast<size_t>(G) * Fp, "scratch");
+  int rc = ring_prepare(idx, static_cast<size_t>(G) * Fp);
   if (rc) return rc;
   bv::TailParams t;
   memset(&t, 0, sizeof(t));
@@ -346,8 +380,12 @@ int enqueue_flat(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStream_
   const size_t tail_smem = bv::tail_smem_layout(idx->dim, t.capc, 0).total;
   for (uint32_t q = 0; q < a->nq; ++q) {
     const float* query = a->queries + static_cast<size_t>(q) * idx->dim;
+    uint32_t epoch = 0, slot = 0;
+    if ((rc = ring_next(idx, s, &epoch, &slot))) return rc;
+    uint64_t* part = idx->d_partials + static_cast<size_t>(slot) * idx->partials_slot;
+    t.partials = part;
     cudaError_t e = bv::launch_flat(idx->d_orig, query, a->mask, static_cast<uint32_t>(idx->rows), idx->dim, Fp,
-                                    idx->d_partials, s);
+                                    part, s);
     if (e != cudaSuccess) return cuda_fail(idx, e, "flat launch");
     t.query = query;
     t.out_rows = a->out_rows + static_cast<size_t>(q) * a->k;
@@ -364,12 +402,15 @@ int enqueue_flat(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStream_
   return BV_OK;
 }
 
+// Enqueue every query of `a` (device pointers) on `s`: per query the scan
+// kernel (CTA candidate lists into the query's ring slot) then the tail kernel
+// (merge + exact re-rank + outputs), chained by programmatic dependent launch.
 int enqueue_search(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStream_t s) {
   if (idx->bits == 0) return enqueue_flat(idx, a, F, s);
   Plan pl;
   int rc = plan_scan(idx, F, &pl);
   if (rc) return rc;
-  rc = grow(idx, &idx->d_partials, &idx->partials_cap, static_cast<size_t>(pl.grid) * pl.Fp, "scratch");
+  rc = ring_prepare(idx, static_cast<size_t>(pl.grid) * pl.Fp);
   if (rc) return rc;
   bv::ScanParams p;
   memset(&p, 0, sizeof(p));
@@ -422,8 +463,11 @@ int enqueue_search(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStrea
 
   for (uint32_t q = 0; q < a->nq; ++q) {
     p.query = a->queries + static_cast<size_t>(q) * idx->dim;
-    p.epoch = ++idx->epoch;
-    p.tile_ctr = idx->d_tile_ctr + (p.epoch & 3u);
+    uint32_t slot = 0;
+    if ((rc = ring_next(idx, s, &p.epoch, &slot))) return rc;
+    p.tile_ctr = idx->d_tile_ctr + slot;
+    p.partials = idx->d_partials + static_cast<size_t>(slot) * idx->partials_slot;
+    t.partials = p.partials;
     cudaError_t e = launch_scan(static_cast<int>(idx->bits), static_cast<int>(idx->scoring), pl.sh,
                                 p, pl.grid, pl.smem, s);
     if (e == cudaErrorNotSupported)
@@ -518,9 +562,10 @@ int bv_create(const bv_config* cfg, bv_index** out) {
   e = cudaMalloc(&idx->d_signs, ns * sizeof(float));
   if (e == cudaSuccess) e = cudaMemcpy(idx->d_signs, hs, ns * sizeof(float), cudaMemcpyHostToDevice);
   delete[] hs;
-  if (e == cudaSuccess) e = cudaMalloc(&idx->d_tile_ctr, 4 * sizeof(unsigned long long));
+  if (e == cudaSuccess) e = cudaMalloc(&idx->d_tile_ctr, kRing * sizeof(unsigned long long));
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&idx->ev_ring, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaMalloc(&idx->d_err, 16);
-  if (e == cudaSuccess) e = cudaMemset(idx->d_tile_ctr, 0, 4 * sizeof(unsigned long long));
+  if (e == cudaSuccess) e = cudaMemset(idx->d_tile_ctr, 0, kRing * sizeof(unsigned long long));
   if (e == cudaSuccess) e = cudaMemset(idx->d_err, 0, 16);
   if (e != cudaSuccess) return bail(cuda_fail(nullptr, e, "index buffers"));
   *out = idx;
@@ -564,6 +609,7 @@ int bv_destroy(bv_index* idx) {
   if (idx->h_pin) cudaFreeHost(idx->h_pin);
   if (idx->ev0) cudaEventDestroy(idx->ev0);
   if (idx->ev1) cudaEventDestroy(idx->ev1);
+  if (idx->ev_ring) cudaEventDestroy(idx->ev_ring);
   if (idx->stream) cudaStreamDestroy(idx->stream);
   delete idx;
   return BV_OK;
@@ -1281,6 +1327,7 @@ extern "C" int bv_search_noalloc(bv_index* idx, const bv_search_args* a, void* s
   p.check_tiles = pl.check_tiles;
   p.partials = reinterpret_cast<uint64_t*>(base);
   p.err = err;
+  p.serial = 1;  // one partials area for every query: each scan waits for the previous tail
 
   bv::TailParams t;
   memset(&t, 0, sizeof(t));

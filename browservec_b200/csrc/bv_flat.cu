@@ -12,7 +12,8 @@
 // One CTA scores 128 rows and writes its best Fp keys (score desc, row asc),
 // sorted, to the per-query partials; the tail kernel (re-rank off: the scores
 // are exact) merges them into the top k, chained by programmatic dependent
-// launch like the quantized scan.
+// launch like the quantized scan; each query writes its own slot of the
+// partials ring, so nothing here waits for an earlier query's tail.
 #include <cstdint>
 
 #include "bv_device.cuh"
@@ -68,7 +69,6 @@ __global__ void __launch_bounds__(kConsumerThreads, 1) flat_kernel(const FlatPar
   } else {
     cta_sort_desc(cand, kFlatRows, ctid);  // 128 keys sorted; slots up to Fp stay zero
   }
-  pdl_wait();  // the previous query's tail has read the partials
   uint64_t* out = p.partials + static_cast<size_t>(blockIdx.x) * p.Fp;
   for (uint32_t i = ctid; i < p.Fp; i += kConsumerThreads) out[i] = cand[i];
 }

@@ -56,9 +56,10 @@ struct ScanParams {
   uint32_t F, Fp;            // fetch, pow2 >= max(F, 32)
   uint32_t capc;             // CTA candidate buffer slots (pow2, <= kSelMax * 512, >= 2*Fp)
   uint32_t check_tiles;      // tiles between candidate-buffer checks
-  uint64_t* partials;        // gridDim.x x Fp keys
+  uint64_t* partials;        // gridDim.x x Fp keys (this query's slot of the partials ring)
   unsigned long long* tile_ctr;  // dynamic tile counter slot: (epoch << 32) | next tile
-  uint32_t epoch;            // launch number owning tile_ctr (slots rotate over 4 launches)
+  uint32_t epoch;            // launch number owning tile_ctr
+  uint32_t serial;           // 1: the partials are shared with the previous query (wait for its tail)
   uint32_t* err;             // error flags
   uint64_t* trace;           // optional: per-CTA phase timestamps (globaltimer ns)
 };
@@ -352,7 +353,15 @@ __device__ __forceinline__ void cta_best_sorted(uint64_t* cand, uint32_t n, int 
 // out[0..Fp), descending.  Warps merge strided lists in registers (the next
 // list loads while the current one merges), then the same 4-level tree
 // through `stage` (16 * Fp keys); out may alias stage.
-template <int E>
+// A key of a CTA list: from shared memory, or from global memory past L1
+// (the lists were written by another kernel).
+template <bool kSmemSrc>
+__device__ __forceinline__ uint64_t load_key(const uint64_t* p) {
+  if constexpr (kSmemSrc) return *p;
+  else return __ldcg(p);
+}
+
+template <int E, bool kSmemSrc = false>
 __device__ __forceinline__ void merge_cta_lists(const uint64_t* partials, uint32_t G, uint64_t* stage,
                                              int ctid) {
   constexpr int Fp = 32 * E;
@@ -361,7 +370,7 @@ __device__ __forceinline__ void merge_cta_lists(const uint64_t* partials, uint32
 #pragma unroll
   for (int r = 0; r < E; ++r) {
     v[r] = 0ull;
-    nx[r] = static_cast<uint32_t>(warp) < G ? __ldcg(partials + static_cast<size_t>(warp) * Fp + lane + 32 * r) : 0ull;
+    nx[r] = static_cast<uint32_t>(warp) < G ? load_key<kSmemSrc>(partials + static_cast<size_t>(warp) * Fp + lane + 32 * r) : 0ull;
   }
 #pragma unroll 1
   for (uint32_t l = warp; l < G; l += kConsumerWarps) {
@@ -370,7 +379,7 @@ __device__ __forceinline__ void merge_cta_lists(const uint64_t* partials, uint32
     for (int r = 0; r < E; ++r) cur[r] = nx[r];
     const uint32_t ln = l + kConsumerWarps;
 #pragma unroll
-    for (int r = 0; r < E; ++r) nx[r] = ln < G ? __ldcg(partials + static_cast<size_t>(ln) * Fp + lane + 32 * r) : 0ull;
+    for (int r = 0; r < E; ++r) nx[r] = ln < G ? load_key<kSmemSrc>(partials + static_cast<size_t>(ln) * Fp + lane + 32 * r) : 0ull;
     wreg_merge_top<E>(v, cur, lane);
   }
 #pragma unroll 1
@@ -414,12 +423,13 @@ __device__ __forceinline__ void cta_best_sorted_dispatch(uint32_t Fp, uint64_t* 
   else if (Fp == 128) cta_best_sorted<4>(cand, n, ctid);
   else cta_best_sorted<8>(cand, n, ctid);
 }
+template <bool kSmemSrc = false>
 __device__ __forceinline__ void merge_cta_lists_dispatch(uint32_t Fp, const uint64_t* partials, uint32_t G,
                                                          uint64_t* stage, int ctid) {
-  if (Fp == 32) merge_cta_lists<1>(partials, G, stage, ctid);
-  else if (Fp == 64) merge_cta_lists<2>(partials, G, stage, ctid);
-  else if (Fp == 128) merge_cta_lists<4>(partials, G, stage, ctid);
-  else merge_cta_lists<8>(partials, G, stage, ctid);
+  if (Fp == 32) merge_cta_lists<1, kSmemSrc>(partials, G, stage, ctid);
+  else if (Fp == 64) merge_cta_lists<2, kSmemSrc>(partials, G, stage, ctid);
+  else if (Fp == 128) merge_cta_lists<4, kSmemSrc>(partials, G, stage, ctid);
+  else merge_cta_lists<8, kSmemSrc>(partials, G, stage, ctid);
 }
 __device__ __forceinline__ void warp0_sort_dispatch(uint32_t Fp, uint64_t* a, int ctid) {
   if (Fp == 32) warp0_sort_smem<1>(a, ctid);
@@ -787,13 +797,13 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
     }
     if (p.Fp <= 256u) {
       cta_best_sorted_dispatch(p.Fp, cand, n, ctid);
-      pdl_wait();  // the previous launch has finished with the shared scratch
+      if (p.serial) pdl_wait();  // the previous query's tail has read the shared partials
       for (uint32_t i = ctid; i < p.Fp; i += kConsumerThreads)
         p.partials[static_cast<size_t>(blockIdx.x) * p.Fp + i] = i < p.F ? cand[i] : 0ull;
     } else {
       // wide F: unsorted best F (the last CTA re-selects them)
       const uint32_t m = n < p.F ? n : p.F;
-      pdl_wait();
+      if (p.serial) pdl_wait();
       for (uint32_t i = ctid; i < p.Fp; i += kConsumerThreads)
         p.partials[static_cast<size_t>(blockIdx.x) * p.Fp + i] = i < m ? cand[i] : 0ull;
     }

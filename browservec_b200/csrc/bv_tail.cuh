@@ -30,7 +30,7 @@ struct TailParams {
 
 // Tail timestamps (globaltimer ns) in the trace record given to the tail.
 enum : int { kTrTailStart = 0, kTrTailMerged = 1, kTrTailDone = 2, kTrTailGathered = 3,
-             kTrTailDotted = 4, kTrTailEntry = 5 };
+             kTrTailDotted = 4, kTrTailEntry = 5, kTrTailStaged = 6 };
 
 struct TailSmem {
   uint32_t cand_off, hist_off, misc_off, q_off, rows_off, bar_off, total;

@@ -157,8 +157,9 @@ BV_API int bv_get_stats(const bv_index* idx, bv_stats* out);
  * caller-owned device buffer of `capacity` u64; a search with scan grid G
  * writes globaltimer ns at trace[b*8 + {0 entry, 1 query rotated, 2 rows
  * scored, 3 CTA list written}] for scan CTA b, and the tail kernel writes
- * trace[G*8 + {5 entry, 0 merge start, 1 merged, 3 rows gathered, 4 re-ranked,
- * 2 done}].  Needs capacity >= (G+1)*8 (G < the SM count); NULL disables. */
+ * trace[G*8 + {5 entry, 0 merge start, 6 CTA lists in shared memory, 1 merged,
+ * 3 rows gathered, 4 re-ranked, 2 done}].  Needs capacity >= (G+1)*8 (G < the
+ * SM count); NULL disables. */
 BV_API int bv_set_phase_trace(bv_index* idx, uint64_t* trace_dev, uint64_t capacity);
 
 /* Kernel launches made by the last bv_search / bv_search_async /
