@@ -91,6 +91,7 @@ struct bv_index {
   uint64_t* d_partials = nullptr;
   size_t partials_cap = 0;
   unsigned long long* d_tile_ctr = nullptr;  // kRing rotating dynamic-tile counters
+  unsigned int* d_done = nullptr;            // kRing per-query finished-CTA counters
   size_t partials_slot = 0;                  // keys per query in the partials ring
   uint32_t ring = 0;                         // slots of the partials ring
   cudaEvent_t ev_ring = nullptr;             // all work before a ring wrap
@@ -111,6 +112,7 @@ struct bv_index {
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   int num_sms = 148;
   int max_smem = 227 * 1024;
+  int smem_per_sm = 228 * 1024;
   float last_ms = 0.0f;
   uint32_t last_launches = 0;
   uint64_t* d_trace = nullptr;   // optional phase-timestamp buffer (caller-owned device memory)
@@ -247,9 +249,12 @@ struct Plan {
   bv::ScanShape sh;
   uint32_t tile_rows, tile_bytes, ntiles, stages, grid, F, Fp, capc, check_tiles;
   size_t smem;
+  bool fold;
 };
 
-int plan_scan(bv_index* idx, uint32_t F, Plan* pl) {
+// fold: the scan's last CTA finishes each query (no tail kernel), for the
+// integer scorings with Fp <= 256; pl->fold says whether the plan does.
+int plan_scan(bv_index* idx, uint32_t F, Plan* pl, bool fold = true) {
   if (!bv::scan_shape(static_cast<int>(idx->bits), static_cast<int>(idx->scoring), idx->P, &pl->sh))
     return fail(BV_ERR_UNSUPPORTED, "padded dimension %u is outside the scan's range", idx->P);
   const uint32_t R = pl->sh.R;
@@ -275,20 +280,31 @@ int plan_scan(bv_index* idx, uint32_t F, Plan* pl) {
   pl->capc = capc;
   pl->check_tiles = (capc - 2 * fp) / tr;
   if (pl->check_tiles < 1) pl->check_tiles = 1;
+  // (asym keeps the tail kernel: its registers allow one CTA per SM, where a
+  // finishing CTA would hold up its SM's next query)
+  pl->fold = fold && fp <= 256 && idx->scoring != BV_SCORE_ASYM;
+  // Folded integer scans run two CTAs per SM (consecutive queries): each CTA
+  // then keeps to half of the SM's shared memory.
+  const bool two = pl->fold && idx->scoring != BV_SCORE_ASYM;
+  const uint32_t limit = two ? static_cast<uint32_t>(idx->smem_per_sm) / 2u - 1024u
+                             : static_cast<uint32_t>(idx->max_smem);
   pl->stages = 0;
-  for (uint32_t st = 4; st >= 2; --st) {
-    bv::ScanSmem lay = bv::scan_smem_layout(pl->tile_bytes, tr, st, idx->P, idx->rounds, capc);
-    if (lay.total <= static_cast<uint32_t>(idx->max_smem)) {
-      pl->stages = st;
-      pl->smem = lay.total;
-      break;
+  for (uint32_t lim : {limit, static_cast<uint32_t>(idx->max_smem)}) {  // two CTAs per SM, else one
+    for (uint32_t st = 4; st >= 2 && !pl->stages; --st) {
+      bv::ScanSmem lay = bv::scan_smem_layout(pl->tile_bytes, tr, st, idx->P, idx->rounds, capc);
+      if (lay.total <= lim) {
+        pl->stages = st;
+        pl->smem = lay.total;
+      }
     }
+    if (pl->stages) break;
   }
   if (!pl->stages) return fail(BV_ERR_UNSUPPORTED, "scan tile does not fit in shared memory");
-  // Two SMs stay free for the tail kernels (one query's merge and re-rank can
-  // still run while the next query's finishes), so a following scan finds a
-  // whole grid's worth of SMs.
-  const uint32_t sms = idx->num_sms > 2 ? static_cast<uint32_t>(idx->num_sms) - 2u : 1u;
+  // Without folding two SMs stay free for the tail kernels (one query's merge
+  // and re-rank can still run while the next query's finishes), so a
+  // following scan finds a whole grid's worth of SMs.
+  const uint32_t sms = pl->fold ? static_cast<uint32_t>(idx->num_sms)
+                                : (idx->num_sms > 2 ? static_cast<uint32_t>(idx->num_sms) - 2u : 1u);
   pl->grid = pl->ntiles < sms ? pl->ntiles : sms;
   return BV_OK;
 }
@@ -461,6 +477,38 @@ int enqueue_search(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStrea
   t.rows_bytes = rows_bytes;
   const size_t tail_smem = bv::tail_smem_layout(idx->dim, pl.capc, rows_bytes).total;
 
+  if (pl.fold) {
+    // one launch per query: its last CTA merges, re-ranks and writes the results
+    p.fold = 1;
+    p.k = a->k;
+    p.rerank = a->rerank ? 1 : 0;
+    p.originals = idx->d_orig;
+    p.row_base = idx->row_base;
+    for (uint32_t q = 0; q < a->nq; ++q) {
+      p.query = a->queries + static_cast<size_t>(q) * idx->dim;
+      uint32_t slot = 0;
+      if ((rc = ring_next(idx, s, &p.epoch, &slot))) return rc;
+      p.tile_ctr = idx->d_tile_ctr + slot;
+      p.done = idx->d_done + slot;
+      p.partials = idx->d_partials + static_cast<size_t>(slot) * idx->partials_slot;
+      p.out_rows = a->out_rows + static_cast<size_t>(q) * a->k;
+      p.out_scores = a->out_scores + static_cast<size_t>(q) * a->k;
+      p.out_count = a->out_counts + q;
+      const bool cand = a->cand_rows && a->cand_scores && a->cand_counts;
+      p.cand_rows = cand ? a->cand_rows + static_cast<size_t>(q) * F : nullptr;
+      p.cand_scores = cand ? a->cand_scores + static_cast<size_t>(q) * F : nullptr;
+      p.cand_count = cand ? a->cand_counts + q : nullptr;
+      p.cand_exact = cand && a->cand_exact ? a->cand_exact + static_cast<size_t>(q) * F : nullptr;
+      cudaError_t e = launch_scan(static_cast<int>(idx->bits), static_cast<int>(idx->scoring), pl.sh, p, pl.grid,
+                                  pl.smem, s);
+      if (e == cudaErrorNotSupported)
+        return fail(BV_ERR_UNSUPPORTED, "no scan kernel for bits=%u scoring=%u P=%u", idx->bits, idx->scoring,
+                    idx->P);
+      if (e != cudaSuccess) return cuda_fail(idx, e, "scan launch");
+    }
+    idx->last_launches = a->nq;
+    return BV_OK;
+  }
   for (uint32_t q = 0; q < a->nq; ++q) {
     p.query = a->queries + static_cast<size_t>(q) * idx->dim;
     uint32_t slot = 0;
@@ -495,6 +543,7 @@ int check_err_flag(bv_index* idx) {
   BV_CUDA(idx, cudaMemcpy(&flag, idx->d_err, 4, cudaMemcpyDeviceToHost), "error flag");
   if (flag) {
     cudaMemset(idx->d_err, 0, 4);
+    cudaMemset(idx->d_done, 0, kRing * sizeof(unsigned int));  // a cut-short query may have left a count
     return fail(BV_ERR_TIMEOUT, "scan kernel wait ran out of budget (flag 0x%x)", flag);
   }
   return BV_OK;
@@ -544,6 +593,7 @@ int bv_create(const bv_config* cfg, bv_index** out) {
   if (e != cudaSuccess) return bail(cuda_fail(nullptr, e, "cudaSetDevice"));
   cudaDeviceGetAttribute(&idx->num_sms, cudaDevAttrMultiProcessorCount, cfg->device);
   cudaDeviceGetAttribute(&idx->max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, cfg->device);
+  cudaDeviceGetAttribute(&idx->smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, cfg->device);
   if ((e = cudaStreamCreateWithFlags(&idx->stream, cudaStreamNonBlocking)) != cudaSuccess ||
       (e = cudaEventCreate(&idx->ev0)) != cudaSuccess || (e = cudaEventCreate(&idx->ev1)) != cudaSuccess)
     return bail(cuda_fail(nullptr, e, "stream"));
@@ -563,6 +613,8 @@ int bv_create(const bv_config* cfg, bv_index** out) {
   if (e == cudaSuccess) e = cudaMemcpy(idx->d_signs, hs, ns * sizeof(float), cudaMemcpyHostToDevice);
   delete[] hs;
   if (e == cudaSuccess) e = cudaMalloc(&idx->d_tile_ctr, kRing * sizeof(unsigned long long));
+  if (e == cudaSuccess) e = cudaMalloc(&idx->d_done, kRing * sizeof(unsigned int));
+  if (e == cudaSuccess) e = cudaMemset(idx->d_done, 0, kRing * sizeof(unsigned int));
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&idx->ev_ring, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaMalloc(&idx->d_err, 16);
   if (e == cudaSuccess) e = cudaMemset(idx->d_tile_ctr, 0, kRing * sizeof(unsigned long long));
@@ -581,6 +633,7 @@ int bv_destroy(bv_index* idx) {
   cudaFree(idx->d_signs);
   cudaFree(idx->d_partials);
   cudaFree(idx->d_tile_ctr);
+  cudaFree(idx->d_done);
   cudaFree(idx->d_err);
   cudaFree(idx->d_q);
   cudaFree(idx->d_mask);
@@ -1299,7 +1352,7 @@ extern "C" int bv_search_noalloc(bv_index* idx, const bv_search_args* a, void* s
     return BV_OK;
   }
   Plan pl;
-  if ((rc = plan_scan(idx, F, &pl))) return rc;
+  if ((rc = plan_scan(idx, F, &pl, false))) return rc;
   if (pl.grid > kNoAllocMaxCtas)
     return fail(BV_ERR_UNSUPPORTED, "bv_search_noalloc: scan grid %u above its scratch bound %u", pl.grid,
                 kNoAllocMaxCtas);

@@ -24,8 +24,9 @@ inline uint32_t code_row_bytes(int bits, uint32_t P) {
 
 // Lane layout of one scan: the asym mode uses the canonical layout (L = min(32,
 // C) lanes per row, the order the oracle defines); the integer modes, whose
-// sums are exact in any order, use at most 8 lanes per row and up to 8 chunks
-// per lane so fewer shuffles reduce each row.
+// sums are exact in any order, use 8 lanes per row up to 32 chunks, 16 lanes at
+// 64 chunks (so one iteration's rows stay within a 32 KB tile and two CTAs fit
+// an SM), and up to 8 chunks per lane beyond.
 inline bool scan_shape(int bits, int mode, uint32_t P, ScanShape* s) {
   const uint32_t R = code_row_bytes(bits, P);
   if (R < 4 || R > 4096) return false;
@@ -36,7 +37,7 @@ inline bool scan_shape(int bits, int mode, uint32_t P, ScanShape* s) {
   if (mode == 0) {
     L = C < 32 ? C : 32;
   } else {
-    L = C <= 8 ? C : (C <= 64 ? 8 : C / 8);
+    L = C <= 8 ? C : (C <= 32 ? 8 : (C <= 64 ? 16 : C / 8));
   }
   s->L = static_cast<int>(L);
   s->CPL = static_cast<int>(C / L);

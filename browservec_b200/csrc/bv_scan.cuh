@@ -60,6 +60,21 @@ struct ScanParams {
   unsigned long long* tile_ctr;  // dynamic tile counter slot: (epoch << 32) | next tile
   uint32_t epoch;            // launch number owning tile_ctr
   uint32_t serial;           // 1: the partials are shared with the previous query (wait for its tail)
+  // The query's finish by its last CTA (fold = 1, Fp <= 256): merge of the CTA
+  // lists, exact re-rank and outputs, as the tail kernel does.
+  uint32_t fold;
+  unsigned int* done;        // CTAs of this query finished (its ring slot); reset by the last one
+  uint32_t k;
+  int rerank;
+  const float* originals;    // rows x dim fp32
+  uint32_t row_base;
+  uint32_t* out_rows;
+  float* out_scores;
+  uint32_t* out_count;
+  uint32_t* cand_rows;       // optional
+  float* cand_scores;
+  uint32_t* cand_count;
+  float* cand_exact;
   uint32_t* err;             // error flags
   uint64_t* trace;           // optional: per-CTA phase timestamps (globaltimer ns)
 };
@@ -132,7 +147,7 @@ __host__ __device__ inline ScanSmem scan_smem_layout(uint32_t tile_bytes, uint32
 }
 
 // misc word slots
-enum : int { kMiscCount = 0, kMiscNc = 5, kMiscRed = 16, kMiscSel = 64 };
+enum : int { kMiscCount = 0, kMiscNc = 5, kMiscTicket = 6, kMiscRed = 16, kMiscSel = 64 };
 
 // ------------------------------------------------------------ code -> value
 // int8 byte of word xb (= x ^ 0x80808080) as a biased float 2^23 + (b + 128):
@@ -438,6 +453,170 @@ __device__ __forceinline__ void warp0_sort_dispatch(uint32_t Fp, uint64_t* a, in
   else warp0_sort_smem<8>(a, ctid);
 }
 
+// The best Fp keys of G sorted lists (descending, Fp keys each, zero padded)
+// (in shared memory, or in global memory read past L1), sorted into cand[0..Fp).  Only the list heads are
+// touched: the first m = ceil(F / G) keys of every list are a set of at least
+// F keys, so their F-th largest, L, is no greater than the F-th best key
+// overall, and every key of the best F is >= L.  Each list's keys >= L (a
+// binary search) are gathered and the few of them sorted.  Returns false,
+// having written nothing, when more than 16 * Fp keys qualify (the caller then
+// merges the whole lists).
+template <bool kSmemSrc>
+__device__ __forceinline__ bool select_list_heads(const uint64_t* lists, uint32_t G, uint32_t F, uint32_t Fp, uint64_t* cand,
+                                  uint32_t* misc, int ctid) {
+  const int lane = ctid & 31, warp = ctid >> 5;
+  if (G > static_cast<uint32_t>(kConsumerThreads)) return false;
+  uint64_t* lsh = reinterpret_cast<uint64_t*>(misc + kMiscSel);
+  const uint32_t m = (F + G - 1) / G;                 // head keys per list
+  const uint32_t H = G * (m < Fp ? m : Fp);           // head set size (>= F unless the lists are short)
+  // (head key h is key h / G of list h % G)
+  if (ctid == 0) *lsh = 0ull;
+  named_bar_sync(kBarConsumers, kConsumerThreads);
+  // L: the head key whose rank among the heads (keys are unique) is F - 1
+  const uint32_t mh = m < Fp ? m : Fp;
+  for (uint32_t h = ctid; h < H; h += kConsumerThreads) {
+    const uint64_t key = load_key<kSmemSrc>(lists + static_cast<size_t>(h % G) * Fp + h / G);
+    uint32_t rank = 0;
+    for (uint32_t pos = 0; pos < mh; ++pos) {  // every thread reads the same key: broadcasts
+      const uint64_t* col = lists + pos;
+#pragma unroll 4
+      for (uint32_t l = 0; l < G; ++l) rank += load_key<kSmemSrc>(col + static_cast<size_t>(l) * Fp) > key ? 1u : 0u;
+    }
+    if (rank == F - 1) *lsh = key;
+  }
+  named_bar_sync(kBarConsumers, kConsumerThreads);
+  const uint64_t L = *lsh;
+  const uint64_t lo = L ? L : 1ull;  // zero keys are empty slots
+  // keys >= lo in this thread's list: its first position below lo
+  uint32_t c = 0;
+  if (static_cast<uint32_t>(ctid) < G) {
+    const uint64_t* li = lists + static_cast<size_t>(ctid) * Fp;
+    uint32_t a = 0, b = Fp;
+    while (a < b) {
+      const uint32_t mid = (a + b) >> 1;
+      if (load_key<kSmemSrc>(li + mid) >= lo) a = mid + 1;
+      else b = mid;
+    }
+    c = a;
+  }
+  uint32_t inc = c;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, inc, off);
+    if (lane >= off) inc += y;
+  }
+  if (lane == 31) misc[kMiscRed + warp] = inc;
+  named_bar_sync(kBarConsumers, kConsumerThreads);
+  uint32_t before = 0, S = 0;
+#pragma unroll
+  for (int w = 0; w < kConsumerWarps; ++w) {
+    const uint32_t t = misc[kMiscRed + w];
+    before += w < warp ? t : 0u;
+    S += t;
+  }
+  named_bar_sync(kBarConsumers, kConsumerThreads);  // misc is reused by the sorts
+  if (S > 16u * Fp) return false;
+  const uint32_t off = before + inc - c;
+  for (uint32_t j = 0; j < c; ++j) cand[off + j] = load_key<kSmemSrc>(lists + static_cast<size_t>(ctid) * Fp + j);
+  const uint32_t span = S <= Fp ? Fp : 16u * Fp;
+  for (uint32_t i = S + ctid; i < span; i += kConsumerThreads) cand[i] = 0ull;
+  named_bar_sync(kBarConsumers, kConsumerThreads);
+  if (S <= Fp) {
+    warp0_sort_dispatch(Fp, cand, ctid);
+    named_bar_sync(kBarConsumers, kConsumerThreads);
+  } else {
+    cta_best_sorted_dispatch(Fp, cand, S, ctid);
+  }
+  return true;
+}
+
+
+
+// The last CTA of a query finishes it (ScanParams::fold): the best F of every
+// CTA's list (list-head selection, else the full merge), the candidate
+// outputs, the exact f64 re-rank of Store.dotRow (src/store/store.ts:114-130:
+// four lanes j accumulating elements j, j+4, ..., summed ((a0+a1)+a2)+a3, then
+// the tail) read straight from the originals, and the best k
+// (src/index.ts:583-594).  Consumer-collective; qx holds >= dim floats of
+// free shared memory, cand >= 16 * Fp keys.
+static __device__ __noinline__ void finish_query(const ScanParams& p, uint64_t* cand, uint32_t* misc, float* qx,
+                                             int ctid) {
+  const int warp = ctid >> 5, lane = ctid & 31;
+  const uint32_t G = gridDim.x;
+  if (!select_list_heads<false>(p.partials, G, p.F, p.Fp, cand, misc, ctid))
+    merge_cta_lists_dispatch(p.Fp, p.partials, G, cand, ctid);
+  if (warp == 0) {
+    uint32_t c = 0;
+    for (uint32_t i = lane; i < p.Fp; i += 32) {
+      if (i >= p.F) cand[i] = 0ull;
+      c += __popc(__ballot_sync(0xffffffffu, i < p.F && cand[i] != 0ull));
+    }
+    if (lane == 0) misc[kMiscNc] = c;
+  }
+  named_bar_sync(kBarConsumers, kConsumerThreads);
+  const uint32_t nc = misc[kMiscNc];
+  if (p.cand_rows) {
+    for (uint32_t i = ctid; i < nc; i += kConsumerThreads) {
+      p.cand_rows[i] = key_row(cand[i]) + p.row_base;
+      p.cand_scores[i] = key_score(cand[i]);
+    }
+    if (ctid == 0) *p.cand_count = nc;
+  }
+  const uint32_t n = nc < p.k ? nc : p.k;
+  if (p.rerank) {
+    for (uint32_t i = ctid; i < p.dim; i += kConsumerThreads) qx[i] = p.query[i];
+    uint64_t* ex = cand + p.Fp;
+    named_bar_sync(kBarConsumers, kConsumerThreads);
+    const uint32_t vec = p.dim & ~3u;
+    for (uint32_t c0 = 0; c0 < nc; c0 += kConsumerThreads / 4) {
+      const uint32_t c = c0 + static_cast<uint32_t>(ctid) / 4u;
+      const uint32_t j = static_cast<uint32_t>(ctid) & 3u;
+      const bool act = c < nc;
+      const uint32_t row = act ? key_row(cand[c]) : 0u;
+      const float* xr = p.originals + static_cast<size_t>(row) * p.dim;
+      double a = 0.0;
+      if (act) {
+#pragma unroll 8
+        for (uint32_t i = j; i < vec; i += 4)
+          a = __fma_rn(static_cast<double>(__ldg(xr + i)), static_cast<double>(qx[i]), a);
+      }
+      const int gl = lane & ~3;
+      const double a0 = __shfl_sync(0xffffffffu, a, gl + 0);
+      const double a1 = __shfl_sync(0xffffffffu, a, gl + 1);
+      const double a2 = __shfl_sync(0xffffffffu, a, gl + 2);
+      const double a3 = __shfl_sync(0xffffffffu, a, gl + 3);
+      if (act && j == 0) {
+        double sacc = __dadd_rn(__dadd_rn(__dadd_rn(a0, a1), a2), a3);
+        for (uint32_t i = vec; i < p.dim; ++i)
+          sacc = __fma_rn(static_cast<double>(xr[i]), static_cast<double>(qx[i]), sacc);
+        ex[c] = make_key(__double2float_rn(sacc), row);
+      }
+    }
+    named_bar_sync(kBarConsumers, kConsumerThreads);
+    if (p.cand_exact)
+      for (uint32_t i = ctid; i < nc; i += kConsumerThreads) p.cand_exact[i] = key_score(ex[i]);
+    for (uint32_t i = nc + static_cast<uint32_t>(ctid); i < p.Fp; i += kConsumerThreads) ex[i] = 0ull;
+    named_bar_sync(kBarConsumers, kConsumerThreads);
+    warp0_sort_dispatch(p.Fp, ex, ctid);
+    if (warp == 0) {
+      __syncwarp();
+      for (uint32_t i = lane; i < n; i += 32) {
+        p.out_rows[i] = key_row(ex[i]) + p.row_base;
+        p.out_scores[i] = key_score(ex[i]);
+      }
+    }
+  } else {
+    for (uint32_t i = ctid; i < n; i += kConsumerThreads) {
+      p.out_rows[i] = key_row(cand[i]) + p.row_base;
+      p.out_scores[i] = key_score(cand[i]);
+    }
+  }
+  if (ctid == 0) {
+    *p.out_count = n;
+    *p.done = 0u;  // the slot's counter starts from zero at its next use
+  }
+}
+
 // ------------------------------------------------------------------ kernel
 // BITS 8/4/1; MODE asym/int/hamming; CB chunk bytes (4, 8 or 16); L lanes per
 // row; CPL chunks per lane; U rows in flight per row-group (asym: even, two
@@ -455,8 +634,10 @@ struct ScanCfg {
                                          : (MODE == kHamming ? W : 1);
 };
 
+// The integer scorings fit two CTAs per SM (consecutive queries overlap on an
+// SM: one streams while the other starts or finishes); asym keeps one.
 template <int BITS, int MODE, int CB, int L, int CPL, int U>
-__global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams p) {
+__global__ void __launch_bounds__(kScanThreads, MODE == kAsym ? 1 : 2) scan_kernel(const ScanParams p) {
   using C = ScanCfg<BITS, MODE, CB, L, CPL, U>;
   extern __shared__ __align__(128) uint8_t smem[];
   const ScanSmem lay = scan_smem_layout(p.tile_bytes, p.tile_rows, p.stages, p.P, p.rounds, p.capc);
@@ -809,6 +990,17 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
     }
     __threadfence();
     if (p.trace && threadIdx.x == 0) p.trace[blockIdx.x * 8 + kTrCtaMerged] = globaltimer();
+    if (p.fold) {
+      // every thread's list writes are fenced; the CTA that finishes last
+      // sees all lists and finishes the query
+      named_bar_sync(kBarConsumers, kConsumerThreads);
+      if (ctid == 0) misc[kMiscTicket] = atomicAdd(p.done, 1u);
+      named_bar_sync(kBarConsumers, kConsumerThreads);
+      if (misc[kMiscTicket] == gridDim.x - 1u) {
+        __threadfence();
+        finish_query(p, cand, misc, reinterpret_cast<float*>(s_codes), ctid);
+      }
+    }
   }
 
 }

@@ -53,11 +53,11 @@ cudaError_t launch_one(const ScanParams& p, unsigned grid, size_t smem, cudaStre
   BV_TRY_SHAPE(BITS, kAsym, 16, 32, 4, 2)                                             \
   BV_TRY_SHAPE(BITS, kAsym, 16, 32, 8, 2)
 
-// Integer-mode layouts of wider rows (<= 8 lanes per row up to 64 chunks).
+// Integer-mode layouts of wider rows (8 lanes per row up to 32 chunks, 16 at 64).
 #define BV_SHAPES_INT(BITS, MODE)                                                     \
   BV_TRY_SHAPE(BITS, MODE, 16, 8, 2, 2)                                               \
   BV_TRY_SHAPE(BITS, MODE, 16, 8, 4, 1)                                               \
-  BV_TRY_SHAPE(BITS, MODE, 16, 8, 8, 1)
+  BV_TRY_SHAPE(BITS, MODE, 16, 16, 4, 1)
 
 #define BV_SHAPES_INT_WIDE(BITS, MODE)                                                \
   BV_TRY_SHAPE(BITS, MODE, 16, 16, 8, 1)                                              \

@@ -16,86 +16,6 @@
 
 namespace bv {
 
-namespace {
-
-// The best Fp keys of G sorted lists (descending, Fp keys each, zero padded)
-// held in shared memory, sorted into cand[0..Fp).  Only the list heads are
-// touched: the first m = ceil(F / G) keys of every list are a set of at least
-// F keys, so their F-th largest, L, is no greater than the F-th best key
-// overall, and every key of the best F is >= L.  Each list's keys >= L (a
-// binary search) are gathered and the few of them sorted.  Returns false,
-// having written nothing, when more than 16 * Fp keys qualify (the caller then
-// merges the whole lists).
-__device__ bool select_list_heads(const uint64_t* lists, uint32_t G, uint32_t F, uint32_t Fp, uint64_t* cand,
-                                  uint32_t* misc, int ctid) {
-  const int lane = ctid & 31, warp = ctid >> 5;
-  if (G > static_cast<uint32_t>(kConsumerThreads)) return false;
-  uint64_t* lsh = reinterpret_cast<uint64_t*>(misc + kMiscSel);
-  const uint32_t m = (F + G - 1) / G;                 // head keys per list
-  const uint32_t H = G * (m < Fp ? m : Fp);           // head set size (>= F unless the lists are short)
-  // (head key h is key h / G of list h % G)
-  if (ctid == 0) *lsh = 0ull;
-  named_bar_sync(kBarConsumers, kConsumerThreads);
-  // L: the head key whose rank among the heads (keys are unique) is F - 1
-  const uint32_t mh = m < Fp ? m : Fp;
-  for (uint32_t h = ctid; h < H; h += kConsumerThreads) {
-    const uint64_t key = lists[static_cast<size_t>(h % G) * Fp + h / G];
-    uint32_t rank = 0;
-    for (uint32_t pos = 0; pos < mh; ++pos) {  // every thread reads the same key: broadcasts
-      const uint64_t* col = lists + pos;
-#pragma unroll 4
-      for (uint32_t l = 0; l < G; ++l) rank += col[static_cast<size_t>(l) * Fp] > key ? 1u : 0u;
-    }
-    if (rank == F - 1) *lsh = key;
-  }
-  named_bar_sync(kBarConsumers, kConsumerThreads);
-  const uint64_t L = *lsh;
-  const uint64_t lo = L ? L : 1ull;  // zero keys are empty slots
-  // keys >= lo in this thread's list: its first position below lo
-  uint32_t c = 0;
-  if (static_cast<uint32_t>(ctid) < G) {
-    const uint64_t* li = lists + static_cast<size_t>(ctid) * Fp;
-    uint32_t a = 0, b = Fp;
-    while (a < b) {
-      const uint32_t mid = (a + b) >> 1;
-      if (li[mid] >= lo) a = mid + 1;
-      else b = mid;
-    }
-    c = a;
-  }
-  uint32_t inc = c;
-#pragma unroll
-  for (int off = 1; off < 32; off <<= 1) {
-    const uint32_t y = __shfl_up_sync(0xffffffffu, inc, off);
-    if (lane >= off) inc += y;
-  }
-  if (lane == 31) misc[kMiscRed + warp] = inc;
-  named_bar_sync(kBarConsumers, kConsumerThreads);
-  uint32_t before = 0, S = 0;
-#pragma unroll
-  for (int w = 0; w < kConsumerWarps; ++w) {
-    const uint32_t t = misc[kMiscRed + w];
-    before += w < warp ? t : 0u;
-    S += t;
-  }
-  named_bar_sync(kBarConsumers, kConsumerThreads);  // misc is reused by the sorts
-  if (S > 16u * Fp) return false;
-  const uint32_t off = before + inc - c;
-  for (uint32_t j = 0; j < c; ++j) cand[off + j] = lists[static_cast<size_t>(ctid) * Fp + j];
-  const uint32_t span = S <= Fp ? Fp : 16u * Fp;
-  for (uint32_t i = S + ctid; i < span; i += kConsumerThreads) cand[i] = 0ull;
-  named_bar_sync(kBarConsumers, kConsumerThreads);
-  if (S <= Fp) {
-    warp0_sort_dispatch(Fp, cand, ctid);
-    named_bar_sync(kBarConsumers, kConsumerThreads);
-  } else {
-    cta_best_sorted_dispatch(Fp, cand, S, ctid);
-  }
-  return true;
-}
-
-}  // namespace
-
 __global__ void __launch_bounds__(kConsumerThreads, 1) tail_kernel(const TailParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   // CTA b of a batched launch serves query b: its own partials, query and outputs
@@ -160,7 +80,7 @@ __global__ void __launch_bounds__(kConsumerThreads, 1) tail_kernel(const TailPar
   if (p.Fp <= 256u) {
     bool selected = false;
     if (staged)
-      selected = select_list_heads(reinterpret_cast<const uint64_t*>(rows_s), p.G, p.F, p.Fp, cand, misc, ctid);
+      selected = select_list_heads<true>(reinterpret_cast<const uint64_t*>(rows_s), p.G, p.F, p.Fp, cand, misc, ctid);
     if (!selected) {
       if (staged)
         merge_cta_lists_dispatch<true>(p.Fp, reinterpret_cast<const uint64_t*>(rows_s), p.G, cand, ctid);

@@ -163,8 +163,9 @@ BV_API int bv_get_stats(const bv_index* idx, bv_stats* out);
 BV_API int bv_set_phase_trace(bv_index* idx, uint64_t* trace_dev, uint64_t capacity);
 
 /* Kernel launches made by the last bv_search / bv_search_async /
- * bv_query_rows_exact on this index (a search launches a scan and a tail
- * kernel per query). */
+ * bv_query_rows_exact on this index (a search launches one scan per query,
+ * whose last CTA finishes the query, when fetch <= 256, else a scan and a
+ * tail kernel per query; a batched search several per batch). */
 BV_API int bv_launches_last_search(const bv_index* idx, uint32_t* launches);
 
 /* Batched search on the tensor cores: the same request and results as
