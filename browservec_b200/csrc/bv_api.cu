@@ -302,9 +302,14 @@ int plan_scan(bv_index* idx, uint32_t F, Plan* pl, bool fold = true) {
   if (!pl->stages) return fail(BV_ERR_UNSUPPORTED, "scan tile does not fit in shared memory");
   // Without folding two SMs stay free for the tail kernels (one query's merge
   // and re-rank can still run while the next query's finishes), so a
-  // following scan finds a whole grid's worth of SMs.
-  const uint32_t sms = pl->fold ? static_cast<uint32_t>(idx->num_sms)
-                                : (idx->num_sms > 2 ? static_cast<uint32_t>(idx->num_sms) - 2u : 1u);
+  // following scan finds a whole grid's worth of SMs.  With two CTAs per SM a
+  // query takes two thirds of the SMs: three queries fit the SMs' slots, so a
+  // query's CTAs all start at once and the next query (launched once they
+  // have) is waiting for every slot that frees.
+  const bool two_per_sm = pl->fold && pl->smem <= limit && idx->scoring != BV_SCORE_ASYM;
+  const uint32_t sms = two_per_sm ? static_cast<uint32_t>(idx->num_sms) * 2u / 3u
+                       : pl->fold ? static_cast<uint32_t>(idx->num_sms)
+                                  : (idx->num_sms > 2 ? static_cast<uint32_t>(idx->num_sms) - 2u : 1u);
   pl->grid = pl->ntiles < sms ? pl->ntiles : sms;
   return BV_OK;
 }
@@ -433,6 +438,8 @@ int enqueue_search(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStrea
   p.codes = idx->d_codes;
   p.scales = idx->d_scales;
   p.signs = idx->d_signs;
+  p.seed = idx->seed;
+  p.sign_scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(idx->P)));
   p.mask = a->mask;
   p.nrows = idx->rows;
   p.dim = idx->dim;
@@ -1364,6 +1371,8 @@ extern "C" int bv_search_noalloc(bv_index* idx, const bv_search_args* a, void* s
   p.codes = idx->d_codes;
   p.scales = idx->d_scales;
   p.signs = idx->d_signs;
+  p.seed = idx->seed;
+  p.sign_scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(idx->P)));
   p.mask = a->mask;
   p.nrows = idx->rows;
   p.dim = idx->dim;

@@ -60,6 +60,8 @@ struct ScanParams {
   unsigned long long* tile_ctr;  // dynamic tile counter slot: (epoch << 32) | next tile
   uint32_t epoch;            // launch number owning tile_ctr
   uint32_t serial;           // 1: the partials are shared with the previous query (wait for its tail)
+  uint32_t seed;             // rotator seed (rotator.ts:66-80): signs computed on the fly
+  float sign_scale;          // f32(1 / sqrt(P) in f64), the signs' magnitude
   // The query's finish by its last CTA (fold = 1, Fp <= 256): merge of the CTA
   // lists, exact re-rank and outputs, as the tail kernel does.
   uint32_t fold;
@@ -103,13 +105,18 @@ __device__ __forceinline__ uint32_t grab_tile(unsigned long long* ctr, uint32_t 
 }
 
 // Phase timestamps: CTA b writes trace[b*8 + phase].
-enum : int { kTrEntry = 0, kTrRotated = 1, kTrScanned = 2, kTrCtaMerged = 3 };
+enum : int { kTrEntry = 0, kTrRotated = 1, kTrScanned = 2, kTrCtaMerged = 3, kTrQueryIn = 4, kTrFirstTile = 5 };
 
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+
+// The rotation of 32 <= P <= 1024 runs in registers (rotate_query_fast) on a
+// padded buffer of P/32 rows of 33 floats, with the signs computed on the fly.
+__host__ __device__ inline bool fast_rotation(uint32_t P) { return P >= 32 && P <= 1024; }
+__host__ __device__ inline uint32_t rotation_pad_floats(uint32_t P) { return (P / 32) * 33; }
 
 // Shared-memory carve-up (host and device agree on it).
 struct ScanSmem {
@@ -132,8 +139,8 @@ __host__ __device__ inline ScanSmem scan_smem_layout(uint32_t tile_bytes, uint32
   o = align_up(o + (2 * stages + 1) * 8 + stages * 4, 16);
   s.q_off = o;
   o = align_up(o + P * 4, 16);
-  s.signs_off = o;
-  o = align_up(o + rounds * P * 4, 16);
+  s.signs_off = o;  // the signs (P > 1024), or the padded rotation buffer (P <= 1024)
+  o = align_up(o + (fast_rotation(P) ? rotation_pad_floats(P) * 4 : rounds * P * 4), 16);
   s.qb_off = o;
   o = align_up(o + P, 16);
   s.cand_off = o;
@@ -240,7 +247,103 @@ __device__ __forceinline__ void rotate_query(float* q, const float* signs, uint3
   }
 }
 
+// Sign i of one rotation round: randomSigns (prng.ts:5-22) draws
+// mulberry32 values in sequence, and mulberry32's state after i + 1 draws is
+// seed + (i + 1) * 0x6d2b79f5, so draw i is computed directly.  Value
+// u < 2^31 gives -1, scaled by f32(1/sqrt(P)) (rotator.ts:66-80).
+__device__ __forceinline__ float rot_sign(uint32_t round_seed, uint32_t i, float scale) {
+  const uint32_t a = round_seed + (i + 1u) * 0x6d2b79f5u;
+  uint32_t t = (a ^ (a >> 15)) * (1u | a);
+  t = (t + (t ^ (t >> 7)) * (61u | t)) ^ t;
+  return ((t ^ (t >> 14)) < 0x80000000u) ? -scale : scale;
+}
+
 // Math.round (halves toward +inf) of an f64.
+__device__ __forceinline__ double js_round(double x);
+
+// The whole query prologue of 32 <= P <= 1024 in ONE warp, no barrier: lane c
+// holds elements i = 32 r + c (r < NR = P / 32) in registers.  Per round the
+// sign multiply, the FWHT stages of bits 0..4 by shuffles and of bits 5.. by
+// register butterflies -- the reference's stage order (rotator.ts:83-92), the
+// same f32 operations as rotate_query.  Then, by mode, the rotated query to
+// q (asym), its int8 codes to qb with the codec of quantize_query8 (int,
+// returns qscale), or its sign bits to qb as words (hamming).
+template <int NR, int MODE>
+__device__ __forceinline__ float prologue_warp(float* q, int8_t* qb, uint32_t seed, float scale, uint32_t rounds,
+                                               int lane) {
+  float x[NR];
+#pragma unroll
+  for (int r = 0; r < NR; ++r) x[r] = q[r * 32 + lane];
+  for (uint32_t rd = 0; rd < rounds; ++rd) {
+    const uint32_t rs = seed ^ (0x9e3779b9u * (rd + 1u));
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+      float v = __fmul_rn(x[r], rot_sign(rs, static_cast<uint32_t>(r * 32 + lane), scale));
+#pragma unroll
+      for (int len = 1; len < 32; len <<= 1) {
+        const float y = __shfl_xor_sync(0xffffffffu, v, len);
+        v = (lane & len) ? __fsub_rn(y, v) : __fadd_rn(v, y);
+      }
+      x[r] = v;
+    }
+#pragma unroll
+    for (int len = 1; len < NR; len <<= 1)
+#pragma unroll
+      for (int r = 0; r < NR; ++r)
+        if ((r & len) == 0) {
+          const float a = x[r], b = x[r + len];
+          x[r] = __fadd_rn(a, b);
+          x[r + len] = __fsub_rn(a, b);
+        }
+  }
+  float qscale = 1.0f;
+  if constexpr (MODE == 0) {  // asym: the rotated query itself
+#pragma unroll
+    for (int r = 0; r < NR; ++r) q[r * 32 + lane] = x[r];
+  } else if constexpr (MODE == 1) {  // int: the corpus int8 codec (codec.ts:132-154)
+    float m = 0.0f;
+#pragma unroll
+    for (int r = 0; r < NR; ++r) m = fmaxf(m, fabsf(x[r]));
+#pragma unroll
+    for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    qscale = m > 0.0f ? m : 1.0f;
+    const double inv = __ddiv_rn(1.0, static_cast<double>(qscale));
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+      double v = __dmul_rn(static_cast<double>(x[r]), inv);
+      v = v < -1.0 ? -1.0 : (v > 1.0 ? 1.0 : v);
+      double b = js_round(__dmul_rn(v, 127.0));
+      b = b < -127.0 ? -127.0 : (b > 127.0 ? 127.0 : b);
+      qb[r * 32 + lane] = static_cast<int8_t>(static_cast<int>(b));
+      q[r * 32 + lane] = x[r];
+    }
+  } else {  // hamming: bit i of the query = rotated element i >= 0
+    uint32_t* qbits = reinterpret_cast<uint32_t*>(qb);
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+      const uint32_t w = __ballot_sync(0xffffffffu, x[r] >= 0.0f);
+      if (lane == 0) qbits[r] = w;
+      q[r * 32 + lane] = x[r];
+    }
+  }
+  return qscale;
+}
+
+// Not inlined: its register arrays get their own allocation instead of
+// pressing on the scan loop's under the two-CTAs-per-SM register cap.
+template <int MODE>
+static __device__ __noinline__ float prologue_warp_dispatch(uint32_t P, float* q, int8_t* qb, uint32_t seed, float scale,
+                                                        uint32_t rounds, int lane) {
+  switch (P) {
+    case 32: return prologue_warp<1, MODE>(q, qb, seed, scale, rounds, lane);
+    case 64: return prologue_warp<2, MODE>(q, qb, seed, scale, rounds, lane);
+    case 128: return prologue_warp<4, MODE>(q, qb, seed, scale, rounds, lane);
+    case 256: return prologue_warp<8, MODE>(q, qb, seed, scale, rounds, lane);
+    case 512: return prologue_warp<16, MODE>(q, qb, seed, scale, rounds, lane);
+    default: return prologue_warp<32, MODE>(q, qb, seed, scale, rounds, lane);
+  }
+}
+
 __device__ __forceinline__ double js_round(double x) {
   double r = floor(x);
   if (__dadd_rn(x, -r) >= 0.5) r = __dadd_rn(r, 1.0);
@@ -683,7 +786,7 @@ __global__ void __launch_bounds__(kScanThreads, MODE == kAsym ? 1 : 2) scan_kern
   if (warp == kConsumerWarps) {
     // ---------------------------------------------------------- producer
     if (lane == 0) {
-      const uint32_t sbytes = p.rounds * p.P * 4u;
+      const uint32_t sbytes = fast_rotation(p.P) ? 0u : p.rounds * p.P * 4u;  // fast: signs on the fly
       mbar_arrive_expect_tx(qbar, q_bulk + sbytes);
       if (q_bulk) bulk_g2s(q, p.query, q_bulk, qbar);
       if (sbytes) bulk_g2s(s_signs, p.signs, sbytes, qbar);
@@ -714,18 +817,30 @@ __global__ void __launch_bounds__(kScanThreads, MODE == kAsym ? 1 : 2) scan_kern
     // ---------------------------------------------------------- consumers
     const int ctid = threadIdx.x;
     mbar_wait_bounded(qbar, 0, p.err);
+    if (p.trace && ctid == 0) p.trace[blockIdx.x * 8 + kTrQueryIn] = globaltimer();
     for (uint32_t i = q_bulk / 4 + ctid; i < p.P; i += kConsumerThreads)
       q[i] = i < p.dim ? p.query[i] : 0.0f;
     named_bar_sync(kBarConsumers, kConsumerThreads);
-    rotate_query(q, s_signs, p.P, p.rounds, ctid);
     float qfac = 1.0f;
-    if constexpr (MODE == kInt) {
-      const float qscale = quantize_query8(q, qb, p.P, ctid, miscf + kMiscRed);
-      qfac = __fmul_rn(qscale, kInv127);
-    } else if constexpr (MODE == kHamming) {
-      uint32_t* qbits = reinterpret_cast<uint32_t*>(qb);
-      for (uint32_t blk = warp; blk < p.P / 32; blk += kConsumerWarps)
-        qbits[blk] = __ballot_sync(0xffffffffu, q[blk * 32 + lane] >= 0.0f);
+    if (fast_rotation(p.P)) {
+      // one warp rotates and codes the query, the others wait at one barrier
+      if (warp == 0) {
+        const float qscale = prologue_warp_dispatch<MODE == kAsym ? 0 : (MODE == kInt ? 1 : 2)>(
+            p.P, q, qb, p.seed, p.sign_scale, p.rounds, lane);
+        if (lane == 0) miscf[kMiscRed] = qscale;
+      }
+      named_bar_sync(kBarConsumers, kConsumerThreads);
+      if constexpr (MODE == kInt) qfac = __fmul_rn(miscf[kMiscRed], kInv127);
+    } else {
+      rotate_query(q, s_signs, p.P, p.rounds, ctid);
+      if constexpr (MODE == kInt) {
+        const float qscale = quantize_query8(q, qb, p.P, ctid, miscf + kMiscRed);
+        qfac = __fmul_rn(qscale, kInv127);
+      } else if constexpr (MODE == kHamming) {
+        uint32_t* qbits = reinterpret_cast<uint32_t*>(qb);
+        for (uint32_t blk = warp; blk < p.P / 32; blk += kConsumerWarps)
+          qbits[blk] = __ballot_sync(0xffffffffu, q[blk * 32 + lane] >= 0.0f);
+      }
     }
     named_bar_sync(kBarConsumers, kConsumerThreads);
     if (p.trace && threadIdx.x == 0) p.trace[blockIdx.x * 8 + kTrRotated] = globaltimer();
@@ -782,6 +897,7 @@ __global__ void __launch_bounds__(kScanThreads, MODE == kAsym ? 1 : 2) scan_kern
       const uint32_t s = it % p.stages, ph = (it / p.stages) & 1u;
       const bool landed = mbar_wait_bounded(&full[s], ph, p.err);
       const uint32_t t = landed ? tile_ids[s] : kNoTile;
+      if (it == 0 && p.trace && threadIdx.x == 0) p.trace[blockIdx.x * 8 + kTrFirstTile] = globaltimer();
       if (t == kNoTile) break;
       const uint8_t* cb = s_codes + static_cast<size_t>(s) * p.tile_bytes;
       const float* sc = s_scales + static_cast<size_t>(s) * p.tile_rows;
