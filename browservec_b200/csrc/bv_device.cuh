@@ -407,4 +407,84 @@ struct WarpTopF {
   __device__ __forceinline__ void finish(int lane) { compact(lane); }
 };
 
+// ------------------------------------------- exact f64 row dot, one warp
+// Store.dotRow (src/store/store.ts:114-130): four f64 accumulators, lane j
+// adding x[i] * q[i] for i = j, j+4, ... below vec = dim & ~3 in order, the
+// sum ((a0 + a1) + a2) + a3, then the dim % 4 tail in order, and the f32 of
+// that (Math.fround, round to nearest even).  Every product of two f32 is
+// exact in f64, so the only roundings are the additions.
+//
+// Fast path: the warp adds the same exact products in another order (lane l
+// takes i = l + 32t into four interleaved partial sums, then a butterfly of
+// commutative adds, which leaves every lane with the same value) together
+// with A = sum |x[i] q[i]|.  With K the most additions any product goes
+// through in either order (K <= dim / 4 + 12) and u = 2^-53, each order is
+// within gamma_K * A of the exact sum (the bound for summation in any order:
+// N. J. Higham, Accuracy and Stability of Numerical Algorithms, 2nd ed.,
+// sec. 4.2), so the two are within 2 gamma_K A <= B = 4 (K + 1) u A' of one
+// another (A' the computed A).  Rounding to f32 is monotone: when both ends
+// of [s' - B, s' + B] (outward-rounded) round to the same f32 bits, that is
+// the reference's result.  Otherwise (an f32 rounding boundary inside the
+// interval -- about one row in 10^5 at unit norms -- or a NaN/Inf) the warp
+// computes the reference's own sequence.  Either way the result is
+// bit-identical to the sequential chain, and the common case costs a
+// dim / 128-step chain per lane instead of dim / 4.
+template <bool kGlobal>
+__device__ __forceinline__ float ld_row_f32(const float* p) {
+  if constexpr (kGlobal) return __ldg(p);
+  else return *p;
+}
+
+template <bool kGlobal>
+__device__ __forceinline__ float dot_row_exact_warp(const float* x, const float* q, uint32_t dim, int lane) {
+  double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0, a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+  uint32_t i = static_cast<uint32_t>(lane);
+  for (; i + 96u < dim; i += 128u) {
+    const double p0 = __dmul_rn(static_cast<double>(ld_row_f32<kGlobal>(x + i)), static_cast<double>(q[i]));
+    const double p1 =
+        __dmul_rn(static_cast<double>(ld_row_f32<kGlobal>(x + i + 32u)), static_cast<double>(q[i + 32u]));
+    const double p2 =
+        __dmul_rn(static_cast<double>(ld_row_f32<kGlobal>(x + i + 64u)), static_cast<double>(q[i + 64u]));
+    const double p3 =
+        __dmul_rn(static_cast<double>(ld_row_f32<kGlobal>(x + i + 96u)), static_cast<double>(q[i + 96u]));
+    s0 = __dadd_rn(s0, p0);
+    s1 = __dadd_rn(s1, p1);
+    s2 = __dadd_rn(s2, p2);
+    s3 = __dadd_rn(s3, p3);
+    a0 = __dadd_rn(a0, fabs(p0));
+    a1 = __dadd_rn(a1, fabs(p1));
+    a2 = __dadd_rn(a2, fabs(p2));
+    a3 = __dadd_rn(a3, fabs(p3));
+  }
+  for (; i < dim; i += 32u) {
+    const double p0 = __dmul_rn(static_cast<double>(ld_row_f32<kGlobal>(x + i)), static_cast<double>(q[i]));
+    s0 = __dadd_rn(s0, p0);
+    a0 = __dadd_rn(a0, fabs(p0));
+  }
+  double s = __dadd_rn(__dadd_rn(s0, s1), __dadd_rn(s2, s3));
+  double a = __dadd_rn(__dadd_rn(a0, a1), __dadd_rn(a2, a3));
+#pragma unroll
+  for (int off = 16; off; off >>= 1) {
+    s = __dadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
+    a = __dadd_rn(a, __shfl_xor_sync(0xffffffffu, a, off));
+  }
+  const double K1 = static_cast<double>(dim / 4u + 13u);  // K + 1
+  const double B = __dmul_ru(__dmul_ru(a, K1), 0x1p-51);  // 4 (K + 1) u A'
+  const float lo = __double2float_rn(__dsub_rd(s, B));
+  const float hi = __double2float_rn(__dadd_ru(s, B));
+  if (lo == lo && __float_as_uint(lo) == __float_as_uint(hi)) return lo;  // warp-uniform
+  // the reference's sequence: lanes 0..3 are its accumulators
+  const uint32_t vec = dim & ~3u;
+  double c = 0.0;
+  if (lane < 4)
+    for (uint32_t k = static_cast<uint32_t>(lane); k < vec; k += 4u)
+      c = __fma_rn(static_cast<double>(ld_row_f32<kGlobal>(x + k)), static_cast<double>(q[k]), c);
+  const double c0 = __shfl_sync(0xffffffffu, c, 0), c1 = __shfl_sync(0xffffffffu, c, 1);
+  const double c2 = __shfl_sync(0xffffffffu, c, 2), c3 = __shfl_sync(0xffffffffu, c, 3);
+  double r = __dadd_rn(__dadd_rn(__dadd_rn(c0, c1), c2), c3);
+  for (uint32_t k = vec; k < dim; ++k)
+    r = __fma_rn(static_cast<double>(ld_row_f32<kGlobal>(x + k)), static_cast<double>(q[k]), r);
+  return __double2float_rn(r);
+}
+
 }  // namespace bv

@@ -1,6 +1,7 @@
 // bv_exact.cu -- exact scan over an explicit row list (BrowserVec.queryRowsExact,
-// src/index.ts:445-464): f64-accumulated dot per row in the lane order of
-// Store.dotRow (src/store/store.ts:114-130), then the best k by
+// src/index.ts:445-464): the f64-accumulated dot of Store.dotRow
+// (src/store/store.ts:114-130) per row, one warp per row (dot_row_exact_warp:
+// bit-identical to the lane-ordered sequence), then the best k by
 // (score desc, row asc).  One CTA; used for filters matching <= 4096 rows.
 #include <cstdint>
 
@@ -18,35 +19,14 @@ __global__ void __launch_bounds__(kExactThreads) exact_rows_kernel(
     uint32_t* out_rows, float* out_scores, uint32_t* out_count) {
   extern __shared__ uint64_t keys[];  // npow2
   const int tid = threadIdx.x, lane = tid & 31;
-  const uint32_t vec = dim & ~3u;
-  for (uint32_t c0 = 0; c0 < npow2; c0 += kExactThreads / 4) {
-    const uint32_t c = c0 + static_cast<uint32_t>(tid) / 4u;
-    const uint32_t j = static_cast<uint32_t>(tid) & 3u;
-    const bool act = c < nrows;
-    double a = 0.0;
-    uint32_t row = 0;
-    if (act) {
-      row = rows[c];
-      const float* xr = originals + static_cast<size_t>(row) * dim;
-      for (uint32_t i = j; i < vec; i += 4)
-        a = __fma_rn(static_cast<double>(xr[i]), static_cast<double>(query[i]), a);
+  const int warp = tid >> 5;
+  for (uint32_t c = static_cast<uint32_t>(warp); c < npow2; c += kExactThreads / 32) {  // a warp per row
+    uint64_t kx = 0;
+    if (c < nrows) {
+      const uint32_t row = rows[c];
+      kx = make_key(dot_row_exact_warp<true>(originals + static_cast<size_t>(row) * dim, query, dim, lane), row);
     }
-    const int gl = lane & ~3;
-    const double a0 = __shfl_sync(0xffffffffu, a, gl + 0);
-    const double a1 = __shfl_sync(0xffffffffu, a, gl + 1);
-    const double a2 = __shfl_sync(0xffffffffu, a, gl + 2);
-    const double a3 = __shfl_sync(0xffffffffu, a, gl + 3);
-    if (c < npow2 && j == 0) {
-      uint64_t kx = 0;
-      if (act) {
-        double s = __dadd_rn(__dadd_rn(__dadd_rn(a0, a1), a2), a3);
-        const float* xr = originals + static_cast<size_t>(row) * dim;
-        for (uint32_t i = vec; i < dim; ++i)
-          s = __fma_rn(static_cast<double>(xr[i]), static_cast<double>(query[i]), s);
-        kx = make_key(__double2float_rn(s), row);
-      }
-      keys[c] = kx;
-    }
+    if (lane == 0) keys[c] = kx;
   }
   __syncthreads();
   // block bitonic sort, descending

@@ -37,6 +37,7 @@ constexpr int kConsumerWarps = 16;
 constexpr int kScanThreads = (kConsumerWarps + 1) * 32;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr uint32_t kBarConsumers = 1;  // named barrier id of the consumer warps
+constexpr uint32_t kBarRotate = 2;     // named barrier id of the warps rotating the query
 constexpr int kSelMax = 8;             // keys per consumer thread in a CTA selection
 constexpr int kMergeMax = 24;          // keys per consumer thread in the last-CTA merge
 
@@ -154,7 +155,7 @@ __host__ __device__ inline ScanSmem scan_smem_layout(uint32_t tile_bytes, uint32
 }
 
 // misc word slots
-enum : int { kMiscCount = 0, kMiscNc = 5, kMiscTicket = 6, kMiscRed = 16, kMiscSel = 64 };
+enum : int { kMiscCount = 0, kMiscNc = 5, kMiscTicket = 6, kMiscQScale = 7, kMiscRed = 16, kMiscSel = 64 };
 
 // ------------------------------------------------------------ code -> value
 // int8 byte of word xb (= x ^ 0x80808080) as a biased float 2^23 + (b + 128):
@@ -342,6 +343,95 @@ static __device__ __noinline__ float prologue_warp_dispatch(uint32_t P, float* q
     case 512: return prologue_warp<16, MODE>(q, qb, seed, scale, rounds, lane);
     default: return prologue_warp<32, MODE>(q, qb, seed, scale, rounds, lane);
   }
+}
+
+// The query prologue of P = 2^(6 + HB) (512 or 1024) over W = 2^HB warps,
+// two elements per lane, with the arithmetic of prologue_warp.  Layout A:
+// warp w, lane l, register r hold element 64 w + 32 r + l, so the FWHT stages
+// of bits 0..5 are five shuffles and one register butterfly.  Layout B: the
+// element ((l & (W-1)) << 6) | (w << (6-HB)) | ((l >> HB) << 1) | r, so the
+// stages of bits 6.. are shuffles over lane bits 0..HB-1.  The layouts meet
+// in `xs` (element i at i + i / 32, conflict-free for layout A): three
+// exchanges for two rounds.  Writes the query codes like prologue_warp and
+// returns qscale (int mode) to every participating thread; warps >= W do not
+// take part.
+template <int HB, int MODE>
+static __device__ __noinline__ float prologue_multi(float* q, int8_t* qb, float* xs, float* red, uint32_t seed,
+                                                    float scale, uint32_t rounds, int warp, int lane) {
+  constexpr int W = 1 << HB;
+  constexpr uint32_t kThreads = W * 32;
+  const uint32_t ia = static_cast<uint32_t>(warp) * 64u + static_cast<uint32_t>(lane);
+  const uint32_t ib = ((static_cast<uint32_t>(lane) & (W - 1u)) << 6) | (static_cast<uint32_t>(warp) << (6 - HB)) |
+                      ((static_cast<uint32_t>(lane) >> HB) << 1);
+  const auto pad = [](uint32_t i) { return i + (i >> 5); };
+  float x0 = q[ia], x1 = q[ia + 32u];
+  for (uint32_t rd = 0; rd < rounds; ++rd) {
+    if (rd > 0) {  // layout B -> A
+      xs[pad(ib)] = x0;
+      xs[pad(ib + 1u)] = x1;
+      named_bar_sync(kBarRotate, kThreads);
+      x0 = xs[pad(ia)];
+      x1 = xs[pad(ia + 32u)];
+    }
+    const uint32_t rs = seed ^ (0x9e3779b9u * (rd + 1u));
+    x0 = __fmul_rn(x0, rot_sign(rs, ia, scale));
+    x1 = __fmul_rn(x1, rot_sign(rs, ia + 32u, scale));
+#pragma unroll
+    for (int len = 1; len < 32; len <<= 1) {
+      const float y0 = __shfl_xor_sync(0xffffffffu, x0, len);
+      const float y1 = __shfl_xor_sync(0xffffffffu, x1, len);
+      x0 = (lane & len) ? __fsub_rn(y0, x0) : __fadd_rn(x0, y0);
+      x1 = (lane & len) ? __fsub_rn(y1, x1) : __fadd_rn(x1, y1);
+    }
+    {
+      const float a = x0, b = x1;  // bit 5: the register pair
+      x0 = __fadd_rn(a, b);
+      x1 = __fsub_rn(a, b);
+    }
+    xs[pad(ia)] = x0;  // layout A -> B
+    xs[pad(ia + 32u)] = x1;
+    named_bar_sync(kBarRotate, kThreads);
+    x0 = xs[pad(ib)];
+    x1 = xs[pad(ib + 1u)];
+#pragma unroll
+    for (int len = 1; len < W; len <<= 1) {  // bits 6.. in stage order
+      const float y0 = __shfl_xor_sync(0xffffffffu, x0, len);
+      const float y1 = __shfl_xor_sync(0xffffffffu, x1, len);
+      x0 = (lane & len) ? __fsub_rn(y0, x0) : __fadd_rn(x0, y0);
+      x1 = (lane & len) ? __fsub_rn(y1, x1) : __fadd_rn(x1, y1);
+    }
+  }
+  q[ib] = x0;
+  q[ib + 1u] = x1;
+  float qscale = 1.0f;
+  if constexpr (MODE == 1) {  // int: the corpus int8 codec (codec.ts:132-154)
+    float m = fmaxf(fabsf(x0), fabsf(x1));
+#pragma unroll
+    for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    if (lane == 0) red[warp] = m;
+    named_bar_sync(kBarRotate, kThreads);
+    m = 0.0f;
+#pragma unroll
+    for (int w = 0; w < W; ++w) m = fmaxf(m, red[w]);
+    qscale = m > 0.0f ? m : 1.0f;
+    const double inv = __ddiv_rn(1.0, static_cast<double>(qscale));
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      double v = __dmul_rn(static_cast<double>(r ? x1 : x0), inv);
+      v = v < -1.0 ? -1.0 : (v > 1.0 ? 1.0 : v);
+      double b = js_round(__dmul_rn(v, 127.0));
+      b = b < -127.0 ? -127.0 : (b > 127.0 ? 127.0 : b);
+      qb[ib + static_cast<uint32_t>(r)] = static_cast<int8_t>(static_cast<int>(b));
+    }
+  } else if constexpr (MODE == 2) {  // hamming: sign bits of 32 consecutive elements per word
+    named_bar_sync(kBarRotate, kThreads);
+    uint32_t* qbits = reinterpret_cast<uint32_t*>(qb);
+    for (uint32_t blk = static_cast<uint32_t>(warp); blk < (64u << HB) / 32u; blk += W) {
+      const uint32_t wd = __ballot_sync(0xffffffffu, q[blk * 32u + static_cast<uint32_t>(lane)] >= 0.0f);
+      if (lane == 0) qbits[blk] = wd;
+    }
+  }
+  return qscale;
 }
 
 __device__ __forceinline__ double js_round(double x) {
@@ -634,20 +724,117 @@ __device__ __forceinline__ bool select_list_heads(const uint64_t* lists, uint32_
 }
 
 
+// select_list_heads for lists in global memory (written by other CTAs of the
+// same grid, read past L1), with the same result: the head keys are staged in
+// shared memory (`heads`, >= G * min(ceil(F / G), Fp) keys) by one round of
+// loads, ranked there, and every list's count of keys >= L is found by
+// probing four keys at a time from its start (the count is a prefix: the
+// lists are sorted), the first four kept in registers for the gather.  Two
+// rounds of memory latency instead of one per head key and per bisection step.
+__device__ __forceinline__ bool select_list_heads_global(const uint64_t* lists, uint32_t G, uint32_t F, uint32_t Fp,
+                                                         uint64_t* cand, uint32_t* misc, uint64_t* heads,
+                                                         int ctid) {
+  const int lane = ctid & 31, warp = ctid >> 5;
+  if (G > static_cast<uint32_t>(kConsumerThreads)) return false;
+  uint64_t* lsh = reinterpret_cast<uint64_t*>(misc + kMiscSel);
+  const uint32_t m = (F + G - 1) / G;
+  const uint32_t mh = m < Fp ? m : Fp;
+  const uint32_t H = G * mh;  // head key h is key h / G of list h % G
+  for (uint32_t h = ctid; h < H; h += kConsumerThreads)
+    heads[h] = __ldcg(lists + static_cast<size_t>(h % G) * Fp + h / G);
+  if (ctid == 0) *lsh = 0ull;
+  named_bar_sync(kBarConsumers, kConsumerThreads);
+  for (uint32_t h = ctid; h < H; h += kConsumerThreads) {
+    const uint64_t key = heads[h];
+    uint32_t rank = 0;
+#pragma unroll 4
+    for (uint32_t i = 0; i < H; ++i) rank += heads[i] > key ? 1u : 0u;  // broadcasts
+    if (rank == F - 1) *lsh = key;
+  }
+  named_bar_sync(kBarConsumers, kConsumerThreads);
+  const uint64_t L = *lsh;
+  const uint64_t lo = L ? L : 1ull;  // zero keys are empty slots
+  uint32_t c = 0;
+  uint64_t k0 = 0ull, k1 = 0ull, k2 = 0ull, k3 = 0ull;
+  const uint64_t* li = lists + static_cast<size_t>(ctid) * Fp;
+  if (static_cast<uint32_t>(ctid) < G) {
+    k0 = __ldcg(li);
+    k1 = __ldcg(li + 1);
+    k2 = __ldcg(li + 2);
+    k3 = __ldcg(li + 3);
+    c = (k0 >= lo) + (k1 >= lo) + (k2 >= lo) + (k3 >= lo);
+    if (c == 4u) {
+      for (uint32_t a = 4; a < Fp; a += 4) {  // Fp is a multiple of 32
+        const uint32_t n = (__ldcg(li + a) >= lo) + (__ldcg(li + a + 1) >= lo) + (__ldcg(li + a + 2) >= lo) +
+                           (__ldcg(li + a + 3) >= lo);
+        c += n;
+        if (n < 4u) break;
+      }
+    }
+  }
+  uint32_t inc = c;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, inc, off);
+    if (lane >= off) inc += y;
+  }
+  if (lane == 31) misc[kMiscRed + warp] = inc;
+  named_bar_sync(kBarConsumers, kConsumerThreads);
+  uint32_t before = 0, S = 0;
+#pragma unroll
+  for (int w = 0; w < kConsumerWarps; ++w) {
+    const uint32_t t = misc[kMiscRed + w];
+    before += w < warp ? t : 0u;
+    S += t;
+  }
+  named_bar_sync(kBarConsumers, kConsumerThreads);  // misc is reused by the sorts
+  if (S > 16u * Fp) return false;
+  const uint32_t off = before + inc - c;
+  if (c > 0u) cand[off] = k0;
+  if (c > 1u) cand[off + 1] = k1;
+  if (c > 2u) cand[off + 2] = k2;
+  if (c > 3u) cand[off + 3] = k3;
+  for (uint32_t j = 4; j < c; ++j) cand[off + j] = __ldcg(li + j);
+  const uint32_t span = S <= Fp ? Fp : 16u * Fp;
+  for (uint32_t i = S + ctid; i < span; i += kConsumerThreads) cand[i] = 0ull;
+  named_bar_sync(kBarConsumers, kConsumerThreads);
+  if (S <= Fp) {
+    warp0_sort_dispatch(Fp, cand, ctid);
+    named_bar_sync(kBarConsumers, kConsumerThreads);
+  } else {
+    cta_best_sorted_dispatch(Fp, cand, S, ctid);
+  }
+  return true;
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 
 // The last CTA of a query finishes it (ScanParams::fold): the best F of every
 // CTA's list (list-head selection, else the full merge), the candidate
 // outputs, the exact f64 re-rank of Store.dotRow (src/store/store.ts:114-130:
 // four lanes j accumulating elements j, j+4, ..., summed ((a0+a1)+a2)+a3, then
-// the tail) read straight from the originals, and the best k
-// (src/index.ts:583-594).  Consumer-collective; qx holds >= dim floats of
-// free shared memory, cand >= 16 * Fp keys.
-static __device__ __noinline__ void finish_query(const ScanParams& p, uint64_t* cand, uint32_t* misc, float* qx,
-                                             int ctid) {
+// the tail), and the best k (src/index.ts:583-594).  The candidates' rows are
+// staged in shared memory by 1-D bulk copies (rows of a multiple of 4 floats;
+// otherwise they are read from global memory), in batches that fit.
+// Consumer-collective; `scratch` is `scratch_bytes` (>= 16 KB, 16-byte
+// aligned) of free shared memory, `bar` an mbarrier whose phase 0 has
+// completed and that nothing else uses now; cand holds >= 16 * Fp keys.
+static __device__ __noinline__ void finish_query(const ScanParams& p, uint64_t* cand, uint32_t* misc,
+                                                 uint8_t* scratch, uint32_t scratch_bytes, uint64_t* bar,
+                                                 int ctid) {
   const int warp = ctid >> 5, lane = ctid & 31;
   const uint32_t G = gridDim.x;
-  if (!select_list_heads<false>(p.partials, G, p.F, p.Fp, cand, misc, ctid))
+  // phase trace of the finishing CTA: the tail kernel's slots after the grid's
+  uint64_t* tr = p.trace && ctid == 0 ? p.trace + static_cast<size_t>(G) * 8 : nullptr;
+  if (tr) tr[0] = globaltimer();
+  const uint32_t mh0 = (p.F + G - 1) / G;
+  const bool heads_fit = static_cast<size_t>(G) * (mh0 < p.Fp ? mh0 : p.Fp) * 8 <= scratch_bytes;
+  if (!(heads_fit && select_list_heads_global(p.partials, G, p.F, p.Fp, cand, misc,
+                                              reinterpret_cast<uint64_t*>(scratch), ctid)))
     merge_cta_lists_dispatch(p.Fp, p.partials, G, cand, ctid);
+  if (tr) tr[1] = globaltimer();
   if (warp == 0) {
     uint32_t c = 0;
     for (uint32_t i = lane; i < p.Fp; i += 32) {
@@ -667,35 +854,49 @@ static __device__ __noinline__ void finish_query(const ScanParams& p, uint64_t* 
   }
   const uint32_t n = nc < p.k ? nc : p.k;
   if (p.rerank) {
+    // scratch: [query: dim floats][staged rows, dim floats each]; a warp
+    // scores one row at a time (dot_row_exact_warp)
+    float* qx = reinterpret_cast<float*>(scratch);
+    const uint32_t qbytes = align_up(p.dim * 4u, 16);
+    float* rows_s = reinterpret_cast<float*>(scratch + qbytes);
+    const uint32_t cap = scratch_bytes > qbytes ? (scratch_bytes - qbytes) / (p.dim * 4u) : 0u;
+    const bool staged = (p.dim & 3u) == 0u && (reinterpret_cast<uintptr_t>(p.originals) & 15u) == 0u && cap > 0u;
+    const uint32_t batch = staged ? cap : (nc > 0u ? nc : 1u);
+    // the head staging above wrote scratch through the generic proxy; the
+    // bulk copies below write it through the async proxy
+    fence_proxy_async_smem();
     for (uint32_t i = ctid; i < p.dim; i += kConsumerThreads) qx[i] = p.query[i];
     uint64_t* ex = cand + p.Fp;
     named_bar_sync(kBarConsumers, kConsumerThreads);
-    const uint32_t vec = p.dim & ~3u;
-    for (uint32_t c0 = 0; c0 < nc; c0 += kConsumerThreads / 4) {
-      const uint32_t c = c0 + static_cast<uint32_t>(ctid) / 4u;
-      const uint32_t j = static_cast<uint32_t>(ctid) & 3u;
-      const bool act = c < nc;
-      const uint32_t row = act ? key_row(cand[c]) : 0u;
-      const float* xr = p.originals + static_cast<size_t>(row) * p.dim;
-      double a = 0.0;
-      if (act) {
-#pragma unroll 8
-        for (uint32_t i = j; i < vec; i += 4)
-          a = __fma_rn(static_cast<double>(__ldg(xr + i)), static_cast<double>(qx[i]), a);
+    uint32_t parity = 1;  // the barrier's phase 0 (the query copy) has completed
+    for (uint32_t c0 = 0; c0 < nc; c0 += batch) {
+      const uint32_t nb = nc - c0 < batch ? nc - c0 : batch;
+      if (staged) {
+        if (warp == 0) {
+          if (lane == 0) mbar_arrive_expect_tx(bar, nb * p.dim * 4u);
+          __syncwarp();
+          for (uint32_t r = lane; r < nb; r += 32)
+            bulk_g2s(rows_s + static_cast<size_t>(r) * p.dim,
+                     p.originals + static_cast<size_t>(key_row(cand[c0 + r])) * p.dim, p.dim * 4u, bar);
+        }
+        mbar_wait_bounded(bar, parity, p.err);
+        if (tr && c0 == 0) tr[3] = globaltimer();
+        parity ^= 1u;
       }
-      const int gl = lane & ~3;
-      const double a0 = __shfl_sync(0xffffffffu, a, gl + 0);
-      const double a1 = __shfl_sync(0xffffffffu, a, gl + 1);
-      const double a2 = __shfl_sync(0xffffffffu, a, gl + 2);
-      const double a3 = __shfl_sync(0xffffffffu, a, gl + 3);
-      if (act && j == 0) {
-        double sacc = __dadd_rn(__dadd_rn(__dadd_rn(a0, a1), a2), a3);
-        for (uint32_t i = vec; i < p.dim; ++i)
-          sacc = __fma_rn(static_cast<double>(xr[i]), static_cast<double>(qx[i]), sacc);
-        ex[c] = make_key(__double2float_rn(sacc), row);
+      for (uint32_t r = static_cast<uint32_t>(warp); r < nb; r += kConsumerWarps) {
+        const uint32_t row = key_row(cand[c0 + r]);
+        const float sc = staged ? dot_row_exact_warp<false>(rows_s + static_cast<size_t>(r) * p.dim, qx, p.dim, lane)
+                                : dot_row_exact_warp<true>(p.originals + static_cast<size_t>(row) * p.dim, qx,
+                                                           p.dim, lane);
+        if (lane == 0) ex[c0 + r] = make_key(sc, row);
+      }
+      if (staged) {  // this batch's rows are read before the next batch's copies land
+        fence_proxy_async_smem();
+        named_bar_sync(kBarConsumers, kConsumerThreads);
       }
     }
     named_bar_sync(kBarConsumers, kConsumerThreads);
+    if (tr) tr[4] = globaltimer();
     if (p.cand_exact)
       for (uint32_t i = ctid; i < nc; i += kConsumerThreads) p.cand_exact[i] = key_score(ex[i]);
     for (uint32_t i = nc + static_cast<uint32_t>(ctid); i < p.Fp; i += kConsumerThreads) ex[i] = 0ull;
@@ -718,6 +919,7 @@ static __device__ __noinline__ void finish_query(const ScanParams& p, uint64_t* 
     *p.out_count = n;
     *p.done = 0u;  // the slot's counter starts from zero at its next use
   }
+  if (tr) tr[2] = globaltimer();
 }
 
 // ------------------------------------------------------------------ kernel
@@ -823,14 +1025,25 @@ __global__ void __launch_bounds__(kScanThreads, MODE == kAsym ? 1 : 2) scan_kern
     named_bar_sync(kBarConsumers, kConsumerThreads);
     float qfac = 1.0f;
     if (fast_rotation(p.P)) {
-      // one warp rotates and codes the query, the others wait at one barrier
-      if (warp == 0) {
-        const float qscale = prologue_warp_dispatch<MODE == kAsym ? 0 : (MODE == kInt ? 1 : 2)>(
-            p.P, q, qb, p.seed, p.sign_scale, p.rounds, lane);
-        if (lane == 0) miscf[kMiscRed] = qscale;
+      // P <= 256: one warp rotates and codes the query; P = 512, 1024: 8 or
+      // 16 warps with three exchanges.  The others wait at one barrier.
+      constexpr int M = MODE == kAsym ? 0 : (MODE == kInt ? 1 : 2);
+      float qscale = 0.0f;
+      bool lead = false;
+      if (p.P == 1024u) {
+        qscale = prologue_multi<4, M>(q, qb, s_signs, miscf + kMiscRed, p.seed, p.sign_scale, p.rounds, warp, lane);
+        lead = ctid == 0;
+      } else if (p.P == 512u) {
+        if (warp < 8)
+          qscale = prologue_multi<3, M>(q, qb, s_signs, miscf + kMiscRed, p.seed, p.sign_scale, p.rounds, warp, lane);
+        lead = ctid == 0;
+      } else if (warp == 0) {
+        qscale = prologue_warp_dispatch<M>(p.P, q, qb, p.seed, p.sign_scale, p.rounds, lane);
+        lead = lane == 0;
       }
+      if (lead) miscf[kMiscQScale] = qscale;
       named_bar_sync(kBarConsumers, kConsumerThreads);
-      if constexpr (MODE == kInt) qfac = __fmul_rn(miscf[kMiscRed], kInv127);
+      if constexpr (MODE == kInt) qfac = __fmul_rn(miscf[kMiscQScale], kInv127);
     } else {
       rotate_query(q, s_signs, p.P, p.rounds, ctid);
       if constexpr (MODE == kInt) {
@@ -1114,7 +1327,7 @@ __global__ void __launch_bounds__(kScanThreads, MODE == kAsym ? 1 : 2) scan_kern
       named_bar_sync(kBarConsumers, kConsumerThreads);
       if (misc[kMiscTicket] == gridDim.x - 1u) {
         __threadfence();
-        finish_query(p, cand, misc, reinterpret_cast<float*>(s_codes), ctid);
+        finish_query(p, cand, misc, s_codes, p.stages * p.tile_bytes, qbar, ctid);
       }
     }
   }

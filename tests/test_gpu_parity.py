@@ -89,9 +89,11 @@ def test_scan_parity(bits, scoring, dim):
 
 
 @pytest.mark.parametrize("bits,dim", [(8, 4), (8, 8), (8, 16), (4, 8), (4, 16), (4, 2048), (8, 2048),
-                                      (8, 4096), (1, 32), (1, 64), (1, 4096), (8, 128)])
+                                      (8, 4096), (1, 32), (1, 64), (1, 4096), (8, 128),
+                                      (8, 37), (4, 250), (1, 70)])
 def test_scan_parity_shapes(bits, dim):
-    """Every lane layout: chunk bytes 4/8/16, lanes 1..32, chunks per lane 1..8."""
+    """Every lane layout: chunk bytes 4/8/16, lanes 1..32, chunks per lane 1..8; dimensions that are
+    not a multiple of 4 (re-rank rows read from global memory instead of staged by bulk copies)."""
     n = 3000
     x = _normal_rows(n, dim, 3000 + dim + bits)
     qs = _normal_rows(3, dim, 4000 + dim)
@@ -187,3 +189,29 @@ def test_c2_shape_parity():
             _check_queries(idx, corpus, qs, 10, 40, scoring)
         finally:
             idx.destroy()
+
+
+@pytest.mark.parametrize("scoring", ["asym", "int"])
+def test_rerank_rounding_boundaries(scoring):
+    """Rows whose exact dot sits on an f32 rounding boundary: the kernels' fast
+    re-rank order must defer to the reference's sequential f64 sum (store.ts:114-130)."""
+    dim = 8
+    rng = np.random.default_rng(21)
+    rows = [rng.standard_normal(dim).astype(np.float32) for _ in range(20)]
+    for tiny in (2.0 ** -60, 2.0 ** -80):
+        for pos in (2, 3):
+            x = np.zeros(dim, np.float32)
+            x[0], x[1], x[pos] = 1.0, 2.0 ** -24, tiny
+            rows.append(x)
+    x = np.stack(rows)
+    n = x.shape[0]
+    q = np.array([[1, 1, 1, 1, 0, 0, 0, 0]], np.float32)
+    idx = _index(dim, 8, scoring)
+    try:
+        idx.append(x, n)
+        _check_queries(idx, O.Corpus(x, dim, 8), q, n, n, scoring)
+        out_rows, out_scores, counts, *_ = idx.search_arrays(q, n, n)
+        for r, s in zip(out_rows[0, :counts[0]], out_scores[0, :counts[0]]):
+            assert np.float32(s).view(np.uint32) == np.float32(O.dot_row(x[r], q[0])).view(np.uint32)
+    finally:
+        idx.destroy()
