@@ -18,7 +18,7 @@ SCORING = {"asym": SCORE_ASYM, "int": SCORE_INT, "hamming": SCORE_HAMMING}
 
 # Every symbol include/browservec.h declares (checked by the CPU test suite).
 EXPORTS = ("bv_create", "bv_destroy", "bv_last_error", "bv_append", "bv_append_device", "bv_size",
-           "bv_search", "bv_search_async", "bv_query_rows_exact", "bv_export_codes", "bv_get_stats",
+           "bv_search", "bv_search_async", "bv_search_async_n", "bv_query_rows_exact", "bv_export_codes", "bv_get_stats",
            "bv_launches_last_search", "bv_set_phase_trace", "bv_search_noalloc",
            "bv_merge_shards", "bv_search_batch", "bv_filter_mask")
 
@@ -90,6 +90,7 @@ def load(path: str = LIB_PATH):
         "bv_size": (C.c_int, [P, C.POINTER(C.c_uint64)]),
         "bv_search": (C.c_int, [P, C.POINTER(BvSearchArgs)]),
         "bv_search_async": (C.c_int, [P, C.POINTER(BvSearchArgs), P]),
+        "bv_search_async_n": (C.c_int, [C.POINTER(P), C.POINTER(BvSearchArgs), C.c_uint32, P]),
         "bv_query_rows_exact": (C.c_int, [P, P, P, C.c_uint32, C.c_uint32, P, P, P]),
         "bv_export_codes": (C.c_int, [P, C.c_uint64, C.c_uint64, P, P]),
         "bv_get_stats": (C.c_int, [P, C.POINTER(BvStats)]),

@@ -114,6 +114,11 @@ struct bv_index {
   int max_smem = 227 * 1024;
   int smem_per_sm = 228 * 1024;
   float last_ms = 0.0f;
+  // TMA descriptor of the originals for the exact flat scan (re-encoded when
+  // the buffer or the row count changes)
+  alignas(64) unsigned char flat_map[128] = {};
+  const float* flat_map_rows = nullptr;
+  uint64_t flat_map_n = 0;
   uint32_t last_launches = 0;
   uint64_t* d_trace = nullptr;   // optional phase-timestamp buffer (caller-owned device memory)
   uint64_t trace_cap = 0;
@@ -387,9 +392,82 @@ int ring_next(bv_index* idx, cudaStream_t s, uint32_t* epoch, uint32_t* slot) {
 
 // Exact fp32 index: per query the flat scan (CTA top lists, WASM-SIMD f32
 // arithmetic) then the tail (merge into the top k; re-rank off).
-int enqueue_flat(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStream_t s) {
+int enqueue_flat(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStream_t s, bool alone) {
   uint32_t Fp = 32;
   while (Fp < F) Fp <<= 1;
+  if (Fp <= 256u && bv::flat_scan_supported(idx->d_orig, idx->dim)) {
+    // TMA-fed scan, finished by its last CTA: one launch per query
+    const uint32_t BR = bv::flat_scan_block_rows();
+    uint32_t capc = 1024;
+    while (capc < 2 * Fp + BR || capc < 16 * Fp) capc <<= 1;
+    const uint32_t check_blocks = (capc - 2 * Fp) / BR;
+    const uint32_t two = static_cast<uint32_t>(idx->smem_per_sm) / 2u - 1024u;
+    uint32_t stages = 0, per_sm = 2;
+    size_t smem = 0;
+    for (uint32_t lim : {two, static_cast<uint32_t>(idx->max_smem)}) {
+      for (uint32_t st = 6; st >= 2 && !stages; --st) {
+        const bv::FlatSmem lay = bv::flat_smem_layout(idx->dim, st, capc);
+        if (lay.total <= lim) {
+          stages = st;
+          smem = lay.total;
+        }
+      }
+      if (stages) break;
+      per_sm = 1;
+    }
+    if (stages && capc <= static_cast<uint32_t>(bv::kSelMax * bv::kConsumerThreads)) {
+      if (idx->flat_map_rows != idx->d_orig || idx->flat_map_n != idx->rows) {
+        cudaError_t e = bv::encode_flat_rows_map(idx->flat_map, idx->d_orig, idx->dim, idx->rows);
+        if (e != cudaSuccess) return cuda_fail(idx, e, "flat scan tensor map");
+        idx->flat_map_rows = idx->d_orig;
+        idx->flat_map_n = idx->rows;
+      }
+      const uint32_t nblocks = static_cast<uint32_t>((idx->rows + BR - 1) / BR);
+      const uint32_t nks = (idx->dim + 31u) / 32u;
+      const uint32_t nsm = static_cast<uint32_t>(idx->num_sms);
+      const uint32_t all = per_sm * nsm;
+      const uint32_t want = alone && a->nq == 1 ? all : (per_sm == 2 ? (nsm / 3u > 0 ? nsm / 3u : 1u) : nsm);
+      const uint32_t grid = nblocks < want ? nblocks : want;
+      int rc = ring_prepare(idx, static_cast<size_t>(nblocks < all ? nblocks : all) * Fp);
+      if (rc) return rc;
+      bv::ScanParams p;
+      memset(&p, 0, sizeof(p));
+      p.mask = a->mask;
+      p.nrows = idx->rows;
+      p.dim = idx->dim;
+      p.stages = stages;
+      p.F = F;
+      p.Fp = Fp;
+      p.capc = capc;
+      p.fold = 1;
+      p.k = a->k;
+      p.rerank = 0;
+      p.originals = idx->d_orig;
+      p.row_base = idx->row_base;
+      p.err = idx->d_err;
+      const bool tracing = idx->d_trace && idx->trace_cap >= (static_cast<uint64_t>(grid) + 1) * 8;
+      p.trace = tracing ? idx->d_trace : nullptr;
+      const bool cand = a->cand_rows && a->cand_scores && a->cand_counts;
+      for (uint32_t q = 0; q < a->nq; ++q) {
+        p.query = a->queries + static_cast<size_t>(q) * idx->dim;
+        uint32_t slot = 0;
+        if ((rc = ring_next(idx, s, &p.epoch, &slot))) return rc;
+        p.tile_ctr = idx->d_tile_ctr + slot;
+        p.done = idx->d_done + slot;
+        p.partials = idx->d_partials + static_cast<size_t>(slot) * idx->partials_slot;
+        p.out_rows = a->out_rows + static_cast<size_t>(q) * a->k;
+        p.out_scores = a->out_scores + static_cast<size_t>(q) * a->k;
+        p.out_count = a->out_counts + q;
+        p.cand_rows = cand ? a->cand_rows + static_cast<size_t>(q) * F : nullptr;
+        p.cand_scores = cand ? a->cand_scores + static_cast<size_t>(q) * F : nullptr;
+        p.cand_count = cand ? a->cand_counts + q : nullptr;
+        cudaError_t e = bv::launch_flat_scan(idx->flat_map, p, nblocks, nks, check_blocks, grid, smem, s);
+        if (e != cudaSuccess) return cuda_fail(idx, e, "flat scan launch");
+      }
+      idx->last_launches = a->nq;
+      return BV_OK;
+    }
+  }
   const uint32_t G = (static_cast<uint32_t>(idx->rows) + bv::flat_rows_per_cta() - 1) / bv::flat_rows_per_cta();
   int rc = ring_prepare(idx, static_cast<size_t>(G) * Fp);
   if (rc) return rc;
@@ -436,7 +514,7 @@ int enqueue_flat(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStream_
 // kernel (CTA candidate lists into the query's ring slot) then the tail kernel
 // (merge + exact re-rank + outputs), chained by programmatic dependent launch.
 int enqueue_search(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStream_t s, bool alone = false) {
-  if (idx->bits == 0) return enqueue_flat(idx, a, F, s);
+  if (idx->bits == 0) return enqueue_flat(idx, a, F, s, alone);
   Plan pl;
   int rc = plan_scan(idx, F, &pl, true, alone && a->nq == 1);
   if (rc) return rc;
@@ -743,6 +821,15 @@ int bv_search_async(bv_index* idx, const bv_search_args* a, void* stream) {
     return BV_OK;
   }
   return enqueue_search(idx, a, F, s);
+}
+
+int bv_search_async_n(bv_index* const* idx, const bv_search_args* args, uint32_t n, void* stream) {
+  if (n && (!idx || !args)) return fail(BV_ERR_INVALID, "null index or args array");
+  for (uint32_t i = 0; i < n; ++i) {
+    const int rc = bv_search_async(idx[i], args + i, stream);
+    if (rc) return rc;
+  }
+  return BV_OK;
 }
 
 int bv_search(bv_index* idx, const bv_search_args* a) {

@@ -96,7 +96,14 @@ inline cudaError_t opt_in_smem(const void* func, size_t need, int* opted) {
   return cudaSuccess;
 }
 
-// bv_flat.cu: exact fp32 flat scan (bits = 0)
+// bv_flat.cu: exact fp32 flat scan (bits = 0).  The TMA-fed scan needs rows
+// of a multiple of 4 floats at a 16-byte aligned base; flat_kernel takes any.
+bool flat_scan_supported(const float* rows, uint32_t dim);
+uint32_t flat_scan_block_rows();
+uint32_t flat_scan_stage_bytes();
+cudaError_t encode_flat_rows_map(void* map128, const float* rows, uint32_t dim, uint64_t nrows);
+cudaError_t launch_flat_scan(const void* map128, const ScanParams& p, uint32_t nblocks, uint32_t nks,
+                             uint32_t check_blocks, unsigned grid, size_t smem, cudaStream_t stream);
 uint32_t flat_rows_per_cta();
 cudaError_t launch_flat(const float* rows, const float* query, const uint32_t* mask, uint32_t nrows, uint32_t dim,
                         uint32_t Fp, uint64_t* partials, cudaStream_t stream);

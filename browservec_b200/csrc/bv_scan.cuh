@@ -154,6 +154,36 @@ __host__ __device__ inline ScanSmem scan_smem_layout(uint32_t tile_bytes, uint32
   return s;
 }
 
+// Shared memory of the exact flat scan (bv_flat.cu), from a 1024-byte aligned
+// base: stages of 128 rows x 32 f32 (16 KB each, swizzled), the query, the
+// barriers, each stage's block and column step, then the candidate buffer,
+// histogram and misc words as in the quantized scan.  `total` includes 1 KB
+// of alignment slack.
+struct FlatSmem {
+  uint32_t rows_off, q_off, bars_off, ids_off, cand_off, hist_off, misc_off, total;
+};
+
+__host__ __device__ inline FlatSmem flat_smem_layout(uint32_t dim, uint32_t stages, uint32_t capc) {
+  FlatSmem s;
+  uint32_t o = 0;
+  s.rows_off = o;
+  o += stages * 16384u;
+  s.q_off = o;
+  o = align_up(o + dim * 4, 16);
+  s.bars_off = o;
+  o = align_up(o + (2 * stages + 1) * 8, 16);
+  s.ids_off = o;
+  o = align_up(o + 2 * stages * 4, 16);
+  s.cand_off = o;
+  o = align_up(o + capc * 8, 16);
+  s.hist_off = o;
+  o = align_up(o + kSelBins * 4, 16);
+  s.misc_off = o;
+  o = align_up(o + 128 * 4, 16);
+  s.total = o + 1024;
+  return s;
+}
+
 // misc word slots
 enum : int { kMiscCount = 0, kMiscNc = 5, kMiscTicket = 6, kMiscQScale = 7, kMiscRed = 16, kMiscSel = 64 };
 
@@ -922,6 +952,91 @@ static __device__ __noinline__ void finish_query(const ScanParams& p, uint64_t* 
   if (tr) tr[2] = globaltimer();
 }
 
+// Consumer-collective, at the same point in every consumer: when more than
+// `high` keys wait in cand, keep the best F and raise the admission threshold
+// `thr` to just below the F-th best, so the next stretch of rows cannot
+// overflow the buffer and no dropped key is re-admitted.
+__device__ __forceinline__ void raise_threshold(uint64_t* cand, uint32_t* hist, uint32_t* misc, uint32_t F,
+                                                uint32_t high, uint64_t& thr, int ctid) {
+  const int warp = ctid >> 5, lane = ctid & 31;
+  float* miscf = reinterpret_cast<float*>(misc);
+  named_bar_sync(kBarConsumers, kConsumerThreads);
+  const uint32_t n = misc[kMiscCount];
+  if (n > high) {  // uniform: every consumer read the same count after the barrier
+    uint64_t v[kSelMax];
+#pragma unroll
+    for (int i = 0; i < kSelMax; ++i) {
+      const uint32_t idx = static_cast<uint32_t>(ctid) + static_cast<uint32_t>(i) * kConsumerThreads;
+      v[i] = idx < n ? cand[idx] : 0ull;
+    }
+    named_bar_sync(kBarConsumers, kConsumerThreads);
+    keep_best<kSelMax>(v, n, F, cand, hist, misc, ctid);
+    // the F-th best key is the smallest kept one; admit only keys above it
+    uint64_t lo = ~0ull;
+    for (uint32_t i = ctid; i < F; i += kConsumerThreads) lo = cand[i] < lo ? cand[i] : lo;
+#pragma unroll
+    for (int off = 16; off; off >>= 1) {
+      const uint64_t o = __shfl_xor_sync(0xffffffffu, lo, off);
+      lo = o < lo ? o : lo;
+    }
+    if (lane == 0) reinterpret_cast<uint64_t*>(miscf + kMiscRed)[warp] = lo;
+    named_bar_sync(kBarConsumers, kConsumerThreads);
+    uint64_t t2 = ~0ull;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) {
+      const uint64_t o = reinterpret_cast<const uint64_t*>(miscf + kMiscRed)[w];
+      t2 = o < t2 ? o : t2;
+    }
+    thr = t2 - 1;  // keys > F-th best - 1, i.e. >= it (never re-admits the dropped ones)
+    named_bar_sync(kBarConsumers, kConsumerThreads);
+  }
+}
+
+// Consumer-collective end of a CTA's scan: its best F keys (sorted for
+// Fp <= 256) into its row of p.partials; with p.fold, the CTA that finishes
+// last takes every list and finishes the query (finish_query, with `scratch`
+// and `bar` as described there).
+__device__ __forceinline__ void cta_publish(const ScanParams& p, uint64_t* cand, uint32_t* hist, uint32_t* misc,
+                                            uint8_t* scratch, uint32_t scratch_bytes, uint64_t* bar, int ctid) {
+  // ---------------------------------------------- best F of this CTA
+  uint32_t n = misc[kMiscCount];
+  if (n > (p.Fp <= 256u ? 16u * p.Fp : p.F)) {  // radix-compact to F first
+    uint64_t v[kSelMax];
+#pragma unroll
+    for (int i = 0; i < kSelMax; ++i) {
+      const uint32_t idx = static_cast<uint32_t>(ctid) + static_cast<uint32_t>(i) * kConsumerThreads;
+      v[i] = idx < n ? cand[idx] : 0ull;
+    }
+    named_bar_sync(kBarConsumers, kConsumerThreads);
+    n = keep_best<kSelMax>(v, n, p.F, cand, hist, misc, ctid);
+  }
+  if (p.Fp <= 256u) {
+    cta_best_sorted_dispatch(p.Fp, cand, n, ctid);
+    if (p.serial) pdl_wait();  // the previous query's tail has read the shared partials
+    for (uint32_t i = ctid; i < p.Fp; i += kConsumerThreads)
+      p.partials[static_cast<size_t>(blockIdx.x) * p.Fp + i] = i < p.F ? cand[i] : 0ull;
+  } else {
+    // wide F: unsorted best F (the last CTA re-selects them)
+    const uint32_t m = n < p.F ? n : p.F;
+    if (p.serial) pdl_wait();
+    for (uint32_t i = ctid; i < p.Fp; i += kConsumerThreads)
+      p.partials[static_cast<size_t>(blockIdx.x) * p.Fp + i] = i < m ? cand[i] : 0ull;
+  }
+  __threadfence();
+  if (p.trace && threadIdx.x == 0) p.trace[blockIdx.x * 8 + kTrCtaMerged] = globaltimer();
+  if (p.fold) {
+    // every thread's list writes are fenced; the CTA that finishes last
+    // sees all lists and finishes the query
+    named_bar_sync(kBarConsumers, kConsumerThreads);
+    if (ctid == 0) misc[kMiscTicket] = atomicAdd(p.done, 1u);
+    named_bar_sync(kBarConsumers, kConsumerThreads);
+    if (misc[kMiscTicket] == gridDim.x - 1u) {
+      __threadfence();
+      finish_query(p, cand, misc, scratch, scratch_bytes, bar, ctid);
+    }
+  }
+}
+
 // ------------------------------------------------------------------ kernel
 // BITS 8/4/1; MODE asym/int/hamming; CB chunk bytes (4, 8 or 16); L lanes per
 // row; CPL chunks per lane; U rows in flight per row-group (asym: even, two
@@ -1257,79 +1372,12 @@ __global__ void __launch_bounds__(kScanThreads, MODE == kAsym ? 1 : 2) scan_kern
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
-      if ((it + 1) % p.check_tiles == 0) {
-        named_bar_sync(kBarConsumers, kConsumerThreads);
-        const uint32_t n = misc[kMiscCount];
-        if (n > high) {  // uniform: every consumer read the same count after the barrier
-          uint64_t v[kSelMax];
-#pragma unroll
-          for (int i = 0; i < kSelMax; ++i) {
-            const uint32_t idx = static_cast<uint32_t>(ctid) + static_cast<uint32_t>(i) * kConsumerThreads;
-            v[i] = idx < n ? cand[idx] : 0ull;
-          }
-          named_bar_sync(kBarConsumers, kConsumerThreads);
-          keep_best<kSelMax>(v, n, p.F, cand, hist, misc, ctid);
-          // the F-th best key is the smallest kept one; admit only keys above it
-          uint64_t lo = ~0ull;
-          for (uint32_t i = ctid; i < p.F; i += kConsumerThreads) lo = cand[i] < lo ? cand[i] : lo;
-#pragma unroll
-          for (int off = 16; off; off >>= 1) {
-            const uint64_t o = __shfl_xor_sync(0xffffffffu, lo, off);
-            lo = o < lo ? o : lo;
-          }
-          if (lane == 0) reinterpret_cast<uint64_t*>(miscf + kMiscRed)[warp] = lo;
-          named_bar_sync(kBarConsumers, kConsumerThreads);
-          uint64_t t2 = ~0ull;
-#pragma unroll
-          for (int w = 0; w < kConsumerWarps; ++w) {
-            const uint64_t o = reinterpret_cast<const uint64_t*>(miscf + kMiscRed)[w];
-            t2 = o < t2 ? o : t2;
-          }
-          thr = t2 - 1;  // keys > F-th best - 1, i.e. >= it (never re-admits the dropped ones)
-          named_bar_sync(kBarConsumers, kConsumerThreads);
-        }
-      }
+      if ((it + 1) % p.check_tiles == 0) raise_threshold(cand, hist, misc, p.F, high, thr, ctid);
     }
     named_bar_sync(kBarConsumers, kConsumerThreads);
     if (p.trace && threadIdx.x == 0) p.trace[blockIdx.x * 8 + kTrScanned] = globaltimer();
 
-    // ---------------------------------------------- best F of this CTA
-    uint32_t n = misc[kMiscCount];
-    if (n > (p.Fp <= 256u ? 16u * p.Fp : p.F)) {  // radix-compact to F first
-      uint64_t v[kSelMax];
-#pragma unroll
-      for (int i = 0; i < kSelMax; ++i) {
-        const uint32_t idx = static_cast<uint32_t>(ctid) + static_cast<uint32_t>(i) * kConsumerThreads;
-        v[i] = idx < n ? cand[idx] : 0ull;
-      }
-      named_bar_sync(kBarConsumers, kConsumerThreads);
-      n = keep_best<kSelMax>(v, n, p.F, cand, hist, misc, ctid);
-    }
-    if (p.Fp <= 256u) {
-      cta_best_sorted_dispatch(p.Fp, cand, n, ctid);
-      if (p.serial) pdl_wait();  // the previous query's tail has read the shared partials
-      for (uint32_t i = ctid; i < p.Fp; i += kConsumerThreads)
-        p.partials[static_cast<size_t>(blockIdx.x) * p.Fp + i] = i < p.F ? cand[i] : 0ull;
-    } else {
-      // wide F: unsorted best F (the last CTA re-selects them)
-      const uint32_t m = n < p.F ? n : p.F;
-      if (p.serial) pdl_wait();
-      for (uint32_t i = ctid; i < p.Fp; i += kConsumerThreads)
-        p.partials[static_cast<size_t>(blockIdx.x) * p.Fp + i] = i < m ? cand[i] : 0ull;
-    }
-    __threadfence();
-    if (p.trace && threadIdx.x == 0) p.trace[blockIdx.x * 8 + kTrCtaMerged] = globaltimer();
-    if (p.fold) {
-      // every thread's list writes are fenced; the CTA that finishes last
-      // sees all lists and finishes the query
-      named_bar_sync(kBarConsumers, kConsumerThreads);
-      if (ctid == 0) misc[kMiscTicket] = atomicAdd(p.done, 1u);
-      named_bar_sync(kBarConsumers, kConsumerThreads);
-      if (misc[kMiscTicket] == gridDim.x - 1u) {
-        __threadfence();
-        finish_query(p, cand, misc, s_codes, p.stages * p.tile_bytes, qbar, ctid);
-      }
-    }
+    cta_publish(p, cand, hist, misc, s_codes, p.stages * p.tile_bytes, qbar, ctid);
   }
 
 }

@@ -252,6 +252,30 @@ class AddonQuantIndex:
             pass
 
 
+class AsyncSearchList:
+    """Device searches submitted together by one bv_search_async_n call.
+
+    entries: (index, q_ptr, k, fetch, rerank, out_rows_ptr, out_scores_ptr, out_counts_ptr) per
+    search, nq = 1 each; the argument array is built once and can be submitted any number of times
+    (the pointers are fixed)."""
+
+    def __init__(self, entries):
+        n = len(entries)
+        if n == 0:
+            raise ValueError("no searches")
+        self.n = n
+        self._keep = [e[0] for e in entries]
+        self._idx = (C.c_void_p * n)(*[e[0]._h.value for e in entries])
+        self._args = (_lib.BvSearchArgs * n)()
+        for i, (ix, q, k, fetch, rerank, r, s, c) in enumerate(entries):
+            self._args[i] = _lib.BvSearchArgs(queries=q, nq=1, k=k, fetch=max(fetch, k), rerank=int(rerank),
+                                              mask=None, mask_words=0, out_rows=r, out_scores=s, out_counts=c)
+        self._L = entries[0][0]._L
+
+    def submit(self, stream: int = 0) -> None:
+        _lib.check(self._L.bv_search_async_n(self._idx, self._args, self.n, C.c_void_p(stream)))
+
+
 @dataclass
 class _Entry:
     id: str

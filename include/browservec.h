@@ -130,6 +130,13 @@ BV_API int bv_search(bv_index* idx, const bv_search_args* args);
  * index's own stream) without a host synchronisation. */
 BV_API int bv_search_async(bv_index* idx, const bv_search_args* args, void* stream);
 
+/* n independent bv_search_async calls in one: entry i searches idx[i] with
+ * args[i] (DEVICE pointers), all enqueued on `stream` in order.  The entries
+ * may name different indexes (the shards or replicas one process serves);
+ * stops at the first failing entry, whose status it returns.  One call
+ * submits a stream of single-query scans without a host round trip each. */
+BV_API int bv_search_async_n(bv_index* const* idx, const bv_search_args* args, uint32_t n, void* stream);
+
 /* BrowserVec.queryRowsExact (src/index.ts:445-464): exact f64-accumulated dot
  * over an explicit list of rows (host pointers), top k.  Used for filters that
  * match at most FILTER_CPU_SCAN_MAX = 4096 rows (src/index.ts:76, :388). */
