@@ -419,13 +419,17 @@ def main():
     ap.add_argument("--sharded-scoring", default=None, choices=["asym", "int", "hamming"],
                     help="scoring of a sharded config (default: the config's)")
     ap.add_argument("--rows", type=int, default=0, help="sharded configs: corpus rows (default: the config's)")
-    ap.add_argument("--queries", type=int, default=0, help="sharded configs: batch size (default: the config's)")
+    ap.add_argument("--queries", type=int, default=0,
+                    help="sharded configs: batch size; single configs: queries per step (default: the config's)")
     ap.add_argument("--per-query", action="store_true",
                     help="sharded configs: per-query scans instead of the batched tensor-core path")
     args = ap.parse_args()
     if args.config in SHARDED:
         return run_sharded(args, args.config)
     _use_single(args.config)
+    if args.queries:  # a shorter step (for ncu captures); the timed line then says so in its config
+        global N_QUERIES
+        N_QUERIES = args.queries
     if BITS == 0:  # the exact index has one scoring
         args.scoring, args.also = "asym", "none"
     corpus_mb = N_ROWS * (DIM * 4 if BITS == 0 else (1 << (DIM - 1).bit_length()) + 4) / 1e6
