@@ -69,6 +69,18 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
       : "r"(taddr)
       : "memory");
 }
+// 128 consecutive 32-bit TMEM columns of this thread's lane (one load, so a
+// tile's 256 columns take two loads and two waits).
+__device__ __forceinline__ void tmem_ld128(uint32_t taddr, uint32_t (&v)[128]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x128.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,%64,%65,%66,%67,%68,%69,%70,%71,%72,%73,%74,%75,%76,%77,%78,%79,%80,%81,%82,%83,%84,%85,%86,%87,%88,%89,%90,%91,%92,%93,%94,%95,%96,%97,%98,%99,%100,%101,%102,%103,%104,%105,%106,%107,%108,%109,%110,%111,%112,%113,%114,%115,%116,%117,%118,%119,%120,%121,%122,%123,%124,%125,%126,%127}, [%128];"
+      : "=r"(v[0]),"=r"(v[1]),"=r"(v[2]),"=r"(v[3]),"=r"(v[4]),"=r"(v[5]),"=r"(v[6]),"=r"(v[7]),"=r"(v[8]),"=r"(v[9]),"=r"(v[10]),"=r"(v[11]),"=r"(v[12]),"=r"(v[13]),"=r"(v[14]),"=r"(v[15]),"=r"(v[16]),"=r"(v[17]),"=r"(v[18]),"=r"(v[19]),"=r"(v[20]),"=r"(v[21]),"=r"(v[22]),"=r"(v[23]),"=r"(v[24]),"=r"(v[25]),"=r"(v[26]),"=r"(v[27]),"=r"(v[28]),"=r"(v[29]),"=r"(v[30]),"=r"(v[31]),"=r"(v[32]),"=r"(v[33]),"=r"(v[34]),"=r"(v[35]),"=r"(v[36]),"=r"(v[37]),"=r"(v[38]),"=r"(v[39]),"=r"(v[40]),"=r"(v[41]),"=r"(v[42]),"=r"(v[43]),"=r"(v[44]),"=r"(v[45]),"=r"(v[46]),"=r"(v[47]),"=r"(v[48]),"=r"(v[49]),"=r"(v[50]),"=r"(v[51]),"=r"(v[52]),"=r"(v[53]),"=r"(v[54]),"=r"(v[55]),"=r"(v[56]),"=r"(v[57]),"=r"(v[58]),"=r"(v[59]),"=r"(v[60]),"=r"(v[61]),"=r"(v[62]),"=r"(v[63]),"=r"(v[64]),"=r"(v[65]),"=r"(v[66]),"=r"(v[67]),"=r"(v[68]),"=r"(v[69]),"=r"(v[70]),"=r"(v[71]),"=r"(v[72]),"=r"(v[73]),"=r"(v[74]),"=r"(v[75]),"=r"(v[76]),"=r"(v[77]),"=r"(v[78]),"=r"(v[79]),"=r"(v[80]),"=r"(v[81]),"=r"(v[82]),"=r"(v[83]),"=r"(v[84]),"=r"(v[85]),"=r"(v[86]),"=r"(v[87]),"=r"(v[88]),"=r"(v[89]),"=r"(v[90]),"=r"(v[91]),"=r"(v[92]),"=r"(v[93]),"=r"(v[94]),"=r"(v[95]),"=r"(v[96]),"=r"(v[97]),"=r"(v[98]),"=r"(v[99]),"=r"(v[100]),"=r"(v[101]),"=r"(v[102]),"=r"(v[103]),"=r"(v[104]),"=r"(v[105]),"=r"(v[106]),"=r"(v[107]),"=r"(v[108]),"=r"(v[109]),"=r"(v[110]),"=r"(v[111]),"=r"(v[112]),"=r"(v[113]),"=r"(v[114]),"=r"(v[115]),"=r"(v[116]),"=r"(v[117]),"=r"(v[118]),"=r"(v[119]),"=r"(v[120]),"=r"(v[121]),"=r"(v[122]),"=r"(v[123]),"=r"(v[124]),"=r"(v[125]),"=r"(v[126]),"=r"(v[127])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld_wait_regs128(uint32_t (&v)[128]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(v[0]),"+r"(v[1]),"+r"(v[2]),"+r"(v[3]),"+r"(v[4]),"+r"(v[5]),"+r"(v[6]),"+r"(v[7]),"+r"(v[8]),"+r"(v[9]),"+r"(v[10]),"+r"(v[11]),"+r"(v[12]),"+r"(v[13]),"+r"(v[14]),"+r"(v[15]),"+r"(v[16]),"+r"(v[17]),"+r"(v[18]),"+r"(v[19]),"+r"(v[20]),"+r"(v[21]),"+r"(v[22]),"+r"(v[23]),"+r"(v[24]),"+r"(v[25]),"+r"(v[26]),"+r"(v[27]),"+r"(v[28]),"+r"(v[29]),"+r"(v[30]),"+r"(v[31]),"+r"(v[32]),"+r"(v[33]),"+r"(v[34]),"+r"(v[35]),"+r"(v[36]),"+r"(v[37]),"+r"(v[38]),"+r"(v[39]),"+r"(v[40]),"+r"(v[41]),"+r"(v[42]),"+r"(v[43]),"+r"(v[44]),"+r"(v[45]),"+r"(v[46]),"+r"(v[47]),"+r"(v[48]),"+r"(v[49]),"+r"(v[50]),"+r"(v[51]),"+r"(v[52]),"+r"(v[53]),"+r"(v[54]),"+r"(v[55]),"+r"(v[56]),"+r"(v[57]),"+r"(v[58]),"+r"(v[59]),"+r"(v[60]),"+r"(v[61]),"+r"(v[62]),"+r"(v[63]),"+r"(v[64]),"+r"(v[65]),"+r"(v[66]),"+r"(v[67]),"+r"(v[68]),"+r"(v[69]),"+r"(v[70]),"+r"(v[71]),"+r"(v[72]),"+r"(v[73]),"+r"(v[74]),"+r"(v[75]),"+r"(v[76]),"+r"(v[77]),"+r"(v[78]),"+r"(v[79]),"+r"(v[80]),"+r"(v[81]),"+r"(v[82]),"+r"(v[83]),"+r"(v[84]),"+r"(v[85]),"+r"(v[86]),"+r"(v[87]),"+r"(v[88]),"+r"(v[89]),"+r"(v[90]),"+r"(v[91]),"+r"(v[92]),"+r"(v[93]),"+r"(v[94]),"+r"(v[95]),"+r"(v[96]),"+r"(v[97]),"+r"(v[98]),"+r"(v[99]),"+r"(v[100]),"+r"(v[101]),"+r"(v[102]),"+r"(v[103]),"+r"(v[104]),"+r"(v[105]),"+r"(v[106]),"+r"(v[107]),"+r"(v[108]),"+r"(v[109]),"+r"(v[110]),"+r"(v[111]),"+r"(v[112]),"+r"(v[113]),"+r"(v[114]),"+r"(v[115]),"+r"(v[116]),"+r"(v[117]),"+r"(v[118]),"+r"(v[119]),"+r"(v[120]),"+r"(v[121]),"+r"(v[122]),"+r"(v[123]),"+r"(v[124]),"+r"(v[125]),"+r"(v[126]),"+r"(v[127])::"memory");
+}
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 // The wait, tied to the registers it makes valid so no use of them can be
 // scheduled above it.
@@ -167,60 +179,75 @@ __global__ void __launch_bounds__(256) scatter_tiles_kernel(const uint32_t* in, 
   out[j] = in[src];
 }
 
-// One CTA per tile, one thread per position: the position's row as int8
-// codes (int4 sign-extended, 1-bit as +-1, zero beyond P) into the tile's K
-// blocks, then the tile maximum of the factors of the positions in use.
+// One CTA per tile; eight threads per position, each writing one 16-byte
+// chunk (16 int8 elements) of the position's row into the tile's K blocks:
+// int8 codes copied 16 bytes at a time, int4 sign-extended, 1-bit as +-1,
+// zero beyond P.  A warp covers four positions, so its loads read whole
+// 128-byte rows and its stores write whole 128-byte tile rows.  Then the tile
+// maximum of the factors of the positions in use.
+template <int BITS>
+__device__ __forceinline__ uint4 expand_chunk(const uint8_t* src, uint32_t e0, uint32_t P, uint32_t R) {
+  // elements e0 .. e0+15 of the row at src (R bytes)
+  if constexpr (BITS == 8) {
+    if (e0 + 16u <= P && (R & 15u) == 0u) return *reinterpret_cast<const uint4*>(src + e0);
+  }
+  alignas(16) int8_t b[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const uint32_t e = e0 + static_cast<uint32_t>(j);
+    int v = 0;
+    if (e < P) {
+      if constexpr (BITS == 8) {
+        v = static_cast<int8_t>(src[e]);
+      } else if constexpr (BITS == 4) {
+        const int n = (src[e >> 1] >> ((e & 1u) * 4u)) & 0xF;
+        v = n > 7 ? n - 16 : n;
+      } else {
+        v = ((src[e >> 3] >> (e & 7u)) & 1u) ? 1 : -1;
+      }
+    }
+    b[j] = static_cast<int8_t>(v);
+  }
+  return *reinterpret_cast<const uint4*>(b);
+}
+
 template <int BITS>
 __global__ void __launch_bounds__(kBRowTile) expand_kernel(const ExpandParams p) {
   const uint32_t tile = p.pos0 / kBRowTile + blockIdx.x;
-  const uint32_t tp = threadIdx.x;
-  const uint32_t pos = tile * kBRowTile + tp;
+  const uint32_t c = threadIdx.x & 7u;  // 16-byte chunk of a 128-byte K block
   __shared__ float red[kBRowTile / 32];
-  if (pos >= p.pos0 && pos < p.pos0 + p.count) {
-    const uint32_t row = p.rows[pos - p.pos0];
-    const uint8_t* src = p.codes + static_cast<size_t>(row) * p.R;
-    p.posfac[pos] = row_factor<BITS>(p.scales[row]);
-    p.posrow[pos] = row;
-    for (uint32_t kb = 0; kb < p.KB; ++kb) {
-      int8_t* dst = p.tiles + (static_cast<size_t>(tile) * p.KB + kb) * kBRowTileBytes;
-      for (uint32_t c = 0; c < 8; ++c) {
-        alignas(16) int8_t b[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const uint32_t e = kb * kKBlock + c * 16 + j;
-          int v = 0;
-          if (e < p.P) {
-            if constexpr (BITS == 8) {
-              v = static_cast<int8_t>(src[e]);
-            } else if constexpr (BITS == 4) {
-              const int n = (src[e >> 1] >> ((e & 1u) * 4u)) & 0xF;
-              v = n > 7 ? n - 16 : n;
-            } else {
-              v = ((src[e >> 3] >> (e & 7u)) & 1u) ? 1 : -1;
-            }
-          }
-          b[j] = static_cast<int8_t>(v);
-        }
-        *reinterpret_cast<uint4*>(dst + sw128_offset(tp, c * 16)) = *reinterpret_cast<const uint4*>(b);
+  for (uint32_t tp = threadIdx.x >> 3; tp < kBRowTile; tp += kBRowTile / 8) {
+    const uint32_t pos = tile * kBRowTile + tp;
+    if (pos >= p.pos0 && pos < p.pos0 + p.count) {
+      const uint32_t row = p.rows[pos - p.pos0];
+      const uint8_t* src = p.codes + static_cast<size_t>(row) * p.R;
+      if (c == 0) {
+        p.posfac[pos] = row_factor<BITS>(p.scales[row]);
+        p.posrow[pos] = row;
       }
-    }
-  } else if (pos >= p.total) {
-    // positions past the end are zeroed so the MMA reads defined values;
-    // positions before pos0 were written by an earlier expansion
-    p.posfac[pos] = 0.0f;
-    for (uint32_t kb = 0; kb < p.KB; ++kb) {
-      int8_t* dst = p.tiles + (static_cast<size_t>(tile) * p.KB + kb) * kBRowTileBytes;
-      for (uint32_t c = 0; c < 8; ++c)
+      for (uint32_t kb = 0; kb < p.KB; ++kb) {
+        int8_t* dst = p.tiles + (static_cast<size_t>(tile) * p.KB + kb) * kBRowTileBytes;
+        *reinterpret_cast<uint4*>(dst + sw128_offset(tp, c * 16)) =
+            expand_chunk<BITS>(src, kb * kKBlock + c * 16, p.P, p.R);
+      }
+    } else if (pos >= p.total) {
+      // positions past the end are zeroed so the MMA reads defined values;
+      // positions before pos0 were written by an earlier expansion
+      if (c == 0) p.posfac[pos] = 0.0f;
+      for (uint32_t kb = 0; kb < p.KB; ++kb) {
+        int8_t* dst = p.tiles + (static_cast<size_t>(tile) * p.KB + kb) * kBRowTileBytes;
         *reinterpret_cast<uint4*>(dst + sw128_offset(tp, c * 16)) = make_uint4(0, 0, 0, 0);
+      }
     }
   }
   __syncthreads();
+  const uint32_t pos = tile * kBRowTile + threadIdx.x;
   float m = pos < p.total ? p.posfac[pos] : 0.0f;
 #pragma unroll
   for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-  if ((tp & 31u) == 0) red[tp >> 5] = m;
+  if ((threadIdx.x & 31u) == 0) red[threadIdx.x >> 5] = m;
   __syncthreads();
-  if (tp == 0) {
+  if (threadIdx.x == 0) {
     float t = 0.0f;
     for (int w = 0; w < static_cast<int>(kBRowTile / 32); ++w) t = fmaxf(t, red[w]);
     p.tmax[tile] = t;
@@ -452,21 +479,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const GemmParams 
           }
         }
       };
-      // two register sets: the next 32 columns load while these are scored
+      // 128 columns per TMEM load: tcgen05.wait::ld waits for every load in
+      // flight, so a few wide loads expose its latency fewer times than many
+      // narrow ones
       const uint32_t taddr = tmem + (lane_base << 16) + buf * kBRowTile;
-      uint32_t va[32], vb[32];
-      tmem_ld32(taddr, va);
-      tmem_ld_wait_regs(va);
 #pragma unroll 1
-      for (uint32_t c0 = 0; c0 < kBRowTile; c0 += 64) {
-        tmem_ld32(taddr + c0 + 32, vb);
-        chunk(va, c0);
-        __syncwarp();
-        tmem_ld_wait_regs(vb);
-        if (c0 + 64 < kBRowTile) tmem_ld32(taddr + c0 + 64, va);
-        chunk(vb, c0 + 32);
-        __syncwarp();
-        if (c0 + 64 < kBRowTile) tmem_ld_wait_regs(va);
+      for (uint32_t h = 0; h < kBRowTile; h += 128) {
+        uint32_t v[128];
+        tmem_ld128(taddr + h, v);
+        tmem_ld_wait_regs128(v);
+#pragma unroll
+        for (uint32_t i = 0; i < 4; ++i) {
+          chunk(*reinterpret_cast<const uint32_t(*)[32]>(&v[32 * i]), h + 32 * i);
+          __syncwarp();
+        }
       }
       tc_fence_before();
       __syncwarp();

@@ -436,7 +436,7 @@ __device__ __forceinline__ float ld_row_f32(const float* p) {
 }
 
 template <bool kGlobal>
-__device__ __forceinline__ float dot_row_exact_warp(const float* x, const float* q, uint32_t dim, int lane) {
+__device__ __noinline__ float dot_row_exact_warp(const float* x, const float* q, uint32_t dim, int lane) {
   double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0, a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
   uint32_t i = static_cast<uint32_t>(lane);
   for (; i + 96u < dim; i += 128u) {
@@ -485,6 +485,74 @@ __device__ __forceinline__ float dot_row_exact_warp(const float* x, const float*
   for (uint32_t k = vec; k < dim; ++k)
     r = __fma_rn(static_cast<double>(ld_row_f32<kGlobal>(x + k)), static_cast<double>(q[k]), r);
   return __double2float_rn(r);
+}
+
+
+// Two rows at once (their latency chains interleave): the same check and
+// fallback per row, with two partial sums per lane and row (lane l takes
+// i = l + 32t; at most dim / 64 + 8 additions per product, within the bound
+// dot_row_exact_warp uses).
+template <bool kGlobal>
+__device__ __forceinline__ float dot_row_check(double s, double a, const float* x, const float* q, uint32_t dim,
+                                               int lane) {
+  const double K1 = static_cast<double>(dim / 4u + 13u);
+  const double B = __dmul_ru(__dmul_ru(a, K1), 0x1p-51);
+  const float lo = __double2float_rn(__dsub_rd(s, B));
+  const float hi = __double2float_rn(__dadd_ru(s, B));
+  if (lo == lo && __float_as_uint(lo) == __float_as_uint(hi)) return lo;  // warp-uniform
+  const uint32_t vec = dim & ~3u;
+  double c = 0.0;
+  if (lane < 4)
+    for (uint32_t k = static_cast<uint32_t>(lane); k < vec; k += 4u)
+      c = __fma_rn(static_cast<double>(ld_row_f32<kGlobal>(x + k)), static_cast<double>(q[k]), c);
+  const double c0 = __shfl_sync(0xffffffffu, c, 0), c1 = __shfl_sync(0xffffffffu, c, 1);
+  const double c2 = __shfl_sync(0xffffffffu, c, 2), c3 = __shfl_sync(0xffffffffu, c, 3);
+  double r = __dadd_rn(__dadd_rn(__dadd_rn(c0, c1), c2), c3);
+  for (uint32_t k = vec; k < dim; ++k)
+    r = __fma_rn(static_cast<double>(ld_row_f32<kGlobal>(x + k)), static_cast<double>(q[k]), r);
+  return __double2float_rn(r);
+}
+
+template <bool kGlobal>
+__device__ __noinline__ void dot_rows2_exact_warp(const float* xa, const float* xb, const float* q, uint32_t dim,
+                                                     int lane, float& ra, float& rb) {
+  double sa0 = 0.0, sa1 = 0.0, aa0 = 0.0, aa1 = 0.0, sb0 = 0.0, sb1 = 0.0, ab0 = 0.0, ab1 = 0.0;
+  uint32_t i = static_cast<uint32_t>(lane);
+  for (; i + 32u < dim; i += 64u) {
+    const double q0 = static_cast<double>(q[i]), q1 = static_cast<double>(q[i + 32u]);
+    const double pa0 = __dmul_rn(static_cast<double>(ld_row_f32<kGlobal>(xa + i)), q0);
+    const double pa1 = __dmul_rn(static_cast<double>(ld_row_f32<kGlobal>(xa + i + 32u)), q1);
+    const double pb0 = __dmul_rn(static_cast<double>(ld_row_f32<kGlobal>(xb + i)), q0);
+    const double pb1 = __dmul_rn(static_cast<double>(ld_row_f32<kGlobal>(xb + i + 32u)), q1);
+    sa0 = __dadd_rn(sa0, pa0);
+    sa1 = __dadd_rn(sa1, pa1);
+    sb0 = __dadd_rn(sb0, pb0);
+    sb1 = __dadd_rn(sb1, pb1);
+    aa0 = __dadd_rn(aa0, fabs(pa0));
+    aa1 = __dadd_rn(aa1, fabs(pa1));
+    ab0 = __dadd_rn(ab0, fabs(pb0));
+    ab1 = __dadd_rn(ab1, fabs(pb1));
+  }
+  if (i < dim) {
+    const double q0 = static_cast<double>(q[i]);
+    const double pa0 = __dmul_rn(static_cast<double>(ld_row_f32<kGlobal>(xa + i)), q0);
+    const double pb0 = __dmul_rn(static_cast<double>(ld_row_f32<kGlobal>(xb + i)), q0);
+    sa0 = __dadd_rn(sa0, pa0);
+    sb0 = __dadd_rn(sb0, pb0);
+    aa0 = __dadd_rn(aa0, fabs(pa0));
+    ab0 = __dadd_rn(ab0, fabs(pb0));
+  }
+  double sa = __dadd_rn(sa0, sa1), aa = __dadd_rn(aa0, aa1);
+  double sb = __dadd_rn(sb0, sb1), ab = __dadd_rn(ab0, ab1);
+#pragma unroll
+  for (int off = 16; off; off >>= 1) {
+    sa = __dadd_rn(sa, __shfl_xor_sync(0xffffffffu, sa, off));
+    sb = __dadd_rn(sb, __shfl_xor_sync(0xffffffffu, sb, off));
+    aa = __dadd_rn(aa, __shfl_xor_sync(0xffffffffu, aa, off));
+    ab = __dadd_rn(ab, __shfl_xor_sync(0xffffffffu, ab, off));
+  }
+  ra = dot_row_check<kGlobal>(sa, aa, xa, q, dim, lane);
+  rb = dot_row_check<kGlobal>(sb, ab, xb, q, dim, lane);
 }
 
 }  // namespace bv

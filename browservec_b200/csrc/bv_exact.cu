@@ -1,6 +1,6 @@
 // bv_exact.cu -- exact scan over an explicit row list (BrowserVec.queryRowsExact,
 // src/index.ts:445-464): the f64-accumulated dot of Store.dotRow
-// (src/store/store.ts:114-130) per row, one warp per row (dot_row_exact_warp:
+// (src/store/store.ts:114-130) per row, two rows a warp (dot_rows2_exact_warp:
 // bit-identical to the lane-ordered sequence), then the best k by
 // (score desc, row asc).  One CTA; used for filters matching <= 4096 rows.
 #include <cstdint>
@@ -20,13 +20,25 @@ __global__ void __launch_bounds__(kExactThreads) exact_rows_kernel(
   extern __shared__ uint64_t keys[];  // npow2
   const int tid = threadIdx.x, lane = tid & 31;
   const int warp = tid >> 5;
-  for (uint32_t c = static_cast<uint32_t>(warp); c < npow2; c += kExactThreads / 32) {  // a warp per row
-    uint64_t kx = 0;
-    if (c < nrows) {
-      const uint32_t row = rows[c];
-      kx = make_key(dot_row_exact_warp<true>(originals + static_cast<size_t>(row) * dim, query, dim, lane), row);
+  constexpr uint32_t W = kExactThreads / 32;
+  for (uint32_t c = static_cast<uint32_t>(warp); c < npow2; c += 2u * W) {  // two rows a warp
+    const uint32_t c2 = c + W;
+    uint64_t ka = 0, kb = 0;
+    if (c2 < nrows) {
+      const uint32_t ra = rows[c], rb = rows[c2];
+      float sa, sb;
+      dot_rows2_exact_warp<true>(originals + static_cast<size_t>(ra) * dim, originals + static_cast<size_t>(rb) * dim,
+                                 query, dim, lane, sa, sb);
+      ka = make_key(sa, ra);
+      kb = make_key(sb, rb);
+    } else if (c < nrows) {
+      const uint32_t ra = rows[c];
+      ka = make_key(dot_row_exact_warp<true>(originals + static_cast<size_t>(ra) * dim, query, dim, lane), ra);
     }
-    if (lane == 0) keys[c] = kx;
+    if (lane == 0) {
+      if (c < npow2) keys[c] = ka;
+      if (c2 < npow2) keys[c2] = kb;
+    }
   }
   __syncthreads();
   // block bitonic sort, descending

@@ -763,7 +763,7 @@ __device__ __forceinline__ bool select_list_heads(const uint64_t* lists, uint32_
 // rounds of memory latency instead of one per head key and per bisection step.
 __device__ __forceinline__ bool select_list_heads_global(const uint64_t* lists, uint32_t G, uint32_t F, uint32_t Fp,
                                                          uint64_t* cand, uint32_t* misc, uint64_t* heads,
-                                                         int ctid) {
+                                                         int ctid, uint64_t* tr = nullptr) {
   const int lane = ctid & 31, warp = ctid >> 5;
   if (G > static_cast<uint32_t>(kConsumerThreads)) return false;
   uint64_t* lsh = reinterpret_cast<uint64_t*>(misc + kMiscSel);
@@ -782,6 +782,7 @@ __device__ __forceinline__ bool select_list_heads_global(const uint64_t* lists, 
     if (rank == F - 1) *lsh = key;
   }
   named_bar_sync(kBarConsumers, kConsumerThreads);
+  if (tr) tr[5] = globaltimer();
   const uint64_t L = *lsh;
   const uint64_t lo = L ? L : 1ull;  // zero keys are empty slots
   uint32_t c = 0;
@@ -828,6 +829,8 @@ __device__ __forceinline__ bool select_list_heads_global(const uint64_t* lists, 
   const uint32_t span = S <= Fp ? Fp : 16u * Fp;
   for (uint32_t i = S + ctid; i < span; i += kConsumerThreads) cand[i] = 0ull;
   named_bar_sync(kBarConsumers, kConsumerThreads);
+  if (tr) tr[6] = globaltimer();
+  if (tr) tr[7] = S;
   if (S <= Fp) {
     warp0_sort_dispatch(Fp, cand, ctid);
     named_bar_sync(kBarConsumers, kConsumerThreads);
@@ -859,10 +862,24 @@ static __device__ __noinline__ void finish_query(const ScanParams& p, uint64_t* 
   // phase trace of the finishing CTA: the tail kernel's slots after the grid's
   uint64_t* tr = p.trace && ctid == 0 ? p.trace + static_cast<size_t>(G) * 8 : nullptr;
   if (tr) tr[0] = globaltimer();
+  // scratch: [query: dim floats][work: the list heads, then the staged rows]
+  float* qx = reinterpret_cast<float*>(scratch);
+  const uint32_t qbytes = align_up(p.dim * 4u, 16);
+  uint8_t* work = scratch + qbytes;
+  const uint32_t work_bytes = scratch_bytes > qbytes ? scratch_bytes - qbytes : 0u;
+  // the query's copy starts now and lands while the lists merge (phase 1 of bar)
+  const bool q_async = p.rerank && (p.dim & 3u) == 0u && (reinterpret_cast<uintptr_t>(p.query) & 15u) == 0u &&
+                       qbytes <= scratch_bytes;
+  if (q_async && ctid == 0) {
+    fence_proxy_async_smem();
+    mbar_arrive_expect_tx(bar, p.dim * 4u);
+    bulk_g2s(qx, p.query, p.dim * 4u, bar);
+  }
   const uint32_t mh0 = (p.F + G - 1) / G;
-  const bool heads_fit = static_cast<size_t>(G) * (mh0 < p.Fp ? mh0 : p.Fp) * 8 <= scratch_bytes;
+  const size_t H0 = static_cast<size_t>(G) * (mh0 < p.Fp ? mh0 : p.Fp);
+  const bool heads_fit = H0 * 8 <= work_bytes;
   if (!(heads_fit && select_list_heads_global(p.partials, G, p.F, p.Fp, cand, misc,
-                                              reinterpret_cast<uint64_t*>(scratch), ctid)))
+                                              reinterpret_cast<uint64_t*>(work), ctid, tr)))
     merge_cta_lists_dispatch(p.Fp, p.partials, G, cand, ctid);
   if (tr) tr[1] = globaltimer();
   if (warp == 0) {
@@ -884,21 +901,24 @@ static __device__ __noinline__ void finish_query(const ScanParams& p, uint64_t* 
   }
   const uint32_t n = nc < p.k ? nc : p.k;
   if (p.rerank) {
-    // scratch: [query: dim floats][staged rows, dim floats each]; a warp
-    // scores one row at a time (dot_row_exact_warp)
-    float* qx = reinterpret_cast<float*>(scratch);
-    const uint32_t qbytes = align_up(p.dim * 4u, 16);
-    float* rows_s = reinterpret_cast<float*>(scratch + qbytes);
-    const uint32_t cap = scratch_bytes > qbytes ? (scratch_bytes - qbytes) / (p.dim * 4u) : 0u;
+    // staged rows (dim floats each) in the work area; a warp scores two rows
+    // at a time (dot_rows2_exact_warp)
+    float* rows_s = reinterpret_cast<float*>(work);
+    const uint32_t cap = work_bytes / (p.dim * 4u);
     const bool staged = (p.dim & 3u) == 0u && (reinterpret_cast<uintptr_t>(p.originals) & 15u) == 0u && cap > 0u;
     const uint32_t batch = staged ? cap : (nc > 0u ? nc : 1u);
-    // the head staging above wrote scratch through the generic proxy; the
-    // bulk copies below write it through the async proxy
+    // the head staging above wrote the work area through the generic proxy;
+    // the bulk copies below write it through the async proxy
     fence_proxy_async_smem();
-    for (uint32_t i = ctid; i < p.dim; i += kConsumerThreads) qx[i] = p.query[i];
+    uint32_t parity = 1;  // the barrier's phase 0 (the scan's query copy) has completed
+    if (q_async) {
+      mbar_wait_bounded(bar, parity, p.err);
+      parity ^= 1u;
+    } else {
+      for (uint32_t i = ctid; i < p.dim; i += kConsumerThreads) qx[i] = p.query[i];
+    }
     uint64_t* ex = cand + p.Fp;
     named_bar_sync(kBarConsumers, kConsumerThreads);
-    uint32_t parity = 1;  // the barrier's phase 0 (the query copy) has completed
     for (uint32_t c0 = 0; c0 < nc; c0 += batch) {
       const uint32_t nb = nc - c0 < batch ? nc - c0 : batch;
       if (staged) {
@@ -913,12 +933,27 @@ static __device__ __noinline__ void finish_query(const ScanParams& p, uint64_t* 
         if (tr && c0 == 0) tr[3] = globaltimer();
         parity ^= 1u;
       }
-      for (uint32_t r = static_cast<uint32_t>(warp); r < nb; r += kConsumerWarps) {
+      for (uint32_t r = static_cast<uint32_t>(warp); r < nb; r += 2u * kConsumerWarps) {
+        const uint32_t r2 = r + kConsumerWarps;
         const uint32_t row = key_row(cand[c0 + r]);
-        const float sc = staged ? dot_row_exact_warp<false>(rows_s + static_cast<size_t>(r) * p.dim, qx, p.dim, lane)
-                                : dot_row_exact_warp<true>(p.originals + static_cast<size_t>(row) * p.dim, qx,
-                                                           p.dim, lane);
-        if (lane == 0) ex[c0 + r] = make_key(sc, row);
+        const float* xa = staged ? rows_s + static_cast<size_t>(r) * p.dim
+                                 : p.originals + static_cast<size_t>(row) * p.dim;
+        if (r2 < nb) {
+          const uint32_t row2 = key_row(cand[c0 + r2]);
+          const float* xb = staged ? rows_s + static_cast<size_t>(r2) * p.dim
+                                   : p.originals + static_cast<size_t>(row2) * p.dim;
+          float sa, sb;
+          if (staged) dot_rows2_exact_warp<false>(xa, xb, qx, p.dim, lane, sa, sb);
+          else dot_rows2_exact_warp<true>(xa, xb, qx, p.dim, lane, sa, sb);
+          if (lane == 0) {
+            ex[c0 + r] = make_key(sa, row);
+            ex[c0 + r2] = make_key(sb, row2);
+          }
+        } else {
+          const float sc = staged ? dot_row_exact_warp<false>(xa, qx, p.dim, lane)
+                                  : dot_row_exact_warp<true>(xa, qx, p.dim, lane);
+          if (lane == 0) ex[c0 + r] = make_key(sc, row);
+        }
       }
       if (staged) {  // this batch's rows are read before the next batch's copies land
         fence_proxy_async_smem();

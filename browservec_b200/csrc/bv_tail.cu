@@ -143,7 +143,7 @@ __global__ void __launch_bounds__(kConsumerThreads, 1) tail_kernel(const TailPar
   const uint32_t n = nc < p.k ? nc : p.k;
   if (p.rerank) {
     // Gather the candidate rows (row stride dim+4 floats), then the exact f64
-    // dot of Store.dotRow, one warp per row (dot_row_exact_warp).
+    // dot of Store.dotRow, two rows a warp (dot_rows2_exact_warp).
     const uint32_t stride = p.dim + 4;
     mbar_wait_bounded(gbar, 0, p.err);
     for (uint32_t i = q_bulk / 4 + ctid; i < p.dim; i += kConsumerThreads) q[i] = query[i];
@@ -173,9 +173,20 @@ __global__ void __launch_bounds__(kConsumerThreads, 1) tail_kernel(const TailPar
         }
       }
       named_bar_sync(kBarConsumers, kConsumerThreads);
-      for (uint32_t c = static_cast<uint32_t>(warp); c < nb; c += kConsumerWarps) {  // a warp per row
-        const float sc = dot_row_exact_warp<false>(rows_s + static_cast<size_t>(c) * stride, q, p.dim, lane);
-        if (lane == 0) ex[c0 + c] = make_key(sc, key_row(cand[c0 + c]));
+      for (uint32_t c = static_cast<uint32_t>(warp); c < nb; c += 2u * kConsumerWarps) {  // two rows a warp
+        const uint32_t c2 = c + kConsumerWarps;
+        if (c2 < nb) {
+          float sa, sb;
+          dot_rows2_exact_warp<false>(rows_s + static_cast<size_t>(c) * stride,
+                                      rows_s + static_cast<size_t>(c2) * stride, q, p.dim, lane, sa, sb);
+          if (lane == 0) {
+            ex[c0 + c] = make_key(sa, key_row(cand[c0 + c]));
+            ex[c0 + c2] = make_key(sb, key_row(cand[c0 + c2]));
+          }
+        } else {
+          const float sc = dot_row_exact_warp<false>(rows_s + static_cast<size_t>(c) * stride, q, p.dim, lane);
+          if (lane == 0) ex[c0 + c] = make_key(sc, key_row(cand[c0 + c]));
+        }
       }
       named_bar_sync(kBarConsumers, kConsumerThreads);
     }

@@ -51,7 +51,27 @@ class QueryResult:
 
 
 def _ptr(a: np.ndarray | None):
-    return None if a is None else a.ctypes.data_as(C.c_void_p)
+    """Address of a contiguous array as an int (c_void_p fields take ints)."""
+    return None if a is None else a.__array_interface__["data"][0]
+
+
+def _outputs(nq: int, k: int, F: int, cand: bool):
+    """The result arrays of one search carved from a single zeroed buffer:
+    (rows[nq,k], scores[nq,k], counts[nq]) and, with cand, (cand_rows[nq,F],
+    cand_scores[nq,F], cand_counts[nq]) -- with their addresses."""
+    sizes = [nq * k, nq * k, nq] + ([nq * F, nq * F, nq] if cand else [])
+    buf = np.zeros(sum(sizes), np.uint32)
+    base = _ptr(buf)
+    arrs, addrs, off = [], [], 0
+    shapes = [(nq, k), (nq, k), (nq,), (nq, F), (nq, F), (nq,)]
+    for i, n in enumerate(sizes):
+        a = buf[off:off + n]
+        if i % 3 == 1:
+            a = a.view(np.float32)
+        arrs.append(a.reshape(shapes[i]))
+        addrs.append(base + 4 * off)
+        off += n
+    return arrs, addrs
 
 
 def normalize_rows(m: np.ndarray) -> np.ndarray:
@@ -129,11 +149,10 @@ class AddonQuantIndex:
         qs = np.ascontiguousarray(qs, dtype=np.float32).reshape(-1, self.dim)
         nq = qs.shape[0]
         F = max(fetch, k)
-        out_rows = np.zeros((nq, k), np.uint32)
-        out_scores = np.zeros((nq, k), np.float32)
-        out_counts = np.zeros(nq, np.uint32)
-        cand = (np.zeros((nq, F), np.uint32), np.zeros((nq, F), np.float32), np.zeros(nq, np.uint32)) \
-            if with_candidates else (None, None, None)
+        o, a = _outputs(nq, k, F, with_candidates)
+        out_rows, out_scores, out_counts = o[:3]
+        cand = tuple(o[3:]) if with_candidates else (None, None, None)
+        ca = a[3:] if with_candidates else (None, None, None)
         m = None if mask is None else np.ascontiguousarray(mask, dtype=np.uint32)
         if m is not None:
             need = (self.size + 31) // 32
@@ -141,9 +160,8 @@ class AddonQuantIndex:
                 raise ValueError(f"mask has {m.size} words, need {need} for {self.size} rows")
         args = _lib.BvSearchArgs(queries=_ptr(qs), nq=nq, k=k, fetch=F, rerank=int(rerank),
                                  mask=_ptr(m), mask_words=0 if m is None else m.size,
-                                 out_rows=_ptr(out_rows), out_scores=_ptr(out_scores),
-                                 out_counts=_ptr(out_counts), cand_rows=_ptr(cand[0]),
-                                 cand_scores=_ptr(cand[1]), cand_counts=_ptr(cand[2]))
+                                 out_rows=a[0], out_scores=a[1], out_counts=a[2], cand_rows=ca[0],
+                                 cand_scores=ca[1], cand_counts=ca[2])
         _lib.check(self._L.bv_search(self._h, C.byref(args)))
         hits = [[FlatHit(int(out_rows[i, j]), float(out_scores[i, j])) for j in range(int(out_counts[i]))]
                 for i in range(nq)]
@@ -158,13 +176,12 @@ class AddonQuantIndex:
         qs = np.ascontiguousarray(qs, dtype=np.float32).reshape(-1, self.dim)
         nq = qs.shape[0]
         F = max(fetch, k)
-        o = [np.zeros((nq, k), np.uint32), np.zeros((nq, k), np.float32), np.zeros(nq, np.uint32),
-             np.zeros((nq, F), np.uint32), np.zeros((nq, F), np.float32), np.zeros(nq, np.uint32)]
+        o, a = _outputs(nq, k, F, True)
         m = None if mask is None else np.ascontiguousarray(mask, dtype=np.uint32)
         args = _lib.BvSearchArgs(queries=_ptr(qs), nq=nq, k=k, fetch=F, rerank=int(rerank),
                                  mask=_ptr(m), mask_words=0 if m is None else m.size,
-                                 out_rows=_ptr(o[0]), out_scores=_ptr(o[1]), out_counts=_ptr(o[2]),
-                                 cand_rows=_ptr(o[3]), cand_scores=_ptr(o[4]), cand_counts=_ptr(o[5]))
+                                 out_rows=a[0], out_scores=a[1], out_counts=a[2],
+                                 cand_rows=a[3], cand_scores=a[4], cand_counts=a[5])
         _lib.check(self._L.bv_search(self._h, C.byref(args)))
         return tuple(o)
 

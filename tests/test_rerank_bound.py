@@ -14,26 +14,31 @@ import numpy as np
 from oracle import oracle as O
 
 
-def fast_dot(x, q):
-    """The warp order of dot_row_exact_warp: lane l, four interleaved partial sums, butterfly."""
+def fast_dot(x, q, nacc=4):
+    """The warp orders of dot_row_exact_warp (nacc 4: four interleaved partial sums per lane) and
+    dot_rows2_exact_warp (nacc 2): lane l takes i = l + 32t, then a butterfly."""
     dim = x.size
     p = x.astype(np.float64) * q.astype(np.float64)  # exact products
     lanes_s, lanes_a = [], []
     for lane in range(32):
-        s = [0.0, 0.0, 0.0, 0.0]
-        a = [0.0, 0.0, 0.0, 0.0]
+        s = [0.0] * nacc
+        a = [0.0] * nacc
         i = lane
-        while i + 96 < dim:
-            for r in range(4):
+        while i + 32 * (nacc - 1) < dim:
+            for r in range(nacc):
                 s[r] = s[r] + p[i + 32 * r]
                 a[r] = a[r] + abs(p[i + 32 * r])
-            i += 128
+            i += 32 * nacc
         while i < dim:
             s[0] = s[0] + p[i]
             a[0] = a[0] + abs(p[i])
             i += 32
-        lanes_s.append((s[0] + s[1]) + (s[2] + s[3]))
-        lanes_a.append((a[0] + a[1]) + (a[2] + a[3]))
+        if nacc == 4:
+            lanes_s.append((s[0] + s[1]) + (s[2] + s[3]))
+            lanes_a.append((a[0] + a[1]) + (a[2] + a[3]))
+        else:
+            lanes_s.append(s[0] + s[1])
+            lanes_a.append(a[0] + a[1])
     off = 16
     while off:
         lanes_s = [lanes_s[l] + lanes_s[l ^ off] for l in range(32)]
@@ -57,11 +62,13 @@ def test_fast_path_agrees_with_dot_row():
         for _ in range(40):
             x = rng.standard_normal(dim).astype(np.float32)
             q = rng.standard_normal(dim).astype(np.float32)
-            got = fast_dot(x, q)
-            if got is not None:
-                accepted += 1
-                assert got.view(np.uint32) == np.float32(O.dot_row(x, q)).view(np.uint32)
-    assert accepted > 500  # the fast path is the common case
+            want = np.float32(O.dot_row(x, q)).view(np.uint32)
+            for nacc in (4, 2):
+                got = fast_dot(x, q, nacc)
+                if got is not None:
+                    accepted += 1
+                    assert got.view(np.uint32) == want
+    assert accepted > 1000  # the fast path is the common case
 
 
 def test_rounding_boundary_rows_fall_back():
@@ -74,4 +81,4 @@ def test_rounding_boundary_rows_fall_back():
             x[0], x[1], x[pos] = 1.0, 2.0 ** -24, tiny
             ref = np.float32(O.dot_row(x, q))
             assert ref == np.float32(1.0)
-            assert fast_dot(x, q) is None  # the interval straddles the midpoint
+            assert fast_dot(x, q, 4) is None and fast_dot(x, q, 2) is None  # the interval straddles the midpoint
