@@ -322,7 +322,11 @@ int plan_scan(bv_index* idx, uint32_t F, Plan* pl, bool fold = true, bool alone 
   const bool two_per_sm = pl->fold && pl->smem <= limit && idx->scoring != BV_SCORE_ASYM;
   const uint32_t nsm = static_cast<uint32_t>(idx->num_sms);
   const uint32_t all = two_per_sm ? 2u * nsm : pl->fold ? nsm : (nsm > 2 ? nsm - 2u : 1u);
-  const uint32_t sms = two_per_sm && !alone ? (nsm / 3u > 0 ? nsm / 3u : 1u) : all;
+  // One CTA per SM (asym, or wide F with the tail kernel): back to back, a
+  // query takes two sevenths of the SMs (asym, 100k x 768 int8: 146 CTAs
+  // 27.0k q/s, 74 28.2k, 49 31.7k, 42 33.1k, 37 32.8k, 29 28.1k).
+  const uint32_t one_sm = nsm * 2u / 7u > 0 ? nsm * 2u / 7u : 1u;
+  const uint32_t sms = alone ? all : two_per_sm ? (nsm / 3u > 0 ? nsm / 3u : 1u) : (pl->fold ? all : one_sm);
   pl->grid = pl->ntiles < sms ? pl->ntiles : sms;
   pl->slots = pl->ntiles < all ? pl->ntiles : all;
   return BV_OK;
