@@ -142,8 +142,9 @@ __global__ void __launch_bounds__(kConsumerThreads, 1) tail_kernel(const TailPar
 
   const uint32_t n = nc < p.k ? nc : p.k;
   if (p.rerank) {
-    // Gather the candidate rows (row stride dim+4 floats), then the exact f64
-    // dot of Store.dotRow, two rows a warp (dot_rows2_exact_warp).
+    // Gather the candidate rows (row stride dim+4 floats, conflict-free for
+    // the four-thread groups), then the exact f64 dot of Store.dotRow: in a
+    // batch four threads per row, alone two rows a warp (dot_rows2_exact_warp).
     const uint32_t stride = p.dim + 4;
     mbar_wait_bounded(gbar, 0, p.err);
     for (uint32_t i = q_bulk / 4 + ctid; i < p.dim; i += kConsumerThreads) q[i] = query[i];
@@ -173,6 +174,37 @@ __global__ void __launch_bounds__(kConsumerThreads, 1) tail_kernel(const TailPar
         }
       }
       named_bar_sync(kBarConsumers, kConsumerThreads);
+      if (gridDim.x > 1) {
+        // a batch (one CTA per query, many CTAs per SM): four threads per row
+        // run Store.dotRow's four f64 lanes in order, the fewest operations
+        // per element; the warp form below trades operations for latency
+        const uint32_t vec = p.dim & ~3u;
+        for (uint32_t cc = 0; cc < nb; cc += kConsumerThreads / 4) {
+          const uint32_t c = cc + static_cast<uint32_t>(ctid) / 4u;
+          const uint32_t j = static_cast<uint32_t>(ctid) & 3u;
+          const bool act = c < nb;
+          const float* xr = rows_s + static_cast<size_t>(act ? c : 0u) * stride;
+          double a = 0.0;
+          if (act) {
+#pragma unroll 8
+            for (uint32_t i = j; i < vec; i += 4)
+              a = __fma_rn(static_cast<double>(xr[i]), static_cast<double>(q[i]), a);
+          }
+          const int gl = lane & ~3;
+          const double a0 = __shfl_sync(0xffffffffu, a, gl + 0);
+          const double a1 = __shfl_sync(0xffffffffu, a, gl + 1);
+          const double a2 = __shfl_sync(0xffffffffu, a, gl + 2);
+          const double a3 = __shfl_sync(0xffffffffu, a, gl + 3);
+          if (act && j == 0) {
+            double sacc = __dadd_rn(__dadd_rn(__dadd_rn(a0, a1), a2), a3);
+            for (uint32_t i = vec; i < p.dim; ++i)
+              sacc = __fma_rn(static_cast<double>(xr[i]), static_cast<double>(q[i]), sacc);
+            ex[c0 + c] = make_key(__double2float_rn(sacc), key_row(cand[c0 + c]));
+          }
+        }
+        named_bar_sync(kBarConsumers, kConsumerThreads);
+        continue;
+      }
       for (uint32_t c = static_cast<uint32_t>(warp); c < nb; c += 2u * kConsumerWarps) {  // two rows a warp
         const uint32_t c2 = c + kConsumerWarps;
         if (c2 < nb) {
