@@ -1353,8 +1353,11 @@ int bv_search_batch(bv_index* idx, const bv_search_args* a, void* stream) {
   t.cand_exact = cand ? a->cand_exact : nullptr;
   const uint32_t row_bytes = (idx->dim + 4) * 4;
   const uint32_t fixed = bv::tail_smem_layout(idx->dim, t.capc, 0).total + 256;
-  uint32_t rows_bytes =
-      static_cast<uint32_t>(idx->max_smem) > fixed ? static_cast<uint32_t>(idx->max_smem) - fixed : 0;
+  // the batch's tail CTAs run two per SM: each stages rows in at most half
+  // of the SM's shared memory (more batches of rows), when one row fits
+  const uint32_t half = static_cast<uint32_t>(idx->smem_per_sm) / 2u - 1024u;
+  const uint32_t lim = half >= fixed + row_bytes ? half : static_cast<uint32_t>(idx->max_smem);
+  uint32_t rows_bytes = lim > fixed ? lim - fixed : 0;
   if (rows_bytes > F * row_bytes) rows_bytes = F * row_bytes;
   rows_bytes = rows_bytes / row_bytes * row_bytes;
   if (rows_bytes < row_bytes) return fail(BV_ERR_UNSUPPORTED, "re-rank row does not fit in shared memory");

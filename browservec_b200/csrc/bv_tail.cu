@@ -16,7 +16,11 @@
 
 namespace bv {
 
-__global__ void __launch_bounds__(kConsumerThreads, 1) tail_kernel(const TailParams p) {
+// MINB CTAs per SM: 1 for the tail of a single query (latency), 2 for a
+// batch's one CTA per query (two CTAs share an SM, so one's memory waits
+// overlap the other's work).
+template <int MINB>
+__global__ void __launch_bounds__(kConsumerThreads, MINB) tail_kernel(const TailParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   // CTA b of a batched launch serves query b: its own partials, query and outputs
   const size_t b = blockIdx.x;
@@ -257,15 +261,15 @@ __global__ void __launch_bounds__(kConsumerThreads, 1) tail_kernel(const TailPar
 
 cudaError_t launch_tail_grid(const TailParams& p, uint32_t nq, size_t smem, cudaStream_t stream) {
   static int opted[kMaxDevices] = {};
-  const cudaError_t e = opt_in_smem(reinterpret_cast<const void*>(tail_kernel), smem, opted);
+  const cudaError_t e = opt_in_smem(reinterpret_cast<const void*>(tail_kernel<2>), smem, opted);
   if (e != cudaSuccess) return e;
-  tail_kernel<<<nq, kConsumerThreads, smem, stream>>>(p);
+  tail_kernel<2><<<nq, kConsumerThreads, smem, stream>>>(p);
   return cudaGetLastError();
 }
 
 cudaError_t launch_tail(const TailParams& p, size_t smem, cudaStream_t stream) {
   static int opted[kMaxDevices] = {};
-  const cudaError_t e = opt_in_smem(reinterpret_cast<const void*>(tail_kernel), smem, opted);
+  const cudaError_t e = opt_in_smem(reinterpret_cast<const void*>(tail_kernel<1>), smem, opted);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(1);
@@ -277,7 +281,7 @@ cudaError_t launch_tail(const TailParams& p, size_t smem, cudaStream_t stream) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, tail_kernel, p);
+  return cudaLaunchKernelEx(&cfg, tail_kernel<1>, p);
 }
 
 }  // namespace bv
