@@ -504,7 +504,12 @@ __global__ void __launch_bounds__(kConsumerThreads, 1) select_kernel(const Selec
   for (uint32_t i = ctid; i < p.Fp; i += kConsumerThreads) kept[i] = 0ull;
   named_bar_sync(kBarConsumers, kConsumerThreads);
   const uint32_t n = keep_best<MAXK>(v, total, p.F, kept, hist, misc, ctid);
-  cta_sort_desc(kept, p.Fp, ctid);
+  if (p.Fp <= 256u) {  // one warp sorts the kept keys in registers, no block barriers
+    warp0_sort_dispatch(p.Fp, kept, ctid);
+    named_bar_sync(kBarConsumers, kConsumerThreads);
+  } else {
+    cta_sort_desc(kept, p.Fp, ctid);
+  }
   for (uint32_t i = ctid; i < p.Fp; i += kConsumerThreads) c[i] = kept[i];
   if (ctid == 0) {
     p.cnt[qi] = n;
