@@ -1418,9 +1418,10 @@ namespace {
 constexpr uint32_t kNoAllocMaxCtas = 160;  // scan grid bound (one CTA per SM, minus one)
 constexpr uint32_t kNoAllocMaxFp = 256;    // candidate slots per CTA: fetch <= 256
 constexpr size_t kNoAllocKeys = static_cast<size_t>(kNoAllocMaxCtas) * kNoAllocMaxFp;
-constexpr size_t kNoAllocCtr = kNoAllocKeys;      // 4 rotating tile counters
-constexpr size_t kNoAllocErr = kNoAllocKeys + 4;  // kernel error word
-constexpr size_t kNoAllocWords = kNoAllocKeys + 5;
+constexpr uint32_t kNoAllocSlots = 64;            // rotating tile counters (one per query in flight)
+constexpr size_t kNoAllocCtr = kNoAllocKeys;
+constexpr size_t kNoAllocErr = kNoAllocKeys + kNoAllocSlots;  // kernel error word
+constexpr size_t kNoAllocWords = kNoAllocErr + 1;
 
 struct NoAllocDevice {
   bool ready = false;
@@ -1440,6 +1441,9 @@ extern "C" int bv_search_noalloc(bv_index* idx, const bv_search_args* a, void* s
   uint32_t F = 0;
   int rc = check_args(idx, a, &F);
   if (rc) return rc;
+  // the exact fp32 index (bits 0) has no codes for the quantized scan
+  if (idx->bits == 0)
+    return fail(BV_ERR_UNSUPPORTED, "bv_search_noalloc: serves quantized indexes only (bits 1, 4, 8), not bits 0");
   uint32_t fp = 32;
   while (fp < F) fp <<= 1;
   if (fp > kNoAllocMaxFp)
@@ -1471,6 +1475,7 @@ extern "C" int bv_search_noalloc(bv_index* idx, const bv_search_args* a, void* s
   }
   if (idx->rows == 0 || a->nq == 0) {
     if (a->nq) BV_CUDA(idx, cudaMemsetAsync(a->out_counts, 0, a->nq * 4, s), "memset");
+    if (a->nq && a->cand_counts) BV_CUDA(idx, cudaMemsetAsync(a->cand_counts, 0, a->nq * 4, s), "memset");
     BV_CUDA(idx, cudaStreamSynchronize(s), "sync");
     idx->last_launches = 0;
     return BV_OK;
@@ -1532,9 +1537,17 @@ extern "C" int bv_search_noalloc(bv_index* idx, const bv_search_args* a, void* s
   const size_t tail_smem = bv::tail_smem_layout(idx->dim, pl.capc, rows_bytes).total;
 
   for (uint32_t q = 0; q < a->nq; ++q) {
+    // Each scan lets the next kernels launch at its start (programmatic
+    // dependent launch), so on a small grid later queries' scans can run while
+    // this one still takes tiles.  Queries q and q + kNoAllocSlots share a
+    // counter: before reusing the slots, the stream waits for all earlier work.
+    if (q && q % kNoAllocSlots == 0) {
+      BV_CUDA(idx, cudaEventRecord(idx->ev_ring, s), "slot event");
+      BV_CUDA(idx, cudaStreamWaitEvent(s, idx->ev_ring, 0), "slot wait");
+    }
     p.query = a->queries + static_cast<size_t>(q) * idx->dim;
     p.epoch = epoch0 + q + 1;  // unique per device; the array starts zeroed (epoch 0)
-    p.tile_ctr = base + kNoAllocCtr + (p.epoch & 3u);
+    p.tile_ctr = base + kNoAllocCtr + (epoch0 + q) % kNoAllocSlots;
     cudaError_t e = launch_scan(static_cast<int>(idx->bits), static_cast<int>(idx->scoring), pl.sh, p,
                                 pl.grid, pl.smem, s);
     if (e == cudaErrorNotSupported)

@@ -252,8 +252,10 @@ BV_API int bv_filter_mask(const bv_column* cols, uint32_t ncols, const bv_filter
  * owns queries and outputs), but all scratch of the scan and tail kernels lives
  * in one fixed array inside this library: 160 x 256 candidate keys plus a few
  * counters, about 320 KB on every GPU that loads the library, held until the
- * process exits.  Limits: fetch = max(fetch, k) <= 256 (BV_ERR_INVALID above
- * that) and a scan grid of at most 160 CTAs (BV_ERR_UNSUPPORTED otherwise).
+ * process exits.  Limits: quantized indexes only (bits 1, 4 or 8; an exact
+ * fp32 index, bits 0, gets BV_ERR_UNSUPPORTED), fetch = max(fetch, k) <= 256
+ * (BV_ERR_INVALID above that) and a scan grid of at most 160 CTAs
+ * (BV_ERR_UNSUPPORTED otherwise).
  * The first call on a device looks up the array's device address with that
  * device current; make that first call before any stream capture.  Every call
  * on a device shares the one array, so calls that overlap on the GPU (other

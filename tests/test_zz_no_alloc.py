@@ -78,6 +78,57 @@ def test_noalloc_matches_search_async(bits, scoring, fetch):
         idx.destroy()
 
 
+@pytest.mark.parametrize("bits,scoring,mode", [(8, "asym", 0), (8, "int", 1), (1, "hamming", 2)])
+def test_noalloc_small_grid_many_queries_matches_oracle(bits, scoring, mode):
+    """About 2,000 rows give a scan grid of a few CTAs, so several of the
+    call's queries are in flight at once and share tile counters in turn;
+    70 queries also wrap the counter rotation once.  Checked against the
+    CPU oracle (rows and exact scores) and against bv_search_async."""
+    import torch
+    from browservec_b200.index import AddonQuantIndex
+    from oracle import oracle as O
+
+    n, d, k, fetch, nq = 2048, 64, 10, 40, 70
+    x = _rows(n, d, 21)
+    idx = AddonQuantIndex(d, seed=0x9E3779B9, rounds=2, bits=bits, scoring=scoring)
+    try:
+        idx.append(x, n)
+        corpus = O.Corpus(x, d, bits)
+        stream = torch.cuda.Stream()
+        for call in range(2):
+            qn = _rows(nq, d, 300 + call)
+            q = torch.from_numpy(qn).cuda()
+            want = _search(idx._L.bv_search_async, idx, q, k, fetch, stream)
+            got = _search(idx._L.bv_search_noalloc, idx, q, k, fetch, stream)
+            for a, b in zip(got, want):
+                assert np.array_equal(np.asarray(a).view(np.uint32), np.asarray(b).view(np.uint32)), call
+            gr, gs, gc, gcr, gcs, gcc = got
+            for i in range(0, nq, 7):
+                wr, ws, wcr, wcs = corpus.query(qn[i], k, fetch, mode)
+                assert int(gcc[i]) == wcr.size and np.array_equal(gcr[i, : wcr.size].astype(np.uint32), wcr)
+                assert np.array_equal(gcs[i, : wcr.size].view(np.uint32), wcs.view(np.uint32)), (call, i)
+                assert int(gc[i]) == wr.size and np.array_equal(gr[i, : wr.size].astype(np.uint32), wr)
+                np.testing.assert_allclose(gs[i, : wr.size], ws, rtol=RERANK_RTOL, atol=0)
+    finally:
+        idx.destroy()
+
+
+def test_noalloc_rejects_exact_index():
+    """An exact fp32 index (bits 0) holds no codes: refused before any launch."""
+    import torch
+    from browservec_b200 import _lib
+    from browservec_b200.index import AddonQuantIndex
+
+    idx = AddonQuantIndex(64, seed=1, rounds=2, bits=0, scoring="asym")
+    try:
+        idx.append(_rows(500, 64, 5), 500)
+        q = torch.from_numpy(_rows(1, 64, 6)).cuda()
+        with pytest.raises(_lib.BvError, match="quantized indexes only"):
+            _search(idx._L.bv_search_noalloc, idx, q, 10, 40, torch.cuda.Stream())
+    finally:
+        idx.destroy()
+
+
 def test_noalloc_rejects_fetch_above_limit():
     import torch
     from browservec_b200 import _lib
