@@ -1,25 +1,31 @@
-"""Benchmark of the quantized flat-scan path on BASELINE config 2.
+"""Benchmark of the quantized flat-scan path (default).
 
-Workload: TurboQuant int8, N=100,000 rows, d=768
-(P=1024), i.i.d. N(0,1) rows L2-normalised (seed 2), cosine, 1,000 queries
-issued one at a time, k=10, 4x oversample (F=40) re-ranked in exact fp32.
-A step is the 1,000 queries; each query is one scan launch.
+Default workload (the largest configuration and the
+one with 1/2/4/8-GPU numbers): 1-bit codes, N=10,000,000 rows, d=768 (P=1024,
+128 B of sign bits per row), a 1,024-centre Gaussian mixture (sigma 0.3),
+L2-normalised, seed 4; queryBatch of 1,000 queries from the same mixture;
+cosine; k=100 with a 10x oversample (F=1,000) re-ranked in exact fp32.  The
+rows are split evenly across the GPUs (one process per GPU, NCCL); a step is
+the whole batch: prep, the tcgen05 kind::i8 GEMM + select rounds, (N > 1) one
+all-gather of the shards' candidate keys and the global F-th key, the exact
+re-rank of each shard's members of the global best F, one all-gather of the
+shard records and the merge.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--config c1|c2|c3|c4|c5]
 
-value  : queries/s with corpus and queries resident in HBM (device timed,
+value  : queries/s of the whole job, inputs resident in HBM (device timed with
          CUDA events on the launch stream, max over ranks).
-e2e    : queries/s through the public host API (AddonQuantIndex.search ->
-         bv_search): per query a pinned H2D of the query, the scan, a D2H of
-         the k results and a host synchronisation.
-L2     : the 102.8 MB corpus would fit in the 126 MB L2, so the index is
-         replicated (4 replicas, 411 MB) and query i scans replica i % 4: each
-         scan reads a corpus that 3 other scans (308 MB) evicted.
-N > 1  : one process per GPU, each serving its own replicas and query stream
-         (replicas only: config 2 does not shard), weak scaling.
---impl reference: the reference's CPU path for this workload -- the WASM-SIMD
-         exact fp32 flat scan (src/fallback/kernel.wat + CpuIndex.query),
-         restated in C (oracle/), on all host threads, bounded query sample.
+e2e    : the same through the public API with host buffers: per step a pinned
+         H2D of the batch, the search, a D2H of the results.
+roofline: the dominant kernel (the GEMM for the batched configs), its
+         algorithmic int8 ops over its own event-timed duration.
+--impl reference: the reference's CPU path for the workload -- the WASM-SIMD
+         exact fp32 flat scan + topK (src/fallback/kernel.wat, cpu.ts:66-88),
+         restated in C (oracle/), one CpuIndex per row shard of at most
+         3.5 GiB merged with mergePartials (gpuTopk.ts:160-189), on all host
+         threads, a bounded query sample per step.
+Single-query configs (c1, c2) keep their own flow (see run_single).
 """
 from __future__ import annotations
 
@@ -226,26 +232,72 @@ def _unpack(torch, words, n):
     return bits.reshape(-1)[:n].bool()
 
 
-def _cpu_sample_qps(torch, dev, cfg, threads, sample_rows, sample_queries):
-    """The reference CPU path (WASM-SIMD exact fp32 scan + topK, restated in C)
-    over the first `sample_rows` rows, scaled to the full corpus (a flat scan's
-    time is linear in the rows).  With a filter the scan covers the sample's
-    rows that pass it, scaled by the kept fraction."""
+SHARD_BYTES = int(3.5 * 2 ** 30)  # one wasm32 CpuIndex holds at most ~4 GiB of corpus (cpu.ts:97-104)
+
+
+def _host_shards(torch, dev, cfg, threads, x=None):
+    """The corpus in host memory as row shards of at most 3.5 GiB, at least one
+    per host thread, for the reference CPU path (one CpuIndex per shard).  A
+    filtered configuration keeps only the rows its filter passes (with their
+    global rows).  x: the corpus already on this device (else generated)."""
     from browservec_b200 import datagen
+
+    n, dim = cfg["n"], cfg["dim"]
+    step = 1 << 20
+    rowmap = None
+    if cfg.get("filter"):
+        parts, maps = [], []
+        for a in range(0, n, step):
+            b = min(n, a + step)
+            xs = x[a:b] if x is not None else datagen.rows(torch, dev, cfg["kind"], cfg["seed"], a, b, dim)
+            dc, flt = _c5_keep(torch, dev, cfg, a, b)
+            keep = _unpack(torch, dc.mask(flt), b - a)
+            parts.append(xs[keep].cpu().numpy())
+            maps.append((torch.nonzero(keep).squeeze(1) + a).cpu().numpy().astype(np.uint32))
+        host = np.concatenate(parts)
+        rowmap = np.concatenate(maps)
+    else:
+        host = np.empty((n, dim), np.float32)
+        ht = torch.from_numpy(host)
+        for a in range(0, n, step):
+            b = min(n, a + step)
+            xs = x[a:b] if x is not None else datagen.rows(torch, dev, cfg["kind"], cfg["seed"], a, b, dim)
+            ht[a:b].copy_(xs)
+    m = host.shape[0]
+    per = max(1, min(SHARD_BYTES // (dim * 4), -(-m // threads)))
+    shards, bases, maps = [], [], []
+    for a in range(0, m, per):
+        b = min(m, a + per)
+        shards.append(host[a:b])
+        bases.append(a if rowmap is None else 0)
+        maps.append(None if rowmap is None else rowmap[a:b])
+    return shards, bases, (maps if rowmap is not None else None)
+
+
+def _cpu_sharded_qps(shards, bases, maps, cfg, qs_np, threads, per_step, steps, warmup):
+    """The reference CPU path over the sharded host corpus: per step
+    `per_step` queries, each scanned by every shard's CpuIndex and merged."""
     from oracle import oracle as O
 
-    xs = datagen.rows(torch, dev, cfg["kind"], cfg["seed"], 0, sample_rows, cfg["dim"])
-    if cfg.get("filter"):
-        dc, flt = _c5_keep(torch, dev, cfg, 0, sample_rows)
-        xs = xs[_unpack(torch, dc.mask(flt), sample_rows)]
-    xs = xs.cpu().numpy()
-    qs = datagen.rows(torch, dev, cfg["kind"], cfg["seed"], 0, sample_queries, cfg["dim"],
-                      stream=datagen.STREAM_QUERIES).cpu().numpy()
-    O.cpu_index_query_batch(xs, cfg["dim"], qs[:threads], cfg["k"], threads=threads)  # warm
-    t0 = time.perf_counter()
-    O.cpu_index_query_batch(xs, cfg["dim"], qs, cfg["k"], threads=threads)
-    dt = time.perf_counter() - t0
-    return sample_queries / dt * (sample_rows / cfg["n"]), dt
+    nq = qs_np.shape[0]
+    times = []
+    for st in range(warmup + steps):
+        sel = qs_np[(np.arange(per_step) + st * per_step) % nq]
+        t0 = time.perf_counter()
+        O.cpu_sharded_query_batch(shards, bases, cfg["n"], cfg["dim"], sel, cfg["k"], threads=threads, maps=maps)
+        dt = time.perf_counter() - t0
+        if st >= warmup:
+            times.append(dt)
+    return per_step * len(times) / sum(times), sum(times)
+
+
+def _baseline_sample(shards, cfg, threads, per_step):
+    kept = sum(a.shape[0] for a in shards)
+    what = f"{kept} kept rows of {cfg['n']}" if cfg.get("filter") else f"all {cfg['n']} rows"
+    return (f"{per_step} queries per step over {what} x {cfg['dim']} fp32 in {len(shards)} row shards "
+            f"(<= 3.5 GiB each, one CpuIndex per shard, {threads} threads), WASM-SIMD exact scan + topK "
+            "restated in C (kernel.wat, cpu.ts:66-88, flat.ts:217-239), shards merged with mergePartials "
+            "(gpuTopk.ts:160-189)")
 
 
 def run_sharded(args, name):
@@ -266,34 +318,39 @@ def run_sharded(args, name):
     lo, hi = shard_bounds(n, world, rank)
     R = {8: 1, 4: 2, 1: 8}[cfg["bits"]]
     P = 1 << (dim - 1).bit_length()
+    metric = (f"queries/sec at fixed recall@10 ({cfg['workload']}, N={n}, d={dim}, k={k}, F={fetch})")
     config = {"workload": cfg["workload"], "rows": n, "dim": dim, "padded_dim": P, "bits": cfg["bits"],
               "queries_per_step": nq, "k": k, "fetch": fetch, "metric": cfg["metric"], "scoring": cfg["scoring"],
               "parallelism": f"row shards x{world} + NCCL all-gather merge", "data_kind": cfg["kind"],
-              "l2": f"each query scans {(hi - lo) * (P // R + 4) / 1e6:.0f} MB of codes per GPU"
-                    + (" (> 126 MB L2)" if (hi - lo) * (P // R + 4) > 126e6 else " (L2-resident shard)"),
-              "search": "per query one scan + one tail launch, then one merge launch per step"}
+              "l2": f"no flush needed: each step reads {(hi - lo) * (P // R + 4) / 1e6:.0f} MB of codes per GPU"
+                    + (" (> 126 MB L2)" if (hi - lo) * (P // R + 4) > 126e6 else " (fits in L2)")}
     threads = os.cpu_count() or 1
     if args.impl == "reference":
         if rank == 0:
-            srows = min(n, 1_000_000 if dim >= 384 else 2_000_000)
-            qps, dt = _cpu_sample_qps(torch, dev, cfg, threads, srows, max(threads, 16))
-            line = {"metric": METRIC_SHARDED, "value": qps, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-                    "warmup": args.warmup, "ms_per_step": nq / qps * 1e3, "higher_is_better": True,
+            shards, bases, maps = _host_shards(torch, dev, cfg, threads)
+            qs_np = datagen.rows(torch, dev, cfg["kind"], cfg["seed"], 0, nq, dim,
+                                 stream=datagen.STREAM_QUERIES).cpu().numpy()
+            torch.cuda.empty_cache()
+            per_step = args.cpu_queries or 4
+            qps, _ = _cpu_sharded_qps(shards, bases, maps, cfg, qs_np, threads, per_step, args.steps, args.warmup)
+            line = {"metric": metric, "value": qps, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                    "warmup": args.warmup, "ms_per_step": per_step / qps * 1e3, "higher_is_better": True,
                     "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
                     "impl": "reference", "config": config,
                     "cpu_baseline": {"value": qps, "unit": UNIT, "cores": threads, "kind": "port",
-                                     "sample": f"{max(threads, 16)} queries over the first {srows} rows, "
-                                               f"scaled to {n} rows (WASM-SIMD exact scan restated in C)"},
+                                     "sample": _baseline_sample(shards, cfg, threads, per_step)},
                     "e2e": {"value": qps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-            print(json.dumps(line))
+            print(json.dumps(line), flush=True)
         dist.destroy_process_group()
         return
 
     scoring = args.sharded_scoring or cfg["scoring"]
     batched = scoring != "asym" and not args.per_query
     config["scoring"] = scoring
-    config["search"] = ("batched: prep + rounds of (tcgen05 kind::i8 GEMM + select) + one re-rank tail "
-                        "per query, then one merge" if batched else
+    config["search"] = ("batched: prep + rounds of (tcgen05 kind::i8 GEMM + select)"
+                        + (", all-gather of candidate keys + global F-th key, exact re-rank of the shard's "
+                           "members of the global best F" if world > 1 else ", exact re-rank of the best F")
+                        + ", all-gather of shard records + merge" if batched else
                         "per query one scan + one tail launch, then one merge launch per step")
     x = datagen.rows(torch, dev, cfg["kind"], cfg["seed"], lo, hi, dim)
     idx = ShardedIndex(dim, n, bits=cfg["bits"], scoring=scoring, metric=cfg["metric"], device=local,
@@ -304,6 +361,7 @@ def run_sharded(args, name):
     if dc is not None:
         config["filter"] = "device predicate (bv_filter_mask) evaluated every step, kept rows compacted"
     torch.cuda.synchronize()
+    eng_index = idx.engine.index
 
     def search(qq):
         # the filter's mask is rebuilt every step from the shard's device columns
@@ -312,6 +370,10 @@ def run_sharded(args, name):
     for _ in range(args.warmup):
         rows, scores, counts = search(qs)
     torch.cuda.synchronize()
+    prof = {"gemm_ms": 0.0, "gemm_macs": 0.0, "gemm_launches": 0, "select_ms": 0.0, "tail_ms": 0.0,
+            "prep_ms": 0.0, "compact_ms": 0.0, "rounds": 0}
+    if batched:
+        eng_index.set_batch_timing(True)
     dist.barrier()
     clk = Clocks(local)
     cur = torch.cuda.current_stream(dev)
@@ -319,36 +381,53 @@ def run_sharded(args, name):
     e0.record(cur)
     for _ in range(args.steps):
         rows, scores, counts = search(qs)
+        if batched:
+            pr = eng_index.batch_profile()
+            for key in prof:
+                prof[key] += pr[key]
     e1.record(cur)
     torch.cuda.synchronize()
     clk_res = clk.stop()
+    if batched:
+        eng_index.set_batch_timing(False)
     ms = e0.elapsed_time(e1)
     t = torch.tensor([ms], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
     qps = args.steps * nq / (ms / 1e3)
-    launches_per_step = idx.engine.index.last_launches()
+    launches_per_step = eng_index.last_launches() + (3 if world > 1 and batched else 1)
 
     ns = min(nq, 100)
     keep = _unpack(torch, dc.mask(flt), hi - lo) if dc is not None else None
     kept_local = int(keep.sum().item()) if keep is not None else hi - lo
     truth = _exact_top10(torch, dist, x, lo, qs[:ns], keep=keep)
-    got = rows[:ns, :10].cpu().numpy()
-    rec = sum(len(set(truth[i].tolist()) & set(got[i].tolist())) for i in range(ns)) / (ns * 10)
 
+    def recall(rr):
+        got = rr[:ns, :10].cpu().numpy()
+        return sum(len(set(truth[i].tolist()) & set(got[i].tolist())) for i in range(ns)) / (ns * 10)
+
+    rec = recall(rows)
     query_ms = ms / (args.steps * nq)
     if batched:
-        # per-GPU roofline of the contraction: 2 * queries * shard rows * paddedDim int8 ops per step
-        ops = 2.0 * nq * kept_local * P  # rows the filter keeps are the rows contracted
-        tops = ops / (ms / args.steps / 1e3) / 1e12
+        # the dominant kernel: the GEMM, 2 x queries x contracted rows x paddedDim int8 ops,
+        # over its own device time (events around each GEMM launch of the timed steps)
+        ops = 2.0 * prof["gemm_macs"]
+        gemm_s = prof["gemm_ms"] / 1e3
+        tops = ops / gemm_s / 1e12 if gemm_s > 0 else 0.0
         peak = 2.0 * tensor_peak()
         roofline = {"bound": "tensor", "achieved": tops, "peak": peak, "unit": "TOP/s (int8)",
                     "frac": tops / peak, "traffic": None,
-                    "peak_kind": "int8 dense = 2 x the measured bf16 burst (MEASURED_PEAKS.json bf16_tflops); "
-                                 "no int8 figure is measured",
-                    "algorithmic_ops_per_step": ops,
-                    "duration": "per step per GPU: prep + GEMM/select rounds + re-rank tails + all-gather + "
-                                "merge"}
+                    "peak_kind": "int8 dense = 2 x the measured bf16 burst (MEASURED_PEAKS.json bf16_tflops, "
+                                 "of measured); no int8 figure is measured on this pool",
+                    "kernel": "gemm_kernel (tcgen05.mma kind::i8)",
+                    "algorithmic_ops_per_step": ops / args.steps,
+                    "gemm_launches_per_step": prof["gemm_launches"] / args.steps,
+                    "gemm_ms_per_step": prof["gemm_ms"] / args.steps,
+                    "duration": "CUDA events around every GEMM launch of the timed steps, on its stream"}
+        step_ms = ms / args.steps
+        breakdown = {kk: prof[kk] / args.steps for kk in ("prep_ms", "gemm_ms", "select_ms", "tail_ms", "compact_ms")}
+        breakdown["other_ms"] = step_ms - sum(breakdown.values())
+        breakdown["rounds"] = prof["rounds"] / args.steps
     else:
         # per-GPU roofline of the scan: codes + scales of the shard, the re-rank rows, the query
         algo_bytes = (hi - lo) * (P // R + 4) + fetch * dim * 4 + dim * 4
@@ -360,6 +439,16 @@ def run_sharded(args, name):
                     "algorithmic_bytes_per_launch": algo_bytes,
                     "duration": "per query per GPU: timed region / queries (scan + tail, all-gather and "
                                 "merge amortised)"}
+        breakdown = None
+
+    # the reference's own arithmetic (asym: fp32 rotated query x codes), per-query scans, for recall
+    also = None
+    if scoring != "asym" and not args.no_asym:
+        idx.set_scoring("asym", batched=False)
+        r2, _, _ = idx.search(qs[:ns], k, fetch, dc.mask(flt) if dc is not None else None)
+        also = {"scoring": "asym (reference arithmetic: fp32 rotated query x codes, per-query scans)",
+                "recall_at_10": recall(r2), "recall_sample": ns}
+        idx.set_scoring(scoring, batched=batched)
 
     # e2e: host queries (pinned) -> device, search, results back to the host, every step
     q_host = qs.cpu().pin_memory()
@@ -377,25 +466,26 @@ def run_sharded(args, name):
     wall = float(t.item())
     e2e = {"value": e2e_steps * nq / wall, "unit": UNIT, "h2d_bytes_per_step": nq * dim * 4,
            "d2h_bytes_per_step": nq * (2 * k + 1) * 4, "steps": e2e_steps,
-           "timing": "host wall clock, max over ranks"}
+           "timing": "host wall clock, max over ranks (pinned H2D of the batch, search, D2H of the results)"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        srows = min(n, 1_000_000 if dim >= 384 else 2_000_000)
-        cqps, _ = _cpu_sample_qps(torch, dev, cfg, threads, srows, max(threads, 16))
+        shards, bases, maps = _host_shards(torch, dev, cfg, threads, x=x)
+        per = args.cpu_queries or 16
+        cqps, _ = _cpu_sharded_qps(shards, bases, maps, cfg, qs.cpu().numpy(), threads, per, 1, 0)
         cpu = {"value": cqps, "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"{max(threads, 16)} queries over the first {srows} rows, scaled to {n} rows "
-                         "(WASM-SIMD exact scan restated in C, one query per thread)"}
+               "sample": _baseline_sample(shards, cfg, threads, per)}
+        del shards
     if rank == 0:
-        line = {"metric": METRIC_SHARDED, "value": qps, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        line = {"metric": metric, "value": qps, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-                "scaling": "strong", "vs_baseline": None, "dtype": {"int": "s8", "hamming": "b1"}.get(
-                    cfg["scoring"], "f32xs8"),
+                "scaling": "strong", "vs_baseline": None,
+                "dtype": {"int": "s8", "hamming": "b1"}.get(scoring, "f32xs8"),
                 "data": f"synthetic (seeded Philox, {cfg['kind']}, L2-normalised)", "config": config,
                 "recall_at_10": rec, "recall_sample": ns, "query_ms": query_ms,
-                "gpu_launches": args.steps * (launches_per_step + 1), "roofline": roofline, "cpu_baseline": cpu,
-                "e2e": e2e, "clocks": clk_res}
-        print(json.dumps(line))
+                "gpu_launches": args.steps * launches_per_step, "roofline": roofline, "cpu_baseline": cpu,
+                "e2e": e2e, "clocks": clk_res, "also": also, "step_breakdown_ms": breakdown}
+        print(json.dumps(line), flush=True)
     idx.destroy()
     dist.destroy_process_group()
 
@@ -415,7 +505,10 @@ def main():
     ap.add_argument("--replicas", type=int, default=4)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--config", default="c2", choices=[*SINGLE, *SHARDED])
+    ap.add_argument("--config", default="c4", choices=[*SINGLE, *SHARDED])
+    ap.add_argument("--cpu-queries", type=int, default=0,
+                    help="sharded configs: queries per CPU-baseline sample (default 16, reference arm 4 per step)")
+    ap.add_argument("--no-asym", action="store_true", help="sharded configs: skip the asym recall figure")
     ap.add_argument("--sharded-scoring", default=None, choices=["asym", "int", "hamming"],
                     help="scoring of a sharded config (default: the config's)")
     ap.add_argument("--rows", type=int, default=0, help="sharded configs: corpus rows (default: the config's)")

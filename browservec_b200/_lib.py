@@ -20,7 +20,8 @@ SCORING = {"asym": SCORE_ASYM, "int": SCORE_INT, "hamming": SCORE_HAMMING}
 EXPORTS = ("bv_create", "bv_destroy", "bv_last_error", "bv_append", "bv_append_device", "bv_size",
            "bv_search", "bv_search_async", "bv_search_async_n", "bv_query_rows_exact", "bv_export_codes", "bv_get_stats",
            "bv_launches_last_search", "bv_set_phase_trace", "bv_search_noalloc",
-           "bv_merge_shards", "bv_search_batch", "bv_filter_mask")
+           "bv_merge_shards", "bv_search_batch", "bv_filter_mask", "bv_batch_select", "bv_batch_finish",
+           "bv_keys_threshold", "bv_set_batch_timing", "bv_last_batch_profile", "bv_set_scoring")
 
 
 class BvConfig(C.Structure):
@@ -41,6 +42,13 @@ class BvStats(C.Structure):
     _fields_ = [("rows", C.c_uint64), ("dim", C.c_uint32), ("padded_dim", C.c_uint32),
                 ("bits", C.c_uint32), ("words_per_row", C.c_uint32), ("chunks", C.c_uint32),
                 ("last_query_gpu_ms", C.c_float), ("device_bytes", C.c_uint64)]
+
+
+class BvBatchProfile(C.Structure):
+    _fields_ = [("prep_ms", C.c_float), ("gemm_ms", C.c_float), ("select_ms", C.c_float),
+                ("tail_ms", C.c_float), ("compact_ms", C.c_float), ("gemm_launches", C.c_uint32),
+                ("rounds", C.c_uint32), ("kept_rows", C.c_uint32), ("nq", C.c_uint32),
+                ("gemm_macs", C.c_double)]
 
 
 class BvColumn(C.Structure):
@@ -101,6 +109,12 @@ def load(path: str = LIB_PATH):
         "bv_search_batch": (C.c_int, [P, C.POINTER(BvSearchArgs), P]),
         "bv_filter_mask": (C.c_int, [C.POINTER(BvColumn), C.c_uint32, C.POINTER(BvFilterTerm), C.c_uint32,
                                      C.c_uint64, P, P, P]),
+        "bv_batch_select": (C.c_int, [P, C.POINTER(BvSearchArgs), P, P]),
+        "bv_batch_finish": (C.c_int, [P, C.POINTER(BvSearchArgs), P, P]),
+        "bv_keys_threshold": (C.c_int, [P, C.c_uint32, C.c_uint32, C.c_uint32, P, P]),
+        "bv_set_batch_timing": (C.c_int, [P, C.c_int]),
+        "bv_last_batch_profile": (C.c_int, [P, C.POINTER(BvBatchProfile)]),
+        "bv_set_scoring": (C.c_int, [P, C.c_uint32]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

@@ -9,6 +9,8 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <utility>
+#include <vector>
 
 #include "../../include/browservec.h"
 #include "bv_internal.h"
@@ -77,6 +79,21 @@ uint32_t pad_to_pow2(uint32_t n) {  // rotator.ts:39-43
 }
 
 }  // namespace
+
+// Batched-search state kept between the phases of one search
+// (bv_batch_select -> bv_batch_finish) and the optional device-time profile.
+struct bv_batch_state {
+  // plan of the last batched rounds (kept for bv_batch_finish)
+  bool pending = false;
+  uint32_t nq = 0, F = 0, Fp = 0, cap = 0, launches = 0, rounds = 0;
+  bool empty = false;  // nothing to rank: outputs are zero counts
+  // timing
+  bool timing = false;
+  std::vector<cudaEvent_t> ev;
+  std::vector<std::pair<int, uint32_t>> marks;  // (phase, event index of its start); end = next event
+  uint32_t used = 0;
+  bv_batch_profile prof = {};
+};
 
 struct bv_index {
   int device = 0;
@@ -171,6 +188,7 @@ struct bv_index {
   float* d_ctmax = nullptr;
   size_t ctmax_cap = 0;
   uint32_t last_kept = 0;
+  bv_batch_state* batch = nullptr;  // batched-search plan kept between phases, timing
 };
 
 namespace {
@@ -767,6 +785,10 @@ int bv_destroy(bv_index* idx) {
   if (idx->ev0) cudaEventDestroy(idx->ev0);
   if (idx->ev1) cudaEventDestroy(idx->ev1);
   if (idx->ev_ring) cudaEventDestroy(idx->ev_ring);
+  if (idx->batch) {
+    for (cudaEvent_t e : idx->batch->ev) cudaEventDestroy(e);
+    delete idx->batch;
+  }
   if (idx->stream) cudaStreamDestroy(idx->stream);
   delete idx;
   return BV_OK;
@@ -1126,35 +1148,104 @@ int ensure_mma(bv_index* idx, cudaStream_t s) {
 
 }  // namespace
 
-int bv_search_batch(bv_index* idx, const bv_search_args* a, void* stream) {
-  uint32_t F = 0;
-  int rc = check_args(idx, a, &F);
-  if (rc) return rc;
-  if (idx->scoring == BV_SCORE_ASYM || idx->bits == 0)
-    return fail(BV_ERR_UNSUPPORTED, "the batched search scores with the integer modes (int, hamming), "
-                                    "not asym");
-  if (idx->rows >= 0x7FFFFF00ull) return fail(BV_ERR_UNSUPPORTED, "batched search takes < 2^31 rows per index");
-  BV_CUDA(idx, cudaSetDevice(idx->device), "cudaSetDevice");
-  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : idx->stream;
-  const uint32_t nq = a->nq;
-  if (idx->rows == 0 || nq == 0) {
-    if (nq) BV_CUDA(idx, cudaMemsetAsync(a->out_counts, 0, nq * 4, s), "memset");
-    if (nq && a->cand_counts) BV_CUDA(idx, cudaMemsetAsync(a->cand_counts, 0, nq * 4, s), "memset");
-    BV_CUDA(idx, cudaStreamSynchronize(s), "sync");
-    idx->last_launches = 0;
-    return BV_OK;
+namespace {
+
+// Device-time accounting of a batched search (bv_set_batch_timing): events
+// recorded on the search stream around each phase's launches, summed once
+// the search has synchronised.
+enum BatchPhase : int { kPhPrep = 0, kPhGemm = 1, kPhSelect = 2, kPhTail = 3, kPhCompact = 4, kPhCount = 5 };
+
+struct PhaseClock {
+  bv_index* idx;
+  cudaStream_t s;
+  int open = -1;
+  explicit PhaseClock(bv_index* i, cudaStream_t st) : idx(i), s(st) {}
+  int begin(int ph);
+  int end();
+};
+
+}  // namespace
+
+namespace {
+
+bv_batch_state* batch_state(bv_index* idx) {
+  if (!idx->batch) idx->batch = new bv_batch_state();
+  return idx->batch;
+}
+
+int PhaseClock::begin(int ph) {
+  bv_batch_state* b = batch_state(idx);
+  if (!b->timing) return BV_OK;
+  if (b->used + 2 > b->ev.size()) {
+    cudaEvent_t e;
+    for (int i = 0; i < 2; ++i) {
+      BV_CUDA(idx, cudaEventCreate(&e), "timing event");
+      b->ev.push_back(e);
+    }
   }
+  BV_CUDA(idx, cudaEventRecord(b->ev[b->used], s), "timing event");
+  b->marks.emplace_back(ph, b->used);
+  b->used += 2;
+  open = ph;
+  return BV_OK;
+}
+
+int PhaseClock::end() {
+  bv_batch_state* b = batch_state(idx);
+  if (!b->timing || open < 0) return BV_OK;
+  BV_CUDA(idx, cudaEventRecord(b->ev[b->marks.back().second + 1], s), "timing event");
+  open = -1;
+  return BV_OK;
+}
+
+// Fold the recorded phases into the profile (the stream has synchronised).
+int fold_phases(bv_index* idx) {
+  bv_batch_state* b = batch_state(idx);
+  if (!b->timing) return BV_OK;
+  for (const auto& m : b->marks) {
+    float ms = 0.0f;
+    BV_CUDA(idx, cudaEventElapsedTime(&ms, b->ev[m.second], b->ev[m.second + 1]), "timing");
+    float* dst = m.first == kPhPrep ? &b->prof.prep_ms
+                 : m.first == kPhGemm ? &b->prof.gemm_ms
+                 : m.first == kPhSelect ? &b->prof.select_ms
+                 : m.first == kPhTail ? &b->prof.tail_ms : &b->prof.compact_ms;
+    *dst += ms;
+    if (m.first == kPhGemm) ++b->prof.gemm_launches;
+  }
+  b->marks.clear();
+  b->used = 0;
+  return BV_OK;
+}
+
+// Prep + rounds of (GEMM, select) of a batched search: on return (stream
+// synchronised) idx->d_bcand holds per query its best F keys (local rows;
+// sorted descending for Fp <= 256, else unsorted), zero padded to Fp.
+int batch_rounds(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStream_t s) {
+  int rc;
+  bv_batch_state* bs = batch_state(idx);
+  bs->pending = false;
+  bs->empty = false;
+  bs->prof = bv_batch_profile{};
+  bs->marks.clear();
+  bs->used = 0;
+  PhaseClock clk(idx, s);
+  const uint32_t nq = a->nq;
   if ((rc = ensure_mma(idx, s))) return rc;
   uint32_t Fp = 32;
   while (Fp < F) Fp <<= 1;
   const uint32_t cap = Fp * 16 > 4096 ? Fp * 16 : 4096;  // <= 16384 (F <= 1024)
   const uint32_t KB = (idx->P + bv::kKBlock - 1) / bv::kKBlock;
   const uint32_t nqt = (nq + bv::kBQTile - 1) / bv::kBQTile;
+  bs->nq = nq;
+  bs->F = F;
+  bs->Fp = Fp;
+  bs->cap = cap;
   // A mask that keeps at most half the rows: contract only the kept rows,
   // gathered into their own tiles (their order, hence the tie rule, is kept).
   bool compact = false;
   uint32_t kept = static_cast<uint32_t>(idx->rows);
   if (a->mask) {
+    if ((rc = clk.begin(kPhCompact))) return rc;
     const uint64_t words = (idx->rows + 31) / 32;
     const uint64_t nb = (words + bv::compact_block_words() - 1) / bv::compact_block_words();
     if ((rc = grow(idx, &idx->d_cwoff, &idx->cwoff_cap, words, "filter scratch"))) return rc;
@@ -1193,16 +1284,22 @@ int bv_search_batch(bv_index* idx, const bv_search_args* a, void* stream) {
       e = bv::launch_expand(ep, s);
       if (e != cudaSuccess) return cuda_fail(idx, e, "filter compaction");
     }
+    if ((rc = clk.end())) return rc;
   }
   idx->last_kept = kept;
+  bs->prof.kept_rows = kept;
+  bs->prof.nq = nq;
   if (a->mask && kept == 0) {  // nothing passes the filter
-    BV_CUDA(idx, cudaMemsetAsync(a->out_counts, 0, nq * 4, s), "memset");
-    if (a->cand_counts) BV_CUDA(idx, cudaMemsetAsync(a->cand_counts, 0, nq * 4, s), "memset");
     BV_CUDA(idx, cudaStreamSynchronize(s), "sync");
-    idx->last_launches = 3;
-    return BV_OK;
+    bs->empty = true;
+    bs->launches = 3;
+    bs->rounds = 0;
+    bs->pending = true;
+    return fold_phases(idx);
   }
-  const uint32_t T = static_cast<uint32_t>(((compact ? kept : idx->rows) + bv::kBRowTile - 1) / bv::kBRowTile);
+  const uint32_t npos = compact ? kept : static_cast<uint32_t>(idx->rows);
+  const uint32_t T = static_cast<uint32_t>((static_cast<uint64_t>(npos) + bv::kBRowTile - 1) / bv::kBRowTile);
+  bs->prof.gemm_macs = static_cast<double>(nq) * static_cast<double>(npos) * static_cast<double>(idx->P);
   if ((rc = grow(idx, &idx->d_qtiles, &idx->qtiles_cap, static_cast<size_t>(nqt) * KB * bv::kBQTileBytes,
                  "batch queries")))
     return rc;
@@ -1234,7 +1331,7 @@ int bv_search_batch(bv_index* idx, const bv_search_args* a, void* stream) {
   g.posrow = compact ? idx->d_cposrow : idx->d_posrow;
   g.tmax = compact ? idx->d_ctmax : idx->d_tmax;
   g.mask = compact ? nullptr : a->mask;
-  g.npos = compact ? kept : static_cast<uint32_t>(idx->rows);
+  g.npos = npos;
   g.nq = nq;
   g.KB = KB;
   g.nqt = nqt;
@@ -1261,14 +1358,29 @@ int bv_search_batch(bv_index* idx, const bv_search_args* a, void* stream) {
     g.rt1 = rt1;
     const uint64_t tiles = static_cast<uint64_t>(rt1 - rt0) * nqt;
     const uint32_t grid = static_cast<uint32_t>(tiles < static_cast<uint64_t>(idx->num_sms) ? tiles : idx->num_sms);
+    int r;
+    if ((r = clk.begin(kPhGemm))) return r;
     const cudaError_t e = bv::launch_gemm(g, grid, s);
     if (e != cudaSuccess) return cuda_fail(idx, e, "batch gemm");
+    if ((r = clk.end())) return r;
     ++launches;
     return BV_OK;
   };
   auto select = [&]() -> int {
+    int r;
+    if ((r = clk.begin(kPhSelect))) return r;
     const cudaError_t e = bv::launch_select(sp, s);
     if (e != cudaSuccess) return cuda_fail(idx, e, "batch select");
+    if ((r = clk.end())) return r;
+    ++launches;
+    return BV_OK;
+  };
+  auto prep = [&]() -> int {
+    int r;
+    if ((r = clk.begin(kPhPrep))) return r;
+    const cudaError_t e = bv::launch_prep(pp, s);
+    if (e != cudaSuccess) return cuda_fail(idx, e, "batch prep");
+    if ((r = clk.end())) return r;
     ++launches;
     return BV_OK;
   };
@@ -1289,9 +1401,7 @@ int bv_search_batch(bv_index* idx, const bv_search_args* a, void* stream) {
   };
 
   BV_CUDA(idx, cudaMemsetAsync(idx->d_overflow, 0, 4, s), "batch flag");
-  cudaError_t e = bv::launch_prep(pp, s);
-  if (e != cudaSuccess) return cuda_fail(idx, e, "batch prep");
-  launches = 1;
+  if ((rc = prep())) return rc;
   uint32_t nrounds = 0;
   for (uint32_t rt = 0; rt < T;) {
     const uint32_t m = rt == 0 ? first : next_size(rt);
@@ -1307,9 +1417,7 @@ int bv_search_batch(bv_index* idx, const bv_search_args* a, void* stream) {
     // A buffer overflowed (rows that arrive in increasing score order, for
     // instance): redo the batch round by round, halving a round that
     // overflows; a round of one tile (256 rows) cannot overflow (cap >= F + 256).
-    e = bv::launch_prep(pp, s);
-    if (e != cudaSuccess) return cuda_fail(idx, e, "batch prep");
-    launches += 1;
+    if ((rc = prep())) return rc;
     uint32_t m = first;
     for (uint32_t rt = 0; rt < T;) {
       const uint32_t rt1 = T - rt < m ? T : rt + m;
@@ -1332,12 +1440,36 @@ int bv_search_batch(bv_index* idx, const bv_search_args* a, void* stream) {
       rt = rt1;
       m = m < 0x7FFFFFFFu ? 2 * m : m;
     }
+    BV_CUDA(idx, cudaStreamSynchronize(s), "batch search");
   }
-  // exact re-rank of each query's best F and the outputs: one tail CTA per query
+  if ((rc = check_err_flag(idx))) return rc;
+  bs->launches = launches;
+  bs->rounds = nrounds;
+  bs->prof.rounds = nrounds;
+  bs->pending = true;
+  return fold_phases(idx);
+}
+
+// The re-rank tail of a batched search (after batch_rounds): one CTA per
+// query re-ranks its best F exactly and writes the outputs.
+int batch_tail(bv_index* idx, const bv_search_args* a, cudaStream_t s) {
+  bv_batch_state* bs = batch_state(idx);
+  const uint32_t nq = a->nq, F = bs->F, Fp = bs->Fp;
+  PhaseClock clk(idx, s);
+  int rc;
+  if (bs->empty) {
+    BV_CUDA(idx, cudaMemsetAsync(a->out_counts, 0, nq * 4, s), "memset");
+    if (a->cand_counts) BV_CUDA(idx, cudaMemsetAsync(a->cand_counts, 0, nq * 4, s), "memset");
+    BV_CUDA(idx, cudaStreamSynchronize(s), "sync");
+    idx->last_launches = bs->launches;
+    idx->last_rounds = 0;
+    bs->pending = false;
+    return BV_OK;
+  }
   bv::TailParams t;
   memset(&t, 0, sizeof(t));
   t.partials = idx->d_bcand;
-  t.partials_stride = cap;
+  t.partials_stride = bs->cap;
   t.G = 1;
   t.F = F;
   t.Fp = Fp;
@@ -1368,13 +1500,136 @@ int bv_search_batch(bv_index* idx, const bv_search_args* a, void* stream) {
   rows_bytes = rows_bytes / row_bytes * row_bytes;
   if (rows_bytes < row_bytes) return fail(BV_ERR_UNSUPPORTED, "re-rank row does not fit in shared memory");
   t.rows_bytes = rows_bytes;
-  e = bv::launch_tail_grid(t, nq, bv::tail_smem_layout(idx->dim, t.capc, rows_bytes).total, s);
+  if ((rc = clk.begin(kPhTail))) return rc;
+  const cudaError_t e = bv::launch_tail_grid(t, nq, bv::tail_smem_layout(idx->dim, t.capc, rows_bytes).total, s);
   if (e != cudaSuccess) return cuda_fail(idx, e, "batch tail");
-  launches += 1;
+  if ((rc = clk.end())) return rc;
   BV_CUDA(idx, cudaStreamSynchronize(s), "batch search");
-  idx->last_launches = launches;
-  idx->last_rounds = nrounds;
+  idx->last_launches = bs->launches + 1;
+  idx->last_rounds = bs->rounds;
+  bs->pending = false;
+  if ((rc = fold_phases(idx))) return rc;
   return check_err_flag(idx);
+}
+
+int batch_check(bv_index* idx, const bv_search_args* a, uint32_t* F) {
+  int rc = check_args(idx, a, F);
+  if (rc) return rc;
+  if (idx->scoring == BV_SCORE_ASYM || idx->bits == 0)
+    return fail(BV_ERR_UNSUPPORTED, "the batched search scores with the integer modes (int, hamming), "
+                                    "not asym");
+  if (idx->rows >= 0x7FFFFF00ull) return fail(BV_ERR_UNSUPPORTED, "batched search takes < 2^31 rows per index");
+  BV_CUDA(idx, cudaSetDevice(idx->device), "cudaSetDevice");
+  return BV_OK;
+}
+
+}  // namespace
+
+int bv_search_batch(bv_index* idx, const bv_search_args* a, void* stream) {
+  uint32_t F = 0;
+  int rc = batch_check(idx, a, &F);
+  if (rc) return rc;
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : idx->stream;
+  const uint32_t nq = a->nq;
+  if (idx->rows == 0 || nq == 0) {
+    if (nq) BV_CUDA(idx, cudaMemsetAsync(a->out_counts, 0, nq * 4, s), "memset");
+    if (nq && a->cand_counts) BV_CUDA(idx, cudaMemsetAsync(a->cand_counts, 0, nq * 4, s), "memset");
+    BV_CUDA(idx, cudaStreamSynchronize(s), "sync");
+    idx->last_launches = 0;
+    return BV_OK;
+  }
+  if ((rc = batch_rounds(idx, a, F, s))) return rc;
+  return batch_tail(idx, a, s);
+}
+
+int bv_batch_select(bv_index* idx, const bv_search_args* a, uint64_t* keys_out, void* stream) {
+  uint32_t F = 0;
+  int rc = batch_check(idx, a, &F);
+  if (rc) return rc;
+  if (!keys_out && a->nq) return fail(BV_ERR_INVALID, "keys_out is null");
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : idx->stream;
+  const uint32_t nq = a->nq;
+  bv_batch_state* bs = batch_state(idx);
+  if (idx->rows == 0 || nq == 0) {
+    if (nq) BV_CUDA(idx, cudaMemsetAsync(keys_out, 0, static_cast<size_t>(nq) * F * 8, s), "memset");
+    BV_CUDA(idx, cudaStreamSynchronize(s), "sync");
+    bs->pending = true;
+    bs->empty = true;
+    bs->nq = nq;
+    bs->F = F;
+    bs->launches = 0;
+    return BV_OK;
+  }
+  if ((rc = batch_rounds(idx, a, F, s))) return rc;
+  if (bs->empty) {
+    BV_CUDA(idx, cudaMemsetAsync(keys_out, 0, static_cast<size_t>(nq) * F * 8, s), "memset");
+  } else {
+    const cudaError_t e =
+        bv::launch_export_keys(idx->d_bcand, bs->cap, idx->d_bcnt, nq, F, idx->row_base, keys_out, s);
+    if (e != cudaSuccess) return cuda_fail(idx, e, "export keys");
+  }
+  BV_CUDA(idx, cudaStreamSynchronize(s), "batch select");
+  return BV_OK;
+}
+
+int bv_batch_finish(bv_index* idx, const bv_search_args* a, const uint64_t* min_keys, void* stream) {
+  uint32_t F = 0;
+  int rc = batch_check(idx, a, &F);
+  if (rc) return rc;
+  bv_batch_state* bs = batch_state(idx);
+  if (!bs->pending || bs->nq != a->nq || bs->F != F)
+    return fail(BV_ERR_INVALID, "bv_batch_finish needs the same request right after bv_batch_select");
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : idx->stream;
+  const uint32_t nq = a->nq;
+  if (idx->rows == 0 || nq == 0) {
+    if (nq) BV_CUDA(idx, cudaMemsetAsync(a->out_counts, 0, nq * 4, s), "memset");
+    if (nq && a->cand_counts) BV_CUDA(idx, cudaMemsetAsync(a->cand_counts, 0, nq * 4, s), "memset");
+    BV_CUDA(idx, cudaStreamSynchronize(s), "sync");
+    bs->pending = false;
+    idx->last_launches = 0;
+    return BV_OK;
+  }
+  if (min_keys && !bs->empty) {
+    const cudaError_t e = bv::launch_trim_keys(idx->d_bcand, bs->cap, bs->Fp, nq, idx->row_base, min_keys, s);
+    if (e != cudaSuccess) return cuda_fail(idx, e, "trim keys");
+  }
+  return batch_tail(idx, a, s);
+}
+
+int bv_keys_threshold(const uint64_t* gathered, uint32_t world, uint32_t nq, uint32_t fetch, uint64_t* thr_out,
+                      void* stream) {
+  if ((nq && (!gathered || !thr_out)) || world == 0 || fetch == 0) return fail(BV_ERR_INVALID, "bad argument");
+  if (static_cast<uint64_t>(world) * fetch > bv::keys_threshold_max())
+    return fail(BV_ERR_UNSUPPORTED, "%u shards x %u candidates exceed the threshold kernel's %u keys", world, fetch,
+                bv::keys_threshold_max());
+  if (nq == 0) return BV_OK;
+  const cudaError_t e = bv::launch_keys_threshold(gathered, world, nq, fetch, thr_out,
+                                                  static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(nullptr, e, "threshold launch");
+  return BV_OK;
+}
+
+int bv_set_batch_timing(bv_index* idx, int enable) {
+  if (!idx) return fail(BV_ERR_INVALID, "null index");
+  batch_state(idx)->timing = enable != 0;
+  return BV_OK;
+}
+
+int bv_last_batch_profile(bv_index* idx, bv_batch_profile* out) {
+  if (!idx || !out) return fail(BV_ERR_INVALID, "null argument");
+  *out = batch_state(idx)->prof;
+  return BV_OK;
+}
+
+int bv_set_scoring(bv_index* idx, uint32_t scoring) {
+  if (!idx) return fail(BV_ERR_INVALID, "null index");
+  if (scoring > BV_SCORE_HAMMING) return fail(BV_ERR_INVALID, "unknown scoring mode %u", scoring);
+  if (idx->bits == 0 && scoring != BV_SCORE_ASYM)
+    return fail(BV_ERR_INVALID, "the exact fp32 index (bits 0) has no quantized scoring");
+  if (scoring == BV_SCORE_HAMMING && idx->bits != 1) return fail(BV_ERR_INVALID, "hamming scoring needs 1-bit codes");
+  if (idx->stream) BV_CUDA(idx, cudaStreamSynchronize(idx->stream), "sync");
+  idx->scoring = scoring;
+  return BV_OK;
 }
 
 int bv_filter_mask(const bv_column* cols, uint32_t ncols, const bv_filter_term* terms, uint32_t nterms,

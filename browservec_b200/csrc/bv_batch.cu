@@ -549,13 +549,33 @@ __global__ void __launch_bounds__(kConsumerThreads, 1) select_kernel(const Selec
   if (p.Fp <= 256u) {  // one warp sorts the kept keys in registers, no block barriers
     warp0_sort_dispatch(p.Fp, kept, ctid);
     named_bar_sync(kBarConsumers, kConsumerThreads);
-  } else {
-    cta_sort_desc(kept, p.Fp, ctid);
+    for (uint32_t i = ctid; i < p.Fp; i += kConsumerThreads) c[i] = kept[i];
+    if (ctid == 0) {
+      p.cnt[qi] = n;
+      p.thr[qi] = n >= p.F ? kept[p.F - 1] : 0ull;
+    }
+    return;
   }
-  for (uint32_t i = ctid; i < p.Fp; i += kConsumerThreads) c[i] = kept[i];
+  // wide F: the kept keys stay unsorted (the re-rank tail selects and sorts
+  // them itself); the F-th best key is the least kept key
+  uint64_t mn = ~0ull;
+  for (uint32_t i = ctid; i < p.Fp; i += kConsumerThreads) {
+    const uint64_t x = kept[i];
+    c[i] = x;
+    if (i < n && x < mn) mn = x;
+  }
+#pragma unroll
+  for (int off = 16; off; off >>= 1) {
+    const uint64_t o = __shfl_xor_sync(0xffffffffu, mn, off);
+    mn = o < mn ? o : mn;
+  }
+  uint64_t* red = reinterpret_cast<uint64_t*>(misc + kMiscSel);
+  if ((ctid & 31) == 0) red[ctid >> 5] = mn;
+  named_bar_sync(kBarConsumers, kConsumerThreads);
   if (ctid == 0) {
+    for (int w = 1; w < kConsumerWarps; ++w) mn = red[w] < mn ? red[w] : mn;
     p.cnt[qi] = n;
-    p.thr[qi] = n >= p.F ? kept[p.F - 1] : 0ull;
+    p.thr[qi] = n >= p.F ? mn : 0ull;
   }
 }
 
@@ -656,6 +676,73 @@ __global__ void __launch_bounds__(256) row_map_kernel(const uint32_t* mask, uint
   }
 }
 
+// ------------------------------------------------------------- shards
+// A key of local row r as a key of global row r + base (same score bits).
+__device__ __forceinline__ uint64_t global_key(uint64_t key, uint32_t base) {
+  const uint32_t row = ~static_cast<uint32_t>(key);
+  return (key & 0xFFFFFFFF00000000ull) | static_cast<uint32_t>(~(row + base));
+}
+
+// keys[q*F + i] = the i-th kept key of query q as a global-row key (zero past
+// the kept count).
+__global__ void __launch_bounds__(256) export_keys_kernel(const uint64_t* cand, uint32_t cap, const uint32_t* cnt,
+                                                          uint32_t nq, uint32_t F, uint32_t base, uint64_t* keys) {
+  const uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= static_cast<uint64_t>(nq) * F) return;
+  const uint32_t q = static_cast<uint32_t>(i / F), j = static_cast<uint32_t>(i % F);
+  const uint32_t n = cnt[q] < F ? cnt[q] : F;
+  const uint64_t x = j < n ? cand[static_cast<size_t>(q) * cap + j] : 0ull;
+  keys[i] = x ? global_key(x, base) : 0ull;
+}
+
+// Drop (zero) the kept keys of query q below thr[q] (global-row keys); a
+// descending list stays descending with its zeros at the end.
+__global__ void __launch_bounds__(256) trim_keys_kernel(uint64_t* cand, uint32_t cap, uint32_t Fp, uint32_t nq,
+                                                        uint32_t base, const uint64_t* thr) {
+  const uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= static_cast<uint64_t>(nq) * Fp) return;
+  const uint32_t q = static_cast<uint32_t>(i / Fp), j = static_cast<uint32_t>(i % Fp);
+  uint64_t* c = cand + static_cast<size_t>(q) * cap + j;
+  const uint64_t x = *c;
+  if (x && global_key(x, base) < thr[q]) *c = 0ull;
+}
+
+// One CTA per query: among the W gathered key lists (W x nq x F, list w of
+// query q at (w * nq + q) * F), a threshold with exactly min(F, total) keys at
+// or above it.
+template <int MAXK>
+__global__ void __launch_bounds__(kConsumerThreads, 1) keys_threshold_kernel(const uint64_t* gathered, uint32_t world,
+                                                                            uint32_t nq, uint32_t F, uint64_t* thr) {
+  __shared__ uint32_t hist[kSelBins];
+  __shared__ uint32_t sh[kSelScratch];
+  __shared__ uint32_t red[kConsumerWarps];
+  const int ctid = threadIdx.x;
+  const uint32_t q = blockIdx.x, total_slots = world * F;
+  uint64_t v[MAXK];
+  uint32_t c = 0;
+#pragma unroll
+  for (int i = 0; i < MAXK; ++i) {
+    const uint32_t idx = static_cast<uint32_t>(ctid) + static_cast<uint32_t>(i) * kConsumerThreads;
+    uint64_t x = 0ull;
+    if (idx < total_slots) {
+      const uint32_t w = idx / F, j = idx - w * F;
+      x = __ldcg(gathered + (static_cast<size_t>(w) * nq + q) * F + j);
+    }
+    v[i] = x;
+    c += x ? 1u : 0u;
+  }
+#pragma unroll
+  for (int off = 16; off; off >>= 1) c += __shfl_xor_sync(0xffffffffu, c, off);
+  if ((ctid & 31) == 0) red[ctid >> 5] = c;
+  named_bar_sync(kBarConsumers, kConsumerThreads);
+  uint32_t total = 0;
+#pragma unroll
+  for (int w = 0; w < kConsumerWarps; ++w) total += red[w];
+  const uint64_t t = block_select_threshold<MAXK, kConsumerThreads>(v, MAXK, F, total, hist, sh, ctid,
+                                                                    kBarConsumers);
+  if (ctid == 0) thr[q] = t;
+}
+
 // ------------------------------------------------------------- launchers
 uint32_t batch_gemm_smem() { return gemm_smem_layout().total + 1024; }
 
@@ -745,6 +832,34 @@ cudaError_t launch_select(const SelectParams& p, cudaStream_t s) {
   if (maxk <= 16) return go(select_kernel<16>);
   if (maxk <= 32) return go(select_kernel<32>);
   return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_export_keys(const uint64_t* cand, uint32_t cap, const uint32_t* cnt, uint32_t nq, uint32_t F,
+                               uint32_t base, uint64_t* keys, cudaStream_t s) {
+  const uint64_t n = static_cast<uint64_t>(nq) * F;
+  if (n == 0) return cudaSuccess;
+  export_keys_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(cand, cap, cnt, nq, F, base, keys);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_trim_keys(uint64_t* cand, uint32_t cap, uint32_t Fp, uint32_t nq, uint32_t base,
+                             const uint64_t* thr, cudaStream_t s) {
+  const uint64_t n = static_cast<uint64_t>(nq) * Fp;
+  if (n == 0) return cudaSuccess;
+  trim_keys_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(cand, cap, Fp, nq, base, thr);
+  return cudaGetLastError();
+}
+
+uint32_t keys_threshold_max() { return 32u * kConsumerThreads; }
+
+cudaError_t launch_keys_threshold(const uint64_t* gathered, uint32_t world, uint32_t nq, uint32_t F, uint64_t* thr,
+                                  cudaStream_t s) {
+  const uint32_t maxk = (world * F + kConsumerThreads - 1) / kConsumerThreads;
+  if (maxk <= 8) keys_threshold_kernel<8><<<nq, kConsumerThreads, 0, s>>>(gathered, world, nq, F, thr);
+  else if (maxk <= 16) keys_threshold_kernel<16><<<nq, kConsumerThreads, 0, s>>>(gathered, world, nq, F, thr);
+  else if (maxk <= 32) keys_threshold_kernel<32><<<nq, kConsumerThreads, 0, s>>>(gathered, world, nq, F, thr);
+  else return cudaErrorInvalidValue;
+  return cudaGetLastError();
 }
 
 }  // namespace bv

@@ -122,6 +122,13 @@ cudaError_t launch_expand(const ExpandParams& p, cudaStream_t s);
 cudaError_t launch_prep(const PrepParams& p, cudaStream_t s);
 cudaError_t launch_gemm(const GemmParams& p, uint32_t grid, cudaStream_t s);
 cudaError_t launch_select(const SelectParams& p, cudaStream_t s);
+cudaError_t launch_export_keys(const uint64_t* cand, uint32_t cap, const uint32_t* cnt, uint32_t nq, uint32_t F,
+                               uint32_t base, uint64_t* keys, cudaStream_t s);
+cudaError_t launch_trim_keys(uint64_t* cand, uint32_t cap, uint32_t Fp, uint32_t nq, uint32_t base,
+                             const uint64_t* thr, cudaStream_t s);
+uint32_t keys_threshold_max();
+cudaError_t launch_keys_threshold(const uint64_t* gathered, uint32_t world, uint32_t nq, uint32_t F, uint64_t* thr,
+                                  cudaStream_t s);
 uint32_t compact_block_words();
 cudaError_t launch_mask_count(const uint32_t* mask, uint64_t rows, uint32_t* word_off, uint32_t* block_sum,
                               uint32_t* count, cudaStream_t s);

@@ -221,6 +221,21 @@ class AddonQuantIndex:
                                  cand_counts=cand_counts_ptr or None, cand_exact=cand_exact_ptr or None)
         _lib.check(self._L.bv_search_batch(self._h, C.byref(args), C.c_void_p(stream)))
 
+    def set_scoring(self, scoring: str) -> None:
+        """Score later searches with another mode (codes are shared by all modes)."""
+        _lib.check(self._L.bv_set_scoring(self._h, _lib.SCORING[scoring]))
+        self.scoring = scoring
+
+    def set_batch_timing(self, enable: bool) -> None:
+        """Record the device time of each phase of batched searches (CUDA events)."""
+        _lib.check(self._L.bv_set_batch_timing(self._h, int(enable)))
+
+    def batch_profile(self) -> dict:
+        """Phase device times (ms) and counts of the last batched search."""
+        pr = _lib.BvBatchProfile()
+        _lib.check(self._L.bv_last_batch_profile(self._h, C.byref(pr)))
+        return {f: getattr(pr, f) for f, _ in pr._fields_}
+
     def query_rows_exact(self, q: np.ndarray, rows: np.ndarray, k: int) -> list[FlatHit]:
         """index.ts:445-464 on the GPU (rows <= 4096)."""
         q = np.ascontiguousarray(q, dtype=np.float32)

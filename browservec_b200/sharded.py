@@ -14,6 +14,13 @@ those by exact score.
 Record layout (u32 words, one per rank, ``record_words(nq, F)`` long):
 ``[rows nq*F | approx nq*F | exact nq*F | counts nq]`` -- rows are global.
 
+Batched engines search in two halves when W > 1: each rank selects its best
+F approximate keys (``select_keys``), one all-gather of those keys gives every
+rank the global F-th best key per query (``keys_threshold``), and each rank
+then re-ranks only its own keys at or above it (``finish_record``) -- its
+members of the global best F, about F / W rows per query instead of F.  The
+records and the merge are unchanged.
+
 The CUDA engine is the only engine shipped; tests substitute their own
 ``engine`` object to exercise the distributed plumbing on CPU ranks.
 """
@@ -110,6 +117,48 @@ class CudaShardEngine:
         fn = self.L.bv_search_batch if self.batched else self.L.bv_search_async
         _lib.check(fn(self.index._h, C.byref(args), C.c_void_p(stream)))
 
+    @property
+    def two_phase(self) -> bool:
+        return self.batched
+
+    def _args(self, q, k, fetch, rec, mask):
+        nq = q.shape[0]
+        v = record_views(rec, nq, fetch) if rec is not None else None
+        if not hasattr(self, "_scratch") or self._scratch.numel() < nq * (2 * k + 1):
+            self._scratch = self.torch.empty(nq * (2 * k + 1), dtype=self.torch.int32, device=self.device)
+        s = self._scratch
+        return _lib.BvSearchArgs(queries=q.data_ptr(), nq=nq, k=k, fetch=fetch, rerank=1,
+                                 mask=None if mask is None else mask.data_ptr(),
+                                 mask_words=0 if mask is None else mask.numel(),
+                                 out_rows=s.data_ptr(), out_scores=s[nq * k:].data_ptr(),
+                                 out_counts=s[2 * nq * k:].data_ptr(),
+                                 cand_rows=v.rows.data_ptr() if v else None,
+                                 cand_scores=v.approx.data_ptr() if v else None,
+                                 cand_counts=v.counts.data_ptr() if v else None,
+                                 cand_exact=v.exact.data_ptr() if v else None)
+
+    def select_keys(self, q, k: int, fetch: int, stream: int, mask=None):
+        """First half of a batched shard search: this shard's best `fetch`
+        approximate keys per query (int64 view of u64 keys, global rows)."""
+        nq = q.shape[0]
+        keys = self.torch.empty(nq * fetch, dtype=self.torch.int64, device=self.device)
+        args = self._args(q, k, fetch, None, mask)
+        _lib.check(self.L.bv_batch_select(self.index._h, C.byref(args), C.c_void_p(keys.data_ptr()),
+                                          C.c_void_p(stream)))
+        return keys
+
+    def keys_threshold(self, gathered, world: int, nq: int, fetch: int, stream: int):
+        thr = self.torch.empty(nq, dtype=self.torch.int64, device=self.device)
+        _lib.check(self.L.bv_keys_threshold(C.c_void_p(gathered.data_ptr()), world, nq, fetch,
+                                            C.c_void_p(thr.data_ptr()), C.c_void_p(stream)))
+        return thr
+
+    def finish_record(self, q, k: int, fetch: int, rec, stream: int, mask, thr) -> None:
+        """Second half: re-rank this shard's candidates at or above thr[q]."""
+        args = self._args(q, k, fetch, rec, mask)
+        _lib.check(self.L.bv_batch_finish(self.index._h, C.byref(args), C.c_void_p(thr.data_ptr()),
+                                          C.c_void_p(stream)))
+
     def merge(self, gathered, world: int, nq: int, k: int, fetch: int, stream: int):
         torch = self.torch
         rows = torch.empty((nq, k), dtype=torch.int32, device=self.device)
@@ -157,6 +206,11 @@ class ShardedIndex:
             self._stream = None
         self.engine = engine
 
+    def set_scoring(self, scoring: str, batched: bool | None = None) -> None:
+        """Score later searches with another mode (every rank must call it)."""
+        self.engine.index.set_scoring(scoring)
+        self.engine.batched = scoring != "asym" if batched is None else batched
+
     @property
     def local_rows(self) -> int:
         return self.hi - self.lo
@@ -186,7 +240,14 @@ class ShardedIndex:
         with ctx:
             sid = self._stream.cuda_stream if self._stream is not None else 0
             rec = self.engine.new_record(nq, fetch)
-            self.engine.search_record(q, k, fetch, rec, sid, mask)
+            if self.world > 1 and getattr(self.engine, "two_phase", False):
+                keys = self.engine.select_keys(q, k, fetch, sid, mask)
+                gk = torch.empty(self.world * keys.numel(), dtype=keys.dtype, device=keys.device)
+                self.dist.all_gather_into_tensor(gk, keys, group=self.group)
+                thr = self.engine.keys_threshold(gk, self.world, nq, fetch, sid)
+                self.engine.finish_record(q, k, fetch, rec, sid, mask, thr)
+            else:
+                self.engine.search_record(q, k, fetch, rec, sid, mask)
             gathered = torch.empty(self.world * rec.numel(), dtype=rec.dtype, device=rec.device)
             self.dist.all_gather_into_tensor(gathered, rec, group=self.group)
             out = self.engine.merge(gathered, self.world, nq, k, fetch, sid)

@@ -188,6 +188,52 @@ BV_API int bv_launches_last_search(const bv_index* idx, uint32_t* launches);
  * device memory).  Synchronises `stream` before returning. */
 BV_API int bv_search_batch(bv_index* idx, const bv_search_args* args, void* stream);
 
+/* The batched search of a row-sharded corpus in two halves, so that each
+ * shard re-ranks only its members of the global best F instead of its own
+ * best F (the per-shard work the reference's chunk loop does not split:
+ * QuantIndex.search, src/index/quant.ts:194-245, over ChunkedCorpus,
+ * src/engine/buffers.ts:92-214).
+ *
+ * bv_batch_select: bv_search_batch's candidate rounds only.  Writes per query
+ * q its best `fetch` approximate keys to keys_out[q*F .. q*F+F) (F = max(fetch,
+ * k); DEVICE memory; u64 key = orderable(score) << 32 | ~global_row, larger =
+ * better; unsorted, zero padded) and keeps the candidates in the index for
+ * bv_batch_finish.  Synchronises `stream`. */
+BV_API int bv_batch_select(bv_index* idx, const bv_search_args* args, uint64_t* keys_out, void* stream);
+
+/* Per query, the least key of the global best F among `world` shards' key
+ * lists as bv_batch_select writes them, gathered in rank order (gathered:
+ * world x nq x fetch u64, DEVICE).  thr_out[q] (DEVICE) is a key such that
+ * exactly min(F, keys present) gathered keys are >= it (1 when fewer than F
+ * keys exist).  world x fetch <= 16384.  Enqueued on `stream`. */
+BV_API int bv_keys_threshold(const uint64_t* gathered, uint32_t world, uint32_t nq, uint32_t fetch,
+                             uint64_t* thr_out, void* stream);
+
+/* The second half: the same request as the preceding bv_batch_select on this
+ * index.  Candidates whose global key is below min_keys[q] (DEVICE; NULL keeps
+ * all) are dropped, the rest re-ranked exactly; outputs as bv_search_batch
+ * (cand_* hold the kept candidates only).  With min_keys from
+ * bv_keys_threshold, the shard records merge (bv_merge_shards) to the single-
+ * index answer.  Synchronises `stream`. */
+BV_API int bv_batch_finish(bv_index* idx, const bv_search_args* args, const uint64_t* min_keys, void* stream);
+
+/* Device time of the phases of the last batched search (events on its stream),
+ * when enabled with bv_set_batch_timing (off by default).  gemm_macs: queries x
+ * contracted rows x paddedDim, the algorithmic multiply-adds of the GEMM. */
+typedef struct bv_batch_profile {
+  float prep_ms, gemm_ms, select_ms, tail_ms, compact_ms;
+  uint32_t gemm_launches, rounds, kept_rows, nq;
+  double gemm_macs;
+} bv_batch_profile;
+BV_API int bv_set_batch_timing(bv_index* idx, int enable);
+BV_API int bv_last_batch_profile(bv_index* idx, bv_batch_profile* out);
+
+/* Change the scoring mode of an index (BV_SCORE_*; hamming needs bits 1, the
+ * exact index keeps asym).  Codes are shared by every mode, so this only
+ * changes how later searches score.  No counterpart in the reference (its
+ * scoring is always asym, src/index/quant.ts:187). */
+BV_API int bv_set_scoring(bv_index* idx, uint32_t scoring);
+
 /* Cross-shard merge of a row-sharded search (DEVICE pointers, enqueued on
  * `stream`).  The corpus is split into W contiguous row ranges, one per GPU;
  * each shard runs bv_search_async with cand_rows/cand_scores/cand_exact/

@@ -685,3 +685,86 @@ int bvo_query_batch(int bits, int mode, int dim, int P, const float *signs, int 
   p.counts_out = counts_out;
   return run_threads(p, nq, nthreads);
 }
+
+/* ------------------------------------------ sharded CPU baseline (bench) */
+
+/* The reference CPU path over a corpus split into row shards, as one
+ * CpuIndex per shard (cpu.ts:66-88: WASM-SIMD dot, then topK of flat.ts:217-239
+ * over the shard's rows) and the final merge of every shard's k hits with
+ * mergePartials (gpuTopk.ts:160-189).  A wasm32 CpuIndex holds at most ~4 GiB
+ * of corpus (cpu.ts:97-104), so a large corpus needs several.  Thread t owns
+ * shards t, t + T, ... and runs the queries in order over them (one process
+ * per shard in the reference's terms); the merge follows a join.  Shard s
+ * holds global rows base[s] .. base[s] + rows[s] (or the rows listed in
+ * map[s] when given: a filtered shard compacted to its kept rows). */
+typedef struct {
+  const float *const *data;
+  const int64_t *rows, *base;
+  const uint32_t *const *map;
+  int nshards, dim, nq, k, t, nthreads;
+  const float *qs;
+  float *part_scores; /* nq x nshards x k */
+  uint32_t *part_rows;
+} shard_job_t;
+
+static void *run_shard_job(void *arg) {
+  shard_job_t *j = (shard_job_t *)arg;
+  int64_t most = 0;
+  for (int s = j->t; s < j->nshards; s += j->nthreads) most = j->rows[s] > most ? j->rows[s] : most;
+  float *sc = (float *)malloc(sizeof(float) * (size_t)(most > 0 ? most : 1));
+  uint32_t *ro = (uint32_t *)malloc(sizeof(uint32_t) * (size_t)j->k);
+  float *so = (float *)malloc(sizeof(float) * (size_t)j->k);
+  for (int i = 0; i < j->nq; i++) {
+    const float *q = j->qs + (size_t)i * j->dim;
+    for (int s = j->t; s < j->nshards; s += j->nthreads) {
+      float *ps = j->part_scores + ((size_t)i * j->nshards + s) * j->k;
+      uint32_t *pr = j->part_rows + ((size_t)i * j->nshards + s) * j->k;
+      int n = 0;
+      if (j->rows[s] > 0) {
+        bvo_wasm_dot(j->data[s], q, sc, j->rows[s], j->dim);
+        n = bvo_topk_ref(sc, j->rows[s], j->k, ro, so);
+      }
+      for (int h = 0; h < j->k; h++) {
+        if (h < n) {
+          ps[h] = so[h];
+          pr[h] = j->map && j->map[s] ? j->map[s][ro[h]] : (uint32_t)(j->base[s] + ro[h]);
+        } else {
+          ps[h] = -3.4028234663852886e38f; /* filler, dropped by the merge */
+          pr[h] = 0xFFFFFFFFu;
+        }
+      }
+    }
+  }
+  free(sc);
+  free(ro);
+  free(so);
+  return NULL;
+}
+
+int bvo_cpu_sharded_query_batch(const float *const *data, const int64_t *rows, const int64_t *base,
+                                const uint32_t *const *map, int nshards, int64_t total_rows, int dim,
+                                const float *qs, int nq, int k, int nthreads, uint32_t *rows_out,
+                                float *scores_out, int32_t *counts_out) {
+  if (nthreads < 1) nthreads = 1;
+  if (nthreads > nshards) nthreads = nshards;
+  float *ps = (float *)malloc(sizeof(float) * (size_t)nq * nshards * k);
+  uint32_t *pr = (uint32_t *)malloc(sizeof(uint32_t) * (size_t)nq * nshards * k);
+  pthread_t *th = (pthread_t *)malloc(sizeof(pthread_t) * (size_t)nthreads);
+  shard_job_t *jobs = (shard_job_t *)malloc(sizeof(shard_job_t) * (size_t)nthreads);
+  for (int t = 0; t < nthreads; t++) {
+    shard_job_t j = {data, rows, base, map, nshards, dim, nq, k, t, nthreads, qs, ps, pr};
+    jobs[t] = j;
+    pthread_create(&th[t], NULL, run_shard_job, &jobs[t]);
+  }
+  for (int t = 0; t < nthreads; t++) pthread_join(th[t], NULL);
+  for (int i = 0; i < nq; i++) {
+    const size_t o = (size_t)i * nshards * k;
+    counts_out[i] = bvo_merge_partials_ref(ps + o, pr + o, (int64_t)nshards * k, total_rows, k,
+                                           rows_out + (size_t)i * k, scores_out + (size_t)i * k);
+  }
+  free(ps);
+  free(pr);
+  free(th);
+  free(jobs);
+  return 0;
+}

@@ -149,6 +149,13 @@ int bvo_query_batch(int bits, int mode, int dim, int P, const float *signs, int 
                     int rerank, int nthreads, uint32_t *rows_out, float *scores_out,
                     int32_t *counts_out);
 
+/* Sharded CPU baseline: one CpuIndex per row shard (cpu.ts:66-88 + flat.ts:217-239),
+ * merged with mergePartials (gpuTopk.ts:160-189); see bv_oracle.c. */
+int bvo_cpu_sharded_query_batch(const float *const *data, const int64_t *rows, const int64_t *base,
+                                const uint32_t *const *map, int nshards, int64_t total_rows, int dim,
+                                const float *qs, int nq, int k, int nthreads, uint32_t *rows_out,
+                                float *scores_out, int32_t *counts_out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -69,6 +69,7 @@ def lib():
             "bvo_cpu_index_query_batch": (i32, [P, i64, i32, P, i32, i32, i32, P, P]),
             "bvo_query_batch": (i32, [i32, i32, i32, i32, P, i32, P, P, P, i64, P, P, i32, i32,
                                       i32, i32, i32, P, P, P]),
+            "bvo_cpu_sharded_query_batch": (i32, [P, P, P, P, i32, i64, i32, P, i32, i32, i32, P, P, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -346,6 +347,33 @@ def cpu_index_query_batch(data, dim: int, qs, k: int, threads: int = 0):
     so = np.zeros((nq, k), np.float32)
     lib().bvo_cpu_index_query_batch(_p(data), rows, dim, _p(qs), nq, k, threads, _p(ro), _p(so))
     return ro, so
+
+
+def cpu_sharded_query_batch(shards, bases, total_rows: int, dim: int, qs, k: int, threads: int = 0,
+                            maps=None):
+    """One CpuIndex per row shard (cpu.ts:66-88: WASM-SIMD dot + topK of
+    flat.ts:217-239), the shards' hits merged with mergePartials
+    (gpuTopk.ts:160-189).  shards: float32 arrays (rows_s, dim); bases: the
+    global row of each shard's first row; maps (optional): per shard, the
+    global row of each of its rows.  Returns (rows, scores, counts)."""
+    shards = [_f32(a).reshape(-1, dim) for a in shards]
+    qs = _f32(qs).reshape(-1, dim)
+    ns, nq = len(shards), qs.shape[0]
+    threads = threads or os.cpu_count() or 1
+    ptrs = (C.c_void_p * ns)(*[a.ctypes.data for a in shards])
+    rows = np.array([a.shape[0] for a in shards], np.int64)
+    base = np.array(bases, np.int64)
+    mp = None
+    if maps is not None:
+        maps = [_u32(m) for m in maps]
+        mp = (C.c_void_p * ns)(*[m.ctypes.data for m in maps])
+    ro = np.zeros((nq, k), np.uint32)
+    so = np.zeros((nq, k), np.float32)
+    cnt = np.zeros(nq, np.int32)
+    lib().bvo_cpu_sharded_query_batch(C.cast(ptrs, C.c_void_p), _p(rows), _p(base),
+                                      None if mp is None else C.cast(mp, C.c_void_p), ns, total_rows, dim,
+                                      _p(qs), nq, k, threads, _p(ro), _p(so), _p(cnt))
+    return ro, so, cnt
 
 
 def keys(scores, rows) -> np.ndarray:

@@ -100,3 +100,72 @@ def test_merge_rejects_bad_arguments():
             e.merge(g, 65, 1, 1, 5, 0)
     finally:
         e.destroy()
+
+
+@pytest.mark.parametrize("bits,scoring,world,n,d,k,fetch,nq", [
+    (1, "hamming", 8, 40000, 768, 100, 1000, 70),
+    (1, "int", 4, 30011, 768, 100, 1000, 130),
+    (4, "int", 3, 20000, 384, 10, 80, 200),
+    (8, "int", 2, 9001, 128, 10, 40, 64),
+    (8, "int", 5, 12, 64, 2, 8, 3),  # fewer rows per shard than fetch: every key is a member
+])
+def test_two_phase_batched_shards_equal_single_index(bits, scoring, world, n, d, k, fetch, nq):
+    """bv_batch_select on every shard, the keys concatenated in rank order (the
+    all-gather), bv_keys_threshold, bv_batch_finish with that threshold, then
+    bv_merge_shards: bit-identical to one index's bv_search_batch, with the
+    shards' members partitioning the global best F."""
+    import torch
+
+    from browservec_b200.index import AddonQuantIndex
+    from browservec_b200.sharded import CudaShardEngine, record_views, shard_bounds
+
+    x = _rows(n, d, bits * 17 + world)
+    qs = _rows(nq, d, 78)
+    engines, single = [], None
+    try:
+        for r in range(world):
+            lo, hi = shard_bounds(n, world, r)
+            e = CudaShardEngine(d, bits, scoring, O.DEFAULT_SEED, 2, "cosine", 0, lo, batched=True)
+            if hi > lo:
+                e.append(x[lo:hi])
+            engines.append(e)
+        single = AddonQuantIndex(d, bits=bits, scoring=scoring)
+        single.append(x, n)
+        stream = torch.cuda.Stream()
+        q = torch.from_numpy(qs).cuda()
+        F = max(fetch, k)
+        wr = torch.zeros((nq, k), dtype=torch.int32, device="cuda")
+        ws = torch.zeros((nq, k), dtype=torch.float32, device="cuda")
+        wc = torch.zeros(nq, dtype=torch.int32, device="cuda")
+        single.search_batch_device(q.data_ptr(), nq, k, F, True, wr.data_ptr(), ws.data_ptr(), wc.data_ptr(),
+                                   stream=stream.cuda_stream)
+        torch.cuda.synchronize()
+        keys = [e.select_keys(q, k, F, stream.cuda_stream) for e in engines]
+        gk = torch.cat(keys)
+        thr = engines[0].keys_threshold(gk, world, nq, F, stream.cuda_stream)
+        stream.synchronize()
+        # the threshold against a host selection over the gathered keys
+        g = gk.cpu().numpy().view(np.uint64).reshape(world, nq, F)
+        t = thr.cpu().numpy().view(np.uint64)
+        for i in range(nq):
+            ks = g[:, i, :].reshape(-1)
+            ks = ks[ks != 0]
+            assert int((ks >= t[i]).sum()) == min(F, ks.size), i
+        recs = []
+        for e in engines:
+            rec = e.new_record(nq, F)
+            e.finish_record(q, k, F, rec, stream.cuda_stream, None, thr)
+            recs.append(rec)
+        gathered = torch.cat(recs)
+        rows, scores, counts = engines[0].merge(gathered, world, nq, k, F, stream.cuda_stream)
+        stream.synchronize()
+        members = sum(int(record_views(r, nq, F).counts.sum().item()) for r in recs)
+        assert members == nq * min(F, n)
+        assert torch.equal(counts, wc)
+        assert torch.equal(rows, wr)
+        assert torch.equal(scores.view(torch.int32), ws.view(torch.int32))
+    finally:
+        for e in engines:
+            e.destroy()
+        if single is not None:
+            single.destroy()

@@ -89,6 +89,48 @@ class OracleShardEngine:
             v.exact[i * fetch:i * fetch + n] = exact.view(np.int32)
             v.counts[i] = n
 
+    # two-phase batched flow (select keys -> all-gather -> global threshold ->
+    # re-rank only this shard's members of the global best F)
+    two_phase = False
+
+    def select_keys(self, q, k, fetch, stream, mask=None):
+        nq = q.shape[0]
+        out = np.zeros((nq, fetch), np.uint64)
+        self._cands = []
+        for i in range(nq):
+            _, _, cr, cs = self.corpus.query(q[i].numpy(), k, fetch, self.mode)
+            self._cands.append((cr, cs))
+            out[i, :cr.size] = O.keys(cs, cr.astype(np.uint32) + np.uint32(self.row_base))
+        return torch.from_numpy(out.reshape(-1).view(np.int64))
+
+    def keys_threshold(self, gathered, world, nq, fetch, stream):
+        g = gathered.numpy().view(np.uint64).reshape(world, nq, fetch)
+        thr = np.ones(nq, np.uint64)
+        for i in range(nq):
+            ks = np.sort(g[:, i, :].reshape(-1))[::-1]
+            ks = ks[ks != 0]
+            if ks.size > fetch:
+                thr[i] = ks[fetch - 1]
+        return torch.from_numpy(thr.view(np.int64))
+
+    def finish_record(self, q, k, fetch, rec, stream, mask, thr):
+        nq = q.shape[0]
+        v = record_views(rec.numpy(), nq, fetch)
+        t = thr.numpy().view(np.uint64)
+        for i in range(nq):
+            cr, cs = self._cands[i]
+            rows = cr.astype(np.uint32) + np.uint32(self.row_base)
+            keep = O.keys(cs, rows) >= t[i]
+            rows, approx = rows[keep], cs[keep].astype(np.float32)
+            exact = np.array([np.float32(O.dot_row(self.corpus.originals[r - self.row_base], q[i].numpy()))
+                              for r in rows], np.float32)
+            n = rows.size
+            v.rows[i * fetch:i * fetch + n] = rows.view(np.int32)
+            v.approx[i * fetch:i * fetch + n] = approx.view(np.int32)
+            v.exact[i * fetch:i * fetch + n] = exact.view(np.int32)
+            v.counts[i] = n
+        self.members = int(v.counts[:nq].sum())
+
     def merge(self, gathered, world, nq, k, fetch, stream):
         g = gathered.numpy().reshape(world, record_words(nq, fetch))
         rows = np.zeros((nq, k), np.int32)
@@ -113,7 +155,7 @@ class OracleShardEngine:
 N, D, BITS, MODE, K, FETCH, NQ = 777, 32, 8, O.MODE_ASYM, 5, 20, 3
 
 
-def _rank_main(rank, world, port, out_dir):
+def _rank_main(rank, world, port, out_dir, two_phase=False):
     import torch.distributed as dist
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
@@ -121,12 +163,15 @@ def _rank_main(rank, world, port, out_dir):
     try:
         x = _rows(N, D, 5)
         lo, _ = shard_bounds(N, world, rank)
-        idx = ShardedIndex(D, N, bits=BITS, engine=OracleShardEngine(D, BITS, MODE, lo))
+        eng = OracleShardEngine(D, BITS, MODE, lo)
+        eng.two_phase = two_phase
+        idx = ShardedIndex(D, N, bits=BITS, engine=eng)
         idx.load(x, global_rows=True)
         q = torch.from_numpy(_rows(NQ, D, 6))
         rows, scores, counts = idx.search(q, K, FETCH)
+        members = torch.tensor([getattr(eng, "members", -1)])
         np.savez(os.path.join(out_dir, f"r{rank}.npz"), rows=rows.numpy(), scores=scores.numpy(),
-                 counts=counts.numpy())
+                 counts=counts.numpy(), members=members.numpy())
     finally:
         dist.destroy_process_group()
 
@@ -154,3 +199,28 @@ def test_gloo_two_ranks_match_single_store(tmp_path):
             assert n == wr.size
             assert np.array_equal(got["rows"][i, :n].view(np.uint32), wr)
             assert np.array_equal(got["scores"][i, :n].view(np.uint32), ws.view(np.uint32))
+
+
+def test_gloo_three_ranks_two_phase_members_only(tmp_path):
+    """The two-phase flow: every rank re-ranks only its members of the global
+    best F (together exactly F per query), and the merged answer is still the
+    single-store answer."""
+    import torch.multiprocessing as mp
+
+    world = 3
+    mp.start_processes(_rank_main, args=(world, _free_port(), str(tmp_path), True), nprocs=world,
+                       start_method="spawn")
+    x = _rows(N, D, 5)
+    full = O.Corpus(x, D, BITS)
+    qs = _rows(NQ, D, 6)
+    members = 0
+    for r in range(world):
+        got = np.load(tmp_path / f"r{r}.npz")
+        members += int(got["members"][0])
+        for i in range(NQ):
+            wr, ws, _, _ = full.query(qs[i], K, FETCH, MODE)
+            n = int(got["counts"][i])
+            assert n == wr.size
+            assert np.array_equal(got["rows"][i, :n].view(np.uint32), wr)
+            assert np.array_equal(got["scores"][i, :n].view(np.uint32), ws.view(np.uint32))
+    assert members == NQ * FETCH  # the shards' members partition the global best F
