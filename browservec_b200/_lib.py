@@ -21,7 +21,8 @@ EXPORTS = ("bv_create", "bv_destroy", "bv_last_error", "bv_append", "bv_append_d
            "bv_search", "bv_search_async", "bv_search_async_n", "bv_query_rows_exact", "bv_export_codes", "bv_get_stats",
            "bv_launches_last_search", "bv_set_phase_trace", "bv_search_noalloc",
            "bv_merge_shards", "bv_search_batch", "bv_filter_mask", "bv_batch_select", "bv_batch_finish",
-           "bv_keys_threshold", "bv_set_batch_timing", "bv_last_batch_profile", "bv_set_scoring")
+           "bv_keys_threshold", "bv_set_batch_timing", "bv_last_batch_profile", "bv_set_scoring",
+           "bv_merge_topk")
 
 
 class BvConfig(C.Structure):
@@ -115,6 +116,7 @@ def load(path: str = LIB_PATH):
         "bv_set_batch_timing": (C.c_int, [P, C.c_int]),
         "bv_last_batch_profile": (C.c_int, [P, C.POINTER(BvBatchProfile)]),
         "bv_set_scoring": (C.c_int, [P, C.c_uint32]),
+        "bv_merge_topk": (C.c_int, [P, C.c_uint32, C.c_uint32, C.c_uint32, P, P, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

@@ -1019,6 +1019,21 @@ int bv_merge_shards(const uint32_t* gathered, uint32_t world, uint32_t nq, uint3
   return BV_OK;
 }
 
+int bv_merge_topk(const uint32_t* gathered, uint32_t world, uint32_t nq, uint32_t k, uint32_t* out_rows,
+                  float* out_scores, uint32_t* out_counts, void* stream) {
+  if (nq && (!gathered || !out_rows || !out_scores || !out_counts)) return fail(BV_ERR_INVALID, "null argument");
+  if (world == 0 || world > bv::merge_max_world())
+    return fail(BV_ERR_INVALID, "world %u outside [1, %u]", world, bv::merge_max_world());
+  if (k == 0 || k > kMaxFetch) return fail(BV_ERR_INVALID, "k %u outside [1, %u]", k, kMaxFetch);
+  if (nq == 0) return BV_OK;
+  const cudaError_t e = bv::launch_merge_topk(gathered, world, nq, k, out_rows, out_scores, out_counts,
+                                              static_cast<cudaStream_t>(stream));
+  if (e == cudaErrorInvalidValue)
+    return fail(BV_ERR_UNSUPPORTED, "merge of %u shards x %u results does not fit in shared memory", world, k);
+  if (e != cudaSuccess) return cuda_fail(nullptr, e, "merge launch");
+  return BV_OK;
+}
+
 // ------------------------------------------------------- batched search
 namespace {
 
@@ -1568,8 +1583,7 @@ int bv_batch_select(bv_index* idx, const bv_search_args* a, uint64_t* keys_out, 
         bv::launch_export_keys(idx->d_bcand, bs->cap, idx->d_bcnt, nq, F, idx->row_base, keys_out, s);
     if (e != cudaSuccess) return cuda_fail(idx, e, "export keys");
   }
-  BV_CUDA(idx, cudaStreamSynchronize(s), "batch select");
-  return BV_OK;
+  return BV_OK;  // the keys are written in stream order (the rounds themselves synchronised)
 }
 
 int bv_batch_finish(bv_index* idx, const bv_search_args* a, const uint64_t* min_keys, void* stream) {

@@ -118,7 +118,60 @@ __global__ void __launch_bounds__(kMergeThreads) merge_shards_kernel(
   if (t == 0) out_counts[q] = n < k ? n : k;
 }
 
+// One CTA per query: the best k of W lists of (row, exact score) pairs, each
+// sorted by (score desc, row asc) with its own count, gathered in rank order
+// as W records of [rows nq*k | scores nq*k | counts nq] u32 words.  An
+// entry's rank is its index in its list plus, in every other list, the
+// entries ahead of it (binary search over the keys staged in shared memory).
+__global__ void __launch_bounds__(kMergeThreads) merge_topk_kernel(
+    const uint32_t* __restrict__ gathered, uint32_t world, uint32_t nq, uint32_t k,
+    uint32_t* __restrict__ out_rows, float* __restrict__ out_scores, uint32_t* __restrict__ out_counts) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  uint64_t* key = reinterpret_cast<uint64_t*>(smem);  // world*k keys
+  __shared__ uint32_t len[kMaxWorld];
+  const uint32_t q = blockIdx.x;
+  const size_t plane = static_cast<size_t>(nq) * k;
+  const size_t rec = 2 * plane + nq;
+  const int t = threadIdx.x;
+  if (t < static_cast<int>(world)) {
+    const uint32_t c = gathered[static_cast<size_t>(t) * rec + 2 * plane + q];
+    len[t] = c < k ? c : k;
+  }
+  __syncthreads();
+  for (uint32_t i = t; i < world * k; i += kMergeThreads) {
+    const uint32_t w = i / k, j = i - w * k;
+    const uint32_t* r = gathered + static_cast<size_t>(w) * rec + static_cast<size_t>(q) * k;
+    key[i] = j < len[w] ? make_key(__uint_as_float(r[plane + j]), r[j]) : 0ull;
+  }
+  __syncthreads();
+  uint32_t total = 0;
+  for (uint32_t w = 0; w < world; ++w) total += len[w];
+  for (uint32_t i = t; i < world * k; i += kMergeThreads) {
+    const uint32_t w = i / k, j = i - w * k;
+    if (j >= len[w]) continue;
+    const uint64_t kk = key[i];
+    uint32_t rank = j;
+    for (uint32_t v = 0; v < world && rank < k; ++v)
+      if (v != w) rank += count_greater(key + static_cast<size_t>(v) * k, len[v], kk);
+    if (rank < k) {
+      out_rows[static_cast<size_t>(q) * k + rank] = key_row(kk);
+      out_scores[static_cast<size_t>(q) * k + rank] = key_score(kk);
+    }
+  }
+  if (t == 0) out_counts[q] = total < k ? total : k;
+}
+
 }  // namespace
+
+cudaError_t launch_merge_topk(const uint32_t* gathered, uint32_t world, uint32_t nq, uint32_t k,
+                              uint32_t* out_rows, float* out_scores, uint32_t* out_counts, cudaStream_t stream) {
+  static int opted[kMaxDevices] = {};
+  const size_t smem = static_cast<size_t>(world) * k * 8;
+  const cudaError_t e = opt_in_smem(reinterpret_cast<const void*>(merge_topk_kernel), smem, opted);
+  if (e != cudaSuccess) return e;
+  merge_topk_kernel<<<nq, kMergeThreads, smem, stream>>>(gathered, world, nq, k, out_rows, out_scores, out_counts);
+  return cudaGetLastError();
+}
 
 size_t merge_smem_bytes(uint32_t world, uint32_t F) {
   return static_cast<size_t>(world) * F * 12 + static_cast<size_t>(F) * 8;

@@ -17,9 +17,12 @@ Record layout (u32 words, one per rank, ``record_words(nq, F)`` long):
 Batched engines search in two halves when W > 1: each rank selects its best
 F approximate keys (``select_keys``), one all-gather of those keys gives every
 rank the global F-th best key per query (``keys_threshold``), and each rank
-then re-ranks only its own keys at or above it (``finish_record``) -- its
-members of the global best F, about F / W rows per query instead of F.  The
-records and the merge are unchanged.
+then re-ranks only its own keys at or above it -- its members of the global
+best F, about F / W rows per query instead of F -- and contributes its best k
+of them by exact score (``finish_topk``: a record of ``topk_words(nq, k)``
+words ``[rows nq*k | scores nq*k | counts nq]``).  A second all-gather and
+``merge_topk`` give the single-store answer, since the members of all ranks
+are exactly the global best F.
 
 The CUDA engine is the only engine shipped; tests substitute their own
 ``engine`` object to exercise the distributed plumbing on CPU ranks.
@@ -48,6 +51,10 @@ def shard_bounds(n: int, world: int, rank: int) -> tuple[int, int]:
 
 def record_words(nq: int, fetch: int) -> int:
     return 3 * nq * fetch + nq
+
+
+def topk_words(nq: int, k: int) -> int:
+    return 2 * nq * k + nq
 
 
 @dataclass
@@ -154,10 +161,35 @@ class CudaShardEngine:
         return thr
 
     def finish_record(self, q, k: int, fetch: int, rec, stream: int, mask, thr) -> None:
-        """Second half: re-rank this shard's candidates at or above thr[q]."""
+        """Second half, full record: re-rank this shard's candidates at or
+        above thr[q] and write them (rows, approximate and exact scores)."""
         args = self._args(q, k, fetch, rec, mask)
         _lib.check(self.L.bv_batch_finish(self.index._h, C.byref(args), C.c_void_p(thr.data_ptr()),
                                           C.c_void_p(stream)))
+
+    def finish_topk(self, q, k: int, fetch: int, stream: int, mask, thr):
+        """Second half: re-rank this shard's candidates at or above thr[q];
+        returns its best k of them as a top-k record (global rows)."""
+        nq = q.shape[0]
+        out = self.torch.empty(topk_words(nq, k), dtype=self.torch.int32, device=self.device)
+        args = _lib.BvSearchArgs(queries=q.data_ptr(), nq=nq, k=k, fetch=fetch, rerank=1,
+                                 mask=None if mask is None else mask.data_ptr(),
+                                 mask_words=0 if mask is None else mask.numel(),
+                                 out_rows=out.data_ptr(), out_scores=out[nq * k:].data_ptr(),
+                                 out_counts=out[2 * nq * k:].data_ptr())
+        _lib.check(self.L.bv_batch_finish(self.index._h, C.byref(args), C.c_void_p(thr.data_ptr()),
+                                          C.c_void_p(stream)))
+        return out
+
+    def merge_topk(self, gathered, world: int, nq: int, k: int, stream: int):
+        torch = self.torch
+        rows = torch.empty((nq, k), dtype=torch.int32, device=self.device)
+        scores = torch.empty((nq, k), dtype=torch.float32, device=self.device)
+        counts = torch.empty(nq, dtype=torch.int32, device=self.device)
+        _lib.check(self.L.bv_merge_topk(C.c_void_p(gathered.data_ptr()), world, nq, k,
+                                        C.c_void_p(rows.data_ptr()), C.c_void_p(scores.data_ptr()),
+                                        C.c_void_p(counts.data_ptr()), C.c_void_p(stream)))
+        return rows, scores, counts
 
     def merge(self, gathered, world: int, nq: int, k: int, fetch: int, stream: int):
         torch = self.torch
@@ -239,18 +271,21 @@ class ShardedIndex:
         ctx = torch.cuda.stream(self._stream) if self._stream is not None else nullcontext()
         with ctx:
             sid = self._stream.cuda_stream if self._stream is not None else 0
-            rec = self.engine.new_record(nq, fetch)
             if self.world > 1 and getattr(self.engine, "two_phase", False):
                 keys = self.engine.select_keys(q, k, fetch, sid, mask)
                 gk = torch.empty(self.world * keys.numel(), dtype=keys.dtype, device=keys.device)
                 self.dist.all_gather_into_tensor(gk, keys, group=self.group)
                 thr = self.engine.keys_threshold(gk, self.world, nq, fetch, sid)
-                self.engine.finish_record(q, k, fetch, rec, sid, mask, thr)
+                rec = self.engine.finish_topk(q, k, fetch, sid, mask, thr)
+                gathered = torch.empty(self.world * rec.numel(), dtype=rec.dtype, device=rec.device)
+                self.dist.all_gather_into_tensor(gathered, rec, group=self.group)
+                out = self.engine.merge_topk(gathered, self.world, nq, k, sid)
             else:
+                rec = self.engine.new_record(nq, fetch)
                 self.engine.search_record(q, k, fetch, rec, sid, mask)
-            gathered = torch.empty(self.world * rec.numel(), dtype=rec.dtype, device=rec.device)
-            self.dist.all_gather_into_tensor(gathered, rec, group=self.group)
-            out = self.engine.merge(gathered, self.world, nq, k, fetch, sid)
+                gathered = torch.empty(self.world * rec.numel(), dtype=rec.dtype, device=rec.device)
+                self.dist.all_gather_into_tensor(gathered, rec, group=self.group)
+                out = self.engine.merge(gathered, self.world, nq, k, fetch, sid)
         if self._stream is not None:
             torch.cuda.current_stream(self.engine.device).wait_stream(self._stream)
         return out

@@ -198,7 +198,8 @@ BV_API int bv_search_batch(bv_index* idx, const bv_search_args* args, void* stre
  * q its best `fetch` approximate keys to keys_out[q*F .. q*F+F) (F = max(fetch,
  * k); DEVICE memory; u64 key = orderable(score) << 32 | ~global_row, larger =
  * better; unsorted, zero padded) and keeps the candidates in the index for
- * bv_batch_finish.  Synchronises `stream`. */
+ * bv_batch_finish.  The rounds synchronise `stream`; the keys themselves are
+ * written in stream order after the call returns. */
 BV_API int bv_batch_select(bv_index* idx, const bv_search_args* args, uint64_t* keys_out, void* stream);
 
 /* Per query, the least key of the global best F among `world` shards' key
@@ -216,6 +217,16 @@ BV_API int bv_keys_threshold(const uint64_t* gathered, uint32_t world, uint32_t 
  * bv_keys_threshold, the shard records merge (bv_merge_shards) to the single-
  * index answer.  Synchronises `stream`. */
 BV_API int bv_batch_finish(bv_index* idx, const bv_search_args* args, const uint64_t* min_keys, void* stream);
+
+/* The final merge of a two-phase sharded batch: each shard's bv_batch_finish
+ * outputs (its best k by exact score among its members of the global best F,
+ * rows global) are all-gathered in rank order as W records of
+ * [rows nq*k | scores nq*k | counts nq] u32 words; writes per query the best k
+ * by (score desc, row asc) -- the single-index answer, since the members of
+ * all shards are exactly the global best F.  DEVICE pointers, enqueued on
+ * `stream`.  world <= 64, k <= 1024. */
+BV_API int bv_merge_topk(const uint32_t* gathered, uint32_t world, uint32_t nq, uint32_t k, uint32_t* out_rows,
+                         float* out_scores, uint32_t* out_counts, void* stream);
 
 /* Device time of the phases of the last batched search (events on its stream),
  * when enabled with bv_set_batch_timing (off by default).  gemm_macs: queries x

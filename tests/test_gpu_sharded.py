@@ -151,6 +151,7 @@ def test_two_phase_batched_shards_equal_single_index(bits, scoring, world, n, d,
             ks = g[:, i, :].reshape(-1)
             ks = ks[ks != 0]
             assert int((ks >= t[i]).sum()) == min(F, ks.size), i
+        # full member records (rows, approximate and exact scores) merged by bv_merge_shards
         recs = []
         for e in engines:
             rec = e.new_record(nq, F)
@@ -164,6 +165,15 @@ def test_two_phase_batched_shards_equal_single_index(bits, scoring, world, n, d,
         assert torch.equal(counts, wc)
         assert torch.equal(rows, wr)
         assert torch.equal(scores.view(torch.int32), ws.view(torch.int32))
+        # and the top-k records of the bench path, merged by bv_merge_topk
+        for e in engines:  # the members are re-selected: select again (the finish consumed them)
+            e.select_keys(q, k, F, stream.cuda_stream)
+        tops = [e.finish_topk(q, k, F, stream.cuda_stream, None, thr) for e in engines]
+        rows2, scores2, counts2 = engines[0].merge_topk(torch.cat(tops), world, nq, k, stream.cuda_stream)
+        stream.synchronize()
+        assert torch.equal(counts2, wc)
+        assert torch.equal(rows2, wr)
+        assert torch.equal(scores2.view(torch.int32), ws.view(torch.int32))
     finally:
         for e in engines:
             e.destroy()

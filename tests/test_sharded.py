@@ -14,7 +14,7 @@ import numpy as np
 import pytest
 import torch
 
-from browservec_b200.sharded import ShardedIndex, record_views, record_words, shard_bounds
+from browservec_b200.sharded import ShardedIndex, record_views, record_words, shard_bounds, topk_words
 from oracle import oracle as O
 
 
@@ -113,23 +113,43 @@ class OracleShardEngine:
                 thr[i] = ks[fetch - 1]
         return torch.from_numpy(thr.view(np.int64))
 
-    def finish_record(self, q, k, fetch, rec, stream, mask, thr):
+    def finish_topk(self, q, k, fetch, stream, mask, thr):
+        """This shard's members of the global best F (keys >= thr), re-ranked
+        exactly; its best k of them as [rows nq*k | scores nq*k | counts nq]."""
         nq = q.shape[0]
-        v = record_views(rec.numpy(), nq, fetch)
+        out = np.zeros(topk_words(nq, k), np.int32)
         t = thr.numpy().view(np.uint64)
+        self.members = 0
         for i in range(nq):
             cr, cs = self._cands[i]
             rows = cr.astype(np.uint32) + np.uint32(self.row_base)
             keep = O.keys(cs, rows) >= t[i]
-            rows, approx = rows[keep], cs[keep].astype(np.float32)
+            rows = rows[keep]
+            self.members += int(rows.size)
             exact = np.array([np.float32(O.dot_row(self.corpus.originals[r - self.row_base], q[i].numpy()))
                               for r in rows], np.float32)
-            n = rows.size
-            v.rows[i * fetch:i * fetch + n] = rows.view(np.int32)
-            v.approx[i * fetch:i * fetch + n] = approx.view(np.int32)
-            v.exact[i * fetch:i * fetch + n] = exact.view(np.int32)
-            v.counts[i] = n
-        self.members = int(v.counts[:nq].sum())
+            order = np.argsort(O.keys(exact, rows))[::-1][:k]
+            n = order.size
+            out[i * k:i * k + n] = rows[order].view(np.int32)
+            out[nq * k + i * k:nq * k + i * k + n] = exact[order].view(np.int32)
+            out[2 * nq * k + i] = n
+        return torch.from_numpy(out)
+
+    def merge_topk(self, gathered, world, nq, k, stream):
+        g = gathered.numpy().reshape(world, topk_words(nq, k))
+        rows = np.zeros((nq, k), np.int32)
+        scores = np.zeros((nq, k), np.float32)
+        counts = np.zeros(nq, np.int32)
+        for i in range(nq):
+            rr, ss = [], []
+            for w in range(world):
+                c = int(g[w, 2 * nq * k + i])
+                rr.append(g[w, i * k:i * k + c].view(np.uint32))
+                ss.append(g[w, nq * k + i * k:nq * k + i * k + c].view(np.float32))
+            rr, ss = np.concatenate(rr), np.concatenate(ss)
+            order = np.argsort(O.keys(ss, rr))[::-1][:k]
+            rows[i, :order.size], scores[i, :order.size], counts[i] = rr[order].view(np.int32), ss[order], order.size
+        return torch.from_numpy(rows), torch.from_numpy(scores), torch.from_numpy(counts)
 
     def merge(self, gathered, world, nq, k, fetch, stream):
         g = gathered.numpy().reshape(world, record_words(nq, fetch))
