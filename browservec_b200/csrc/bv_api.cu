@@ -72,7 +72,7 @@ uint32_t mulberry32_next(uint32_t* state) {
   return t ^ (t >> 14);
 }
 
-uint32_t pad_to_pow2(uint32_t n) {  // rotator.ts:39-43
+uint32_t pad_to_pow2(uint32_t n) {  // rotator.ts:16-21
   uint32_t p = 4;
   while (p < n) p <<= 1;
   return p;
@@ -719,7 +719,7 @@ int bv_create(const bv_config* cfg, bv_index** out) {
   if ((e = cudaStreamCreateWithFlags(&idx->stream, cudaStreamNonBlocking)) != cudaSuccess ||
       (e = cudaEventCreate(&idx->ev0)) != cudaSuccess || (e = cudaEventCreate(&idx->ev1)) != cudaSuccess)
     return bail(cuda_fail(nullptr, e, "stream"));
-  // rotator.ts:66-80: per round, signs from mulberry32((seed ^ 0x9e3779b9*(r+1)) >>> 0),
+  // rotator.ts:44-58: per round, signs from mulberry32((seed ^ 0x9e3779b9*(r+1)) >>> 0),
   // pre-scaled by f32(+-1 * (1/sqrt(P) in f64)).
   const size_t ns = static_cast<size_t>(P) * (cfg->rounds ? cfg->rounds : 1);
   float* hs = new float[ns];
@@ -1633,6 +1633,18 @@ int bv_last_batch_profile(bv_index* idx, bv_batch_profile* out) {
   if (!idx || !out) return fail(BV_ERR_INVALID, "null argument");
   *out = batch_state(idx)->prof;
   return BV_OK;
+}
+
+int bv_check_wait_timeout(bv_index* idx, uint32_t polls) {
+  if (!idx) return fail(BV_ERR_INVALID, "null index");
+  if (idx->lost) return fail(BV_ERR_DEVICE_LOST, "%s", kLostMsg);
+  if (polls == 0 || polls > bv::kWaitBudget)
+    return fail(BV_ERR_INVALID, "polls must be in [1, %u], got %u", bv::kWaitBudget, polls);
+  BV_CUDA(idx, cudaSetDevice(idx->device), "cudaSetDevice");
+  const cudaError_t e = bv::launch_wait_probe(idx->d_err, polls, idx->stream);
+  if (e != cudaSuccess) return cuda_fail(idx, e, "wait probe");
+  BV_CUDA(idx, cudaStreamSynchronize(idx->stream), "wait probe");
+  return check_err_flag(idx);
 }
 
 int bv_set_scoring(bv_index* idx, uint32_t scoring) {

@@ -2,8 +2,8 @@
 //
 //   expand_kernel  codes -> swizzled int8 row tiles + per-row score factor
 //                  (the layout the MMA reads; built once per appended row)
-//   prep_kernel    per query: rotation (rotator.ts:83-92), int8 codec
-//                  (codec.ts:132-154) or signs, swizzled query tiles
+//   prep_kernel    per query: rotation (rotator.ts:60-70), int8 codec
+//                  (codec.ts:32-54) or signs, swizzled query tiles
 //   gemm_kernel    persistent; warp-specialised: one producer warp (bulk
 //                  copies), one MMA warp (tcgen05.mma kind::i8, accumulators
 //                  double-buffered in TMEM), four epilogue warps (tcgen05.ld,

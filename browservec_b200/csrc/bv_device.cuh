@@ -9,7 +9,7 @@
 namespace bv {
 
 // f32(1/127) and f32(1/7): the row factors of the int8 and int4 scorers
-// (distanceQ4.ts:145 folds 1/7 the same way).
+// (distanceQ4.ts:61 folds 1/7 the same way).
 __device__ __constant__ static const float kInv127 = 0x1.020408p-7f;
 __device__ __constant__ static const float kInv7 = 0x1.24924ap-3f;
 
@@ -72,10 +72,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 // Bounded wait: gives up after `budget` polls (each poll is a hardware
 // try_wait that may itself suspend briefly), raising kErrWaitTimeout.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
-                                                  uint32_t* err_flag) {
-  constexpr uint32_t kBudget = 1u << 22;
-  for (uint32_t i = 0; i < kBudget; ++i)
+constexpr uint32_t kWaitBudget = 1u << 22;
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t* err_flag,
+                                                  uint32_t budget = kWaitBudget) {
+  for (uint32_t i = 0; i < budget; ++i)
     if (mbar_try_wait(bar, parity)) return true;
   if (err_flag) atomicOr(err_flag, kErrWaitTimeout);
   return false;

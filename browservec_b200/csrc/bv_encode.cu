@@ -1,6 +1,6 @@
 // bv_encode.cu -- on-device corpus encoder: rotate + quantize each appended row
 // with the exact arithmetic of the reference's ingest path
-// (encode.ts:64-78 -> rotator.ts:83-92 -> codec.ts:132-154 / :186-208 / :236-254),
+// (encode.ts:64-78 -> rotator.ts:60-70 -> codec.ts:32-54 / :85-108 / :135-154),
 // so the codes are bit-identical to the CPU encoder's.  One warp per row.
 #include <cstdint>
 
@@ -15,7 +15,7 @@ __device__ __forceinline__ double js_round_d(double x) {
   return r;
 }
 
-// codec.ts:122-129 / :177-183: clamp to [-1,1], Math.round(c*levels), clamp.
+// codec.ts:22-30 / :77-83: clamp to [-1,1], Math.round(c*levels), clamp.
 __device__ __forceinline__ int snorm_level(double v, double levels) {
   double c = v < -1.0 ? -1.0 : (v > 1.0 ? 1.0 : v);
   double b = js_round_d(__dmul_rn(c, levels));
@@ -99,7 +99,7 @@ __global__ void encode_kernel(const float* __restrict__ rows, uint64_t count, ui
       if (lane == 0) out[blk] = w;
     }
     if (lane == 0) {
-      double abs_sum = 0.0;  // sequential, as codec.ts:240-241
+      double abs_sum = 0.0;  // sequential, as codec.ts:140-141
       for (uint32_t i = 0; i < P; ++i) abs_sum = __dadd_rn(abs_sum, fabs(static_cast<double>(a[i])));
       scales[row] = abs_sum > 0.0 ? __double2float_rn(__ddiv_rn(abs_sum, static_cast<double>(P))) : 1.0f;
     }

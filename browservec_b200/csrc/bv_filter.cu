@@ -1,6 +1,6 @@
 // bv_filter.cu -- the metadata predicate of a filtered query on the GPU.
 //
-// compileFilter (src/store/filter.ts:18-85) builds an AND of per-field
+// compileFilter (src/store/filter.ts:18-68) builds an AND of per-field
 // operator tests with strict JS equality; src/index.ts:372-395 runs it over
 // every live record to build the score mask of a filtered query.  Here the
 // store's metadata lives in device columns (type tag, f64 number, string

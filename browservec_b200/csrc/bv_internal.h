@@ -147,6 +147,7 @@ cudaError_t launch_filter(const bv_column* cols, uint32_t ncols, const bv_filter
 // bv_merge.cu: cross-shard merge of all-gathered shard records
 size_t merge_smem_bytes(uint32_t world, uint32_t F);
 uint32_t merge_max_world();
+cudaError_t launch_wait_probe(uint32_t* err, uint32_t polls, cudaStream_t s);
 cudaError_t launch_merge_topk(const uint32_t* gathered, uint32_t world, uint32_t nq, uint32_t k,
                               uint32_t* out_rows, float* out_scores, uint32_t* out_counts, cudaStream_t stream);
 cudaError_t launch_merge_shards(const uint32_t* gathered, uint32_t world, uint32_t nq, uint32_t F, uint32_t k,

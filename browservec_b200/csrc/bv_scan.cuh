@@ -5,9 +5,9 @@
 //      and the rotation signs into shared memory, then it streams code tiles
 //      into a 2..4-stage ring;
 //   2. meanwhile the 16 consumer warps rotate the query (random-sign diagonal
-//      + FWHT in the operation order of rotator.ts:83-92: warp-shuffle stages
+//      + FWHT in the operation order of rotator.ts:60-70: warp-shuffle stages
 //      for len < 32, shared-memory stages above) and, for the integer modes,
-//      code it with the reference int8 codec (codec.ts:132-154);
+//      code it with the reference int8 codec (codec.ts:32-54);
 //   3. the consumers score every row of every tile in the canonical lane order
 //      (asym: exact integer codes x fp32 query in fmaf chains, two rows per
 //      f32x2 instruction -- the restatement of distanceQ8.ts:56-66,
@@ -44,7 +44,7 @@ constexpr int kMergeMax = 24;          // keys per consumer thread in the last-C
 struct ScanParams {
   const uint8_t* codes;      // rows x R bytes (capacity padded to whole tiles)
   const float* scales;       // one per row (padded like codes)
-  const float* signs;        // rounds x P, pre-scaled (rotator.ts:66-80)
+  const float* signs;        // rounds x P, pre-scaled (rotator.ts:44-58)
   const float* query;        // dim fp32, normalized by the host (store.ts:209-217)
   const uint32_t* mask;      // optional: bit r of mask[r>>5] = row r passes
   uint64_t nrows;
@@ -61,7 +61,7 @@ struct ScanParams {
   unsigned long long* tile_ctr;  // dynamic tile counter slot: (epoch << 32) | next tile
   uint32_t epoch;            // launch number owning tile_ctr
   uint32_t serial;           // 1: the partials are shared with the previous query (wait for its tail)
-  uint32_t seed;             // rotator seed (rotator.ts:66-80): signs computed on the fly
+  uint32_t seed;             // rotator seed (rotator.ts:44-58): signs computed on the fly
   float sign_scale;          // f32(1 / sqrt(P) in f64), the signs' magnitude
   // The query's finish by its last CTA (fold = 1, Fp <= 256): merge of the CTA
   // lists, exact re-rank and outputs, as the tail kernel does.
@@ -232,7 +232,7 @@ __device__ __forceinline__ Chunk<W> lds_chunk(const uint8_t* p) {
 }
 
 // ----------------------------------------------------------- query prologue
-// Rotate q[0..P) in place (rotator.ts:83-92): per round a sign multiply and
+// Rotate q[0..P) in place (rotator.ts:60-70): per round a sign multiply and
 // the FWHT stages len = 1, 2, ..., P/2 in order.  Consumer-collective.
 __device__ __forceinline__ void rotate_query(float* q, const float* signs, uint32_t P,
                                              uint32_t rounds, int ctid) {
@@ -281,7 +281,7 @@ __device__ __forceinline__ void rotate_query(float* q, const float* signs, uint3
 // Sign i of one rotation round: randomSigns (prng.ts:5-22) draws
 // mulberry32 values in sequence, and mulberry32's state after i + 1 draws is
 // seed + (i + 1) * 0x6d2b79f5, so draw i is computed directly.  Value
-// u < 2^31 gives -1, scaled by f32(1/sqrt(P)) (rotator.ts:66-80).
+// u < 2^31 gives -1, scaled by f32(1/sqrt(P)) (rotator.ts:44-58).
 __device__ __forceinline__ float rot_sign(uint32_t round_seed, uint32_t i, float scale) {
   const uint32_t a = round_seed + (i + 1u) * 0x6d2b79f5u;
   uint32_t t = (a ^ (a >> 15)) * (1u | a);
@@ -295,7 +295,7 @@ __device__ __forceinline__ double js_round(double x);
 // The whole query prologue of 32 <= P <= 1024 in ONE warp, no barrier: lane c
 // holds elements i = 32 r + c (r < NR = P / 32) in registers.  Per round the
 // sign multiply, the FWHT stages of bits 0..4 by shuffles and of bits 5.. by
-// register butterflies -- the reference's stage order (rotator.ts:83-92), the
+// register butterflies -- the reference's stage order (rotator.ts:60-70), the
 // same f32 operations as rotate_query.  Then, by mode, the rotated query to
 // q (asym), its int8 codes to qb with the codec of quantize_query8 (int,
 // returns qscale), or its sign bits to qb as words (hamming).
@@ -331,7 +331,7 @@ __device__ __forceinline__ float prologue_warp(float* q, int8_t* qb, uint32_t se
   if constexpr (MODE == 0) {  // asym: the rotated query itself
 #pragma unroll
     for (int r = 0; r < NR; ++r) q[r * 32 + lane] = x[r];
-  } else if constexpr (MODE == 1) {  // int: the corpus int8 codec (codec.ts:132-154)
+  } else if constexpr (MODE == 1) {  // int: the corpus int8 codec (codec.ts:32-54)
     float m = 0.0f;
 #pragma unroll
     for (int r = 0; r < NR; ++r) m = fmaxf(m, fabsf(x[r]));
@@ -434,7 +434,7 @@ static __device__ __noinline__ float prologue_multi(float* q, int8_t* qb, float*
   q[ib] = x0;
   q[ib + 1u] = x1;
   float qscale = 1.0f;
-  if constexpr (MODE == 1) {  // int: the corpus int8 codec (codec.ts:132-154)
+  if constexpr (MODE == 1) {  // int: the corpus int8 codec (codec.ts:32-54)
     float m = fmaxf(fabsf(x0), fabsf(x1));
 #pragma unroll
     for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
@@ -470,7 +470,7 @@ __device__ __forceinline__ double js_round(double x) {
   return r;
 }
 
-// int8 code of the rotated query with the corpus codec (codec.ts:132-154):
+// int8 code of the rotated query with the corpus codec (codec.ts:32-54):
 // qb[i] in [-127,127]; returns the f32 scale (max |rq|, or 1).
 __device__ __forceinline__ float quantize_query8(const float* rq, int8_t* qb, uint32_t P, int ctid,
                                                  float* red /* >= 16 floats */) {

@@ -82,7 +82,7 @@ def _is_ops(cond: Any) -> bool:
 
 
 def compile_filter(flt: Mapping[str, Any]) -> Callable[[Mapping | None], bool]:
-    """filter.ts:69-85: AND across fields and operators; a bare value is $eq."""
+    """filter.ts:52-68: AND across fields and operators; a bare value is $eq."""
     tests = []
     for field, cond in flt.items():
         if _is_ops(cond):

@@ -45,7 +45,7 @@ typedef enum bv_status {
  *  BV_SCORE_ASYM    fp32 rotated query x integer codes, the reference's own
  *                   asymmetric kernels (distanceQ8.ts:56-66, distanceQ4.ts:44-62,
  *                   distanceQ1.ts:44-66) in a fixed canonical order;
- *  BV_SCORE_INT     int8-coded query (codec.ts:132-154 applied to the rotated
+ *  BV_SCORE_INT     int8-coded query (codec.ts:32-54 applied to the rotated
  *                   query) x codes, exact integer dot: dp4a for int8/int4,
  *                   bit-plane popc for 1-bit;
  *  BV_SCORE_HAMMING 1-bit corpus only: sign-bit query, xor + popc. */
@@ -239,6 +239,16 @@ typedef struct bv_batch_profile {
 BV_API int bv_set_batch_timing(bv_index* idx, int enable);
 BV_API int bv_last_batch_profile(bv_index* idx, bv_batch_profile* out);
 
+/* Self-test of the kernels' bounded waits: one thread waits, with a budget of
+ * `polls` mbarrier polls (1 .. 2^22, the budget every kernel wait uses), on a
+ * barrier nothing completes, raises the index's timeout flag and returns; the
+ * call then reports exactly what a search whose wait ran out reports --
+ * BV_ERR_TIMEOUT, "scan kernel wait ran out of budget (flag 0x1)" -- and clears
+ * the flag, so the index stays usable.  Nothing else runs.  No counterpart in
+ * the reference (WebGPU has no device-side timeouts; its device-loss path is
+ * src/engine/device.ts). */
+BV_API int bv_check_wait_timeout(bv_index* idx, uint32_t polls);
+
 /* Change the scoring mode of an index (BV_SCORE_*; hamming needs bits 1, the
  * exact index keeps asym).  Codes are shared by every mode, so this only
  * changes how later searches score.  No counterpart in the reference (its
@@ -263,7 +273,7 @@ BV_API int bv_merge_shards(const uint32_t* gathered, uint32_t world, uint32_t nq
 
 /* ---------------------------------------------------------- metadata filter
  * The per-row metadata predicate of a filtered query (compileFilter,
- * src/store/filter.ts:18-85, applied row by row at src/index.ts:372-395),
+ * src/store/filter.ts:18-68, applied row by row at src/index.ts:372-395),
  * evaluated on the GPU over device columns.  One column per metadata field:
  * a type tag per row, the value as a JS number (f64; booleans as 0/1), and
  * for strings a dictionary code.  A filter is an AND of terms, one per

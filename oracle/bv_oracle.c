@@ -17,7 +17,7 @@
 #include <emmintrin.h>
 
 #define INV127 0x1.020408p-7f /* f32(1/127) */
-#define INV7 0x1.24924ap-3f   /* f32(1/7), the WGSL constant of distanceQ4.ts:145 */
+#define INV7 0x1.24924ap-3f   /* f32(1/7), the WGSL constant of distanceQ4.ts:61 */
 
 /* ------------------------------------------------------------------ prng */
 
@@ -43,7 +43,7 @@ void bvo_random_signs(float *out, int n, uint32_t seed) {
 
 /* -------------------------------------------------------------- rotation */
 
-/* rotator.ts:39-43 */
+/* rotator.ts:16-21 */
 int bvo_pad_to_pow2(int n) {
   int p = 4;
   while (p < n) p <<= 1;
@@ -62,7 +62,7 @@ void bvo_fwht(float *a, int n) {
       }
 }
 
-/* rotator.ts:66-80.  Round seed (seed ^ (0x9e3779b9*(r+1))) >>> 0 is a uint32
+/* rotator.ts:44-58.  Round seed (seed ^ (0x9e3779b9*(r+1))) >>> 0 is a uint32
  * multiply-wrap; the sign vector is Float32Array(+-1) *= f64 1/sqrt(P). */
 int bvo_rotator_signs(int dim, uint32_t seed, int rounds, float *signs_out) {
   int P = bvo_pad_to_pow2(dim);
@@ -76,7 +76,7 @@ int bvo_rotator_signs(int dim, uint32_t seed, int rounds, float *signs_out) {
   return P;
 }
 
-/* rotator.ts:83-92 */
+/* rotator.ts:60-70 */
 void bvo_rotate(const float *signs, int rounds, int dim, int P, const float *src, float *dst) {
   memcpy(dst, src, sizeof(float) * (size_t)dim);
   for (int i = dim; i < P; i++) dst[i] = 0.0f;
@@ -96,7 +96,7 @@ static double js_round(double x) {
   return r;
 }
 
-/* codec.ts:122-129 (levels = 127) and :177-183 (levels = 7). */
+/* codec.ts:22-30 (levels = 127) and :77-83 (levels = 7). */
 static int snorm_level(double v, double levels) {
   double c = v < -1.0 ? -1.0 : (v > 1.0 ? 1.0 : v);
   double b = js_round(c * levels);
@@ -114,7 +114,7 @@ static float max_abs_scale(const float *rot, int n) {
   return m > 0.0f ? m : 1.0f;
 }
 
-/* codec.ts:132-154 */
+/* codec.ts:32-54 */
 int bvo_quantize_row8(const float *rot, int n, uint32_t *words, float *scale) {
   if (n % 4 != 0) return -1;
   float sc = max_abs_scale(rot, n);
@@ -129,7 +129,7 @@ int bvo_quantize_row8(const float *rot, int n, uint32_t *words, float *scale) {
   return 0;
 }
 
-/* codec.ts:186-208 */
+/* codec.ts:85-108 */
 int bvo_quantize_row4(const float *rot, int n, uint32_t *words, float *scale) {
   if (n % 8 != 0) return -1;
   float sc = max_abs_scale(rot, n);
@@ -144,7 +144,7 @@ int bvo_quantize_row4(const float *rot, int n, uint32_t *words, float *scale) {
   return 0;
 }
 
-/* codec.ts:236-254: scale = f32(f64 sum|x| / n), bit j of word g = x[32g+j] >= 0. */
+/* codec.ts:135-154: scale = f32(f64 sum|x| / n), bit j of word g = x[32g+j] >= 0. */
 int bvo_quantize_row1(const float *rot, int n, uint32_t *words, float *scale) {
   if (n % 32 != 0) return -1;
   double abs_sum = 0.0;
@@ -159,7 +159,7 @@ int bvo_quantize_row1(const float *rot, int n, uint32_t *words, float *scale) {
   return 0;
 }
 
-/* codec.ts:157-167 */
+/* codec.ts:56-66 */
 void bvo_dequant_row8(const uint32_t *words, int nwords, float scale, float *out) {
   for (int g = 0; g < nwords; g++)
     for (int j = 0; j < 4; j++) {
@@ -171,7 +171,7 @@ void bvo_dequant_row8(const uint32_t *words, int nwords, float scale, float *out
     }
 }
 
-/* codec.ts:211-222 */
+/* codec.ts:110-120 */
 void bvo_dequant_row4(const uint32_t *words, int nwords, float scale, float *out) {
   for (int g = 0; g < nwords; g++)
     for (int j = 0; j < 8; j++) {
@@ -183,7 +183,7 @@ void bvo_dequant_row4(const uint32_t *words, int nwords, float scale, float *out
     }
 }
 
-/* codec.ts:257-267 */
+/* codec.ts:156-167 */
 void bvo_dequant_row1(const uint32_t *words, int nwords, float scale, float *out) {
   for (int g = 0; g < nwords; g++)
     for (int j = 0; j < 32; j++) out[g * 32 + j] = ((words[g] >> j) & 1u) ? scale : -scale;
@@ -404,7 +404,7 @@ static void stable_sort_hits(hit_t *h, int n, int descending) {
   }
 }
 
-/* flat.ts:504-526 */
+/* flat.ts:217-239 */
 int bvo_topk_ref(const float *scores, int64_t n, int k, uint32_t *rows_out, float *scores_out) {
   int64_t limit64 = k < n ? k : n;
   int limit = (int)limit64;

@@ -30,20 +30,20 @@
  *   - the L lane sums reduce with an xor butterfly: for off = L/2 .. 1,
  *     s[l] = s[l] + s[l ^ off]; the result is s[0];
  *   - the row factor is applied last: int8 acc * (scale * f32(1/127)),
- *     int4 acc * (scale * f32(1/7)) (distanceQ4.ts:145), 1-bit acc * scale
- *     (distanceQ1.ts:230).
+ *     int4 acc * (scale * f32(1/7)) (distanceQ4.ts:61), 1-bit acc * scale
+ *     (distanceQ1.ts:66).
  *   - int mode (integer query, the dp4a / popc / tensor-core path): the
  *     rotated query is quantized with the reference's own int8 codec
- *     (quantizeRow, codec.ts:132-154) to bytes qb and scale qs; the integer dot
+ *     (quantizeRow, codec.ts:32-54) to bytes qb and scale qs; the integer dot
  *     idot = sum(v_i * qb_i) is exact; score = (f32(idot) * rowfac) * qfac with
  *     rowfac = scale*f32(1/127) | scale*f32(1/7) | scale and
  *     qfac = qs * f32(1/127).
  *   - hamming mode (1-bit corpus only): the query's sign bits (rq >= 0, the
- *     bit rule of quantizeRow1, codec.ts:236-254); idot = P - 2*popc(x ^ y);
+ *     bit rule of quantizeRow1, codec.ts:135-154); idot = P - 2*popc(x ^ y);
  *     score = f32(idot) * scale (the query's own scale is one positive factor
  *     per query and is left out).
  * Top-k order is (score desc, row asc) for both membership and output, the
- * north_star's tie rule; the reference's heap (flat.ts:504-526) agrees on every
+ * north_star's tie rule; the reference's heap (flat.ts:217-239) agrees on every
  * set without exact ties at the k boundary.
  */
 #ifndef BV_ORACLE_H
@@ -64,20 +64,20 @@ uint32_t bvo_mulberry32_next(uint32_t *state);
 void bvo_mulberry32_doubles(uint32_t seed, double *out, int64_t n);
 /* prng.ts:17-22 */
 void bvo_random_signs(float *out, int n, uint32_t seed);
-/* rotator.ts:39-43 */
+/* rotator.ts:16-21 */
 int bvo_pad_to_pow2(int n);
 /* rotator.ts:46-58 (in place, n a power of two) */
 void bvo_fwht(float *a, int n);
-/* rotator.ts:66-80 -- rounds*P pre-scaled signs; returns P. */
+/* rotator.ts:44-58 -- rounds*P pre-scaled signs; returns P. */
 int bvo_rotator_signs(int dim, uint32_t seed, int rounds, float *signs_out);
-/* rotator.ts:83-92 -- rotate one row: src[dim] -> dst[P]. */
+/* rotator.ts:60-70 -- rotate one row: src[dim] -> dst[P]. */
 void bvo_rotate(const float *signs, int rounds, int dim, int P, const float *src, float *dst);
 
-/* codec.ts:132-154 / :186-208 / :236-254 -- returns 0, or -1 on a bad length. */
+/* codec.ts:32-54 / :85-108 / :135-154 -- returns 0, or -1 on a bad length. */
 int bvo_quantize_row8(const float *rot, int n, uint32_t *words, float *scale);
 int bvo_quantize_row4(const float *rot, int n, uint32_t *words, float *scale);
 int bvo_quantize_row1(const float *rot, int n, uint32_t *words, float *scale);
-/* codec.ts:157-167 / :211-222 / :257-267 */
+/* codec.ts:56-66 / :110-120 / :156-167 */
 void bvo_dequant_row8(const uint32_t *words, int nwords, float scale, float *out);
 void bvo_dequant_row4(const uint32_t *words, int nwords, float scale, float *out);
 void bvo_dequant_row1(const uint32_t *words, int nwords, float scale, float *out);
@@ -107,7 +107,7 @@ uint32_t bvo_key_row(uint64_t key);
 int bvo_topk(const float *scores, int64_t n, const uint32_t *mask, int k,
              uint32_t *rows_out, float *scores_out);
 
-/* flat.ts:504-526 -- the reference's own heap selection, ties included. */
+/* flat.ts:217-239 -- the reference's own heap selection, ties included. */
 int bvo_topk_ref(const float *scores, int64_t n, int k, uint32_t *rows_out, float *scores_out);
 /* gpuTopk.ts:160-189 -- the reference's merge of per-segment partials. */
 int bvo_merge_partials_ref(const float *scores, const uint32_t *rows, int64_t count, int64_t n, int k,

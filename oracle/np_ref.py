@@ -91,7 +91,7 @@ def js_round(x: float) -> float:
 
 
 def quantize_row(rot: np.ndarray, bits: int):
-    """codec.ts:132-154 / :186-208 / :236-254 in Python floats (f64)."""
+    """codec.ts:32-54 / :85-108 / :135-154 in Python floats (f64)."""
     rot = rot.astype(np.float32)
     n = rot.size
     if bits == 1:

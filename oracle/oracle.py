@@ -108,7 +108,7 @@ def random_signs(n: int, seed: int) -> np.ndarray:
 
 # ------------------------------------------------------------- rotator.ts
 def pad_to_pow2(n: int) -> int:
-    """rotator.ts:39-43"""
+    """rotator.ts:16-21"""
     return lib().bvo_pad_to_pow2(n)
 
 
@@ -120,7 +120,7 @@ def fwht(a) -> np.ndarray:
 
 
 def rotator_signs(dim: int, seed: int = DEFAULT_SEED, rounds: int = 2) -> np.ndarray:
-    """rotator.ts:66-80 -- (rounds, P) pre-scaled sign vectors."""
+    """rotator.ts:44-58 -- (rounds, P) pre-scaled sign vectors."""
     P = pad_to_pow2(dim)
     out = np.empty((max(rounds, 1), P), np.float32)
     lib().bvo_rotator_signs(dim, seed & 0xFFFFFFFF, rounds, _p(out))
@@ -128,7 +128,7 @@ def rotator_signs(dim: int, seed: int = DEFAULT_SEED, rounds: int = 2) -> np.nda
 
 
 def rotate(x, dim: int, seed: int = DEFAULT_SEED, rounds: int = 2, signs=None) -> np.ndarray:
-    """rotator.ts:83-92"""
+    """rotator.ts:60-70"""
     P = pad_to_pow2(dim)
     s = rotator_signs(dim, seed, rounds) if signs is None else _f32(signs)
     x = _f32(x)
@@ -139,7 +139,7 @@ def rotate(x, dim: int, seed: int = DEFAULT_SEED, rounds: int = 2, signs=None) -
 
 # --------------------------------------------------------------- codec.ts
 def quantize_row(rot, bits: int):
-    """codec.ts:132-154 (8), :186-208 (4), :236-254 (1) -> (words, scale)."""
+    """codec.ts:32-54 (8), :85-108 (4), :135-154 (1) -> (words, scale)."""
     rot = _f32(rot)
     n = rot.size
     per = {8: 4, 4: 8, 1: 32}[bits]
@@ -154,7 +154,7 @@ def quantize_row(rot, bits: int):
 
 
 def dequant_row(words, scale: float, bits: int) -> np.ndarray:
-    """codec.ts:157-167 / :211-222 / :257-267"""
+    """codec.ts:56-66 / :110-120 / :156-167"""
     words = _u32(words)
     per = {8: 4, 4: 8, 1: 32}[bits]
     out = np.empty(words.size * per, np.float32)
@@ -226,7 +226,7 @@ def topk(scores, k: int, mask=None):
 
 
 def topk_ref(scores, k: int):
-    """flat.ts:504-526 -- the reference heap selection, exactly."""
+    """flat.ts:217-239 -- the reference heap selection, exactly."""
     scores = _f32(scores)
     rows = np.empty(max(k, 1), np.uint32)
     out = np.empty(max(k, 1), np.float32)

@@ -1,7 +1,7 @@
 """Device metadata predicate (bv_filter_mask) against the reference semantics.
 
 The host mirror (FilterColumns, vectorised compileFilter of
-src/store/filter.ts:18-85) is itself checked against the row-by-row predicate;
+src/store/filter.ts:18-68) is itself checked against the row-by-row predicate;
 the device mask must equal it bit for bit for every operator and every value
 type (numbers, strings, booleans, null, missing fields), with tombstones.
 Filtered batched searches then compact the kept rows (tested beside the
