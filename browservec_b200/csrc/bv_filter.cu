@@ -41,6 +41,16 @@ __device__ __forceinline__ bool strict_eq(const bv_column& c, uint64_t r, uint32
   }
 }
 
+// Set.has (filter.ts:29-30) compares with SameValueZero: as ===, except that
+// NaN matches NaN (+0 and -0 are already equal under ==).
+__device__ __forceinline__ bool same_value_zero(const bv_column& c, uint64_t r, uint32_t tag, const bv_value& v) {
+  if (tag == BV_TAG_NUMBER && v.tag == BV_TAG_NUMBER && v.num != v.num) {
+    const double x = c.num[r];
+    return x != x;
+  }
+  return strict_eq(c, r, tag, v);
+}
+
 __global__ void __launch_bounds__(256) filter_kernel(const __grid_constant__ FilterParams p) {
   const uint64_t r = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   bool ok = r < p.rows;
@@ -58,7 +68,7 @@ __global__ void __launch_bounds__(256) filter_kernel(const __grid_constant__ Fil
           break;
         case BV_OP_IN: {
           bool any = false;
-          for (uint32_t i = 0; i < term.nvals && !any; ++i) any = strict_eq(c, r, tag, term.vals[i]);
+          for (uint32_t i = 0; i < term.nvals && !any; ++i) any = same_value_zero(c, r, tag, term.vals[i]);
           ok = any;
           break;
         }

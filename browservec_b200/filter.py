@@ -7,7 +7,9 @@ filtered query is built from (src/index.ts:372-395).
 
 JavaScript equality is strict (===): a bool never equals a number, ``None``
 (null) never equals a missing field (undefined), and numbers compare by value
-(1 === 1.0).  Range operators match stored numbers only.
+(1 === 1.0).  ``$in`` tests membership with ``Set.has`` (filter.ts:29-30),
+whose SameValueZero also matches NaN to NaN.  Range operators match stored
+numbers only.
 """
 from __future__ import annotations
 
@@ -39,6 +41,13 @@ def strict_eq(a: Any, b: Any) -> bool:
     return False
 
 
+def same_value_zero(a: Any, b: Any) -> bool:
+    """JS SameValueZero (Set.has): === except that NaN equals NaN."""
+    if _is_number(a) and _is_number(b) and a != a and b != b:
+        return True
+    return strict_eq(a, b)
+
+
 def _get(m: Mapping | None, field: str) -> Any:
     if m is None:
         return _MISSING
@@ -55,7 +64,7 @@ def _compile_op(field: str, op: str, arg: Any) -> Callable[[Mapping | None], boo
         if not isinstance(arg, (list, tuple)):
             raise ValueError(f'filter: $in on "{field}" expects an array, got {_js_typeof(arg)}')
         vals = list(arg)
-        return lambda m: any(strict_eq(_get(m, field), v) for v in vals)
+        return lambda m: any(same_value_zero(_get(m, field), v) for v in vals)
     if op in ("$gt", "$gte", "$lt", "$lte"):
         if not _is_number(arg):
             raise ValueError(f'filter: {op} on "{field}" expects a number, got {_js_typeof(arg)}')
@@ -201,7 +210,12 @@ class FilterColumns:
                 raise ValueError(f'filter: $in on "{field}" expects an array, got {_js_typeof(arg)}')
             out = np.zeros(self.n, bool)
             for v in arg:
-                out |= self._eq(field, v)
+                if _is_number(v) and v != v:  # SameValueZero: NaN finds stored NaN
+                    c = self.cols.get(field)
+                    if c is not None:
+                        out |= (c["tag"] == self.T_NUM) & np.isnan(c["num"])
+                else:
+                    out |= self._eq(field, v)
             return out
         if op in ("$gt", "$gte", "$lt", "$lte"):
             if not _is_number(arg):
@@ -293,12 +307,11 @@ class DeviceColumns:
             return _lib.BvValue(tag=_lib.TAG_STRING, code=self.fields[field]["dict"].get(v, -1), num=0.0)
         return _lib.BvValue(tag=_lib.TAG_MISSING + 99, code=-1, num=0.0)  # objects never match
 
-    def compile(self, flt: Mapping[str, Any]):
-        """The reference filter as device terms.  Returns (columns, terms,
-        always_false); raises the reference's errors (filter.ts:49-66)."""
-        from . import _lib
-
-        names, terms, never = [], [], False
+    def units(self, flt: Mapping[str, Any]):
+        """The reference filter as (field, op, values) tests over present
+        fields, and whether it can match nothing at all.  Raises the
+        reference's errors (filter.ts:18-68)."""
+        out, never = [], False
         for field, cond in flt.items():
             ops = cond.items() if _is_ops(cond) else [("$eq", cond)]
             for op, arg in ops:
@@ -312,45 +325,81 @@ class DeviceColumns:
                     never |= op != "$ne"
                     continue
                 vals = list(arg) if op == "$in" else [arg]
-                if op == "$in" and not vals:
-                    never = True
-                    continue
-                if len(vals) > _lib.FILTER_MAX_IN:
-                    raise ValueError(f"filter: $in on \"{field}\" takes at most {_lib.FILTER_MAX_IN} values here")
                 bad = [v for v in vals if not (v is None or isinstance(v, (bool, int, float, str)))]
                 if bad:  # objects and arrays never equal a stored value
                     if op == "$ne":
                         continue
-                    vals = [v for v in vals if v not in bad]
-                    if not vals:
-                        never = True
-                        continue
-                if field not in names:
-                    names.append(field)
-                t = _lib.BvFilterTerm(column=names.index(field), op=_lib.OP_CODES[op], nvals=len(vals))
-                for i, v in enumerate(vals):
-                    t.vals[i] = self._value(field, v)
-                terms.append(t)
-        if len(terms) > _lib.FILTER_MAX_TERMS or len(names) > _lib.FILTER_MAX_TERMS:
-            raise ValueError(f"filter: at most {_lib.FILTER_MAX_TERMS} operator terms here")
+                    vals = [v for v in vals if not any(v is b for b in bad)]
+                if not vals:
+                    never = True
+                    continue
+                out.append((field, op, vals))
+        return out, never
+
+    def _launch(self, tests, live, out, stream: int) -> None:
+        """One bv_filter_mask call: the AND of at most FILTER_MAX_TERMS tests,
+        each with at most FILTER_MAX_IN values."""
+        from . import _lib
+
+        names = []
+        terms = (_lib.BvFilterTerm * max(1, len(tests)))()
+        for t, (field, op, vals) in enumerate(tests):
+            if field not in names:
+                names.append(field)
+            terms[t] = _lib.BvFilterTerm(column=names.index(field), op=_lib.OP_CODES[op], nvals=len(vals))
+            for i, v in enumerate(vals):
+                terms[t].vals[i] = self._value(field, v)
         cols = (_lib.BvColumn * max(1, len(names)))()
         for i, f in enumerate(names):
             c = self.fields[f]
             cols[i] = _lib.BvColumn(tag=c["tag"].data_ptr(), num=None if c["num"] is None else c["num"].data_ptr(),
                                     code=None if c["code"] is None else c["code"].data_ptr())
-        arr = (_lib.BvFilterTerm * max(1, len(terms)))(*terms)
-        return cols, len(names), arr, len(terms), never
+        L = _lib.load()
+        _lib.check(L.bv_filter_mask(cols, len(names), terms, len(tests), self.n,
+                                    C.c_void_p(live.data_ptr()) if live is not None else None,
+                                    C.c_void_p(out.data_ptr()), C.c_void_p(stream)))
 
     def mask(self, flt: Mapping[str, Any], live=None, stream: int = 0):
-        """uint32 mask words (a device tensor) of the rows the filter keeps."""
+        """uint32 mask words (a device tensor) of the rows the filter keeps,
+        ANDed with `live` (tombstones cleared) when given.  The library call
+        takes at most FILTER_MAX_TERMS tests of at most FILTER_MAX_IN values;
+        larger filters are evaluated as several calls whose masks are ANDed
+        (more tests) or ORed (a longer $in list), so no limit reaches the user."""
         from . import _lib
 
         torch = self.torch
         words = max((self.n + 31) // 32, 1)
         out = torch.zeros(words, dtype=torch.int32, device=self.device)
-        cols, ncols, terms, nterms, never = self.compile(flt)
+        tests, never = self.units(flt)
         if never or self.n == 0:
             return out
+        small = [t for t in tests if len(t[2]) <= _lib.FILTER_MAX_IN]
+        big = [t for t in tests if len(t[2]) > _lib.FILTER_MAX_IN]
+        first = True
+        for g in range(0, max(len(small), 1), _lib.FILTER_MAX_TERMS):
+            grp = small[g:g + _lib.FILTER_MAX_TERMS]
+            if not grp and small:
+                break
+            dst = out if first else torch.empty_like(out)
+            if grp:
+                self._launch(grp, live, dst, stream)
+            elif live is not None:
+                dst.copy_(live[:words])
+            else:
+                dst.fill_(-1)
+            if not first:
+                out &= dst
+            first = False
+        for field, op, vals in big:  # a long $in: OR of its chunks
+            acc = torch.zeros_like(out)
+            part = torch.empty_like(out)
+            for c0 in range(0, len(vals), _lib.FILTER_MAX_IN):
+                self._launch([(field, op, vals[c0:c0 + _lib.FILTER_MAX_IN])], live, part, stream)
+                acc |= part
+            out &= acc
+        if self.n % 32:  # bits past the last row stay clear
+            out[-1] &= (1 << (self.n % 32)) - 1
+        return out
         L = _lib.load()
         _lib.check(L.bv_filter_mask(cols, ncols, terms, nterms, self.n,
                                     C.c_void_p(live.data_ptr()) if live is not None else None,

@@ -11,21 +11,28 @@ probes, over the C ABI of libbvcuda.so.
 (exact scan for <= 4096 matches, else an in-index mask), the fetch/re-rank
 rule and the id mapping.  The re-rank runs on the GPU inside the search call,
 so ``query_batch`` re-ranks as well (the reference's batched branch skips it,
-src/index.ts:495-516).
+src/index.ts:495-516).  A filter's mask is built by the GPU predicate over
+device copies of the metadata columns, once per (filter, store version) --
+the reference rebuilds it in JS for every query (src/index.ts:372-395) -- and
+a filtered ``query_batch`` searches all its queries in one call instead of
+looping over ``query`` (src/index.ts:477-481).
 """
 from __future__ import annotations
 
 import ctypes as C
+import json
+from collections import OrderedDict
 from dataclasses import dataclass, field
 from typing import Any, Mapping, Sequence
 
 import numpy as np
 
 from . import _lib
-from .filter import FilterColumns, compile_filter, pack_mask
+from .filter import DeviceColumns, FilterColumns, compile_filter, pack_mask
 
 DEFAULT_SEED = 0x9E3779B9          # src/index.ts:71
 FILTER_CPU_SCAN_MAX = 4096         # src/index.ts:76
+MASK_CACHE_ENTRIES = 16            # filter masks kept per store (least recently used dropped)
 
 
 def default_rerank_factor(bits: int) -> int:
@@ -221,6 +228,39 @@ class AddonQuantIndex:
                                  cand_counts=cand_counts_ptr or None, cand_exact=cand_exact_ptr or None)
         _lib.check(self._L.bv_search_batch(self._h, C.byref(args), C.c_void_p(stream)))
 
+    def search_masked(self, qs: np.ndarray, k: int, fetch: int, rerank: bool, mask_dev) -> list[list[FlatHit]]:
+        """Search with a score mask already on the device (uint32 words as a
+        CUDA tensor, e.g. DeviceColumns.mask): the queries go to the device,
+        integer scorings of 64+ queries run as one tensor-core batch, the
+        results come back to the host."""
+        import torch
+
+        qs = np.ascontiguousarray(qs, dtype=np.float32).reshape(-1, self.dim)
+        nq = qs.shape[0]
+        F = max(fetch, k)
+        dev = mask_dev.device
+        if getattr(self, "_stream", None) is None:
+            self._stream = torch.cuda.Stream(device=dev)
+        st = self._stream
+        st.wait_stream(torch.cuda.current_stream(dev))  # the mask was built on the current stream
+        with torch.cuda.stream(st):
+            q = torch.from_numpy(qs).to(dev, non_blocking=False)
+            out = torch.empty(nq * (2 * k + 1), dtype=torch.int32, device=dev)
+            args = _lib.BvSearchArgs(queries=q.data_ptr(), nq=nq, k=k, fetch=F, rerank=int(rerank),
+                                     mask=mask_dev.data_ptr(), mask_words=mask_dev.numel(),
+                                     out_rows=out.data_ptr(), out_scores=out[nq * k:].data_ptr(),
+                                     out_counts=out[2 * nq * k:].data_ptr())
+            batched = self.scoring != "asym" and self.bits != 0 and nq >= 64
+            fn = self._L.bv_search_batch if batched else self._L.bv_search_async
+            _lib.check(fn(self._h, C.byref(args), C.c_void_p(st.cuda_stream)))
+            host = out.cpu().numpy()
+        st.synchronize()
+        rows = host[:nq * k].reshape(nq, k)
+        scores = host[nq * k:2 * nq * k].view(np.float32).reshape(nq, k)
+        counts = host[2 * nq * k:]
+        return [[FlatHit(int(rows[i, j]), float(scores[i, j])) for j in range(int(counts[i]))]
+                for i in range(nq)]
+
     def set_scoring(self, scoring: str) -> None:
         """Score later searches with another mode (codes are shared by all modes)."""
         _lib.check(self._L.bv_set_scoring(self._h, _lib.SCORING[scoring]))
@@ -351,6 +391,9 @@ class BrowserVec:
                                      quant_bits, scoring, device, metric)
         self.last_query_ms: float | None = None
         self.last_query_gpu_ms: float | None = None
+        self._version = 0       # bumped by every add and delete
+        self._dev = None        # (version, DeviceColumns, live-row mask words) on the index's GPU
+        self._masks: OrderedDict = OrderedDict()  # (filter, version) -> (mask words, matches, rows)
 
     @classmethod
     def create(cls, config: Mapping[str, Any]) -> "BrowserVec":
@@ -383,6 +426,7 @@ class BrowserVec:
             vecs = normalize_rows(vecs)
         self.store.columns.append(metas)
         self.index.append(vecs, len(records))
+        self._version += 1
 
     def add(self, record: Mapping[str, Any]) -> None:
         self.add_batch([record])
@@ -406,12 +450,14 @@ class BrowserVec:
         else:
             self.store.columns.append([None] * n)
         self.index.append(vectors, n)
+        self._version += 1
 
     def delete(self, id: str) -> bool:
         e = self.store.by_id.pop(id, None)
         if e is None:
             return False
         self.store.deleted.add(e.row)
+        self._version += 1
         return True
 
     @property
@@ -430,16 +476,52 @@ class BrowserVec:
     def _meta_of(self, row: int):
         return self.store.by_row[row].metadata
 
-    def _filter_rows(self, flt, predicate) -> np.ndarray:
-        """Rows (not deleted) matching the filter: src/index.ts:372-386."""
-        rows_total = len(self.store.by_row)
-        try:
-            match = self.store.columns.match(flt)
-        except ValueError:
-            raise
-        if self.store.deleted:
-            match[np.fromiter(self.store.deleted, np.int64)] = False
-        return np.flatnonzero(match[:rows_total]).astype(np.uint32)
+    def _device_mask(self, flt: Mapping[str, Any]):
+        """The score mask of a filter -- its rows that are not deleted
+        (src/index.ts:372-386) -- built by the GPU predicate over device
+        copies of the metadata columns and kept per (filter, store version):
+        (mask words as a CUDA tensor, match count, the matching rows when at
+        most FILTER_CPU_SCAN_MAX, else None)."""
+        import torch
+
+        key = (json.dumps(flt, sort_keys=True, default=repr), self._version)
+        hit = self._masks.get(key)
+        if hit is not None:
+            self._masks.move_to_end(key)
+            return hit
+        dev = torch.device("cuda", self.index.device)
+        if self._dev is None or self._dev[0] != self._version:
+            dc = DeviceColumns.from_host(self.store.columns, dev)
+            live = np.ones(len(self.store.by_row), bool)
+            if self.store.deleted:
+                live[np.fromiter(self.store.deleted, np.int64)] = False
+            live_w = torch.from_numpy(pack_mask(live).view(np.int32)).to(dev)
+            self._dev = (self._version, dc, live_w)
+            self._masks.clear()  # masks of older versions are stale
+        _, dc, live_w = self._dev
+        m = dc.mask(flt, live=live_w)
+        if not hasattr(self, "_popc"):
+            self._popc = torch.tensor([bin(i).count("1") for i in range(256)], dtype=torch.int64, device=dev)
+        b = m.view(torch.uint8)
+        count = int(self._popc[b.long()].sum().item())
+        rows = None
+        if 0 < count <= FILTER_CPU_SCAN_MAX:
+            bits = ((b.unsqueeze(1) >> torch.arange(8, device=dev, dtype=torch.uint8)) & 1).flatten()
+            rows = torch.nonzero(bits).squeeze(1).cpu().numpy().astype(np.uint32)
+        entry = (m, count, rows)
+        self._masks[key] = entry
+        while len(self._masks) > MASK_CACHE_ENTRIES:
+            self._masks.popitem(last=False)
+        return entry
+
+    def _fetch(self, k: int, masked: bool, rerank: bool | None):
+        """src/index.ts:405-417: k_eff (oversampled by the tombstones unless a
+        mask already drops them) and the candidate fetch."""
+        total = self.index.size
+        k_eff = min(total, k) if masked else min(total, k + len(self.store.deleted))
+        do_rerank = rerank if rerank is not None else self.rerank_factor > 1
+        fetch = min(total, max(k_eff, k_eff * self.rerank_factor)) if do_rerank else k_eff
+        return k_eff, fetch, do_rerank
 
     def query(self, query, k: int = 10, filter: Mapping[str, Any] | None = None,
               rerank: bool | None = None) -> list[QueryResult]:
@@ -448,25 +530,322 @@ class BrowserVec:
 
         q = self._prep_query(query)
         predicate = compile_filter(filter) if filter else None
-        mask = None
+        t0 = time.perf_counter()
         if predicate is not None:
-            match_rows = self._filter_rows(filter, predicate)
-            if match_rows.size == 0:
+            m, count, rows = self._device_mask(filter)
+            if count == 0:
                 return []
-            if match_rows.size <= FILTER_CPU_SCAN_MAX:
-                return self._query_rows_exact(q, match_rows, k)
-            bits = np.zeros(len(self.store.by_row), bool)
-            bits[match_rows] = True
-            mask = pack_mask(bits)
-        deleted = len(self.store.deleted)
-        total = self.index.size
-        k_eff = min(total, k) if mask is not None else min(total, k + deleted)
+            if rows is not None:
+                return self._query_rows_exact(q, rows, k)
+            k_eff, fetch, do_rerank = self._fetch(k, True, rerank)
+            if k_eff <= 0:
+                return []
+            hits = self.index.search_masked(q[None, :], k_eff, fetch, do_rerank, m)[0]
+            self.last_query_ms = (time.perf_counter() - t0) * 1e3
+            self.last_query_gpu_ms = None
+            return self._map_hits(hits, k, predicate)
+        k_eff, fetch, do_rerank = self._fetch(k, False, rerank)
         if k_eff <= 0:
             return []
+        hits = self.index.search(q[None, :], k_eff, fetch, rerank=do_rerank)[0]
+        self.last_query_ms = (time.perf_counter() - t0) * 1e3
+        self.last_query_gpu_ms = min(self.index.stats()["last_query_gpu_ms"], self.last_query_ms)
+        return self._map_hits(hits, k, predicate)
+
+    def _map_hits(self, hits, k, predicate=None) -> list[QueryResult]:
+        out = []
+        for h in hits:
+            if self.store.deleted and h.row in self.store.deleted:
+                continue
+            e = self.store.by_row[h.row]
+            if predicate is not None and not predicate(e.metadata):
+                continue
+            out.append(QueryResult(e.id, h.score, e.metadata))
+            if len(out) == k:
+                break
+        return out
+
+    def _query_rows_exact(self, q, rows, k) -> list[QueryResult]:
+        """src/index.ts:445-464"""
+        hits = self.index.query_rows_exact(q, rows, k)
+        return [QueryResult(self.store.by_row[h.row].id, h.score, self.store.by_row[h.row].metadata)
+                for h in hits]
+
+    def query_batch(self, queries, k: int = 10, filter: Mapping[str, Any] | None = None,
+                    rerank: bool | None = None) -> list[list[QueryResult]]:
+        """src/index.ts:473-517, with the re-rank the batched reference branch
+        lacks; a filtered batch shares one device mask and one search call
+        (the reference loops over query(), rebuilding the mask each time)."""
+        queries = list(queries) if not isinstance(queries, np.ndarray) else queries
+        if len(queries) == 0:
+            return []
+        qs = np.stack([self._prep_query(q) for q in queries])
+        if filter:
+            predicate = compile_filter(filter)
+            m, count, rows = self._device_mask(filter)
+            if count == 0:
+                return [[] for _ in range(qs.shape[0])]
+            if rows is not None:
+                return [self._query_rows_exact(q, rows, k) for q in qs]
+            k_eff, fetch, do_rerank = self._fetch(k, True, rerank)
+            batch = self.index.search_masked(qs, k_eff, fetch, do_rerank, m)
+            return [self._map_hits(h, k, predicate) for h in batch]
+        k_eff, fetch, do_rerank = self._fetch(k, False, rerank)
+        if k_eff <= 0:
+            return [[] for _ in range(qs.shape[0])]
+        batch = self.index.search(qs, k_eff, fetch, rerank=do_rerank)
+        return [self._map_hits(h, k) for h in batch]
+
+    def stats(self) -> dict:
+        s = _lib.BvStats()
+        _lib.check(self._L.bv_get_stats(self._h, C.byref(s)))
+        return {f: getattr(s, f) for f, _ in s._fields_}
+
+    def set_phase_trace(self, ptr: int, capacity: int) -> None:
+        """Device buffer (u64) receiving per-phase timestamps of each scan launch."""
+        _lib.check(self._L.bv_set_phase_trace(self._h, C.c_void_p(ptr) if ptr else None, capacity))
+
+    def last_launches(self) -> int:
+        n = C.c_uint32()
+        _lib.check(self._L.bv_launches_last_search(self._h, C.byref(n)))
+        return int(n.value)
+
+    def destroy(self) -> None:
+        if getattr(self, "_h", None):
+            self._L.bv_destroy(self._h)
+            self._h = None
+
+    def __del__(self):  # pragma: no cover - best effort
+        try:
+            self.destroy()
+        except Exception:
+            pass
+
+
+class AsyncSearchList:
+    """Device searches submitted together by one bv_search_async_n call.
+
+    entries: (index, q_ptr, k, fetch, rerank, out_rows_ptr, out_scores_ptr, out_counts_ptr) per
+    search, nq = 1 each; the argument array is built once and can be submitted any number of times
+    (the pointers are fixed)."""
+
+    def __init__(self, entries):
+        n = len(entries)
+        if n == 0:
+            raise ValueError("no searches")
+        self.n = n
+        self._keep = [e[0] for e in entries]
+        self._idx = (C.c_void_p * n)(*[e[0]._h.value for e in entries])
+        self._args = (_lib.BvSearchArgs * n)()
+        for i, (ix, q, k, fetch, rerank, r, s, c) in enumerate(entries):
+            self._args[i] = _lib.BvSearchArgs(queries=q, nq=1, k=k, fetch=max(fetch, k), rerank=int(rerank),
+                                              mask=None, mask_words=0, out_rows=r, out_scores=s, out_counts=c)
+        self._L = entries[0][0]._L
+
+    def submit(self, stream: int = 0) -> None:
+        _lib.check(self._L.bv_search_async_n(self._idx, self._args, self.n, C.c_void_p(stream)))
+
+
+@dataclass
+class _Entry:
+    id: str
+    row: int
+    metadata: Mapping[str, Any] | None = None
+
+
+@dataclass
+class _Store:
+    """src/store/store.ts: id<->row map, tombstones, metadata columns."""
+
+    dimension: int
+    metric: str
+    normalize: bool
+    by_id: dict = field(default_factory=dict)
+    by_row: list = field(default_factory=list)
+    deleted: set = field(default_factory=set)
+    columns: FilterColumns = field(default_factory=FilterColumns)
+
+
+class BrowserVec:
+    """The flat branches of src/index.ts over AddonQuantIndex: quantBits 1/4/8
+    (the quantized scan, QuantIndex) and 0 (the exact fp32 scan, FlatIndex,
+    src/index/flat.ts:132-211, scored with the WASM-SIMD f32 arithmetic of the
+    reference's CPU path)."""
+
+    def __init__(self, dimension: int, metric: str = "cosine", normalize: bool | None = None,
+                 quant_bits: int = 8, quant: Mapping[str, Any] | None = None, scoring: str = "asym",
+                 device: int = 0):
+        if not isinstance(dimension, int) or dimension <= 0:
+            raise ValueError(f"dimension must be a positive integer, got {dimension}")
+        quant = dict(quant or {})
+        if quant_bits not in (0, 1, 4, 8):
+            raise ValueError(f"quantBits {quant_bits} not supported (ships 0, 1, 4, 8)")
+        if quant_bits == 0:
+            scoring = "asym"  # exact scores: no quantized scoring mode applies
+        self.store = _Store(dimension, metric, metric == "cosine" if normalize is None else normalize)
+        self.quant_bits = quant_bits
+        self.rerank_factor = int(quant.get("rerankFactor", default_rerank_factor(quant_bits)))
+        self.index = AddonQuantIndex(dimension, quant.get("seed", DEFAULT_SEED), quant.get("rounds", 2),
+                                     quant_bits, scoring, device, metric)
+        self.last_query_ms: float | None = None
+        self.last_query_gpu_ms: float | None = None
+        self._version = 0       # bumped by every add and delete
+        self._dev = None        # (version, DeviceColumns, live-row mask words) on the index's GPU
+        self._masks: OrderedDict = OrderedDict()  # (filter, version) -> (mask words, matches, rows)
+
+    @classmethod
+    def create(cls, config: Mapping[str, Any]) -> "BrowserVec":
+        """BrowserVec.create (src/index.ts:232-263), quantized flat stores only."""
+        return cls(config["dimension"], config.get("metric", "cosine"), config.get("normalize"),
+                   config.get("quantBits", 8), config.get("quant"), config.get("scoring", "asym"),
+                   config.get("device", 0))
+
+    # ---- ingest -----------------------------------------------------------
+    def add_batch(self, records: Sequence[Mapping[str, Any]]) -> None:
+        """src/index.ts:293-305"""
+        if not records:
+            return
+        d = self.store.dimension
+        vecs = np.zeros((len(records), d), np.float32)
+        metas = []
+        for i, r in enumerate(records):
+            v = np.asarray(r["vector"], np.float32)
+            if v.size != d:
+                raise ValueError(f"vector dim {v.size} != store dim {d}")
+            if r["id"] in self.store.by_id:
+                raise ValueError(f"duplicate id: {r['id']}")
+            vecs[i] = v
+            row = len(self.store.by_row)
+            e = _Entry(r["id"], row, r.get("metadata"))
+            self.store.by_id[r["id"]] = e
+            self.store.by_row.append(e)
+            metas.append(r.get("metadata"))
+        if self.store.normalize:
+            vecs = normalize_rows(vecs)
+        self.store.columns.append(metas)
+        self.index.append(vecs, len(records))
+        self._version += 1
+
+    def add(self, record: Mapping[str, Any]) -> None:
+        self.add_batch([record])
+
+    def add_arrays(self, vectors: np.ndarray, ids: Sequence[str] | None = None,
+                   columns: Mapping[str, np.ndarray] | None = None,
+                   dictionaries: Mapping[str, list] | None = None) -> None:
+        """Bulk ingest of prepared arrays (rows normalized like store.prepare)."""
+        vectors = np.ascontiguousarray(vectors, np.float32)
+        n = vectors.shape[0]
+        base = len(self.store.by_row)
+        for i in range(n):
+            rid = ids[i] if ids is not None else f"v{base + i}"
+            e = _Entry(rid, base + i, None)
+            self.store.by_id[rid] = e
+            self.store.by_row.append(e)
+        if self.store.normalize:
+            vectors = normalize_rows(vectors)
+        if columns:
+            self.store.columns.append_columns(n, columns, dictionaries)
+        else:
+            self.store.columns.append([None] * n)
+        self.index.append(vectors, n)
+        self._version += 1
+
+    def delete(self, id: str) -> bool:
+        e = self.store.by_id.pop(id, None)
+        if e is None:
+            return False
+        self.store.deleted.add(e.row)
+        self._version += 1
+        return True
+
+    @property
+    def count(self) -> int:
+        return len(self.store.by_id)
+
+    # ---- query ------------------------------------------------------------
+    def _prep_query(self, query) -> np.ndarray:
+        q = np.asarray(query, np.float32).reshape(-1).copy()
+        if q.size != self.store.dimension:
+            raise ValueError(f"query dim {q.size} != store dim {self.store.dimension}")
+        if self.store.normalize:
+            q = normalize_rows(q[None, :])[0]
+        return q
+
+    def _meta_of(self, row: int):
+        return self.store.by_row[row].metadata
+
+    def _device_mask(self, flt: Mapping[str, Any]):
+        """The score mask of a filter -- its rows that are not deleted
+        (src/index.ts:372-386) -- built by the GPU predicate over device
+        copies of the metadata columns and kept per (filter, store version):
+        (mask words as a CUDA tensor, match count, the matching rows when at
+        most FILTER_CPU_SCAN_MAX, else None)."""
+        import torch
+
+        key = (json.dumps(flt, sort_keys=True, default=repr), self._version)
+        hit = self._masks.get(key)
+        if hit is not None:
+            self._masks.move_to_end(key)
+            return hit
+        dev = torch.device("cuda", self.index.device)
+        if self._dev is None or self._dev[0] != self._version:
+            dc = DeviceColumns.from_host(self.store.columns, dev)
+            live = np.ones(len(self.store.by_row), bool)
+            if self.store.deleted:
+                live[np.fromiter(self.store.deleted, np.int64)] = False
+            live_w = torch.from_numpy(pack_mask(live).view(np.int32)).to(dev)
+            self._dev = (self._version, dc, live_w)
+            self._masks.clear()  # masks of older versions are stale
+        _, dc, live_w = self._dev
+        m = dc.mask(flt, live=live_w)
+        if not hasattr(self, "_popc"):
+            self._popc = torch.tensor([bin(i).count("1") for i in range(256)], dtype=torch.int64, device=dev)
+        b = m.view(torch.uint8)
+        count = int(self._popc[b.long()].sum().item())
+        rows = None
+        if 0 < count <= FILTER_CPU_SCAN_MAX:
+            bits = ((b.unsqueeze(1) >> torch.arange(8, device=dev, dtype=torch.uint8)) & 1).flatten()
+            rows = torch.nonzero(bits).squeeze(1).cpu().numpy().astype(np.uint32)
+        entry = (m, count, rows)
+        self._masks[key] = entry
+        while len(self._masks) > MASK_CACHE_ENTRIES:
+            self._masks.popitem(last=False)
+        return entry
+
+    def _fetch(self, k: int, masked: bool, rerank: bool | None):
+        """src/index.ts:405-417: k_eff (oversampled by the tombstones unless a
+        mask already drops them) and the candidate fetch."""
+        total = self.index.size
+        k_eff = min(total, k) if masked else min(total, k + len(self.store.deleted))
         do_rerank = rerank if rerank is not None else self.rerank_factor > 1
         fetch = min(total, max(k_eff, k_eff * self.rerank_factor)) if do_rerank else k_eff
+        return k_eff, fetch, do_rerank
+
+    def query(self, query, k: int = 10, filter: Mapping[str, Any] | None = None,
+              rerank: bool | None = None) -> list[QueryResult]:
+        """src/index.ts:343-436 (quantized branch)."""
+        import time
+
+        q = self._prep_query(query)
+        predicate = compile_filter(filter) if filter else None
         t0 = time.perf_counter()
-        hits = self.index.search(q[None, :], k_eff, fetch, rerank=do_rerank, mask=mask)[0]
+        if predicate is not None:
+            m, count, rows = self._device_mask(filter)
+            if count == 0:
+                return []
+            if rows is not None:
+                return self._query_rows_exact(q, rows, k)
+            k_eff, fetch, do_rerank = self._fetch(k, True, rerank)
+            if k_eff <= 0:
+                return []
+            hits = self.index.search_masked(q[None, :], k_eff, fetch, do_rerank, m)[0]
+            self.last_query_ms = (time.perf_counter() - t0) * 1e3
+            self.last_query_gpu_ms = None
+            return self._map_hits(hits, k, predicate)
+        k_eff, fetch, do_rerank = self._fetch(k, False, rerank)
+        if k_eff <= 0:
+            return []
+        hits = self.index.search(q[None, :], k_eff, fetch, rerank=do_rerank)[0]
         self.last_query_ms = (time.perf_counter() - t0) * 1e3
         self.last_query_gpu_ms = min(self.index.stats()["last_query_gpu_ms"], self.last_query_ms)
         return self._map_hits(hits, k, predicate)

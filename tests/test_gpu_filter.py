@@ -18,6 +18,14 @@ FILTERS = [
     {"nofield": {"$ne": 1}}, {"nofield": 1}, {"lang": "en", "year": {"$gte": 2020}}, {"year": "2020"},
     {"year": 2020.0}, {"lang": {"$in": []}}, {"lang": "zz"}, {"year": {"$lte": 1995}, "flag": {"$ne": True}},
     {"score": {"$lt": 0.25}}, {"year": {"$in": [1990, 2029, None, "2020"]}},
+    # Set.has is SameValueZero (filter.ts:29-30): NaN in $in finds stored NaN; $eq NaN finds nothing
+    {"score": {"$in": [float("nan"), 0.5]}}, {"score": float("nan")}, {"score": {"$ne": float("nan")}},
+    # more values than one device term holds (an OR of calls) and more terms than one call holds (an AND)
+    {"year": {"$in": list(range(1990, 2030, 1))}},
+    {"year": {"$gte": 1990, "$lte": 2029, "$ne": 2001, "$gt": 1989, "$lt": 2030, "$in": list(range(1990, 2030))},
+     "lang": {"$ne": "zz", "$in": ["en", "fr", "de", "es", 5], "$eq": "en"},
+     "score": {"$gte": 0.0, "$lte": 1.0, "$ne": 0.5, "$gt": -1, "$lt": 2},
+     "flag": {"$ne": None, "$in": [True, False], "$eq": True}},
 ]
 
 
@@ -41,7 +49,7 @@ def _records(n, seed):
         if rng.random() < 0.5:
             m["flag"] = bool(rng.integers(2))
         if rng.random() < 0.6:
-            m["score"] = float(rng.random())
+            m["score"] = float(rng.random()) if rng.random() < 0.9 else float("nan")
         out.append(m if m or rng.random() < 0.5 else None)
     return out
 
@@ -63,11 +71,11 @@ def test_compile_errors_match_reference():
     fc.append(_records(10, 2))
     dc = DeviceColumns.from_host(fc, torch.device("cpu"))
     with pytest.raises(ValueError, match='filter: \\$gt on "year" expects a number, got string'):
-        dc.compile({"year": {"$gt": "x"}})
+        dc.units({"year": {"$gt": "x"}})
     with pytest.raises(ValueError, match='filter: \\$in on "lang" expects an array, got string'):
-        dc.compile({"lang": {"$in": "en"}})
+        dc.units({"lang": {"$in": "en"}})
     with pytest.raises(ValueError, match='filter: unknown operator "\\$regex" on field "lang"'):
-        dc.compile({"lang": {"$regex": "e"}})
+        dc.units({"lang": {"$regex": "e"}})
 
 
 @pytest.mark.gpu
