@@ -575,7 +575,7 @@ def main():
             dist.destroy_process_group()
         return
 
-    from browservec_b200.index import AddonQuantIndex, AsyncSearchList
+    from browservec_b200.index import AddonQuantIndex, AsyncSearchList, PreparedSearch
 
     corpus = make_data(torch, dev, SEED, N_ROWS, DIM)
     queries = make_data(torch, dev, SEED + 1, N_QUERIES, DIM)
@@ -660,8 +660,9 @@ def main():
     e2e = None
     if not args.no_e2e:
         q_np = queries.cpu().numpy()
+        calls = [PreparedSearch(ix, 1, K, fetch, True) for ix in reps]  # host buffers, one query per call
         for i in range(min(64, N_QUERIES)):
-            reps[i % len(reps)].search_arrays(q_np[i:i + 1], K, fetch, True)
+            calls[i % len(calls)](q_np[i:i + 1])
         if dist:
             dist.barrier()
         torch.cuda.synchronize()
@@ -669,16 +670,17 @@ def main():
         e2e_steps = max(1, min(args.steps, 3))
         for _ in range(e2e_steps):
             for i in range(N_QUERIES):
-                reps[i % len(reps)].search_arrays(q_np[i:i + 1], K, fetch, True)
+                calls[i % len(calls)](q_np[i:i + 1])
         wall = time.perf_counter() - t0
         if dist:
             t = torch.tensor([wall], device=dev, dtype=torch.float64)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             wall = float(t.item())
-        out_words = 2 * K + 1 + 2 * fetch + 1
+        out_words = 2 * K + 1
         e2e = {"value": max(world, 1) * e2e_steps * N_QUERIES / wall, "unit": UNIT,
                "h2d_bytes_per_step": N_QUERIES * DIM * 4, "d2h_bytes_per_step": N_QUERIES * out_words * 4,
-               "steps": e2e_steps, "timing": "host wall clock around synchronous bv_search calls"}
+               "steps": e2e_steps, "timing": "host wall clock around synchronous bv_search calls (one query "
+                                             "per call, host buffers, PreparedSearch)"}
     for ix in reps:
         ix.destroy()
 

@@ -306,12 +306,10 @@ int plan_scan(bv_index* idx, uint32_t F, Plan* pl, bool fold = true, bool alone 
   pl->capc = capc;
   pl->check_tiles = (capc - 2 * fp) / tr;
   if (pl->check_tiles < 1) pl->check_tiles = 1;
-  // (asym keeps the tail kernel: its registers allow one CTA per SM, where a
-  // finishing CTA would hold up its SM's next query)
-  pl->fold = fold && fp <= 256 && idx->scoring != BV_SCORE_ASYM;
-  // Folded integer scans run two CTAs per SM (consecutive queries): each CTA
-  // then keeps to half of the SM's shared memory.
-  const bool two = pl->fold && idx->scoring != BV_SCORE_ASYM;
+  pl->fold = fold && fp <= 256;
+  // Folded scans run two CTAs per SM (consecutive queries): each CTA then
+  // keeps to half of the SM's shared memory.
+  const bool two = pl->fold;
   const uint32_t limit = two ? static_cast<uint32_t>(idx->smem_per_sm) / 2u - 1024u
                              : static_cast<uint32_t>(idx->max_smem);
   pl->stages = 0;
@@ -337,12 +335,13 @@ int plan_scan(bv_index* idx, uint32_t F, Plan* pl, bool fold = true, bool alone 
   // epilogue are spread over more tiles.  Measured on B200 (100k x 768 int8,
   // back-to-back queries): 98 CTAs 47.1k q/s, 74 50.4k, 59 53.4k, 49 55.6k,
   // 42 53.6k.
-  const bool two_per_sm = pl->fold && pl->smem <= limit && idx->scoring != BV_SCORE_ASYM;
+  const bool two_per_sm = pl->fold && pl->smem <= limit;
   const uint32_t nsm = static_cast<uint32_t>(idx->num_sms);
   const uint32_t all = two_per_sm ? 2u * nsm : pl->fold ? nsm : (nsm > 2 ? nsm - 2u : 1u);
-  // One CTA per SM (asym, or wide F with the tail kernel): back to back, a
-  // query takes two sevenths of the SMs (asym, 100k x 768 int8: 146 CTAs
-  // 27.0k q/s, 74 28.2k, 49 31.7k, 42 33.1k, 37 32.8k, 29 28.1k).
+  // One CTA per SM (wide F with the tail kernel): back to back, a query takes
+  // two sevenths of the SMs (measured when asym ran one CTA per SM, 100k x
+  // 768 int8: 146 CTAs 27.0k q/s, 74 28.2k, 49 31.7k, 42 33.1k, 37 32.8k,
+  // 29 28.1k).
   const uint32_t one_sm = nsm * 2u / 7u > 0 ? nsm * 2u / 7u : 1u;
   const uint32_t sms = alone ? all : two_per_sm ? (nsm / 3u > 0 ? nsm / 3u : 1u) : (pl->fold ? all : one_sm);
   pl->grid = pl->ntiles < sms ? pl->ntiles : sms;

@@ -1076,6 +1076,12 @@ __device__ __forceinline__ void cta_publish(const ScanParams& p, uint64_t* cand,
 // BITS 8/4/1; MODE asym/int/hamming; CB chunk bytes (4, 8 or 16); L lanes per
 // row; CPL chunks per lane; U rows in flight per row-group (asym: even, two
 // rows per f32x2 accumulator).
+// Largest per-lane query slice (elements) the asym scan keeps in registers;
+// longer slices are read from shared memory.
+#ifndef BV_ASYM_QREG_MAX
+#define BV_ASYM_QREG_MAX 64
+#endif
+
 template <int BITS, int MODE, int CB, int L, int CPL, int U>
 struct ScanCfg {
   static constexpr int W = CB / 4;                                     // words per chunk
@@ -1083,16 +1089,16 @@ struct ScanCfg {
   static constexpr int EPC = W * EPW;                                  // elements per chunk
   static constexpr int G = 32 / L;                                     // rows per warp step
   static constexpr int RPI = kConsumerWarps * G * U;                   // rows per iteration
-  static constexpr bool kQReg = (MODE == kAsym) && (CPL * EPC <= 64);  // fp32 query in registers
+  static constexpr bool kQReg = (MODE == kAsym) && (CPL * EPC <= BV_ASYM_QREG_MAX);  // fp32 query in registers
   // per-chunk integer query words: int8 W, int4 2W (even/odd), 1-bit 8W planes, hamming W
   static constexpr int QW = MODE == kInt ? (BITS == 8 ? W : (BITS == 4 ? 2 * W : 8 * W))
                                          : (MODE == kHamming ? W : 1);
 };
 
-// The integer scorings fit two CTAs per SM (consecutive queries overlap on an
-// SM: one streams while the other starts or finishes); asym keeps one.
+// Two CTAs per SM (consecutive queries overlap on an SM: one streams while
+// the other starts or finishes): at most 56 registers a thread.
 template <int BITS, int MODE, int CB, int L, int CPL, int U>
-__global__ void __launch_bounds__(kScanThreads, MODE == kAsym ? 1 : 2) scan_kernel(const ScanParams p) {
+__global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(const ScanParams p) {
   using C = ScanCfg<BITS, MODE, CB, L, CPL, U>;
   extern __shared__ __align__(128) uint8_t smem[];
   const ScanSmem lay = scan_smem_layout(p.tile_bytes, p.tile_rows, p.stages, p.P, p.rounds, p.capc);

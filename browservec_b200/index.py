@@ -324,6 +324,33 @@ class AddonQuantIndex:
             pass
 
 
+class PreparedSearch:
+    """A host-memory search request whose buffers and argument block are made
+    once: each call copies a batch of queries in and runs bv_search (the
+    call search() makes), so a caller issuing one query at a time pays no
+    per-call allocation.  The returned arrays are reused by the next call."""
+
+    def __init__(self, index: "AddonQuantIndex", nq: int, k: int, fetch: int, rerank: bool = True):
+        self.q = np.zeros((nq, index.dim), np.float32)
+        self.rows = np.zeros((nq, k), np.uint32)
+        self.scores = np.zeros((nq, k), np.float32)
+        self.counts = np.zeros(nq, np.uint32)
+        self.args = _lib.BvSearchArgs(queries=self.q.ctypes.data, nq=nq, k=k, fetch=max(fetch, k),
+                                      rerank=int(rerank), mask=None, mask_words=0,
+                                      out_rows=self.rows.ctypes.data, out_scores=self.scores.ctypes.data,
+                                      out_counts=self.counts.ctypes.data)
+        self._ref = C.byref(self.args)
+        self._fn = index._L.bv_search
+        self._index = index
+
+    def __call__(self, qs: np.ndarray):
+        np.copyto(self.q, qs.reshape(self.q.shape), casting="same_kind")
+        rc = self._fn(self._index._h, self._ref)
+        if rc:
+            _lib.check(rc)
+        return self.rows, self.scores, self.counts
+
+
 class AsyncSearchList:
     """Device searches submitted together by one bv_search_async_n call.
 
@@ -620,6 +647,33 @@ class BrowserVec:
             self.destroy()
         except Exception:
             pass
+
+
+class PreparedSearch:
+    """A host-memory search request whose buffers and argument block are made
+    once: each call copies a batch of queries in and runs bv_search (the
+    call search() makes), so a caller issuing one query at a time pays no
+    per-call allocation.  The returned arrays are reused by the next call."""
+
+    def __init__(self, index: "AddonQuantIndex", nq: int, k: int, fetch: int, rerank: bool = True):
+        self.q = np.zeros((nq, index.dim), np.float32)
+        self.rows = np.zeros((nq, k), np.uint32)
+        self.scores = np.zeros((nq, k), np.float32)
+        self.counts = np.zeros(nq, np.uint32)
+        self.args = _lib.BvSearchArgs(queries=self.q.ctypes.data, nq=nq, k=k, fetch=max(fetch, k),
+                                      rerank=int(rerank), mask=None, mask_words=0,
+                                      out_rows=self.rows.ctypes.data, out_scores=self.scores.ctypes.data,
+                                      out_counts=self.counts.ctypes.data)
+        self._ref = C.byref(self.args)
+        self._fn = index._L.bv_search
+        self._index = index
+
+    def __call__(self, qs: np.ndarray):
+        np.copyto(self.q, qs.reshape(self.q.shape), casting="same_kind")
+        rc = self._fn(self._index._h, self._ref)
+        if rc:
+            _lib.check(rc)
+        return self.rows, self.scores, self.counts
 
 
 class AsyncSearchList:
