@@ -300,7 +300,8 @@ def _baseline_sample(shards, cfg, threads, per_step):
             "(gpuTopk.ts:160-189)")
 
 
-def run_sharded(args, name):
+def run_sharded(args, name, ds):
+    """One row-sharded configuration; returns rank 0's JSON line (else None)."""
     import torch
 
     from browservec_b200 import datagen
@@ -311,7 +312,7 @@ def run_sharded(args, name):
         cfg["n"] = args.rows
     if args.queries:
         cfg["nq"] = args.queries
-    dist, world, rank, local = _init_dist(torch)
+    dist, world, rank, local = ds
     dev = torch.device("cuda", local)
     n, dim, nq, k = cfg["n"], cfg["dim"], cfg["nq"], cfg["k"]
     fetch = min(n, max(k, k * cfg["rf"]))  # src/index.ts:414-417
@@ -340,9 +341,8 @@ def run_sharded(args, name):
                     "cpu_baseline": {"value": qps, "unit": UNIT, "cores": threads, "kind": "port",
                                      "sample": _baseline_sample(shards, cfg, threads, per_step)},
                     "e2e": {"value": qps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-            print(json.dumps(line), flush=True)
-        dist.destroy_process_group()
-        return
+            return line
+        return None
 
     scoring = args.sharded_scoring or cfg["scoring"]
     batched = scoring != "asym" and not args.per_query
@@ -485,9 +485,8 @@ def run_sharded(args, name):
                 "recall_at_10": rec, "recall_sample": ns, "query_ms": query_ms,
                 "gpu_launches": args.steps * launches_per_step, "roofline": roofline, "cpu_baseline": cpu,
                 "e2e": e2e, "clocks": clk_res, "also": also, "step_breakdown_ms": breakdown}
-        print(json.dumps(line), flush=True)
     idx.destroy()
-    dist.destroy_process_group()
+    return line if rank == 0 else None
 
 
 METRIC_SHARDED = "queries/sec at fixed recall@10 (row-sharded quantized flat scan)"
@@ -505,7 +504,9 @@ def main():
     ap.add_argument("--replicas", type=int, default=4)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--config", default="c4", choices=[*SINGLE, *SHARDED])
+    ap.add_argument("--config", default=None, choices=[*SINGLE, *SHARDED],
+                    help="one configuration only (default: config 4 as the headline line, with configs "
+                         "1, 2, 3 and 5 measured in the same run under its 'configs' key)")
     ap.add_argument("--cpu-queries", type=int, default=0,
                     help="sharded configs: queries per CPU-baseline sample (default 16, reference arm 4 per step)")
     ap.add_argument("--no-asym", action="store_true", help="sharded configs: skip the asym recall figure")
@@ -517,8 +518,53 @@ def main():
     ap.add_argument("--per-query", action="store_true",
                     help="sharded configs: per-query scans instead of the batched tensor-core path")
     args = ap.parse_args()
-    if args.config in SHARDED:
-        return run_sharded(args, args.config)
+    import torch
+
+    ds = _init_dist(torch)
+    dist, world, rank, local = ds
+    try:
+        if args.config is not None:
+            line = run_config(args, args.config, ds)
+        else:
+            line = run_config(args, "c4", ds)
+            if args.impl == "ours":
+                extra = {}
+                for name in ("c3", "c5", "c2", "c1"):
+                    sub = argparse.Namespace(**vars(args))
+                    try:
+                        r = run_config(sub, name, ds)
+                        if r is not None:
+                            extra[name] = _summary(r)
+                    except Exception as e:  # a failing side configuration must not lose the headline
+                        extra[name] = {"error": f"{type(e).__name__}: {e}"[:400]}
+                    torch.cuda.empty_cache()
+                if line is not None:
+                    line["configs"] = extra
+        if line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        dist.destroy_process_group()
+
+
+def _summary(line):
+    """The figures of one configuration's line kept under the headline's 'configs'."""
+    keys = ("metric", "value", "unit", "ms_per_step", "dtype", "recall_at_10", "recall_sample", "gpu_launches",
+            "roofline", "cpu_baseline", "e2e", "also", "step_breakdown_ms", "clocks")
+    out = {k: line[k] for k in keys if k in line}
+    out["config"] = line.get("config")
+    return out
+
+
+def run_config(args, name, ds):
+    if name in SHARDED:
+        return run_sharded(args, name, ds)
+    return run_single(args, name, ds)
+
+
+def run_single(args, name, ds):
+    """One single-query configuration (replicas per GPU); returns rank 0's
+    JSON line (else None)."""
+    args.config = name
     _use_single(args.config)
     if args.queries:  # a shorter step (for ncu captures); the timed line then says so in its config
         global N_QUERIES
@@ -530,18 +576,9 @@ def main():
 
     import torch
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    dist = None
-    if world > 1:
-        import torch.distributed as dist
-        from datetime import timedelta
-
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
-    torch.cuda.set_device(local)
+    dist, world, rank, local = ds
+    if world == 1:
+        dist = None  # replicas need no collective on one GPU
     dev = torch.device("cuda", local)
     fetch = min(N_ROWS, max(K, K * RERANK_FACTOR))  # src/index.ts:414-417
     config = {"workload": WORKLOAD, "rows": N_ROWS, "dim": DIM, "bits": BITS,
@@ -554,9 +591,7 @@ def main():
 
     if args.impl == "reference":
         if rank != 0:
-            if dist:
-                dist.destroy_process_group()
-            return
+            return None
         corpus = make_data(torch, dev, SEED, N_ROWS, DIM)
         queries = make_data(torch, dev, SEED + 1, N_QUERIES, DIM)
         c_np, q_np = corpus.cpu().numpy(), queries.cpu().numpy()
@@ -570,10 +605,7 @@ def main():
                                  "sample": f"{per_step} queries per step over the full {N_ROWS} x {DIM} fp32 corpus "
                                            "(WASM-SIMD scan restated in C, one query per thread)"},
                 "e2e": {"value": qps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-        print(json.dumps(line))
-        if dist:
-            dist.destroy_process_group()
-        return
+        return line
 
     from browservec_b200.index import AddonQuantIndex, AsyncSearchList, PreparedSearch
 
@@ -709,9 +741,8 @@ def main():
                 "data": "synthetic (seeded Philox N(0,1), L2-normalised)", "config": config,
                 "recall_at_10": rec, "query_ms": query_ms, "gpu_launches": launches,
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk, "also": also}
-        print(json.dumps(line))
-    if dist:
-        dist.destroy_process_group()
+        return line
+    return None
 
 
 if __name__ == "__main__":

@@ -973,6 +973,18 @@ int bv_export_codes(const bv_index* idx, uint64_t row0, uint64_t count, uint32_t
   return BV_OK;
 }
 
+int bv_export_originals(const bv_index* idx, uint64_t row0, uint64_t count, float* out) {
+  if (!idx || (count && !out)) return fail(BV_ERR_INVALID, "null argument");
+  if (row0 + count > idx->rows) return fail(BV_ERR_INVALID, "rows out of range");
+  if (count == 0) return BV_OK;
+  bv_index* m = const_cast<bv_index*>(idx);
+  BV_CUDA(m, cudaSetDevice(idx->device), "cudaSetDevice");
+  BV_CUDA(m, cudaStreamSynchronize(idx->stream), "sync");
+  BV_CUDA(m, cudaMemcpy(out, idx->d_orig + row0 * idx->dim, count * idx->dim * sizeof(float), cudaMemcpyDeviceToHost),
+          "D2H");
+  return BV_OK;
+}
+
 int bv_get_stats(const bv_index* idx, bv_stats* out) {
   if (!idx || !out) return fail(BV_ERR_INVALID, "null argument");
   out->rows = idx->rows;

@@ -298,6 +298,13 @@ class AddonQuantIndex:
         _lib.check(self._L.bv_export_codes(self._h, row0, count, _ptr(words), _ptr(scales)))
         return words, scales
 
+    def export_originals(self, row0: int = 0, count: int | None = None) -> np.ndarray:
+        """The stored (normalized) fp32 rows, (count, dim)."""
+        count = self.size - row0 if count is None else count
+        out = np.empty((count, self.dim), np.float32)
+        _lib.check(self._L.bv_export_originals(self._h, row0, count, _ptr(out)))
+        return out
+
     def stats(self) -> dict:
         s = _lib.BvStats()
         _lib.check(self._L.bv_get_stats(self._h, C.byref(s)))
@@ -477,6 +484,56 @@ class BrowserVec:
         else:
             self.store.columns.append([None] * n)
         self.index.append(vectors, n)
+        self._version += 1
+
+    # ---- snapshots (src/index.ts:608-700, src/persist/format.ts) ----------
+    def export(self) -> bytes:
+        """BrowserVec.export: a snapshot of the live rows (tombstones compacted
+        out, src/index.ts:646-671), in the reference's format."""
+        from .persist import serialize
+
+        live = [e for e in self.store.by_row if e.row not in self.store.deleted]
+        vecs = self.index.export_originals() if self.index.size else np.zeros((0, self.store.dimension), np.float32)
+        if self.store.deleted:
+            vecs = vecs[np.array([e.row for e in live], np.int64)]
+        entries = [{"id": e.id, "metadata": e.metadata} for e in live]
+        return serialize(self.store.dimension, self.store.metric, self.store.normalize, entries, vecs)
+
+    @classmethod
+    def import_(cls, buf, config: Mapping[str, Any] | None = None) -> "BrowserVec":
+        """BrowserVec.import (src/index.ts:616-644): a store built from a
+        snapshot (quantBits from `config`, default 0 as in the reference)."""
+        from .persist import deserialize
+
+        snap = deserialize(buf)
+        config = dict(config or {})
+        db = cls(snap.dimension, snap.metric, snap.normalize, config.get("quantBits", 0), config.get("quant"),
+                 config.get("scoring", "asym"), config.get("device", 0))
+        db.load_snapshot(snap)
+        return db
+
+    def load_snapshot(self, snap) -> None:
+        """src/index.ts:673-700: ids and metadata into the store, and the
+        stored vectors (already normalized when the store normalizes) into
+        the index in one bulk append -- the GPU encodes them -- instead of a
+        per-row insert."""
+        if self.count > 0 or self.store.by_row:
+            raise ValueError("cannot load into a non-empty store")
+        if snap.dimension != self.store.dimension:
+            raise ValueError(f"snapshot dim {snap.dimension} != store dim {self.store.dimension}")
+        if snap.metric != self.store.metric:
+            raise ValueError(f"snapshot metric {snap.metric} != store metric {self.store.metric}")
+        metas = []
+        for row, e in enumerate(snap.entries):
+            if e["id"] in self.store.by_id:
+                raise ValueError(f"duplicate id: {e['id']}")
+            ent = _Entry(e["id"], row, e.get("metadata"))
+            self.store.by_id[e["id"]] = ent
+            self.store.by_row.append(ent)
+            metas.append(e.get("metadata"))
+        self.store.columns.append(metas)
+        if snap.count:
+            self.index.append(snap.vectors, snap.count)
         self._version += 1
 
     def delete(self, id: str) -> bool:
@@ -623,6 +680,13 @@ class BrowserVec:
         batch = self.index.search(qs, k_eff, fetch, rerank=do_rerank)
         return [self._map_hits(h, k) for h in batch]
 
+    def export_originals(self, row0: int = 0, count: int | None = None) -> np.ndarray:
+        """The stored (normalized) fp32 rows, (count, dim)."""
+        count = self.size - row0 if count is None else count
+        out = np.empty((count, self.dim), np.float32)
+        _lib.check(self._L.bv_export_originals(self._h, row0, count, _ptr(out)))
+        return out
+
     def stats(self) -> dict:
         s = _lib.BvStats()
         _lib.check(self._L.bv_get_stats(self._h, C.byref(s)))
@@ -802,6 +866,56 @@ class BrowserVec:
         else:
             self.store.columns.append([None] * n)
         self.index.append(vectors, n)
+        self._version += 1
+
+    # ---- snapshots (src/index.ts:608-700, src/persist/format.ts) ----------
+    def export(self) -> bytes:
+        """BrowserVec.export: a snapshot of the live rows (tombstones compacted
+        out, src/index.ts:646-671), in the reference's format."""
+        from .persist import serialize
+
+        live = [e for e in self.store.by_row if e.row not in self.store.deleted]
+        vecs = self.index.export_originals() if self.index.size else np.zeros((0, self.store.dimension), np.float32)
+        if self.store.deleted:
+            vecs = vecs[np.array([e.row for e in live], np.int64)]
+        entries = [{"id": e.id, "metadata": e.metadata} for e in live]
+        return serialize(self.store.dimension, self.store.metric, self.store.normalize, entries, vecs)
+
+    @classmethod
+    def import_(cls, buf, config: Mapping[str, Any] | None = None) -> "BrowserVec":
+        """BrowserVec.import (src/index.ts:616-644): a store built from a
+        snapshot (quantBits from `config`, default 0 as in the reference)."""
+        from .persist import deserialize
+
+        snap = deserialize(buf)
+        config = dict(config or {})
+        db = cls(snap.dimension, snap.metric, snap.normalize, config.get("quantBits", 0), config.get("quant"),
+                 config.get("scoring", "asym"), config.get("device", 0))
+        db.load_snapshot(snap)
+        return db
+
+    def load_snapshot(self, snap) -> None:
+        """src/index.ts:673-700: ids and metadata into the store, and the
+        stored vectors (already normalized when the store normalizes) into
+        the index in one bulk append -- the GPU encodes them -- instead of a
+        per-row insert."""
+        if self.count > 0 or self.store.by_row:
+            raise ValueError("cannot load into a non-empty store")
+        if snap.dimension != self.store.dimension:
+            raise ValueError(f"snapshot dim {snap.dimension} != store dim {self.store.dimension}")
+        if snap.metric != self.store.metric:
+            raise ValueError(f"snapshot metric {snap.metric} != store metric {self.store.metric}")
+        metas = []
+        for row, e in enumerate(snap.entries):
+            if e["id"] in self.store.by_id:
+                raise ValueError(f"duplicate id: {e['id']}")
+            ent = _Entry(e["id"], row, e.get("metadata"))
+            self.store.by_id[e["id"]] = ent
+            self.store.by_row.append(ent)
+            metas.append(e.get("metadata"))
+        self.store.columns.append(metas)
+        if snap.count:
+            self.index.append(snap.vectors, snap.count)
         self._version += 1
 
     def delete(self, id: str) -> bool:

@@ -149,6 +149,12 @@ BV_API int bv_query_rows_exact(bv_index* idx, const float* query, const uint32_t
 BV_API int bv_export_codes(const bv_index* idx, uint64_t row0, uint64_t count, uint32_t* words,
                     float* scales);
 
+/* Copy `count` stored fp32 rows (the normalized originals the re-rank reads,
+ * count*dim floats) to host memory from row `row0`: the vectors a snapshot
+ * holds (the reference keeps them in its host store for
+ * BrowserVec.export / save, src/index.ts:646-671). */
+BV_API int bv_export_originals(const bv_index* idx, uint64_t row0, uint64_t count, float* out);
+
 /* Stats the index contributes to BrowserVec.stats() (src/index.ts:702-750). */
 typedef struct bv_stats {
   uint64_t rows;

@@ -94,3 +94,39 @@ def test_filter_errors_are_the_reference_errors():
             db.query_batch([q], 5, filter={"lang": {"$regex": "e"}})
     finally:
         db.destroy()
+
+
+@pytest.mark.parametrize("bits", [8, 1, 0])
+def test_snapshot_round_trip_bulk_load(bits):
+    """export -> import (src/index.ts:608-700): the snapshot holds the live rows
+    only; the imported store, loaded in one bulk append encoded on the GPU,
+    answers exactly as a store built record by record from those rows."""
+    from browservec_b200.index import BrowserVec
+
+    rng = np.random.default_rng(3)
+    n, d = 3000, 48
+    x = rng.standard_normal((n, d)).astype(np.float32)
+    recs = [{"id": f"r{i}", "vector": x[i], "metadata": {"g": int(i % 5)}} for i in range(n)]
+    a = BrowserVec.create({"dimension": d, "quantBits": bits})
+    b = c = None
+    try:
+        a.add_batch(recs)
+        for i in range(0, n, 11):
+            a.delete(f"r{i}")
+        snap = a.export()
+        b = BrowserVec.import_(snap, {"quantBits": bits})
+        live = [r for i, r in enumerate(recs) if i % 11]
+        c = BrowserVec.create({"dimension": d, "quantBits": bits})
+        c.add_batch(live)
+        assert b.count == c.count == len(live)
+        qs = rng.standard_normal((4, d)).astype(np.float32)
+        for q in qs:
+            for flt in (None, {"g": 2}):
+                rb, rc = b.query(q, 10, filter=flt), c.query(q, 10, filter=flt)
+                assert [h.id for h in rb] == [h.id for h in rc]
+                assert [h.score for h in rb] == [h.score for h in rc]
+                assert [h.metadata for h in rb] == [h.metadata for h in rc]
+    finally:
+        for s in (a, b, c):
+            if s is not None:
+                s.destroy()
