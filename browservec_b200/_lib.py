@@ -22,7 +22,8 @@ EXPORTS = ("bv_create", "bv_destroy", "bv_last_error", "bv_append", "bv_append_d
            "bv_launches_last_search", "bv_set_phase_trace", "bv_search_noalloc",
            "bv_merge_shards", "bv_search_batch", "bv_filter_mask", "bv_batch_select", "bv_batch_finish",
            "bv_keys_threshold", "bv_set_batch_timing", "bv_last_batch_profile", "bv_set_scoring",
-           "bv_merge_topk", "bv_check_wait_timeout", "bv_export_originals")
+           "bv_merge_topk", "bv_check_wait_timeout", "bv_export_originals",
+           "bv_search_rows")
 
 
 class BvConfig(C.Structure):
@@ -119,6 +120,7 @@ def load(path: str = LIB_PATH):
         "bv_merge_topk": (C.c_int, [P, C.c_uint32, C.c_uint32, C.c_uint32, P, P, P, P]),
         "bv_check_wait_timeout": (C.c_int, [P, C.c_uint32]),
         "bv_export_originals": (C.c_int, [P, C.c_uint64, C.c_uint64, P]),
+        "bv_search_rows": (C.c_int, [P, C.POINTER(BvSearchArgs), P, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

@@ -19,7 +19,7 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libbvcuda.so")
-SOURCES = ["bv_api.cu", "bv_encode.cu", "bv_exact.cu", "bv_tail.cu", "bv_merge.cu", "bv_batch.cu", "bv_filter.cu", "bv_flat.cu", "bv_probe.cu", "bv_scan8a.cu", "bv_scan8i.cu",
+SOURCES = ["bv_api.cu", "bv_encode.cu", "bv_exact.cu", "bv_tail.cu", "bv_merge.cu", "bv_batch.cu", "bv_filter.cu", "bv_flat.cu", "bv_probe.cu", "bv_rows.cu", "bv_scan8a.cu", "bv_scan8i.cu",
            "bv_scan4a.cu", "bv_scan4i.cu", "bv_scan1a.cu", "bv_scan1i.cu", "bv_scan1h.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",

@@ -6,6 +6,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -189,6 +190,21 @@ struct bv_index {
   size_t ctmax_cap = 0;
   uint32_t last_kept = 0;
   bv_batch_state* batch = nullptr;  // batched-search plan kept between phases, timing
+  // candidate-list search: gathered codes, scales and their rows; rowmap is
+  // set only while such a search enqueues its scans
+  uint8_t* d_gcodes = nullptr;
+  size_t gcodes_cap = 0;
+  float* d_gscales = nullptr;
+  size_t gscales_cap = 0;
+  uint32_t* d_growmap = nullptr;
+  size_t growmap_cap = 0;
+  uint32_t* d_goffs = nullptr;  // per query: candidate offset, segment start
+  size_t goffs_cap = 0;
+  const uint32_t* rowmap = nullptr;
+  // batched GEMM on CTA pairs (cta_group::2) for batches of two or more query
+  // tiles, chosen with BV_GEMM_PAIR=1 in the environment; off by default: on
+  // B200 it measured slower than the one-CTA GEMM (config 4 10.1 vs 9.2 ms)
+  bool gemm_pair = false;
 };
 
 namespace {
@@ -390,6 +406,9 @@ int check_args(bv_index* idx, const bv_search_args* a, uint32_t* F_out) {
 int ring_prepare(bv_index* idx, size_t keys) {
   uint32_t r = kRing;
   while (r > 2 && static_cast<size_t>(r) * keys * 8 > kRingMaxBytes) r >>= 1;
+  // a ring with at least as many slots of at least this size serves as is
+  // (searches over candidate lists of varying length would otherwise resize it)
+  if (idx->partials_slot >= keys && idx->ring >= r && idx->ring && idx->d_partials) return BV_OK;
   if (idx->partials_slot != keys || idx->ring != r) {
     // a new geometry: earlier queries' slots must be out of use before reuse
     BV_CUDA(idx, cudaDeviceSynchronize(), "ring resize");
@@ -564,6 +583,7 @@ int enqueue_search(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStrea
   p.check_tiles = pl.check_tiles;
   p.partials = idx->d_partials;
   p.err = idx->d_err;
+  p.rowmap = idx->rowmap;
   const bool tracing = idx->d_trace && idx->trace_cap >= (static_cast<uint64_t>(pl.grid) + 1) * 8;
   p.trace = tracing ? idx->d_trace : nullptr;
 
@@ -580,6 +600,7 @@ int enqueue_search(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStrea
   t.dim = idx->dim;
   t.row_base = idx->row_base;
   t.err = idx->d_err;
+  t.rowmap = idx->rowmap;
   t.trace = tracing ? idx->d_trace + static_cast<size_t>(pl.grid) * 8 : nullptr;
   // gathered-row staging: as many rows of stride dim+4 as fit beside the rest
   const uint32_t row_bytes = (idx->dim + 4) * 4;
@@ -705,6 +726,7 @@ int bv_create(const bv_config* cfg, bv_index** out) {
   idx->scoring = cfg->scoring;
   idx->row_base = cfg->row_base;
   idx->P = P;
+  if (const char* gp = std::getenv("BV_GEMM_PAIR")) idx->gemm_pair = std::strcmp(gp, "1") == 0;
   idx->R = cfg->bits ? bv::code_row_bytes(static_cast<int>(cfg->bits), P) : 0;  // bits 0: originals only
   auto bail = [&](int rc) {
     bv_destroy(idx);
@@ -780,6 +802,10 @@ int bv_destroy(bv_index* idx) {
   cudaFree(idx->d_cposfac);
   cudaFree(idx->d_cposrow);
   cudaFree(idx->d_ctmax);
+  cudaFree(idx->d_gcodes);
+  cudaFree(idx->d_gscales);
+  cudaFree(idx->d_growmap);
+  cudaFree(idx->d_goffs);
   if (idx->h_pin) cudaFreeHost(idx->h_pin);
   if (idx->ev0) cudaEventDestroy(idx->ev0);
   if (idx->ev1) cudaEventDestroy(idx->ev1);
@@ -1326,7 +1352,10 @@ int batch_rounds(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStream_
   const uint32_t npos = compact ? kept : static_cast<uint32_t>(idx->rows);
   const uint32_t T = static_cast<uint32_t>((static_cast<uint64_t>(npos) + bv::kBRowTile - 1) / bv::kBRowTile);
   bs->prof.gemm_macs = static_cast<double>(nq) * static_cast<double>(npos) * static_cast<double>(idx->P);
-  if ((rc = grow(idx, &idx->d_qtiles, &idx->qtiles_cap, static_cast<size_t>(nqt) * KB * bv::kBQTileBytes,
+  // query tiles for an even count (the pair GEMM takes two at a time; an odd
+  // last tile's partner holds no valid query)
+  const uint32_t nqt_pad = (nqt + 1u) & ~1u;
+  if ((rc = grow(idx, &idx->d_qtiles, &idx->qtiles_cap, static_cast<size_t>(nqt_pad) * KB * bv::kBQTileBytes,
                  "batch queries")))
     return rc;
   if ((rc = grow(idx, &idx->d_qfac, &idx->qfac_cap, nq, "batch queries"))) return rc;
@@ -1378,6 +1407,17 @@ int batch_rounds(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStream_
   sp.cnt = idx->d_bcnt;
   sp.thr = idx->d_thr;
 
+  // Two or more query tiles: the CTA-pair GEMM (cta_group::2, 256 queries x
+  // 256 rows per pair), its operands read by TMA tensor copies.
+  const bool pair = nqt >= 2 && idx->gemm_pair;
+  alignas(64) unsigned char amap[128], bmap[128];
+  if (pair) {
+    cudaError_t e = bv::encode_tile_rows_map(amap, idx->d_qtiles, static_cast<uint64_t>(nqt_pad) * KB * bv::kBQTile,
+                                             bv::kBQTile);
+    if (e == cudaSuccess)
+      e = bv::encode_tile_rows_map(bmap, g.ctiles, static_cast<uint64_t>(T) * KB * bv::kBRowTile, bv::kBRowTile / 2);
+    if (e != cudaSuccess) return cuda_fail(idx, e, "batch tensor maps");
+  }
   uint32_t launches = 0;
   auto gemm = [&](uint32_t rt0, uint32_t rt1) -> int {
     g.rt0 = rt0;
@@ -1386,7 +1426,14 @@ int batch_rounds(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStream_
     const uint32_t grid = static_cast<uint32_t>(tiles < static_cast<uint64_t>(idx->num_sms) ? tiles : idx->num_sms);
     int r;
     if ((r = clk.begin(kPhGemm))) return r;
-    const cudaError_t e = bv::launch_gemm(g, grid, s);
+    cudaError_t e;
+    if (pair) {
+      const uint64_t tiles2 = static_cast<uint64_t>(rt1 - rt0) * ((nqt + 1u) / 2u);
+      const uint32_t max_pairs = static_cast<uint32_t>(idx->num_sms) / 2u;
+      e = bv::launch_gemm_pair(g, amap, bmap, static_cast<uint32_t>(tiles2 < max_pairs ? tiles2 : max_pairs), s);
+    } else {
+      e = bv::launch_gemm(g, grid, s);
+    }
     if (e != cudaSuccess) return cuda_fail(idx, e, "batch gemm");
     if ((r = clk.end())) return r;
     ++launches;
@@ -1644,6 +1691,100 @@ int bv_last_batch_profile(bv_index* idx, bv_batch_profile* out) {
   if (!idx || !out) return fail(BV_ERR_INVALID, "null argument");
   *out = batch_state(idx)->prof;
   return BV_OK;
+}
+
+int bv_search_rows(bv_index* idx, const bv_search_args* a, const uint32_t* offsets, const uint32_t* cand_rows,
+                   void* stream) {
+  uint32_t F = 0;
+  int rc = check_args(idx, a, &F);
+  if (rc) return rc;
+  if (idx->bits == 0) return fail(BV_ERR_UNSUPPORTED, "the candidate-list search scans quantized codes (bits 1, 4, 8)");
+  if (a->mask) return fail(BV_ERR_UNSUPPORTED, "the candidate-list search takes no score mask");
+  const uint32_t nq = a->nq;
+  if (nq && !offsets) return fail(BV_ERR_INVALID, "offsets is null");
+  uint32_t max_n = 0;
+  for (uint32_t q = 0; q < nq; ++q) {
+    if (offsets[q + 1] < offsets[q]) return fail(BV_ERR_INVALID, "offsets decrease at query %u", q);
+    max_n = std::max(max_n, offsets[q + 1] - offsets[q]);
+  }
+  const uint64_t total = nq ? static_cast<uint64_t>(offsets[nq]) - offsets[0] : 0;
+  if (total && !cand_rows) return fail(BV_ERR_INVALID, "cand_rows is null");
+  BV_CUDA(idx, cudaSetDevice(idx->device), "cudaSetDevice");
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : idx->stream;
+  // Per query a segment of whole scan tiles (the scan reads whole tiles and
+  // ignores the rows past its count), starting on a tile boundary.
+  Plan pl0;
+  const uint64_t saved_rows = idx->rows;
+  idx->rows = 1;
+  rc = plan_scan(idx, F, &pl0, true, false);
+  idx->rows = saved_rows;
+  if (rc) return rc;
+  const uint32_t tr = pl0.tile_rows;
+  std::vector<uint32_t> host(2 * static_cast<size_t>(nq) + 1);
+  uint64_t seg = 0;
+  for (uint32_t q = 0; q < nq; ++q) {
+    host[nq + 1 + q] = static_cast<uint32_t>(seg);
+    seg += (static_cast<uint64_t>(offsets[q + 1] - offsets[q]) + tr - 1) / tr * tr;
+  }
+  if (seg >= 0xFFFFFFFFull) return fail(BV_ERR_UNSUPPORTED, "candidate lists too long for one call");
+  for (uint32_t q = 0; q <= nq; ++q) host[q] = offsets[q];
+  if ((rc = grow(idx, &idx->d_gcodes, &idx->gcodes_cap, (seg + tr) * idx->R, "candidate codes"))) return rc;
+  if ((rc = grow(idx, &idx->d_gscales, &idx->gscales_cap, seg + tr, "candidate scales"))) return rc;
+  if ((rc = grow(idx, &idx->d_growmap, &idx->growmap_cap, seg + tr, "candidate rows"))) return rc;
+  if ((rc = grow(idx, &idx->d_goffs, &idx->goffs_cap, host.size() + 1, "candidate offsets"))) return rc;
+  uint32_t* bad = idx->d_err + 1;  // the gather's out-of-range flag
+  BV_CUDA(idx, cudaMemcpyAsync(idx->d_goffs, host.data(), host.size() * 4, cudaMemcpyHostToDevice, s), "H2D");
+  BV_CUDA(idx, cudaMemsetAsync(bad, 0, 4, s), "flag");
+  cudaError_t e = bv::launch_gather_rows(idx->d_codes, idx->d_scales, idx->R, idx->rows, cand_rows, idx->d_goffs,
+                                         idx->d_goffs + nq + 1, nq, max_n, idx->d_gcodes, idx->d_gscales,
+                                         idx->d_growmap, bad, s);
+  if (e != cudaSuccess) return cuda_fail(idx, e, "candidate gather");
+  // each query scans its segment as if it were the whole index
+  uint8_t* const codes0 = idx->d_codes;
+  float* const scales0 = idx->d_scales;
+  const uint64_t rows0 = idx->rows;
+  const bool cand = a->cand_rows && a->cand_scores && a->cand_counts;
+  uint32_t launches = 0;
+  for (uint32_t q = 0; q < nq && rc == BV_OK; ++q) {
+    const uint32_t n = offsets[q + 1] - offsets[q];
+    if (n == 0) {
+      BV_CUDA(idx, cudaMemsetAsync(a->out_counts + q, 0, 4, s), "memset");
+      if (cand) BV_CUDA(idx, cudaMemsetAsync(a->cand_counts + q, 0, 4, s), "memset");
+      continue;
+    }
+    const uint32_t s0 = host[nq + 1 + q];
+    idx->d_codes = idx->d_gcodes + static_cast<size_t>(s0) * idx->R;
+    idx->d_scales = idx->d_gscales + s0;
+    idx->rows = n;
+    idx->rowmap = idx->d_growmap + s0;
+    bv_search_args sub = *a;
+    sub.queries = a->queries + static_cast<size_t>(q) * idx->dim;
+    sub.nq = 1;
+    sub.out_rows = a->out_rows + static_cast<size_t>(q) * a->k;
+    sub.out_scores = a->out_scores + static_cast<size_t>(q) * a->k;
+    sub.out_counts = a->out_counts + q;
+    sub.cand_rows = cand ? a->cand_rows + static_cast<size_t>(q) * F : nullptr;
+    sub.cand_scores = cand ? a->cand_scores + static_cast<size_t>(q) * F : nullptr;
+    sub.cand_counts = cand ? a->cand_counts + q : nullptr;
+    sub.cand_exact = cand && a->cand_exact ? a->cand_exact + static_cast<size_t>(q) * F : nullptr;
+    rc = enqueue_search(idx, &sub, F, s, false);
+    launches += idx->last_launches;
+  }
+  idx->d_codes = codes0;
+  idx->d_scales = scales0;
+  idx->rows = rows0;
+  idx->rowmap = nullptr;
+  if (rc) return rc;
+  idx->last_launches = launches + 1;
+  uint32_t flags[2] = {0, 0};
+  BV_CUDA(idx, cudaStreamSynchronize(s), "candidate search");
+  BV_CUDA(idx, cudaMemcpy(flags, idx->d_err, 8, cudaMemcpyDeviceToHost), "error flag");
+  if (flags[1]) {
+    BV_CUDA(idx, cudaMemset(bad, 0, 4), "flag");
+    return fail(BV_ERR_INVALID, "a candidate row is outside the index (%llu rows)",
+                static_cast<unsigned long long>(idx->rows));
+  }
+  return report_err_flag(idx, flags[0]);
 }
 
 int bv_check_wait_timeout(bv_index* idx, uint32_t polls) {

@@ -10,6 +10,8 @@
 //                  threshold filter, candidate append)
 //   select_kernel  per query: keep the best F candidates, sorted, and set the
 //                  threshold for the next round
+#include <cuda.h>
+
 #include <climits>
 #include <cstdint>
 
@@ -142,18 +144,102 @@ constexpr uint32_t kTmemCols = 2 * kBRowTile;  // two accumulator buffers
 
 constexpr uint32_t kSlotWords = 36;  // per epilogue thread: 32 accumulators, padded for STS.128
 
+// The CTA-pair GEMM (cta_group::2): each CTA of a cluster of two holds 128
+// queries (A) and half of a row tile (B, 128 rows) per stage, and the pair's
+// MMA computes 256 queries x 256 rows; per CTA a stage is then 32 KB for the
+// same MMA time as the single CTA's 48 KB, so the operands need two thirds of
+// the shared-memory fill bandwidth.
+#ifndef BV_PAIR_STAGES
+#define BV_PAIR_STAGES 4
+#endif
+constexpr int kPairStages = BV_PAIR_STAGES;
+constexpr uint32_t kBHalfBytes = kBRowTileBytes / 2;
+constexpr uint32_t kPairStageBytes = kBQTileBytes + kBHalfBytes;
+// Instruction descriptor of the pair: M = 256 (both CTAs' queries), N = 256.
+constexpr uint32_t kIdescI8Pair = (2u << 4) | (1u << 7) | (1u << 10) | ((kBRowTile >> 3) << 17) |
+                                  ((2u * kBQTile >> 4) << 24);
+
 struct GemmSmem {
   uint32_t slots_off, rowfac_off, rowid_off, bars_off, total;
 };
-__host__ __device__ inline GemmSmem gemm_smem_layout() {
+__host__ __device__ inline GemmSmem gemm_smem_layout(bool pair = false) {
   GemmSmem s;
-  s.slots_off = kGemmStages * kStageBytes;
+  const int stages = pair ? kPairStages : kGemmStages;
+  s.slots_off = stages * (pair ? kPairStageBytes : kStageBytes);
   s.rowfac_off = s.slots_off + kEpiWarps * 32 * kSlotWords * 4;  // per epilogue warp: the tile's factors
   s.rowid_off = s.rowfac_off + kEpiWarps * kBRowTile * 4;        // ... and the tile's rows
   s.bars_off = s.rowid_off + kEpiWarps * kBRowTile * 4;
   // full[S], empty[S], tfull[2], tempty[2], done, then the TMEM address word
-  s.total = s.bars_off + (2 * kGemmStages + 5) * 8 + 16;
+  s.total = s.bars_off + (2 * stages + 5) * 8 + 16;
   return s;
+}
+
+// ------------------------------------------------------------- clusters
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_count() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+// The shared::cluster address of this CTA's `p` in the cluster's CTA `rank`.
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+  uint32_t a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_addr(p)), "r"(rank));
+  return a;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Arrive on an mbarrier of another CTA of the cluster (shared::cluster address).
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+// 2-D tiled tensor load for a CTA pair: the box lands in this CTA's shared
+// memory and its bytes complete on `cluster_bar` (the pair leader's barrier).
+// No multicast: every CTA loads only its own operand halves.
+__device__ __forceinline__ void tma_load_pair(void* dst, const CUtensorMap* map, uint32_t x, uint32_t y,
+                                              uint32_t cluster_bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(cluster_bar)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// D[tmem of both CTAs] (+)= A[both CTAs' smem] x B[both CTAs' smem]^T.
+__device__ __forceinline__ void mma_i8_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+// Arrive on `bar` in every CTA of `mask` once the pair's MMAs issued so far complete.
+__device__ __forceinline__ void mma_commit_pair_mc(uint64_t* bar, uint16_t mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_addr(bar)),
+      "h"(mask)
+      : "memory");
 }
 
 }  // namespace
@@ -308,6 +394,135 @@ __global__ void __launch_bounds__(kConsumerThreads, 1) prep_kernel(const PrepPar
 }
 
 // ------------------------------------------------------------- gemm
+// Epilogue warps of one CTA.  Group g drains accumulator buffer g for this
+// CTA's tiles tc = g, g + 2, ... of the tile sequence t = first, first +
+// stride, ...; tile t covers row tile rt0 + t / nqt and query tile t % nqt
+// (kPair: query tile 2 * (t % nqt) + rank, this CTA's half of the pair's 256
+// queries, and the buffer is released on the pair leader's barrier).
+template <bool kPair>
+__device__ __forceinline__ void gemm_epilogue(const GemmParams& p, uint8_t* smem, const GemmSmem& lay,
+                                              uint64_t* tfull, uint64_t* tempty, uint32_t tmem, uint32_t first,
+                                              uint32_t stride, uint32_t ntiles, uint32_t nqt, uint32_t rank,
+                                              int warp, int lane) {
+  // ------------------------------------------------------ epilogue
+  const uint32_t grp = static_cast<uint32_t>(warp) / 4u;
+  const uint32_t lane_base = static_cast<uint32_t>(warp % 4) * 32u;
+  float* rf_s = reinterpret_cast<float*>(smem + lay.rowfac_off) + warp * kBRowTile;
+  uint32_t* rid_s = reinterpret_cast<uint32_t*>(smem + lay.rowid_off) + warp * kBRowTile;
+  // this CTA's tiles in order are tc = 0, 1, 2, ...; group g takes tc = g mod groups
+  uint32_t tc = grp;
+  for (uint32_t t = first + grp * stride; t < ntiles; t += kEpiGroups * stride, tc += kEpiGroups) {
+    const uint32_t rt = p.rt0 + t / nqt, qt = kPair ? 2u * (t % nqt) + rank : t % nqt;
+    const uint32_t buf = tc & 1u, use = tc >> 1;
+    const uint32_t qi = qt * kBQTile + lane_base + static_cast<uint32_t>(lane);
+    const bool qvalid = qi < p.nq;
+    // the tile's inputs are loaded before the accumulator wait, so their
+    // latency hides behind the MMA
+    const uint64_t thr = qvalid ? p.thr[qi] : 0ull;
+    const float qf = qvalid ? p.qfac[qi] : 0.0f;
+    const float tm = p.tmax[rt];
+    float rf[kBRowTile / 32];
+    uint32_t rid[kBRowTile / 32];
+#pragma unroll
+    for (int i = 0; i < static_cast<int>(kBRowTile / 32); ++i) {
+      const uint32_t pos = rt * kBRowTile + static_cast<uint32_t>(lane + 32 * i);
+      rf[i] = pos < p.npos ? p.posfac[pos] : 0.0f;
+      rid[i] = pos < p.npos ? p.posrow[pos] : 0u;
+    }
+    const bool ready = mbar_wait_bounded(&tfull[buf], use & 1u, p.err);
+    if (!__all_sync(0xffffffffu, ready)) break;  // tcgen05.ld below is warp-collective
+    tc_fence_after();
+#pragma unroll
+    for (int i = 0; i < static_cast<int>(kBRowTile / 32); ++i) {
+      rf_s[lane + 32 * i] = rf[i];
+      rid_s[lane + 32 * i] = rid[i];
+    }
+    __syncwarp();
+    int bound = INT_MIN;
+    if (qvalid && thr != 0ull) {
+      const float ts = key_score(thr);
+      const float den = __fmul_rn(tm, qf);
+      if (ts > 0.0f && den > 0.0f) {
+        // score = ((f32(idot) * rowfac) * qfac) >= ts needs idot >= ts / (tmax * qfac)
+        // up to five f32 roundings (three in the score, two here): a 2^-16
+        // margin keeps the bound below every idot that can pass
+        const float b = floorf(__fmul_rn(__fdiv_rn(ts, den), 1.0f - 0x1p-16f));
+        bound = b >= 2147483520.0f ? INT_MAX : static_cast<int>(b);
+      }
+    }
+    uint64_t* cq = p.cand + static_cast<size_t>(qvalid ? qi : 0) * p.cap;
+    uint32_t* slot = reinterpret_cast<uint32_t*>(smem + lay.slots_off) + threadIdx.x * kSlotWords;
+    // Columns [c0, c0 + 32) of this lane's accumulator row, in registers:
+    // prefilter, then exact scores of the hits only.
+    auto chunk = [&](const uint32_t (&v)[32], uint32_t c0) {
+      // the common case is a chunk with no hit: one 3-input max tree decides it
+      int mx[11];
+#pragma unroll
+      for (int i = 0; i < 10; ++i)
+        mx[i] = __vimax3_s32(static_cast<int>(v[3 * i]), static_cast<int>(v[3 * i + 1]), static_cast<int>(v[3 * i + 2]));
+      mx[10] = max(static_cast<int>(v[30]), static_cast<int>(v[31]));
+      const int top = __vimax3_s32(__vimax3_s32(mx[0], mx[1], mx[2]), __vimax3_s32(mx[3], mx[4], mx[5]),
+                                   __vimax3_s32(__vimax3_s32(mx[6], mx[7], mx[8]), mx[9], mx[10]));
+      if (!qvalid || top < bound) return;
+      const uint32_t pbase = rt * kBRowTile + c0;
+      const uint32_t valid =
+          pbase >= p.npos ? 0u : (p.npos - pbase >= 32u ? 0xFFFFFFFFu : ((1u << (p.npos - pbase)) - 1u));
+      uint32_t m = 0;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) m |= (static_cast<int>(v[j]) >= bound ? 1u : 0u) << j;
+      m &= valid;
+      if (m) {
+        // this lane's 32 accumulators go to its own shared-memory slot, and
+        // only the columns that passed the prefilter are scored exactly
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          reinterpret_cast<uint4*>(slot)[i] = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        uint32_t pass = 0;
+        for (uint32_t mm = m; mm; mm &= mm - 1u) {
+          const uint32_t j = __ffs(mm) - 1u;
+          const uint32_t row = rid_s[c0 + j];
+          if (p.mask && !((p.mask[row >> 5] >> (row & 31u)) & 1u)) continue;
+          const float sc = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(slot[j])), rf_s[c0 + j]), qf);
+          if (make_key(sc, row) > thr) pass |= 1u << j;
+        }
+        if (pass) {
+          const uint32_t n = __popc(pass);
+          const uint32_t base = atomicAdd(p.cnt + qi, n);
+          if (base + n > p.cap) atomicOr(p.overflow, 1u);
+          uint32_t w = base;
+          for (uint32_t mm = pass; mm; mm &= mm - 1u, ++w) {
+            const uint32_t j = __ffs(mm) - 1u;
+            const uint32_t row = rid_s[c0 + j];
+            const float sc = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(slot[j])), rf_s[c0 + j]), qf);
+            if (w < p.cap) cq[w] = make_key(sc, row);
+          }
+        }
+      }
+    };
+    // 128 columns per TMEM load: tcgen05.wait::ld waits for every load in
+    // flight, so a few wide loads expose its latency fewer times than many
+    // narrow ones
+    const uint32_t taddr = tmem + (lane_base << 16) + buf * kBRowTile;
+#pragma unroll 1
+    for (uint32_t h = 0; h < kBRowTile; h += 128) {
+      uint32_t v[128];
+      tmem_ld128(taddr + h, v);
+      tmem_ld_wait_regs128(v);
+#pragma unroll
+      for (uint32_t i = 0; i < 4; ++i) {
+        chunk(*reinterpret_cast<const uint32_t(*)[32]>(&v[32 * i]), h + 32 * i);
+        __syncwarp();
+      }
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) {
+      if constexpr (kPair) mbar_arrive_remote(cluster_addr(&tempty[buf], 0));  // the pair leader's barrier
+      else mbar_arrive(&tempty[buf]);
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte aligned base for the swizzled operand tiles
@@ -400,126 +615,127 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const GemmParams 
       mbar_wait_bounded(done, 0, p.err);
     }
   } else {
-    // ------------------------------------------------------ epilogue
-    const uint32_t grp = static_cast<uint32_t>(warp) / 4u;
-    const uint32_t lane_base = static_cast<uint32_t>(warp % 4) * 32u;
-    float* rf_s = reinterpret_cast<float*>(smem + lay.rowfac_off) + warp * kBRowTile;
-    uint32_t* rid_s = reinterpret_cast<uint32_t*>(smem + lay.rowid_off) + warp * kBRowTile;
-    // this CTA's tiles in order are tc = 0, 1, 2, ...; group g takes tc = g mod groups
-    uint32_t tc = grp;
-    for (uint32_t t = blockIdx.x + grp * gridDim.x; t < ntiles; t += kEpiGroups * gridDim.x, tc += kEpiGroups) {
-      const uint32_t rt = p.rt0 + t / p.nqt, qt = t % p.nqt;
-      const uint32_t buf = tc & 1u, use = tc >> 1;
-      const uint32_t qi = qt * kBQTile + lane_base + static_cast<uint32_t>(lane);
-      const bool qvalid = qi < p.nq;
-      // the tile's inputs are loaded before the accumulator wait, so their
-      // latency hides behind the MMA
-      const uint64_t thr = qvalid ? p.thr[qi] : 0ull;
-      const float qf = qvalid ? p.qfac[qi] : 0.0f;
-      const float tm = p.tmax[rt];
-      float rf[kBRowTile / 32];
-      uint32_t rid[kBRowTile / 32];
-#pragma unroll
-      for (int i = 0; i < static_cast<int>(kBRowTile / 32); ++i) {
-        const uint32_t pos = rt * kBRowTile + static_cast<uint32_t>(lane + 32 * i);
-        rf[i] = pos < p.npos ? p.posfac[pos] : 0.0f;
-        rid[i] = pos < p.npos ? p.posrow[pos] : 0u;
-      }
-      const bool ready = mbar_wait_bounded(&tfull[buf], use & 1u, p.err);
-      if (!__all_sync(0xffffffffu, ready)) break;  // tcgen05.ld below is warp-collective
-      tc_fence_after();
-#pragma unroll
-      for (int i = 0; i < static_cast<int>(kBRowTile / 32); ++i) {
-        rf_s[lane + 32 * i] = rf[i];
-        rid_s[lane + 32 * i] = rid[i];
-      }
-      __syncwarp();
-      int bound = INT_MIN;
-      if (qvalid && thr != 0ull) {
-        const float ts = key_score(thr);
-        const float den = __fmul_rn(tm, qf);
-        if (ts > 0.0f && den > 0.0f) {
-          // score = ((f32(idot) * rowfac) * qfac) >= ts needs idot >= ts / (tmax * qfac)
-          // up to five f32 roundings (three in the score, two here): a 2^-16
-          // margin keeps the bound below every idot that can pass
-          const float b = floorf(__fmul_rn(__fdiv_rn(ts, den), 1.0f - 0x1p-16f));
-          bound = b >= 2147483520.0f ? INT_MAX : static_cast<int>(b);
-        }
-      }
-      uint64_t* cq = p.cand + static_cast<size_t>(qvalid ? qi : 0) * p.cap;
-      uint32_t* slot = reinterpret_cast<uint32_t*>(smem + lay.slots_off) + threadIdx.x * kSlotWords;
-      // Columns [c0, c0 + 32) of this lane's accumulator row, in registers:
-      // prefilter, then exact scores of the hits only.
-      auto chunk = [&](const uint32_t (&v)[32], uint32_t c0) {
-        // the common case is a chunk with no hit: one 3-input max tree decides it
-        int mx[11];
-#pragma unroll
-        for (int i = 0; i < 10; ++i)
-          mx[i] = __vimax3_s32(static_cast<int>(v[3 * i]), static_cast<int>(v[3 * i + 1]), static_cast<int>(v[3 * i + 2]));
-        mx[10] = max(static_cast<int>(v[30]), static_cast<int>(v[31]));
-        const int top = __vimax3_s32(__vimax3_s32(mx[0], mx[1], mx[2]), __vimax3_s32(mx[3], mx[4], mx[5]),
-                                     __vimax3_s32(__vimax3_s32(mx[6], mx[7], mx[8]), mx[9], mx[10]));
-        if (!qvalid || top < bound) return;
-        const uint32_t pbase = rt * kBRowTile + c0;
-        const uint32_t valid =
-            pbase >= p.npos ? 0u : (p.npos - pbase >= 32u ? 0xFFFFFFFFu : ((1u << (p.npos - pbase)) - 1u));
-        uint32_t m = 0;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) m |= (static_cast<int>(v[j]) >= bound ? 1u : 0u) << j;
-        m &= valid;
-        if (m) {
-          // this lane's 32 accumulators go to its own shared-memory slot, and
-          // only the columns that passed the prefilter are scored exactly
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-            reinterpret_cast<uint4*>(slot)[i] = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-          uint32_t pass = 0;
-          for (uint32_t mm = m; mm; mm &= mm - 1u) {
-            const uint32_t j = __ffs(mm) - 1u;
-            const uint32_t row = rid_s[c0 + j];
-            if (p.mask && !((p.mask[row >> 5] >> (row & 31u)) & 1u)) continue;
-            const float sc = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(slot[j])), rf_s[c0 + j]), qf);
-            if (make_key(sc, row) > thr) pass |= 1u << j;
-          }
-          if (pass) {
-            const uint32_t n = __popc(pass);
-            const uint32_t base = atomicAdd(p.cnt + qi, n);
-            if (base + n > p.cap) atomicOr(p.overflow, 1u);
-            uint32_t w = base;
-            for (uint32_t mm = pass; mm; mm &= mm - 1u, ++w) {
-              const uint32_t j = __ffs(mm) - 1u;
-              const uint32_t row = rid_s[c0 + j];
-              const float sc = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(slot[j])), rf_s[c0 + j]), qf);
-              if (w < p.cap) cq[w] = make_key(sc, row);
-            }
-          }
-        }
-      };
-      // 128 columns per TMEM load: tcgen05.wait::ld waits for every load in
-      // flight, so a few wide loads expose its latency fewer times than many
-      // narrow ones
-      const uint32_t taddr = tmem + (lane_base << 16) + buf * kBRowTile;
-#pragma unroll 1
-      for (uint32_t h = 0; h < kBRowTile; h += 128) {
-        uint32_t v[128];
-        tmem_ld128(taddr + h, v);
-        tmem_ld_wait_regs128(v);
-#pragma unroll
-        for (uint32_t i = 0; i < 4; ++i) {
-          chunk(*reinterpret_cast<const uint32_t(*)[32]>(&v[32 * i]), h + 32 * i);
-          __syncwarp();
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[buf]);
-    }
+    gemm_epilogue<false>(p, smem, lay, tfull, tempty, tmem, blockIdx.x, gridDim.x, ntiles, p.nqt, 0u, warp, lane);
   }
   tc_fence_before();
   __syncthreads();
   if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+
+// The CTA-pair GEMM (cluster of two, tcgen05.mma.cta_group::2, M = 256
+// queries x N = 256 rows x K = 32 per instruction).  Both CTAs run the same
+// tile sequence.  Each CTA's producer loads its 128 queries and its 128 of the
+// row tile's 256 rows by TMA tensor copies (no multicast) whose bytes complete
+// on the leader's (rank 0) full barrier; the leader's MMA thread issues the
+// pair's MMAs and multicasts its commits to both CTAs' empty / tfull barriers;
+// each CTA's epilogue drains its own TMEM (its 128 queries x 256 rows) and
+// frees the buffer on the leader's tempty barrier.  Every wait is bounded.
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ GemmParams p, const __grid_constant__ CUtensorMap amap,
+                     const __grid_constant__ CUtensorMap bmap) {
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte aligned base (the same offset in both CTAs: the MMA reads the
+  // peer's operands at this CTA's addresses)
+  const uint32_t raw = smem_addr(smem_raw);
+  uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  const GemmSmem lay = gemm_smem_layout(true);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + lay.bars_off);
+  uint64_t* empty = full + kPairStages;
+  uint64_t* tfull = empty + kPairStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* done = tempty + 2;
+  uint32_t* tmem_word = reinterpret_cast<uint32_t*>(done + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank(), pair = cluster_id(), npairs = cluster_count();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(&full[s], 1);   // the leader's expect_tx; both CTAs' bytes complete it
+      mbar_init(&empty[s], 1);  // the leader's commit
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 8);  // the four warps draining buffer b, in each CTA
+    }
+    mbar_init(done, 1);
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc_pair(tmem_word, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers and TMEM of both CTAs are ready before any copy or remote arrive
+  tc_fence_after();
+  const uint32_t tmem = *tmem_word;
+  const uint32_t nqt2 = (p.nqt + 1u) / 2u;
+  const uint32_t ntiles = (p.rt1 - p.rt0) * nqt2;
+  const uint32_t KB = p.KB;
+
+  if (warp == kProdWarp) {
+    if (lane == 0) {
+      const uint32_t lead_full = cluster_addr(&full[0], 0);  // full[s] of the leader: + 8 s
+      uint32_t it = 0;
+      bool ok = true;
+      for (uint32_t t = pair; t < ntiles && ok; t += npairs) {
+        const uint32_t rt = p.rt0 + t / nqt2, qt = 2u * (t % nqt2) + rank;
+        for (uint32_t kb = 0; kb < KB; ++kb, ++it) {
+          const uint32_t s = it % kPairStages, ph = (it / kPairStages) & 1u;
+          if (it >= kPairStages && !mbar_wait_bounded(&empty[s], ph ^ 1u, p.err)) {
+            ok = false;
+            break;
+          }
+          uint8_t* a = smem + s * kPairStageBytes;
+          uint8_t* b = a + kBQTileBytes;
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2u * kPairStageBytes);
+          const uint32_t fb = lead_full + 8u * s;
+          tma_load_pair(a, &amap, 0u, (qt * KB + kb) * kBQTile, fb);
+          tma_load_pair(b, &bmap, 0u, (rt * KB + kb) * kBRowTile + rank * (kBRowTile / 2u), fb);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == kMmaWarp) {
+    if (rank == 0 && lane == 0) {
+      uint32_t it = 0, tc = 0;
+      bool ok = true;
+      for (uint32_t t = pair; t < ntiles && ok; t += npairs, ++tc) {
+        const uint32_t buf = tc & 1u, use = tc >> 1;
+        if (use > 0 && !mbar_wait_bounded(&tempty[buf], (use - 1u) & 1u, p.err)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + buf * kBRowTile;
+        for (uint32_t kb = 0; kb < KB; ++kb, ++it) {
+          const uint32_t s = it % kPairStages, ph = (it / kPairStages) & 1u;
+          if (!mbar_wait_bounded(&full[s], ph, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = smem_addr(smem + s * kPairStageBytes);
+          const uint64_t ad = sw128_desc(a), bd = sw128_desc(a + kBQTileBytes);
+#pragma unroll
+          for (uint32_t j = 0; j < kKBlock / 32; ++j)  // K = 32 bytes per instruction
+            mma_i8_pair(d, ad + 2u * j, bd + 2u * j, kIdescI8Pair, (kb | j) != 0u ? 1u : 0u);
+          mma_commit_pair_mc(&empty[s], 0x3);  // both CTAs' stage s is free once these MMAs have read it
+        }
+        if (ok) mma_commit_pair_mc(&tfull[buf], 0x3);
+      }
+      // every MMA issued has completed before either CTA's TMEM or stages go
+      mma_commit_pair_mc(done, 0x1);
+      mbar_wait_bounded(done, 0, p.err);
+    }
+  } else {
+    gemm_epilogue<true>(p, smem, lay, tfull, tempty, tmem, pair, npairs, ntiles, nqt2, rank, warp, lane);
+  }
+  tc_fence_before();
+  cluster_sync_all();  // the pair's MMAs are complete and both epilogues have drained their TMEM
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, kTmemCols);
   }
 }
 
@@ -816,6 +1032,33 @@ cudaError_t launch_gemm(const GemmParams& p, uint32_t grid, cudaStream_t s) {
   if (e != cudaSuccess) return e;
   gemm_kernel<<<grid, kGemmThreads, smem, s>>>(p);
   return cudaGetLastError();
+}
+
+uint32_t batch_gemm_pair_smem() { return gemm_smem_layout(true).total + 1024; }
+
+// The pair GEMM over `npairs` clusters of two CTAs; amap / bmap: tensor maps
+// (encode_tile_rows_map) of the query tiles (128-row boxes) and the row tiles
+// (128-row boxes, half a tile).
+cudaError_t launch_gemm_pair(const GemmParams& p, const void* amap, const void* bmap, uint32_t npairs,
+                             cudaStream_t s) {
+  const size_t smem = batch_gemm_pair_smem();
+  static int opted[kMaxDevices] = {};
+  cudaError_t e = opt_in_smem(reinterpret_cast<const void*>(gemm_pair_kernel), smem, opted);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2u * npairs);
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemm_pair_kernel, p, *static_cast<const CUtensorMap*>(amap),
+                            *static_cast<const CUtensorMap*>(bmap));
 }
 
 cudaError_t launch_select(const SelectParams& p, cudaStream_t s) {

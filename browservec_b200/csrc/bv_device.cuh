@@ -34,6 +34,12 @@ __device__ __forceinline__ float key_score(uint64_t key) {
   u = (u & 0x80000000u) ? (u & 0x7fffffffu) : ~u;
   return __uint_as_float(u);
 }
+// Row of a key's position: a candidate-list search scores gathered rows, and
+// its keys carry the position in the list (rowmap maps it back); else the
+// position is the row.
+__device__ __forceinline__ uint32_t map_row(const uint32_t* rowmap, uint32_t pos) {
+  return rowmap ? __ldg(rowmap + pos) : pos;
+}
 __device__ __forceinline__ uint32_t key_row(uint64_t key) {
   return ~static_cast<uint32_t>(key);
 }

@@ -270,6 +270,22 @@ bool flat_scan_supported(const float* rows, uint32_t dim) {
 uint32_t flat_scan_block_rows() { return kFsRows; }
 uint32_t flat_scan_stage_bytes() { return kFsStageBytes; }
 
+// A tensor map over an array of 128-byte rows (the batched search's MMA
+// tiles, already in their shared-memory image): boxes of box_rows whole
+// rows, copied byte for byte (no swizzle: the tiles are pre-swizzled).
+cudaError_t encode_tile_rows_map(void* map128, const void* base, uint64_t nrows, uint32_t box_rows) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc) return cudaErrorNotSupported;
+  const cuuint64_t dims[2] = {128, nrows};
+  const cuuint64_t strides[1] = {128};
+  const cuuint32_t box[2] = {128, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(static_cast<CUtensorMap*>(map128), CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base),
+                         dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 cudaError_t encode_flat_rows_map(void* map128, const float* rows, uint32_t dim, uint64_t nrows) {
   static_assert(sizeof(CUtensorMap) == 128, "tensor map size");
   PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();

@@ -102,6 +102,7 @@ bool flat_scan_supported(const float* rows, uint32_t dim);
 uint32_t flat_scan_block_rows();
 uint32_t flat_scan_stage_bytes();
 cudaError_t encode_flat_rows_map(void* map128, const float* rows, uint32_t dim, uint64_t nrows);
+cudaError_t encode_tile_rows_map(void* map128, const void* base, uint64_t nrows, uint32_t box_rows);
 cudaError_t launch_flat_scan(const void* map128, const ScanParams& p, uint32_t nblocks, uint32_t nks,
                              uint32_t check_blocks, unsigned grid, size_t smem, cudaStream_t stream);
 uint32_t flat_rows_per_cta();
@@ -121,6 +122,9 @@ uint32_t batch_gemm_smem();
 cudaError_t launch_expand(const ExpandParams& p, cudaStream_t s);
 cudaError_t launch_prep(const PrepParams& p, cudaStream_t s);
 cudaError_t launch_gemm(const GemmParams& p, uint32_t grid, cudaStream_t s);
+uint32_t batch_gemm_pair_smem();
+cudaError_t launch_gemm_pair(const GemmParams& p, const void* amap, const void* bmap, uint32_t npairs,
+                             cudaStream_t s);
 cudaError_t launch_select(const SelectParams& p, cudaStream_t s);
 cudaError_t launch_export_keys(const uint64_t* cand, uint32_t cap, const uint32_t* cnt, uint32_t nq, uint32_t F,
                                uint32_t base, uint64_t* keys, cudaStream_t s);
@@ -148,6 +152,10 @@ cudaError_t launch_filter(const bv_column* cols, uint32_t ncols, const bv_filter
 size_t merge_smem_bytes(uint32_t world, uint32_t F);
 uint32_t merge_max_world();
 cudaError_t launch_wait_probe(uint32_t* err, uint32_t polls, cudaStream_t s);
+cudaError_t launch_gather_rows(const uint8_t* codes, const float* scales, uint32_t R, uint64_t rows,
+                               const uint32_t* cand, const uint32_t* offs, const uint32_t* seg, uint32_t nq,
+                               uint32_t max_n, uint8_t* gcodes, float* gscales, uint32_t* growmap,
+                               uint32_t* bad_row, cudaStream_t s);
 cudaError_t launch_merge_topk(const uint32_t* gathered, uint32_t world, uint32_t nq, uint32_t k,
                               uint32_t* out_rows, float* out_scores, uint32_t* out_counts, cudaStream_t stream);
 cudaError_t launch_merge_shards(const uint32_t* gathered, uint32_t world, uint32_t nq, uint32_t F, uint32_t k,

@@ -80,6 +80,7 @@ struct ScanParams {
   float* cand_exact;
   uint32_t* err;             // error flags
   uint64_t* trace;           // optional: per-CTA phase timestamps (globaltimer ns)
+  const uint32_t* rowmap;    // optional: row of each scanned position (candidate-list search)
 };
 
 // Next tile of this launch from the shared counter.  The slot still holds an
@@ -894,7 +895,7 @@ static __device__ __noinline__ void finish_query(const ScanParams& p, uint64_t* 
   const uint32_t nc = misc[kMiscNc];
   if (p.cand_rows) {
     for (uint32_t i = ctid; i < nc; i += kConsumerThreads) {
-      p.cand_rows[i] = key_row(cand[i]) + p.row_base;
+      p.cand_rows[i] = map_row(p.rowmap, key_row(cand[i])) + p.row_base;
       p.cand_scores[i] = key_score(cand[i]);
     }
     if (ctid == 0) *p.cand_count = nc;
@@ -927,7 +928,8 @@ static __device__ __noinline__ void finish_query(const ScanParams& p, uint64_t* 
           __syncwarp();
           for (uint32_t r = lane; r < nb; r += 32)
             bulk_g2s(rows_s + static_cast<size_t>(r) * p.dim,
-                     p.originals + static_cast<size_t>(key_row(cand[c0 + r])) * p.dim, p.dim * 4u, bar);
+                     p.originals + static_cast<size_t>(map_row(p.rowmap, key_row(cand[c0 + r]))) * p.dim,
+                     p.dim * 4u, bar);
         }
         mbar_wait_bounded(bar, parity, p.err);
         if (tr && c0 == 0) tr[3] = globaltimer();
@@ -937,11 +939,11 @@ static __device__ __noinline__ void finish_query(const ScanParams& p, uint64_t* 
         const uint32_t r2 = r + kConsumerWarps;
         const uint32_t row = key_row(cand[c0 + r]);
         const float* xa = staged ? rows_s + static_cast<size_t>(r) * p.dim
-                                 : p.originals + static_cast<size_t>(row) * p.dim;
+                                 : p.originals + static_cast<size_t>(map_row(p.rowmap, row)) * p.dim;
         if (r2 < nb) {
           const uint32_t row2 = key_row(cand[c0 + r2]);
           const float* xb = staged ? rows_s + static_cast<size_t>(r2) * p.dim
-                                   : p.originals + static_cast<size_t>(row2) * p.dim;
+                                   : p.originals + static_cast<size_t>(map_row(p.rowmap, row2)) * p.dim;
           float sa, sb;
           if (staged) dot_rows2_exact_warp<false>(xa, xb, qx, p.dim, lane, sa, sb);
           else dot_rows2_exact_warp<true>(xa, xb, qx, p.dim, lane, sa, sb);
@@ -970,13 +972,13 @@ static __device__ __noinline__ void finish_query(const ScanParams& p, uint64_t* 
     if (warp == 0) {
       __syncwarp();
       for (uint32_t i = lane; i < n; i += 32) {
-        p.out_rows[i] = key_row(ex[i]) + p.row_base;
+        p.out_rows[i] = map_row(p.rowmap, key_row(ex[i])) + p.row_base;
         p.out_scores[i] = key_score(ex[i]);
       }
     }
   } else {
     for (uint32_t i = ctid; i < n; i += kConsumerThreads) {
-      p.out_rows[i] = key_row(cand[i]) + p.row_base;
+      p.out_rows[i] = map_row(p.rowmap, key_row(cand[i])) + p.row_base;
       p.out_scores[i] = key_score(cand[i]);
     }
   }

@@ -138,7 +138,7 @@ __global__ void __launch_bounds__(kConsumerThreads, MINB) tail_kernel(const Tail
   if (trace && ctid == 0) trace[kTrTailMerged] = globaltimer();
   if (cand_rows) {
     for (uint32_t i = ctid; i < nc; i += kConsumerThreads) {
-      cand_rows[i] = key_row(cand[i]) + p.row_base;
+      cand_rows[i] = map_row(p.rowmap, key_row(cand[i])) + p.row_base;
       cand_scores[i] = key_score(cand[i]);
     }
     if (ctid == 0) *cand_count = nc;
@@ -165,14 +165,15 @@ __global__ void __launch_bounds__(kConsumerThreads, MINB) tail_kernel(const Tail
           __syncwarp();
           for (uint32_t c = lane; c < nb; c += 32)
             bulk_g2s(rows_s + static_cast<size_t>(c) * stride,
-                     p.originals + static_cast<size_t>(key_row(cand[c0 + c])) * p.dim, p.dim * 4u, gbar);
+                     p.originals + static_cast<size_t>(map_row(p.rowmap, key_row(cand[c0 + c]))) * p.dim,
+                     p.dim * 4u, gbar);
         }
         mbar_wait_bounded(gbar, gph, p.err);
         gph ^= 1u;
         if (trace && ctid == 0) trace[kTrTailGathered] = globaltimer();
       } else {
         for (uint32_t c = 0; c < nb; ++c) {
-          const float* src = p.originals + static_cast<size_t>(key_row(cand[c0 + c])) * p.dim;
+          const float* src = p.originals + static_cast<size_t>(map_row(p.rowmap, key_row(cand[c0 + c]))) * p.dim;
           for (uint32_t i = ctid; i < p.dim; i += kConsumerThreads)
             rows_s[static_cast<size_t>(c) * stride + i] = src[i];
         }
@@ -236,20 +237,20 @@ __global__ void __launch_bounds__(kConsumerThreads, MINB) tail_kernel(const Tail
       if (warp == 0) {
         __syncwarp();
         for (uint32_t i = lane; i < n; i += 32) {
-          out_rows[i] = key_row(ex[i]) + p.row_base;
+          out_rows[i] = map_row(p.rowmap, key_row(ex[i])) + p.row_base;
           out_scores[i] = key_score(ex[i]);
         }
       }
     } else {
       cta_sort_desc(ex, p.Fp, ctid);
       for (uint32_t i = ctid; i < n; i += kConsumerThreads) {
-        out_rows[i] = key_row(ex[i]) + p.row_base;
+        out_rows[i] = map_row(p.rowmap, key_row(ex[i])) + p.row_base;
         out_scores[i] = key_score(ex[i]);
       }
     }
   } else {
     for (uint32_t i = ctid; i < n; i += kConsumerThreads) {
-      out_rows[i] = key_row(cand[i]) + p.row_base;
+      out_rows[i] = map_row(p.rowmap, key_row(cand[i])) + p.row_base;
       out_scores[i] = key_score(cand[i]);
     }
   }

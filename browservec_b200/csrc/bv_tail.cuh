@@ -26,6 +26,7 @@ struct TailParams {
   // grid of queries (batched search): CTA b serves query b, its partials at
   // partials + b * partials_stride; 0 for the one-CTA launch of a scan
   uint32_t partials_stride;
+  const uint32_t* rowmap;    // optional: row of each key position (candidate-list search)
 };
 
 // Tail timestamps (globaltimer ns) in the trace record given to the tail.

@@ -261,6 +261,51 @@ class AddonQuantIndex:
         return [[FlatHit(int(rows[i, j]), float(scores[i, j])) for j in range(int(counts[i]))]
                 for i in range(nq)]
 
+    def search_candidates(self, qs: np.ndarray, lists, k: int, fetch: int, rerank: bool = True,
+                          with_candidates: bool = False):
+        """The IVF x quant candidate-list scan (src/index/ivfquant.ts:468-490):
+        query i is scored against the rows lists[i] only (its probed lists'
+        rows).  Returns (rows, scores, counts[, cand_rows, cand_scores,
+        cand_counts]) numpy arrays, rows global."""
+        import torch
+
+        qs = np.ascontiguousarray(qs, dtype=np.float32).reshape(-1, self.dim)
+        nq = qs.shape[0]
+        F = max(fetch, k)
+        lists = [np.ascontiguousarray(x, dtype=np.uint32).reshape(-1) for x in lists]
+        if len(lists) != nq:
+            raise ValueError(f"{nq} queries but {len(lists)} candidate lists")
+        offs = np.zeros(nq + 1, np.uint32)
+        offs[1:] = np.cumsum([x.size for x in lists])
+        dev = torch.device("cuda", self.device)
+        if getattr(self, "_stream", None) is None:
+            self._stream = torch.cuda.Stream(device=dev)
+        st = self._stream
+        with torch.cuda.stream(st):
+            q = torch.from_numpy(qs).to(dev)
+            flat = np.concatenate(lists) if int(offs[-1]) else np.zeros(1, np.uint32)
+            cand = torch.from_numpy(flat.view(np.int32)).to(dev)
+            out = torch.empty(nq * (2 * k + 1) + (nq * (2 * F + 1) if with_candidates else 0), dtype=torch.int32,
+                              device=dev)
+            b = 2 * nq * k + nq
+            args = _lib.BvSearchArgs(queries=q.data_ptr(), nq=nq, k=k, fetch=F, rerank=int(rerank),
+                                     out_rows=out.data_ptr(), out_scores=out[nq * k:].data_ptr(),
+                                     out_counts=out[2 * nq * k:].data_ptr(),
+                                     cand_rows=out[b:].data_ptr() if with_candidates else None,
+                                     cand_scores=out[b + nq * F:].data_ptr() if with_candidates else None,
+                                     cand_counts=out[b + 2 * nq * F:].data_ptr() if with_candidates else None)
+            _lib.check(self._L.bv_search_rows(self._h, C.byref(args), _ptr(offs), C.c_void_p(cand.data_ptr()),
+                                              C.c_void_p(st.cuda_stream)))
+            host = out.cpu().numpy()
+        st.synchronize()
+        res = (host[:nq * k].view(np.uint32).reshape(nq, k), host[nq * k:2 * nq * k].view(np.float32).reshape(nq, k),
+               host[2 * nq * k:b].view(np.uint32))
+        if with_candidates:
+            res += (host[b:b + nq * F].view(np.uint32).reshape(nq, F),
+                    host[b + nq * F:b + 2 * nq * F].view(np.float32).reshape(nq, F),
+                    host[b + 2 * nq * F:].view(np.uint32))
+        return res
+
     def set_scoring(self, scoring: str) -> None:
         """Score later searches with another mode (codes are shared by all modes)."""
         _lib.check(self._L.bv_set_scoring(self._h, _lib.SCORING[scoring]))

@@ -245,6 +245,20 @@ typedef struct bv_batch_profile {
 BV_API int bv_set_batch_timing(bv_index* idx, int enable);
 BV_API int bv_last_batch_profile(bv_index* idx, bv_batch_profile* out);
 
+/* The IVF x quant scan in candidate-list mode (src/index/ivfquant.ts:468-490:
+ * the quantized shaders with indexed: true, src/engine/wgsl/distanceQ8.ts:25-41,
+ * distanceQ4.ts, distanceQ1.ts): query q is scored against only the index
+ * rows cand_rows[offsets[q] - offsets[0] .. offsets[q+1] - offsets[0]) (the
+ * probed lists' rows, any order; offsets: nq + 1 HOST u32, cand_rows DEVICE
+ * u32), with the index's scoring, then re-ranked and written like
+ * bv_search_async (DEVICE args; no mask).  Ties among equal scores keep the
+ * earlier candidate, as the reference's topK over candidate slots does.  A
+ * candidate outside the index is BV_ERR_INVALID.  The candidates' codes are
+ * gathered into per-query segments of scratch memory first.  Synchronises
+ * `stream`. */
+BV_API int bv_search_rows(bv_index* idx, const bv_search_args* args, const uint32_t* offsets,
+                          const uint32_t* cand_rows, void* stream);
+
 /* Self-test of the kernels' bounded waits: one thread waits, with a budget of
  * `polls` mbarrier polls (1 .. 2^22, the budget every kernel wait uses), on a
  * barrier nothing completes, raises the index's timeout flag and returns; the

@@ -304,6 +304,21 @@ class Corpus:
                                                                bitorder="little")[: self.n].sum()))
         return ro[:n], so[:n], cr[:nc], cs[:nc]
 
+    def query_candidates(self, q, cand, k: int, fetch: int, mode: int = MODE_ASYM, rerank: bool = True):
+        """The indexed (candidate-list) scan of ivfquant.ts:468-490: the same
+        query over only the rows `cand`, scored and ranked by candidate slot
+        (distanceQ8.ts:25-41 with indexed: true, ties to the earlier slot),
+        then mapped back to rows.  -> (rows, scores, cand_rows, cand_scores)."""
+        cand = _u32(cand)
+        if cand.size == 0:
+            e = np.zeros(0, np.uint32)
+            return e, np.zeros(0, np.float32), e, np.zeros(0, np.float32)
+        wpr = self.codes.size // self.n
+        sub = Corpus(self.originals[cand], self.dim, self.bits, self.seed, self.rounds,
+                     codes=self.codes.reshape(self.n, wpr)[cand], scales=self.scales[cand])
+        r, s, cr, cs = sub.query(q, k, fetch, mode, rerank=rerank)
+        return cand[r], s, cand[cr], cs
+
     def query_batch(self, qs, k: int, fetch: int, mode: int = MODE_ASYM, mask=None,
                     rerank: bool = True, threads: int = 0):
         qs = _f32(qs).reshape(-1, self.dim)

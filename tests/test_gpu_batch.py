@@ -171,3 +171,27 @@ def test_batch_rejects_asym():
             _run(idx, "batch", q, 5, 10)
     finally:
         idx.destroy()
+
+
+@pytest.mark.parametrize("bits,scoring,n,d,nq,k,fetch", [
+    (8, "int", 20011, 768, 130, 10, 40),
+    (4, "int", 30000, 384, 385, 10, 80),    # an odd number of query tiles (4): the last pair is half empty
+    (1, "hamming", 40000, 768, 300, 100, 1000),
+])
+def test_pair_gemm_matches_per_query(bits, scoring, n, d, nq, k, fetch, monkeypatch):
+    """The CTA-pair GEMM (cta_group::2, chosen with BV_GEMM_PAIR=1 when a batch
+    has two or more query tiles) gives the same bits as the per-query scans."""
+    import torch
+
+    from browservec_b200.index import AddonQuantIndex
+
+    monkeypatch.setenv("BV_GEMM_PAIR", "1")
+    x = _rows(n, d, bits * 37 + nq)
+    qs = _rows(nq, d, 9 + nq)
+    idx = AddonQuantIndex(d, bits=bits, scoring=scoring)
+    try:
+        idx.append(x, n)
+        q = torch.from_numpy(qs).cuda()
+        _compare(_run(idx, "batch", q, k, fetch), _run(idx, "single", q, k, fetch), nq, k, fetch)
+    finally:
+        idx.destroy()
