@@ -171,6 +171,8 @@ struct bv_index {
   size_t bcnt_cap = 0;
   uint64_t* d_bcand = nullptr;
   size_t bcand_cap = 0;
+  uint32_t* d_scnt = nullptr;  // per query, per GEMM slice: candidates appended
+  size_t scnt_cap = 0;
   uint32_t* d_overflow = nullptr;
   uint32_t last_rounds = 0;
   // filtered batches: the kept rows gathered into their own tiles
@@ -794,6 +796,7 @@ int bv_destroy(bv_index* idx) {
   cudaFree(idx->d_thr);
   cudaFree(idx->d_bcnt);
   cudaFree(idx->d_bcand);
+  cudaFree(idx->d_scnt);
   cudaFree(idx->d_overflow);
   cudaFree(idx->d_cwoff);
   cudaFree(idx->d_cbsum);
@@ -1363,6 +1366,9 @@ int batch_rounds(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStream_
   if ((rc = grow(idx, &idx->d_bcnt, &idx->bcnt_cap, 2 * static_cast<size_t>(nq), "batch counts"))) return rc;
   if ((rc = grow(idx, &idx->d_bcand, &idx->bcand_cap, static_cast<size_t>(nq) * cap, "batch candidates")))
     return rc;
+  const uint32_t max_slices = static_cast<uint32_t>(idx->num_sms);
+  if ((rc = grow(idx, &idx->d_scnt, &idx->scnt_cap, static_cast<size_t>(nq) * max_slices, "batch counts")))
+    return rc;
   if (!idx->d_overflow) BV_CUDA(idx, cudaMalloc(&idx->d_overflow, 8), "batch flag");
 
   bv::PrepParams pp;
@@ -1394,7 +1400,9 @@ int batch_rounds(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStream_
   g.qfac = idx->d_qfac;
   g.cand = idx->d_bcand;
   g.cap = cap;
-  g.cnt = idx->d_bcnt;
+  g.Fp = Fp;
+  g.scnt = idx->d_scnt;
+  g.max_slices = max_slices;
   g.overflow = idx->d_overflow;
   g.err = idx->d_err;
 
@@ -1406,6 +1414,8 @@ int batch_rounds(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStream_
   sp.nq = nq;
   sp.cnt = idx->d_bcnt;
   sp.thr = idx->d_thr;
+  sp.scnt = idx->d_scnt;
+  sp.max_slices = max_slices;
 
   // Two or more query tiles: the CTA-pair GEMM (cta_group::2, 256 queries x
   // 256 rows per pair), its operands read by TMA tensor copies.
@@ -1419,11 +1429,33 @@ int batch_rounds(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStream_
     if (e != cudaSuccess) return cuda_fail(idx, e, "batch tensor maps");
   }
   uint32_t launches = 0;
-  auto gemm = [&](uint32_t rt0, uint32_t rt1) -> int {
+  // A GEMM launch appends densely behind the kept keys (one slice, a global
+  // counter per query) when `dense`, else each CTA into its own slice of the
+  // queries it serves: CTA c of grid G serves query tiles qt = c (mod g),
+  // g = gcd(nqt, G), as slice c / g of G / g, its counters in shared memory.
+  // The first launch of a batch (nothing kept yet) appends from slot 0.
+  auto gemm = [&](uint32_t rt0, uint32_t rt1, bool dense, bool first_launch) -> int {
     g.rt0 = rt0;
     g.rt1 = rt1;
     const uint64_t tiles = static_cast<uint64_t>(rt1 - rt0) * nqt;
     const uint32_t grid = static_cast<uint32_t>(tiles < static_cast<uint64_t>(idx->num_sms) ? tiles : idx->num_sms);
+    g.sbase = first_launch ? 0u : Fp;
+    g.slice_g = 0;
+    g.slice_cap = cap - g.sbase;
+    g.cnt_words = 0;
+    if (!dense && !pair) {
+      const uint32_t gg = static_cast<uint32_t>(gcd_u64(nqt, grid));
+      const uint32_t nslices = grid / gg, words = (nqt / gg) * (bv::kBQTile / 2u);
+      const uint32_t scap = (cap - Fp) / nslices;
+      if (scap >= 64u && bv::batch_gemm_smem(words) <= static_cast<uint32_t>(idx->max_smem)) {
+        g.slice_g = gg;
+        g.slice_cap = scap;
+        g.cnt_words = words;
+      }
+    }
+    sp.nslices = g.slice_g ? grid / g.slice_g : 1u;
+    sp.slice_cap = g.slice_cap;
+    sp.sbase = g.sbase;
     int r;
     if ((r = clk.begin(kPhGemm))) return r;
     cudaError_t e;
@@ -1458,12 +1490,12 @@ int batch_rounds(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStream_
     return BV_OK;
   };
   // Round sizes in row tiles: the first takes cap rows (every row is a
-  // candidate); later ones take four times the rows already seen, or fewer
-  // when that would expect more than (cap - F) / 2 rows to beat the
-  // threshold of the rows seen.  Rows that beat the threshold each cost the
-  // GEMM epilogue a global atomic, so a tighter threshold (more, smaller
-  // rounds) pays for the extra selects: growth capped at 4 took config 5 from
-  // 436k to 553k q/s and config 3 from 1.02M to 1.11M (uncapped, about 50x).
+  // candidate, appended densely from slot 0); later ones take four times the rows already
+  // seen, or fewer when that would expect more than (cap - F) / 2 rows to
+  // beat the threshold of the rows seen.  Growth capped at 4 took config 5
+  // from 436k to 553k q/s and config 3 from 1.02M to 1.11M (uncapped, about
+  // 50x), when every row that beat the threshold cost the epilogue a global
+  // atomic; it also keeps a CTA's slice well below its capacity.
   constexpr double kMaxGrow = 4.0;
   const uint32_t first = cap / bv::kBRowTile;
   auto next_size = [&](uint32_t seen_tiles) -> uint32_t {
@@ -1473,13 +1505,15 @@ int batch_rounds(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStream_
     return m < 1.0 ? 1u : (m > 4.0e9 ? 0xFFFFFFFFu : static_cast<uint32_t>(m));
   };
 
+  const size_t scnt_bytes = static_cast<size_t>(nq) * max_slices * 4;
   BV_CUDA(idx, cudaMemsetAsync(idx->d_overflow, 0, 4, s), "batch flag");
+  BV_CUDA(idx, cudaMemsetAsync(idx->d_scnt, 0, scnt_bytes, s), "batch counts");
   if ((rc = prep())) return rc;
   uint32_t nrounds = 0;
   for (uint32_t rt = 0; rt < T;) {
     const uint32_t m = rt == 0 ? first : next_size(rt);
     const uint32_t rt1 = T - rt < m ? T : rt + m;
-    if ((rc = gemm(rt, rt1)) || (rc = select())) return rc;
+    if ((rc = gemm(rt, rt1, rt == 0, rt == 0)) || (rc = select())) return rc;
     ++nrounds;
     rt = rt1;
   }
@@ -1490,21 +1524,21 @@ int batch_rounds(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStream_
     // A buffer overflowed (rows that arrive in increasing score order, for
     // instance): redo the batch round by round, halving a round that
     // overflows; a round of one tile (256 rows) cannot overflow (cap >= F + 256).
+    // (the fallback appends densely: one slice of cap - Fp slots per query)
+    BV_CUDA(idx, cudaMemsetAsync(idx->d_scnt, 0, scnt_bytes, s), "batch counts");
     if ((rc = prep())) return rc;
     uint32_t m = first;
     for (uint32_t rt = 0; rt < T;) {
       const uint32_t rt1 = T - rt < m ? T : rt + m;
-      BV_CUDA(idx, cudaMemcpyAsync(idx->d_bcnt + nq, idx->d_bcnt, nq * 4, cudaMemcpyDeviceToDevice, s), "backup");
       BV_CUDA(idx, cudaMemsetAsync(idx->d_overflow, 0, 4, s), "batch flag");
-      if ((rc = gemm(rt, rt1))) return rc;
+      if ((rc = gemm(rt, rt1, true, rt == 0))) return rc;
       BV_CUDA(idx, cudaMemcpyAsync(&flag, idx->d_overflow, 4, cudaMemcpyDeviceToHost, s), "batch flag");
       BV_CUDA(idx, cudaStreamSynchronize(s), "batch search");
       if (flag) {
-        // the round's appends are discarded (the lists' first entries and the
-        // thresholds are untouched by the GEMM) and the round is repeated smaller
+        // the round's appends are discarded (the kept keys and the thresholds
+        // are untouched by the GEMM) and the round is repeated smaller
         if (rt1 - rt == 1) return fail(BV_ERR_CUDA, "batch candidate buffer overflow on a single tile");
-        BV_CUDA(idx, cudaMemcpyAsync(idx->d_bcnt, idx->d_bcnt + nq, nq * 4, cudaMemcpyDeviceToDevice, s),
-                "restore");
+        BV_CUDA(idx, cudaMemsetAsync(idx->d_scnt, 0, scnt_bytes, s), "batch counts");
         m = (rt1 - rt) / 2;
         continue;
       }

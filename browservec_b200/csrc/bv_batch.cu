@@ -160,9 +160,9 @@ constexpr uint32_t kIdescI8Pair = (2u << 4) | (1u << 7) | (1u << 10) | ((kBRowTi
                                   ((2u * kBQTile >> 4) << 24);
 
 struct GemmSmem {
-  uint32_t slots_off, rowfac_off, rowid_off, bars_off, total;
+  uint32_t slots_off, rowfac_off, rowid_off, bars_off, cnt_off, total;
 };
-__host__ __device__ inline GemmSmem gemm_smem_layout(bool pair = false) {
+__host__ __device__ inline GemmSmem gemm_smem_layout(bool pair = false, uint32_t cnt_words = 0) {
   GemmSmem s;
   const int stages = pair ? kPairStages : kGemmStages;
   s.slots_off = stages * (pair ? kPairStageBytes : kStageBytes);
@@ -170,7 +170,9 @@ __host__ __device__ inline GemmSmem gemm_smem_layout(bool pair = false) {
   s.rowid_off = s.rowfac_off + kEpiWarps * kBRowTile * 4;        // ... and the tile's rows
   s.bars_off = s.rowid_off + kEpiWarps * kBRowTile * 4;
   // full[S], empty[S], tfull[2], tempty[2], done, then the TMEM address word
-  s.total = s.bars_off + (2 * stages + 5) * 8 + 16;
+  s.cnt_off = s.bars_off + (2 * stages + 5) * 8 + 16;
+  // the slice counters (two 16-bit counters a word)
+  s.total = s.cnt_off + cnt_words * 4;
   return s;
 }
 
@@ -403,7 +405,7 @@ template <bool kPair>
 __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, uint8_t* smem, const GemmSmem& lay,
                                               uint64_t* tfull, uint64_t* tempty, uint32_t tmem, uint32_t first,
                                               uint32_t stride, uint32_t ntiles, uint32_t nqt, uint32_t rank,
-                                              int warp, int lane) {
+                                              uint32_t* cnt_s, int warp, int lane) {
   // ------------------------------------------------------ epilogue
   const uint32_t grp = static_cast<uint32_t>(warp) / 4u;
   const uint32_t lane_base = static_cast<uint32_t>(warp % 4) * 32u;
@@ -487,14 +489,23 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, uint8_t* smem
         }
         if (pass) {
           const uint32_t n = __popc(pass);
-          const uint32_t base = atomicAdd(p.cnt + qi, n);
-          if (base + n > p.cap) atomicOr(p.overflow, 1u);
+          uint32_t base, off;
+          if (p.slice_g) {
+            // this CTA's slice of the query: a 16-bit counter in shared memory
+            const uint32_t jc = (qt / p.slice_g) * kBQTile + (qi % kBQTile), sh = (jc & 1u) * 16u;
+            base = (atomicAdd(cnt_s + (jc >> 1), n << sh) >> sh) & 0xFFFFu;
+            off = p.sbase + (blockIdx.x / p.slice_g) * p.slice_cap;
+          } else {
+            base = atomicAdd(p.scnt + qi, n);  // slice 0: the queries' counters are contiguous
+            off = p.sbase;
+          }
+          if (base + n > p.slice_cap) atomicOr(p.overflow, 1u);
           uint32_t w = base;
           for (uint32_t mm = pass; mm; mm &= mm - 1u, ++w) {
             const uint32_t j = __ffs(mm) - 1u;
             const uint32_t row = rid_s[c0 + j];
             const float sc = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(slot[j])), rf_s[c0 + j]), qf);
-            if (w < p.cap) cq[w] = make_key(sc, row);
+            if (w < p.slice_cap) cq[off + w] = make_key(sc, row);
           }
         }
       }
@@ -528,7 +539,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const GemmParams 
   // 1024-byte aligned base for the swizzled operand tiles
   const uint32_t raw = smem_addr(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  const GemmSmem lay = gemm_smem_layout();
+  const GemmSmem lay = gemm_smem_layout(false, p.slice_g ? p.cnt_words : 0u);
+  uint32_t* cnt_s = reinterpret_cast<uint32_t*>(smem + lay.cnt_off);
+  if (p.slice_g)
+    for (uint32_t i = threadIdx.x; i < p.cnt_words; i += blockDim.x) cnt_s[i] = 0u;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + lay.bars_off);
   uint64_t* empty = full + kGemmStages;
   uint64_t* tfull = empty + kGemmStages;
@@ -615,13 +629,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const GemmParams 
       mbar_wait_bounded(done, 0, p.err);
     }
   } else {
-    gemm_epilogue<false>(p, smem, lay, tfull, tempty, tmem, blockIdx.x, gridDim.x, ntiles, p.nqt, 0u, warp, lane);
+    gemm_epilogue<false>(p, smem, lay, tfull, tempty, tmem, blockIdx.x, gridDim.x, ntiles, p.nqt, 0u, cnt_s, warp,
+                         lane);
   }
   tc_fence_before();
   __syncthreads();
   if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
+  } else if (p.slice_g && warp < kEpiWarps) {
+    // publish this CTA's slice counts: every query of its query tiles, zeros
+    // included (the select reads each slice's count)
+    const uint32_t slice = blockIdx.x / p.slice_g, qt0 = blockIdx.x % p.slice_g;
+    const uint32_t nlocal = p.nqt / p.slice_g;
+    for (uint32_t e = threadIdx.x; e < nlocal * kBQTile; e += kEpiWarps * 32) {
+      const uint32_t qi = (qt0 + (e / kBQTile) * p.slice_g) * kBQTile + e % kBQTile;
+      if (qi < p.nq) p.scnt[static_cast<size_t>(slice) * p.nq + qi] = (cnt_s[e >> 1] >> ((e & 1u) * 16u)) & 0xFFFFu;
+    }
   }
 }
 
@@ -729,7 +753,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_wait_bounded(done, 0, p.err);
     }
   } else {
-    gemm_epilogue<true>(p, smem, lay, tfull, tempty, tmem, pair, npairs, ntiles, nqt2, rank, warp, lane);
+    gemm_epilogue<true>(p, smem, lay, tfull, tempty, tmem, pair, npairs, ntiles, nqt2, rank, nullptr, warp, lane);
   }
   tc_fence_before();
   cluster_sync_all();  // the pair's MMAs are complete and both epilogues have drained their TMEM
@@ -748,19 +772,57 @@ __global__ void __launch_bounds__(kConsumerThreads, 1) select_kernel(const Selec
   uint64_t* kept = reinterpret_cast<uint64_t*>(smem);          // Fp
   uint32_t* hist = reinterpret_cast<uint32_t*>(kept + p.Fp);   // kSelBins
   uint32_t* misc = hist + kSelBins;                            // 128
+  uint32_t* pre = misc + 128;                                  // nslices + 1: keys before each slice
   const int ctid = threadIdx.x;
   const uint32_t qi = blockIdx.x;
   uint64_t* c = p.cand + static_cast<size_t>(qi) * p.cap;
-  uint32_t total = p.cnt[qi];
-  total = total < p.cap ? total : p.cap;
+  uint32_t* sc = p.scnt + qi;  // slice s at sc[s * nq]
+  const uint32_t nk = p.sbase == 0 ? 0u : (p.cnt[qi] < p.Fp ? p.cnt[qi] : p.Fp);  // the kept region
+  if (ctid < 32) {  // one warp: the slices' counts (capped at their size) and their prefix
+    uint32_t carry = 0;
+    for (uint32_t s0 = 0; s0 < p.nslices; s0 += 32) {
+      const uint32_t s = s0 + static_cast<uint32_t>(ctid);
+      uint32_t m = s < p.nslices ? sc[static_cast<size_t>(s) * p.nq] : 0u;
+      m = m < p.slice_cap ? m : p.slice_cap;
+      uint32_t x = m;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, x, off);
+        if (ctid >= off) x += y;
+      }
+      if (s < p.nslices) pre[s] = carry + x - m;
+      carry += __shfl_sync(0xffffffffu, x, 31);
+    }
+    if (ctid == 0) pre[p.nslices] = carry;
+  }
+  named_bar_sync(kBarConsumers, kConsumerThreads);
+  const uint32_t total = nk + pre[p.nslices];
+  // candidate u: the kept keys first, then slice by slice (the slice of a key
+  // by binary search over the prefix)
   uint64_t v[MAXK];
 #pragma unroll
   for (int i = 0; i < MAXK; ++i) {
-    const uint32_t idx = static_cast<uint32_t>(ctid) + static_cast<uint32_t>(i) * kConsumerThreads;
-    v[i] = idx < total ? c[idx] : 0ull;
+    const uint32_t u = static_cast<uint32_t>(ctid) + static_cast<uint32_t>(i) * kConsumerThreads;
+    uint64_t x = 0ull;
+    if (u < nk) {
+      x = c[u];
+    } else if (u < total && p.nslices == 1u) {
+      x = c[p.sbase + (u - nk)];
+    } else if (u < total) {
+      const uint32_t w = u - nk;
+      uint32_t lo = 0, hi = p.nslices - 1u;  // the last slice with pre[s] <= w
+      while (lo < hi) {
+        const uint32_t mid = (lo + hi + 1u) >> 1;
+        if (pre[mid] <= w) lo = mid;
+        else hi = mid - 1u;
+      }
+      x = c[p.sbase + lo * p.slice_cap + (w - pre[lo])];
+    }
+    v[i] = x;
   }
   for (uint32_t i = ctid; i < p.Fp; i += kConsumerThreads) kept[i] = 0ull;
   named_bar_sync(kBarConsumers, kConsumerThreads);
+  for (uint32_t s = ctid; s < p.nslices; s += kConsumerThreads) sc[static_cast<size_t>(s) * p.nq] = 0u;  // next GEMM starts empty
   const uint32_t n = keep_best<MAXK>(v, total, p.F, kept, hist, misc, ctid);
   if (p.Fp <= 256u) {  // one warp sorts the kept keys in registers, no block barriers
     warp0_sort_dispatch(p.Fp, kept, ctid);
@@ -960,7 +1022,7 @@ __global__ void __launch_bounds__(kConsumerThreads, 1) keys_threshold_kernel(con
 }
 
 // ------------------------------------------------------------- launchers
-uint32_t batch_gemm_smem() { return gemm_smem_layout().total + 1024; }
+uint32_t batch_gemm_smem(uint32_t cnt_words) { return gemm_smem_layout(false, cnt_words).total + 1024; }
 
 cudaError_t launch_mask_count(const uint32_t* mask, uint64_t rows, uint32_t* word_off, uint32_t* block_sum,
                               uint32_t* count, cudaStream_t s) {
@@ -1026,7 +1088,7 @@ cudaError_t launch_prep(const PrepParams& p, cudaStream_t s) {
 }
 
 cudaError_t launch_gemm(const GemmParams& p, uint32_t grid, cudaStream_t s) {
-  const size_t smem = batch_gemm_smem();
+  const size_t smem = batch_gemm_smem(p.slice_g ? p.cnt_words : 0u);
   static int opted[kMaxDevices] = {};
   cudaError_t e = opt_in_smem(reinterpret_cast<const void*>(gemm_kernel), smem, opted);
   if (e != cudaSuccess) return e;
@@ -1062,7 +1124,7 @@ cudaError_t launch_gemm_pair(const GemmParams& p, const void* amap, const void* 
 }
 
 cudaError_t launch_select(const SelectParams& p, cudaStream_t s) {
-  const size_t smem = static_cast<size_t>(p.Fp) * 8 + kSelBins * 4 + 128 * 4;
+  const size_t smem = static_cast<size_t>(p.Fp) * 8 + kSelBins * 4 + 128 * 4 + (static_cast<size_t>(p.nslices) + 1) * 4;
   const uint32_t maxk = (p.cap + kConsumerThreads - 1) / kConsumerThreads;
   auto go = [&](auto kern) -> cudaError_t {
     static int opted[kMaxDevices] = {};

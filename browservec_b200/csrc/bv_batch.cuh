@@ -21,6 +21,13 @@
 // per-query buffer, then a per-query select keeps the best F and raises the
 // threshold for the next round.  A buffer that would overflow is flagged and
 // the host repeats the batch with rounds small enough that it cannot.
+//
+// Per query the buffer is [kept: Fp slots | slices]: the select leaves the
+// best F (sorted for Fp <= 256) in the kept region; the GEMM appends behind it
+// either densely (one slice; a global atomic counter per query, used by the
+// first round, whose rows all qualify) or, in later rounds, into one slice per
+// GEMM CTA that handles the query, counted by shared-memory atomics and
+// published at the CTA's end (no global atomic on the epilogue's hit path).
 #pragma once
 
 #include <cstdint>
@@ -77,9 +84,15 @@ struct GemmParams {
   uint32_t rt0, rt1;     // row tiles of this round
   const uint64_t* thr;
   const float* qfac;
-  uint64_t* cand;        // nq x cap keys
-  uint32_t cap;
-  uint32_t* cnt;
+  uint64_t* cand;        // nq x cap keys: [kept Fp | slices]
+  uint32_t cap, Fp;
+  uint32_t sbase;        // first slot of the slices: Fp, or 0 while nothing is kept (first round)
+  uint32_t* scnt;        // per slice, per query: keys appended (slice s of query q at s * nq + q)
+  uint32_t max_slices;
+  uint32_t slice_g;      // 0: one dense slice, global counters; else CTA c owns slice c / slice_g
+                         //    of the queries of query tiles qt = c mod slice_g (mod slice_g)
+  uint32_t slice_cap;    // slots per slice
+  uint32_t cnt_words;    // shared-memory counter words (two 16-bit counters each), slice_g != 0
   uint32_t* overflow;    // set when a buffer would overflow
   uint32_t* err;
 };
@@ -87,8 +100,10 @@ struct GemmParams {
 struct SelectParams {
   uint64_t* cand;        // nq x cap
   uint32_t cap, F, Fp, nq;
-  uint32_t* cnt;
+  uint32_t* cnt;         // per query: keys in the kept region
   uint64_t* thr;
+  uint32_t* scnt;        // per slice, per query: keys appended by the last GEMM (zeroed here)
+  uint32_t max_slices, nslices, slice_cap, sbase;
 };
 
 }  // namespace bv

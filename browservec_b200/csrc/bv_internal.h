@@ -118,7 +118,7 @@ struct ExpandParams;
 struct PrepParams;
 struct GemmParams;
 struct SelectParams;
-uint32_t batch_gemm_smem();
+uint32_t batch_gemm_smem(uint32_t cnt_words);
 cudaError_t launch_expand(const ExpandParams& p, cudaStream_t s);
 cudaError_t launch_prep(const PrepParams& p, cudaStream_t s);
 cudaError_t launch_gemm(const GemmParams& p, uint32_t grid, cudaStream_t s);
