@@ -75,6 +75,12 @@ def peaks():
     return 6650.0, "fallback"
 
 
+def _measured_traffic():
+    """DRAM bytes of the dominant kernels from ncu captures (profiles/dram_traffic.json)."""
+    p = os.path.join(ROOT, "profiles", "dram_traffic.json")
+    return json.load(open(p)) if os.path.exists(p) else {}
+
+
 def tensor_peak():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -415,8 +421,17 @@ def run_sharded(args, name, ds):
         gemm_s = prof["gemm_ms"] / 1e3
         tops = ops / gemm_s / 1e12 if gemm_s > 0 else 0.0
         peak = 2.0 * tensor_peak()
+        # DRAM bytes of the step's GEMM launches, scaled by row tiles from the ncu capture of
+        # one config-4 launch (rows of the same padded width only); None for other widths
+        traffic = None
+        gt = _measured_traffic().get("gemm_c4", {})
+        if gt and P == gt["row_bytes"] and kept_local == hi - lo:
+            traffic = gt["bytes_per_row_tile"] * (-(-(hi - lo) // 256))
         roofline = {"bound": "tensor", "achieved": tops, "peak": peak, "unit": "TOP/s (int8)",
-                    "frac": tops / peak, "traffic": None,
+                    "frac": tops / peak, "traffic": traffic,
+                    "traffic_scope": "DRAM bytes of one step's GEMM launches (the span 'achieved' covers), "
+                                     "scaled by row tiles from one ncu capture (profiles/gemm_c4_full.md)",
+                    "algorithmic_operand_bytes_per_step": float((hi - lo) * P + nq * P),
                     "peak_kind": "int8 dense = 2 x the measured bf16 burst (MEASURED_PEAKS.json bf16_tflops, "
                                  "of measured); no int8 figure is measured on this pool",
                     "kernel": "gemm_kernel (tcgen05.mma kind::i8)",
@@ -679,9 +694,8 @@ def run_single(args, name, ds):
     peak, peak_kind = peaks()
     achieved = algo_bytes / (query_ms / 1e3) / 1e9
     traffic = None
-    tp = os.path.join(ROOT, "profiles", "scan_c2_traffic.json")
-    if os.path.exists(tp) and BITS == 8 and N_ROWS == 100_000:
-        traffic = json.load(open(tp)).get(args.scoring)
+    if BITS == 8 and N_ROWS == 100_000:
+        traffic = _measured_traffic().get("scan_c2", {}).get(args.scoring)
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "traffic": traffic,
                 "peak_kind": f"{peak_kind} (copy bandwidth, MEASURED_PEAKS.json hbm_gbs)",
