@@ -766,6 +766,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // ------------------------------------------------------------- select
 // One CTA per query: the best F of the query's candidates, sorted descending
 // into cand[0..Fp) (zero padded); thr = the F-th best key once F exist.
+//
+// select_run<K>: the selection with K key registers a thread, for at most
+// K x 512 candidates.  The kernel sizes K to the candidates present (the
+// kept list plus the round's hits, usually a few thousand), so the radix
+// passes walk a few registers a thread rather than the buffer's capacity.
+template <int MAXK>
+__device__ __forceinline__ void select_run(const SelectParams& p, uint64_t* c, uint32_t* sc, uint32_t nk,
+                                           uint32_t total, uint64_t* kept, uint32_t* hist, uint32_t* misc,
+                                           const uint32_t* pre, int ctid, uint32_t qi);
+
 template <int MAXK>
 __global__ void __launch_bounds__(kConsumerThreads, 1) select_kernel(const SelectParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
@@ -797,6 +807,17 @@ __global__ void __launch_bounds__(kConsumerThreads, 1) select_kernel(const Selec
   }
   named_bar_sync(kBarConsumers, kConsumerThreads);
   const uint32_t total = nk + pre[p.nslices];
+  const uint32_t per = (total + kConsumerThreads - 1) / kConsumerThreads;  // uniform in the CTA
+  if (MAXK > 4 && per <= 4) return select_run<(MAXK > 4 ? 4 : MAXK)>(p, c, sc, nk, total, kept, hist, misc, pre, ctid, qi);
+  if (MAXK > 8 && per <= 8) return select_run<(MAXK > 8 ? 8 : MAXK)>(p, c, sc, nk, total, kept, hist, misc, pre, ctid, qi);
+  if (MAXK > 16 && per <= 16) return select_run<(MAXK > 16 ? 16 : MAXK)>(p, c, sc, nk, total, kept, hist, misc, pre, ctid, qi);
+  select_run<MAXK>(p, c, sc, nk, total, kept, hist, misc, pre, ctid, qi);
+}
+
+template <int MAXK>
+__device__ __forceinline__ void select_run(const SelectParams& p, uint64_t* c, uint32_t* sc, uint32_t nk,
+                                           uint32_t total, uint64_t* kept, uint32_t* hist, uint32_t* misc,
+                                           const uint32_t* pre, int ctid, uint32_t qi) {
   // candidate u: the kept keys first, then slice by slice (the slice of a key
   // by binary search over the prefix)
   uint64_t v[MAXK];

@@ -201,6 +201,26 @@ __device__ __forceinline__ float s4_biased(uint32_t xn, int nib) {
 constexpr float kBias8 = 8388736.0f;  // 2^23 + 128
 constexpr float kBias4 = 8388616.0f;  // 2^23 + 8
 
+// Butterfly sum of two rows over the L lanes of a row group with one shuffle
+// per level: at the first level (offset L/2) lanes of the lower half keep row
+// 0 and send row 1, the upper half the reverse, so each lane then carries one
+// row.  Every level adds the same two values as the per-row butterfly (t[l] =
+// s[l] + s[l ^ off]; the add is commutative), so each sum is bitwise the
+// per-row butterfly's.  `own` receives the row (0 or 1) this lane holds.
+__device__ __forceinline__ float lane_add(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ int lane_add(int a, int b) { return a + b; }
+template <int L, typename T>
+__device__ __forceinline__ T group_sum2(const T (&v)[2], int sl, uint32_t& own) {
+  const bool upper = (sl & (L / 2)) != 0;
+  own = upper ? 1u : 0u;
+  const T keep = upper ? v[1] : v[0];
+  const T send = upper ? v[0] : v[1];
+  T t = lane_add(keep, __shfl_xor_sync(0xffffffffu, send, L / 2));
+#pragma unroll
+  for (int off = L / 4; off >= 1; off >>= 1) t = lane_add(t, __shfl_xor_sync(0xffffffffu, t, off));
+  return t;
+}
+
 __device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
   int d;
   asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
@@ -1289,8 +1309,13 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(const ScanParams 
           for (int j = 0; j < CPL; ++j)
             x[u][j] = lds_chunk<C::W>(cb + static_cast<size_t>(rr) * p.R + (sl + j * L) * CB);
         }
-        float score[U];
+        // kTr: two rows per lane group share one butterfly (group_sum2); the
+        // lane then holds one of them (`own`) and offers its key alone.
+        constexpr bool kTr = (U == 2 && L >= 2);
+        float score[kTr ? 1 : U];
+        uint32_t own = 0;
         if constexpr (MODE == kAsym) {
+          float lsum[U];  // the lane's two chains added, per row
           // per row one f32x2 accumulator {even, odd}: the lane's elements
           // alternate between the two chains (canonical order), so one packed
           // FMA takes an element pair of one row and a register pair of q.
@@ -1353,12 +1378,24 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(const ScanParams 
           for (int u = 0; u < U; ++u) {
             float ev, od;
             f2_unpack(acc[u], ev, od);
-            float a = __fadd_rn(ev, od);
-#pragma unroll
-            for (int off = L / 2; off >= 1; off >>= 1) a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, off));
-            const float sv = sc[rho[u] < p.tile_rows ? rho[u] : 0u];
+            lsum[u] = __fadd_rn(ev, od);
+          }
+          if constexpr (kTr) {
+            const float a = group_sum2<L>(lsum, sl, own);
+            const uint32_t r = own ? rho[1] : rho[0];
+            const float sv = sc[r < p.tile_rows ? r : 0u];
             const float f = BITS == 8 ? __fmul_rn(sv, kInv127) : (BITS == 4 ? __fmul_rn(sv, kInv7) : sv);
-            score[u] = __fmul_rn(a, f);
+            score[0] = __fmul_rn(a, f);
+          } else {
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+              float a = lsum[u];
+#pragma unroll
+              for (int off = L / 2; off >= 1; off >>= 1) a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, off));
+              const float sv = sc[rho[u] < p.tile_rows ? rho[u] : 0u];
+              const float f = BITS == 8 ? __fmul_rn(sv, kInv127) : (BITS == 4 ? __fmul_rn(sv, kInv7) : sv);
+              score[u] = __fmul_rn(a, f);
+            }
           }
         } else {
           int iacc[U];
@@ -1387,14 +1424,28 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(const ScanParams 
               }
             }
           }
+          int vs[U];
 #pragma unroll
           for (int u = 0; u < U; ++u) {
             int v = iacc[u];
             if constexpr (MODE == kInt && BITS == 4) v -= 8 * qsum;
             if constexpr (MODE == kInt && BITS == 1) v = 2 * v - qsum;
+            vs[u] = v;
+          }
 #pragma unroll
-            for (int off = L / 2; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-            const float scale = sc[rho[u] < p.tile_rows ? rho[u] : 0u];
+          for (int u = 0; u < (kTr ? 1 : U); ++u) {
+            int v;
+            uint32_t r;
+            if constexpr (kTr) {
+              v = group_sum2<L>(vs, sl, own);
+              r = own ? rho[1] : rho[0];
+            } else {
+              v = vs[u];
+#pragma unroll
+              for (int off = L / 2; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+              r = rho[u];
+            }
+            const float scale = sc[r < p.tile_rows ? r : 0u];
             if constexpr (MODE == kHamming) {
               score[u] = __fmul_rn(__int2float_rn(static_cast<int>(p.P) - 2 * v), scale);
             } else {
@@ -1404,13 +1455,23 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(const ScanParams 
             }
           }
         }
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const uint64_t row = base + rho[u];
-          bool valid = (sl == 0) && rho[u] < nvalid;
+        if constexpr (kTr) {
+          // lane 0 of the group offers row 0, lane L/2 row 1
+          const uint32_t r = own ? rho[1] : rho[0];
+          const uint64_t row = base + r;
+          bool valid = (sl & (L / 2 - 1)) == 0 && r < nvalid;
           if (valid && p.mask) valid = (p.mask[row >> 5] >> (row & 31)) & 1u;
-          const uint64_t key = make_key(score[u], static_cast<uint32_t>(row));
+          const uint64_t key = make_key(score[0], static_cast<uint32_t>(row));
           append_keys(cand, &misc[kMiscCount], key, valid && key > thr, lane);
+        } else {
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            const uint64_t row = base + rho[u];
+            bool valid = (sl == 0) && rho[u] < nvalid;
+            if (valid && p.mask) valid = (p.mask[row >> 5] >> (row & 31)) & 1u;
+            const uint64_t key = make_key(score[u], static_cast<uint32_t>(row));
+            append_keys(cand, &misc[kMiscCount], key, valid && key > thr, lane);
+          }
         }
       }
       __syncwarp();

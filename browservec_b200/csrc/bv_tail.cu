@@ -133,7 +133,9 @@ __global__ void __launch_bounds__(kConsumerThreads, MINB) tail_kernel(const Tail
     }
     for (uint32_t i = nc + static_cast<uint32_t>(ctid); i < p.Fp; i += kConsumerThreads) cand[i] = 0ull;
     named_bar_sync(kBarConsumers, kConsumerThreads);
-    cta_sort_desc(cand, p.Fp, ctid);
+    // the candidates' order is output only through cand_rows or, without the
+    // re-rank, as the result; the re-rank orders by its exact keys itself
+    if (cand_rows || !p.rerank) cta_sort_desc(cand, p.Fp, ctid);
   }
   if (trace && ctid == 0) trace[kTrTailMerged] = globaltimer();
   if (cand_rows) {
@@ -156,9 +158,21 @@ __global__ void __launch_bounds__(kConsumerThreads, MINB) tail_kernel(const Tail
     const uint32_t batch = p.rows_bytes / (stride * 4u);
     uint64_t* ex = cand + p.Fp;  // exact keys (cand has capc >= 2*Fp slots)
     uint32_t gph = 1;
+    // Rows are gathered a batch at a time into the staging buffer; to keep
+    // more bytes in flight than the buffer holds, warp 1 asks L2 for the rows
+    // of the next two batches (bulk prefetch) while a batch is copied and dotted.
+    auto prefetch = [&](uint32_t c0) {
+      if (c0 >= nc) return;
+      const uint32_t nb = nc - c0 < batch ? nc - c0 : batch;
+      for (uint32_t c = lane; c < nb; c += 32)
+        bulk_prefetch_l2(p.originals + static_cast<size_t>(map_row(p.rowmap, key_row(cand[c0 + c]))) * p.dim,
+                         p.dim * 4u);
+    };
     named_bar_sync(kBarConsumers, kConsumerThreads);
+    if (bulk && warp == 1) prefetch(batch);
     for (uint32_t c0 = 0; c0 < nc; c0 += batch) {
       const uint32_t nb = nc - c0 < batch ? nc - c0 : batch;
+      if (bulk && warp == 1) prefetch(c0 + 2u * batch);
       if (bulk) {
         if (warp == 0) {
           if (lane == 0) mbar_arrive_expect_tx(gbar, nb * p.dim * 4u);
@@ -234,6 +248,28 @@ __global__ void __launch_bounds__(kConsumerThreads, MINB) tail_kernel(const Tail
     if (trace && ctid == 0) trace[kTrTailDotted] = globaltimer();
     if (p.Fp <= 256u) {
       warp0_sort_dispatch(p.Fp, ex, ctid);
+      if (warp == 0) {
+        __syncwarp();
+        for (uint32_t i = lane; i < n; i += 32) {
+          out_rows[i] = map_row(p.rowmap, key_row(ex[i])) + p.row_base;
+          out_scores[i] = key_score(ex[i]);
+        }
+      }
+    } else if (n <= 256u && p.Fp <= 2u * kConsumerThreads) {
+      // the best n exact keys (radix select), then one warp sorts those few
+      uint64_t v2[2];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const uint32_t u = static_cast<uint32_t>(ctid) + static_cast<uint32_t>(i) * kConsumerThreads;
+        v2[i] = u < nc ? ex[u] : 0ull;
+      }
+      named_bar_sync(kBarConsumers, kConsumerThreads);
+      const uint32_t kept = keep_best<2>(v2, nc, n, ex, hist, misc, ctid);
+      uint32_t np = 32;
+      while (np < n) np <<= 1;
+      for (uint32_t i = kept + static_cast<uint32_t>(ctid); i < np; i += kConsumerThreads) ex[i] = 0ull;
+      named_bar_sync(kBarConsumers, kConsumerThreads);
+      warp0_sort_dispatch(np, ex, ctid);
       if (warp == 0) {
         __syncwarp();
         for (uint32_t i = lane; i < n; i += 32) {
