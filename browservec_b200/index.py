@@ -725,382 +725,6 @@ class BrowserVec:
         batch = self.index.search(qs, k_eff, fetch, rerank=do_rerank)
         return [self._map_hits(h, k) for h in batch]
 
-    def export_originals(self, row0: int = 0, count: int | None = None) -> np.ndarray:
-        """The stored (normalized) fp32 rows, (count, dim)."""
-        count = self.size - row0 if count is None else count
-        out = np.empty((count, self.dim), np.float32)
-        _lib.check(self._L.bv_export_originals(self._h, row0, count, _ptr(out)))
-        return out
-
-    def stats(self) -> dict:
-        s = _lib.BvStats()
-        _lib.check(self._L.bv_get_stats(self._h, C.byref(s)))
-        return {f: getattr(s, f) for f, _ in s._fields_}
-
-    def set_phase_trace(self, ptr: int, capacity: int) -> None:
-        """Device buffer (u64) receiving per-phase timestamps of each scan launch."""
-        _lib.check(self._L.bv_set_phase_trace(self._h, C.c_void_p(ptr) if ptr else None, capacity))
-
-    def last_launches(self) -> int:
-        n = C.c_uint32()
-        _lib.check(self._L.bv_launches_last_search(self._h, C.byref(n)))
-        return int(n.value)
-
-    def destroy(self) -> None:
-        if getattr(self, "_h", None):
-            self._L.bv_destroy(self._h)
-            self._h = None
-
-    def __del__(self):  # pragma: no cover - best effort
-        try:
-            self.destroy()
-        except Exception:
-            pass
-
-
-class PreparedSearch:
-    """A host-memory search request whose buffers and argument block are made
-    once: each call copies a batch of queries in and runs bv_search (the
-    call search() makes), so a caller issuing one query at a time pays no
-    per-call allocation.  The returned arrays are reused by the next call."""
-
-    def __init__(self, index: "AddonQuantIndex", nq: int, k: int, fetch: int, rerank: bool = True):
-        self.q = np.zeros((nq, index.dim), np.float32)
-        self.rows = np.zeros((nq, k), np.uint32)
-        self.scores = np.zeros((nq, k), np.float32)
-        self.counts = np.zeros(nq, np.uint32)
-        self.args = _lib.BvSearchArgs(queries=self.q.ctypes.data, nq=nq, k=k, fetch=max(fetch, k),
-                                      rerank=int(rerank), mask=None, mask_words=0,
-                                      out_rows=self.rows.ctypes.data, out_scores=self.scores.ctypes.data,
-                                      out_counts=self.counts.ctypes.data)
-        self._ref = C.byref(self.args)
-        self._fn = index._L.bv_search
-        self._index = index
-
-    def __call__(self, qs: np.ndarray):
-        np.copyto(self.q, qs.reshape(self.q.shape), casting="same_kind")
-        rc = self._fn(self._index._h, self._ref)
-        if rc:
-            _lib.check(rc)
-        return self.rows, self.scores, self.counts
-
-
-class AsyncSearchList:
-    """Device searches submitted together by one bv_search_async_n call.
-
-    entries: (index, q_ptr, k, fetch, rerank, out_rows_ptr, out_scores_ptr, out_counts_ptr) per
-    search, nq = 1 each; the argument array is built once and can be submitted any number of times
-    (the pointers are fixed)."""
-
-    def __init__(self, entries):
-        n = len(entries)
-        if n == 0:
-            raise ValueError("no searches")
-        self.n = n
-        self._keep = [e[0] for e in entries]
-        self._idx = (C.c_void_p * n)(*[e[0]._h.value for e in entries])
-        self._args = (_lib.BvSearchArgs * n)()
-        for i, (ix, q, k, fetch, rerank, r, s, c) in enumerate(entries):
-            self._args[i] = _lib.BvSearchArgs(queries=q, nq=1, k=k, fetch=max(fetch, k), rerank=int(rerank),
-                                              mask=None, mask_words=0, out_rows=r, out_scores=s, out_counts=c)
-        self._L = entries[0][0]._L
-
-    def submit(self, stream: int = 0) -> None:
-        _lib.check(self._L.bv_search_async_n(self._idx, self._args, self.n, C.c_void_p(stream)))
-
-
-@dataclass
-class _Entry:
-    id: str
-    row: int
-    metadata: Mapping[str, Any] | None = None
-
-
-@dataclass
-class _Store:
-    """src/store/store.ts: id<->row map, tombstones, metadata columns."""
-
-    dimension: int
-    metric: str
-    normalize: bool
-    by_id: dict = field(default_factory=dict)
-    by_row: list = field(default_factory=list)
-    deleted: set = field(default_factory=set)
-    columns: FilterColumns = field(default_factory=FilterColumns)
-
-
-class BrowserVec:
-    """The flat branches of src/index.ts over AddonQuantIndex: quantBits 1/4/8
-    (the quantized scan, QuantIndex) and 0 (the exact fp32 scan, FlatIndex,
-    src/index/flat.ts:132-211, scored with the WASM-SIMD f32 arithmetic of the
-    reference's CPU path)."""
-
-    def __init__(self, dimension: int, metric: str = "cosine", normalize: bool | None = None,
-                 quant_bits: int = 8, quant: Mapping[str, Any] | None = None, scoring: str = "asym",
-                 device: int = 0):
-        if not isinstance(dimension, int) or dimension <= 0:
-            raise ValueError(f"dimension must be a positive integer, got {dimension}")
-        quant = dict(quant or {})
-        if quant_bits not in (0, 1, 4, 8):
-            raise ValueError(f"quantBits {quant_bits} not supported (ships 0, 1, 4, 8)")
-        if quant_bits == 0:
-            scoring = "asym"  # exact scores: no quantized scoring mode applies
-        self.store = _Store(dimension, metric, metric == "cosine" if normalize is None else normalize)
-        self.quant_bits = quant_bits
-        self.rerank_factor = int(quant.get("rerankFactor", default_rerank_factor(quant_bits)))
-        self.index = AddonQuantIndex(dimension, quant.get("seed", DEFAULT_SEED), quant.get("rounds", 2),
-                                     quant_bits, scoring, device, metric)
-        self.last_query_ms: float | None = None
-        self.last_query_gpu_ms: float | None = None
-        self._version = 0       # bumped by every add and delete
-        self._dev = None        # (version, DeviceColumns, live-row mask words) on the index's GPU
-        self._masks: OrderedDict = OrderedDict()  # (filter, version) -> (mask words, matches, rows)
-
-    @classmethod
-    def create(cls, config: Mapping[str, Any]) -> "BrowserVec":
-        """BrowserVec.create (src/index.ts:232-263), quantized flat stores only."""
-        return cls(config["dimension"], config.get("metric", "cosine"), config.get("normalize"),
-                   config.get("quantBits", 8), config.get("quant"), config.get("scoring", "asym"),
-                   config.get("device", 0))
-
-    # ---- ingest -----------------------------------------------------------
-    def add_batch(self, records: Sequence[Mapping[str, Any]]) -> None:
-        """src/index.ts:293-305"""
-        if not records:
-            return
-        d = self.store.dimension
-        vecs = np.zeros((len(records), d), np.float32)
-        metas = []
-        for i, r in enumerate(records):
-            v = np.asarray(r["vector"], np.float32)
-            if v.size != d:
-                raise ValueError(f"vector dim {v.size} != store dim {d}")
-            if r["id"] in self.store.by_id:
-                raise ValueError(f"duplicate id: {r['id']}")
-            vecs[i] = v
-            row = len(self.store.by_row)
-            e = _Entry(r["id"], row, r.get("metadata"))
-            self.store.by_id[r["id"]] = e
-            self.store.by_row.append(e)
-            metas.append(r.get("metadata"))
-        if self.store.normalize:
-            vecs = normalize_rows(vecs)
-        self.store.columns.append(metas)
-        self.index.append(vecs, len(records))
-        self._version += 1
-
-    def add(self, record: Mapping[str, Any]) -> None:
-        self.add_batch([record])
-
-    def add_arrays(self, vectors: np.ndarray, ids: Sequence[str] | None = None,
-                   columns: Mapping[str, np.ndarray] | None = None,
-                   dictionaries: Mapping[str, list] | None = None) -> None:
-        """Bulk ingest of prepared arrays (rows normalized like store.prepare)."""
-        vectors = np.ascontiguousarray(vectors, np.float32)
-        n = vectors.shape[0]
-        base = len(self.store.by_row)
-        for i in range(n):
-            rid = ids[i] if ids is not None else f"v{base + i}"
-            e = _Entry(rid, base + i, None)
-            self.store.by_id[rid] = e
-            self.store.by_row.append(e)
-        if self.store.normalize:
-            vectors = normalize_rows(vectors)
-        if columns:
-            self.store.columns.append_columns(n, columns, dictionaries)
-        else:
-            self.store.columns.append([None] * n)
-        self.index.append(vectors, n)
-        self._version += 1
-
-    # ---- snapshots (src/index.ts:608-700, src/persist/format.ts) ----------
-    def export(self) -> bytes:
-        """BrowserVec.export: a snapshot of the live rows (tombstones compacted
-        out, src/index.ts:646-671), in the reference's format."""
-        from .persist import serialize
-
-        live = [e for e in self.store.by_row if e.row not in self.store.deleted]
-        vecs = self.index.export_originals() if self.index.size else np.zeros((0, self.store.dimension), np.float32)
-        if self.store.deleted:
-            vecs = vecs[np.array([e.row for e in live], np.int64)]
-        entries = [{"id": e.id, "metadata": e.metadata} for e in live]
-        return serialize(self.store.dimension, self.store.metric, self.store.normalize, entries, vecs)
-
-    @classmethod
-    def import_(cls, buf, config: Mapping[str, Any] | None = None) -> "BrowserVec":
-        """BrowserVec.import (src/index.ts:616-644): a store built from a
-        snapshot (quantBits from `config`, default 0 as in the reference)."""
-        from .persist import deserialize
-
-        snap = deserialize(buf)
-        config = dict(config or {})
-        db = cls(snap.dimension, snap.metric, snap.normalize, config.get("quantBits", 0), config.get("quant"),
-                 config.get("scoring", "asym"), config.get("device", 0))
-        db.load_snapshot(snap)
-        return db
-
-    def load_snapshot(self, snap) -> None:
-        """src/index.ts:673-700: ids and metadata into the store, and the
-        stored vectors (already normalized when the store normalizes) into
-        the index in one bulk append -- the GPU encodes them -- instead of a
-        per-row insert."""
-        if self.count > 0 or self.store.by_row:
-            raise ValueError("cannot load into a non-empty store")
-        if snap.dimension != self.store.dimension:
-            raise ValueError(f"snapshot dim {snap.dimension} != store dim {self.store.dimension}")
-        if snap.metric != self.store.metric:
-            raise ValueError(f"snapshot metric {snap.metric} != store metric {self.store.metric}")
-        metas = []
-        for row, e in enumerate(snap.entries):
-            if e["id"] in self.store.by_id:
-                raise ValueError(f"duplicate id: {e['id']}")
-            ent = _Entry(e["id"], row, e.get("metadata"))
-            self.store.by_id[e["id"]] = ent
-            self.store.by_row.append(ent)
-            metas.append(e.get("metadata"))
-        self.store.columns.append(metas)
-        if snap.count:
-            self.index.append(snap.vectors, snap.count)
-        self._version += 1
-
-    def delete(self, id: str) -> bool:
-        e = self.store.by_id.pop(id, None)
-        if e is None:
-            return False
-        self.store.deleted.add(e.row)
-        self._version += 1
-        return True
-
-    @property
-    def count(self) -> int:
-        return len(self.store.by_id)
-
-    # ---- query ------------------------------------------------------------
-    def _prep_query(self, query) -> np.ndarray:
-        q = np.asarray(query, np.float32).reshape(-1).copy()
-        if q.size != self.store.dimension:
-            raise ValueError(f"query dim {q.size} != store dim {self.store.dimension}")
-        if self.store.normalize:
-            q = normalize_rows(q[None, :])[0]
-        return q
-
-    def _meta_of(self, row: int):
-        return self.store.by_row[row].metadata
-
-    def _device_mask(self, flt: Mapping[str, Any]):
-        """The score mask of a filter -- its rows that are not deleted
-        (src/index.ts:372-386) -- built by the GPU predicate over device
-        copies of the metadata columns and kept per (filter, store version):
-        (mask words as a CUDA tensor, match count, the matching rows when at
-        most FILTER_CPU_SCAN_MAX, else None)."""
-        import torch
-
-        key = (json.dumps(flt, sort_keys=True, default=repr), self._version)
-        hit = self._masks.get(key)
-        if hit is not None:
-            self._masks.move_to_end(key)
-            return hit
-        dev = torch.device("cuda", self.index.device)
-        if self._dev is None or self._dev[0] != self._version:
-            dc = DeviceColumns.from_host(self.store.columns, dev)
-            live = np.ones(len(self.store.by_row), bool)
-            if self.store.deleted:
-                live[np.fromiter(self.store.deleted, np.int64)] = False
-            live_w = torch.from_numpy(pack_mask(live).view(np.int32)).to(dev)
-            self._dev = (self._version, dc, live_w)
-            self._masks.clear()  # masks of older versions are stale
-        _, dc, live_w = self._dev
-        m = dc.mask(flt, live=live_w)
-        if not hasattr(self, "_popc"):
-            self._popc = torch.tensor([bin(i).count("1") for i in range(256)], dtype=torch.int64, device=dev)
-        b = m.view(torch.uint8)
-        count = int(self._popc[b.long()].sum().item())
-        rows = None
-        if 0 < count <= FILTER_CPU_SCAN_MAX:
-            bits = ((b.unsqueeze(1) >> torch.arange(8, device=dev, dtype=torch.uint8)) & 1).flatten()
-            rows = torch.nonzero(bits).squeeze(1).cpu().numpy().astype(np.uint32)
-        entry = (m, count, rows)
-        self._masks[key] = entry
-        while len(self._masks) > MASK_CACHE_ENTRIES:
-            self._masks.popitem(last=False)
-        return entry
-
-    def _fetch(self, k: int, masked: bool, rerank: bool | None):
-        """src/index.ts:405-417: k_eff (oversampled by the tombstones unless a
-        mask already drops them) and the candidate fetch."""
-        total = self.index.size
-        k_eff = min(total, k) if masked else min(total, k + len(self.store.deleted))
-        do_rerank = rerank if rerank is not None else self.rerank_factor > 1
-        fetch = min(total, max(k_eff, k_eff * self.rerank_factor)) if do_rerank else k_eff
-        return k_eff, fetch, do_rerank
-
-    def query(self, query, k: int = 10, filter: Mapping[str, Any] | None = None,
-              rerank: bool | None = None) -> list[QueryResult]:
-        """src/index.ts:343-436 (quantized branch)."""
-        import time
-
-        q = self._prep_query(query)
-        predicate = compile_filter(filter) if filter else None
-        t0 = time.perf_counter()
-        if predicate is not None:
-            m, count, rows = self._device_mask(filter)
-            if count == 0:
-                return []
-            if rows is not None:
-                return self._query_rows_exact(q, rows, k)
-            k_eff, fetch, do_rerank = self._fetch(k, True, rerank)
-            if k_eff <= 0:
-                return []
-            hits = self.index.search_masked(q[None, :], k_eff, fetch, do_rerank, m)[0]
-            self.last_query_ms = (time.perf_counter() - t0) * 1e3
-            self.last_query_gpu_ms = None
-            return self._map_hits(hits, k, predicate)
-        k_eff, fetch, do_rerank = self._fetch(k, False, rerank)
-        if k_eff <= 0:
-            return []
-        hits = self.index.search(q[None, :], k_eff, fetch, rerank=do_rerank)[0]
-        self.last_query_ms = (time.perf_counter() - t0) * 1e3
-        self.last_query_gpu_ms = min(self.index.stats()["last_query_gpu_ms"], self.last_query_ms)
-        return self._map_hits(hits, k, predicate)
-
-    def _map_hits(self, hits, k, predicate=None) -> list[QueryResult]:
-        out = []
-        for h in hits:
-            if self.store.deleted and h.row in self.store.deleted:
-                continue
-            e = self.store.by_row[h.row]
-            if predicate is not None and not predicate(e.metadata):
-                continue
-            out.append(QueryResult(e.id, h.score, e.metadata))
-            if len(out) == k:
-                break
-        return out
-
-    def _query_rows_exact(self, q, rows, k) -> list[QueryResult]:
-        """src/index.ts:445-464"""
-        hits = self.index.query_rows_exact(q, rows, k)
-        return [QueryResult(self.store.by_row[h.row].id, h.score, self.store.by_row[h.row].metadata)
-                for h in hits]
-
-    def query_batch(self, queries, k: int = 10, filter: Mapping[str, Any] | None = None,
-                    rerank: bool | None = None) -> list[list[QueryResult]]:
-        """src/index.ts:473-517, with the re-rank the batched reference branch lacks."""
-        queries = list(queries) if not isinstance(queries, np.ndarray) else queries
-        if len(queries) == 0:
-            return []
-        if filter:
-            return [self.query(q, k, filter, rerank) for q in queries]
-        qs = np.stack([self._prep_query(q) for q in queries])
-        deleted = len(self.store.deleted)
-        total = self.index.size
-        k_eff = min(total, k + deleted)
-        if k_eff <= 0:
-            return [[] for _ in range(qs.shape[0])]
-        do_rerank = rerank if rerank is not None else self.rerank_factor > 1
-        fetch = min(total, max(k_eff, k_eff * self.rerank_factor)) if do_rerank else k_eff
-        batch = self.index.search(qs, k_eff, fetch, rerank=do_rerank)
-        return [self._map_hits(h, k) for h in batch]
-
     def stats(self) -> dict:
         """src/index.ts:702-750 (fields this path produces)."""
         s = {"count": self.count, "dimension": self.store.dimension, "metric": self.store.metric,
