@@ -142,11 +142,10 @@ __global__ void __launch_bounds__(kScanThreads, 2)
       mbar_arrive_expect_tx(qbar, q_bulk);
       if (q_bulk) bulk_g2s(q, p.query, q_bulk, qbar);
       uint32_t b = grab_tile(p.tile_ctr, p.epoch, p.err);
-      uint32_t it = 0;
+      uint32_t it = 0, s = 0, ph = 0;  // stage and phase advance with it
       bool more = true;
       while (more) {
-        for (uint32_t ks = 0; ks < nks; ++ks, ++it) {
-          const uint32_t s = it % p.stages, ph = (it / p.stages) & 1u;
+        for (uint32_t ks = 0; ks < nks; ++ks, ++it, s = s + 1u == p.stages ? 0u : s + 1u, ph ^= s == 0u ? 1u : 0u) {
           if (it >= p.stages && !mbar_wait_bounded(&empty[s], ph ^ 1u, p.err)) {
             more = false;
             break;
@@ -181,8 +180,8 @@ __global__ void __launch_bounds__(kScanThreads, 2)
     const uint32_t sw = r & 7u;  // 16-byte chunk c of row r sits at chunk c ^ sw
     float acc = 0.0f;
     uint32_t blocks_done = 0;
-    for (uint32_t it = 0;; ++it) {
-      const uint32_t s = it % p.stages, ph = (it / p.stages) & 1u;
+    uint32_t s = 0, ph = 0;
+    for (uint32_t it = 0;; ++it, s = s + 1u == p.stages ? 0u : s + 1u, ph ^= s == 0u ? 1u : 0u) {
       const bool landed = mbar_wait_bounded(&full[s], ph, p.err);
       const uint32_t b = landed ? stage_blk[s] : kNoTile;
       if (it == 0 && p.trace && ctid == 0) p.trace[blockIdx.x * 8 + kTrFirstTile] = globaltimer();

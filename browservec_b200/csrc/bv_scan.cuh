@@ -201,23 +201,50 @@ __device__ __forceinline__ float s4_biased(uint32_t xn, int nib) {
 constexpr float kBias8 = 8388736.0f;  // 2^23 + 128
 constexpr float kBias4 = 8388616.0f;  // 2^23 + 8
 
-// Butterfly sum of two rows over the L lanes of a row group with one shuffle
-// per level: at the first level (offset L/2) lanes of the lower half keep row
-// 0 and send row 1, the upper half the reverse, so each lane then carries one
-// row.  Every level adds the same two values as the per-row butterfly (t[l] =
-// s[l] + s[l ^ off]; the add is commutative), so each sum is bitwise the
-// per-row butterfly's.  `own` receives the row (0 or 1) this lane holds.
+// Butterfly sums of N = 2 or 4 rows over the L lanes of a row group with one
+// shuffle per row per level while a lane still carries several rows: at
+// offset L/2 the lanes of the lower half keep the first half of the rows and
+// send the second (the upper half the reverse), at L/4 (N = 4) the same within
+// each half, so from then on each lane carries one row.  Every level adds the
+// same two values as the per-row butterfly (t[l] = s[l] + s[l ^ off]; the add
+// is commutative), so each sum is bitwise the per-row butterfly's.  `own`
+// receives the row this lane holds; lanes whose low log2(L/N) bits are zero
+// hold one each.
 __device__ __forceinline__ float lane_add(float a, float b) { return __fadd_rn(a, b); }
 __device__ __forceinline__ int lane_add(int a, int b) { return a + b; }
-template <int L, typename T>
-__device__ __forceinline__ T group_sum2(const T (&v)[2], int sl, uint32_t& own) {
-  const bool upper = (sl & (L / 2)) != 0;
-  own = upper ? 1u : 0u;
-  const T keep = upper ? v[1] : v[0];
-  const T send = upper ? v[0] : v[1];
-  T t = lane_add(keep, __shfl_xor_sync(0xffffffffu, send, L / 2));
+template <int N>
+__device__ __forceinline__ uint32_t pick_row(const uint32_t (&rho)[N], uint32_t own) {
+  if constexpr (N == 2) return own ? rho[1] : rho[0];
+  else return own < 2u ? (own ? rho[1] : rho[0]) : (own == 3u ? rho[3] : rho[2]);
+}
+template <int L, int N, typename T>
+__device__ __forceinline__ T group_sum(const T (&v)[N], int sl, uint32_t& own) {
+  static_assert(N == 2 || N == 4, "two or four rows");
+  static_assert(L >= N, "a lane per row at least");
+  T a[N / 2];
+  const bool up1 = (sl & (L / 2)) != 0;
 #pragma unroll
-  for (int off = L / 4; off >= 1; off >>= 1) t = lane_add(t, __shfl_xor_sync(0xffffffffu, t, off));
+  for (int i = 0; i < N / 2; ++i) {
+    const T keep = up1 ? v[N / 2 + i] : v[i];
+    const T send = up1 ? v[i] : v[N / 2 + i];
+    a[i] = lane_add(keep, __shfl_xor_sync(0xffffffffu, send, L / 2));
+  }
+  T t;
+  int next;
+  if constexpr (N == 4) {
+    const bool up2 = (sl & (L / 4)) != 0;
+    own = (up1 ? 2u : 0u) + (up2 ? 1u : 0u);
+    const T keep = up2 ? a[1] : a[0];
+    const T send = up2 ? a[0] : a[1];
+    t = lane_add(keep, __shfl_xor_sync(0xffffffffu, send, L / 4));
+    next = L / 8;
+  } else {
+    own = up1 ? 1u : 0u;
+    t = a[0];
+    next = L / 4;
+  }
+#pragma unroll
+  for (int off = next; off >= 1; off >>= 1) t = lane_add(t, __shfl_xor_sync(0xffffffffu, t, off));
   return t;
 }
 
@@ -1174,9 +1201,10 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(const ScanParams 
       const uint64_t stream_policy = l2_policy_evict_first();  // codes are read once per query
       // tiles come from a shared counter, so faster SMs take more of them
       uint32_t t = grab_tile(p.tile_ctr, p.epoch, p.err);
-      uint32_t it = 0;
-      for (;; ++it) {
-        const uint32_t s = it % p.stages, ph = (it / p.stages) & 1u;
+      // stage s and its phase ph advance with the loop (no division by the
+      // runtime stage count)
+      uint32_t s = 0, ph = 0;
+      for (uint32_t it = 0;; ++it, s = s + 1u == p.stages ? 0u : s + 1u, ph ^= s == 0u ? 1u : 0u) {
         if (it >= p.stages && !mbar_wait_bounded(&empty[s], ph ^ 1u, p.err)) break;
         if (t >= p.ntiles) {  // no more work: an empty stage tells the consumers
           tile_ids[s] = kNoTile;
@@ -1284,8 +1312,8 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(const ScanParams 
     // candidate buffer: keys above thr are appended; checked every check_tiles
     const uint32_t high = p.capc - p.check_tiles * p.tile_rows;
     uint64_t thr = 0;
-    for (uint32_t it = 0;; ++it) {
-      const uint32_t s = it % p.stages, ph = (it / p.stages) & 1u;
+    uint32_t s = 0, ph = 0, until_check = p.check_tiles;
+    for (uint32_t it = 0;; ++it, s = s + 1u == p.stages ? 0u : s + 1u, ph ^= s == 0u ? 1u : 0u) {
       const bool landed = mbar_wait_bounded(&full[s], ph, p.err);
       const uint32_t t = landed ? tile_ids[s] : kNoTile;
       if (it == 0 && p.trace && threadIdx.x == 0) p.trace[blockIdx.x * 8 + kTrFirstTile] = globaltimer();
@@ -1309,9 +1337,10 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(const ScanParams 
           for (int j = 0; j < CPL; ++j)
             x[u][j] = lds_chunk<C::W>(cb + static_cast<size_t>(rr) * p.R + (sl + j * L) * CB);
         }
-        // kTr: two rows per lane group share one butterfly (group_sum2); the
-        // lane then holds one of them (`own`) and offers its key alone.
-        constexpr bool kTr = (U == 2 && L >= 2);
+        // kTr: the U (2 or 4) rows of a lane group share one butterfly
+        // (group_sum); the lane then holds one of them (`own`) and offers its
+        // key alone.
+        constexpr bool kTr = ((U == 2 || U == 4) && L >= U);
         float score[kTr ? 1 : U];
         uint32_t own = 0;
         if constexpr (MODE == kAsym) {
@@ -1381,8 +1410,8 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(const ScanParams 
             lsum[u] = __fadd_rn(ev, od);
           }
           if constexpr (kTr) {
-            const float a = group_sum2<L>(lsum, sl, own);
-            const uint32_t r = own ? rho[1] : rho[0];
+            const float a = group_sum<L, U>(lsum, sl, own);
+            const uint32_t r = pick_row<U>(rho, own);
             const float sv = sc[r < p.tile_rows ? r : 0u];
             const float f = BITS == 8 ? __fmul_rn(sv, kInv127) : (BITS == 4 ? __fmul_rn(sv, kInv7) : sv);
             score[0] = __fmul_rn(a, f);
@@ -1437,8 +1466,8 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(const ScanParams 
             int v;
             uint32_t r;
             if constexpr (kTr) {
-              v = group_sum2<L>(vs, sl, own);
-              r = own ? rho[1] : rho[0];
+              v = group_sum<L, U>(vs, sl, own);
+              r = pick_row<U>(rho, own);
             } else {
               v = vs[u];
 #pragma unroll
@@ -1456,10 +1485,10 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(const ScanParams 
           }
         }
         if constexpr (kTr) {
-          // lane 0 of the group offers row 0, lane L/2 row 1
-          const uint32_t r = own ? rho[1] : rho[0];
+          // one lane per row offers it: lanes 0 and L/2 (U = 2); 0, L/4, L/2, 3L/4 (U = 4)
+          const uint32_t r = pick_row<U>(rho, own);
           const uint64_t row = base + r;
-          bool valid = (sl & (L / 2 - 1)) == 0 && r < nvalid;
+          bool valid = (sl & (L / U - 1)) == 0 && r < nvalid;
           if (valid && p.mask) valid = (p.mask[row >> 5] >> (row & 31)) & 1u;
           const uint64_t key = make_key(score[0], static_cast<uint32_t>(row));
           append_keys(cand, &misc[kMiscCount], key, valid && key > thr, lane);
@@ -1476,7 +1505,10 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(const ScanParams 
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
-      if ((it + 1) % p.check_tiles == 0) raise_threshold(cand, hist, misc, p.F, high, thr, ctid);
+      if (--until_check == 0) {
+        until_check = p.check_tiles;
+        raise_threshold(cand, hist, misc, p.F, high, thr, ctid);
+      }
     }
     named_bar_sync(kBarConsumers, kConsumerThreads);
     if (p.trace && threadIdx.x == 0) p.trace[blockIdx.x * 8 + kTrScanned] = globaltimer();
