@@ -955,6 +955,12 @@ static __device__ __noinline__ void finish_query(const ScanParams& p, uint64_t* 
     const uint32_t cap = work_bytes / (p.dim * 4u);
     const bool staged = (p.dim & 3u) == 0u && (reinterpret_cast<uintptr_t>(p.originals) & 15u) == 0u && cap > 0u;
     const uint32_t batch = staged ? cap : (nc > 0u ? nc : 1u);
+    // rows past the first batch are asked of L2 now, so the later batches'
+    // copies do not wait on HBM one batch after another
+    if (staged && nc > batch && warp == 1)
+      for (uint32_t r = batch + static_cast<uint32_t>(lane); r < nc; r += 32)
+        bulk_prefetch_l2(p.originals + static_cast<size_t>(map_row(p.rowmap, key_row(cand[r]))) * p.dim,
+                         p.dim * 4u);
     // the head staging above wrote the work area through the generic proxy;
     // the bulk copies below write it through the async proxy
     fence_proxy_async_smem();
