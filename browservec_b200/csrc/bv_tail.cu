@@ -193,10 +193,12 @@ __global__ void __launch_bounds__(kConsumerThreads, MINB) tail_kernel(const Tail
         }
       }
       named_bar_sync(kBarConsumers, kConsumerThreads);
-      if (gridDim.x > 1) {
-        // a batch (one CTA per query, many CTAs per SM): four threads per row
-        // run Store.dotRow's four f64 lanes in order, the fewest operations
-        // per element; the warp form below trades operations for latency
+      if (gridDim.x > 1 && p.F <= 256u) {
+        // a batch (one CTA per query, many CTAs per SM) with few candidates a
+        // query: four threads per row run Store.dotRow's four f64 lanes in
+        // order, the fewest operations per element; the warp form below trades
+        // operations for latency, which wins for wide F (config 4 tail 1.00 ->
+        // 0.83 ms a step; config 3, F = 80: 0.84 vs 0.88 ms)
         const uint32_t vec = p.dim & ~3u;
         for (uint32_t cc = 0; cc < nb; cc += kConsumerThreads / 4) {
           const uint32_t c = cc + static_cast<uint32_t>(ctid) / 4u;
