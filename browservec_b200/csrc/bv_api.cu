@@ -1443,6 +1443,10 @@ int batch_rounds(bv_index* idx, const bv_search_args* a, uint32_t F, cudaStream_
     const uint64_t tiles = static_cast<uint64_t>(rt1 - rt0) * nqt;
     const uint32_t grid = static_cast<uint32_t>(tiles < static_cast<uint64_t>(idx->num_sms) ? tiles : idx->num_sms);
     g.sbase = first_launch ? 0u : Fp;
+    // the first round writes every position's key at its own slot (no
+    // threshold yet, so no filter and no append counters)
+    g.direct = first_launch && rt0 == 0 && g.mask == nullptr && !pair &&
+                       static_cast<uint64_t>(rt1 - rt0) * bv::kBRowTile <= cap ? 1u : 0u;
     g.slice_g = 0;
     g.slice_cap = cap - g.sbase;
     g.cnt_words = 0;

@@ -401,7 +401,7 @@ __global__ void __launch_bounds__(kConsumerThreads, 1) prep_kernel(const PrepPar
 // stride, ...; tile t covers row tile rt0 + t / nqt and query tile t % nqt
 // (kPair: query tile 2 * (t % nqt) + rank, this CTA's half of the pair's 256
 // queries, and the buffer is released on the pair leader's barrier).
-template <bool kPair>
+template <bool kPair, bool kDirect = false>
 __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, uint8_t* smem, const GemmSmem& lay,
                                               uint64_t* tfull, uint64_t* tempty, uint32_t tmem, uint32_t first,
                                               uint32_t stride, uint32_t ntiles, uint32_t nqt, uint32_t rank,
@@ -457,6 +457,26 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, uint8_t* smem
     // Columns [c0, c0 + 32) of this lane's accumulator row, in registers:
     // prefilter, then exact scores of the hits only.
     auto chunk = [&](const uint32_t (&v)[32], uint32_t c0) {
+      if constexpr (kDirect) {
+        // first round: every position is a candidate, its key at its own slot
+        if (!qvalid) return;
+        const uint32_t pbase = rt * kBRowTile + c0;
+        uint64_t* dst = cq + (pbase - p.rt0 * kBRowTile);
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          const uint64_t k0 = make_key(
+              __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(v[j])), rf_s[c0 + j]), qf), rid_s[c0 + j]);
+          const uint64_t k1 = make_key(
+              __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(v[j + 1])), rf_s[c0 + j + 1]), qf),
+              rid_s[c0 + j + 1]);
+          if (pbase + j + 1 < p.npos) {
+            *reinterpret_cast<ulonglong2*>(dst + j) = make_ulonglong2(k0, k1);
+          } else if (pbase + j < p.npos) {
+            dst[j] = k0;
+          }
+        }
+        return;
+      }
       // the common case is a chunk with no hit: one 3-input max tree decides it
       int mx[11];
 #pragma unroll
@@ -525,6 +545,11 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, uint8_t* smem
         __syncwarp();
       }
     }
+    if (kDirect && qvalid) {  // the tile's positions in use, counted for the select
+      const uint32_t p0 = rt * kBRowTile;
+      const uint32_t nv = p.npos <= p0 ? 0u : (p.npos - p0 < kBRowTile ? p.npos - p0 : kBRowTile);
+      if (nv) atomicAdd(p.scnt + qi, nv);
+    }
     tc_fence_before();
     __syncwarp();
     if (lane == 0) {
@@ -534,6 +559,9 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, uint8_t* smem
   }
 }
 
+// kDirect: the first round's variant (GemmParams::direct), a separate
+// instantiation so the filtering epilogue of the later rounds is unchanged.
+template <bool kDirect>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte aligned base for the swizzled operand tiles
@@ -629,7 +657,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const GemmParams 
       mbar_wait_bounded(done, 0, p.err);
     }
   } else {
-    gemm_epilogue<false>(p, smem, lay, tfull, tempty, tmem, blockIdx.x, gridDim.x, ntiles, p.nqt, 0u, cnt_s, warp,
+    gemm_epilogue<false, kDirect>(p, smem, lay, tfull, tempty, tmem, blockIdx.x, gridDim.x, ntiles, p.nqt, 0u, cnt_s, warp,
                          lane);
   }
   tc_fence_before();
@@ -1212,10 +1240,11 @@ cudaError_t launch_prep(const PrepParams& p, cudaStream_t s) {
 
 cudaError_t launch_gemm(const GemmParams& p, uint32_t grid, cudaStream_t s) {
   const size_t smem = batch_gemm_smem(p.slice_g ? p.cnt_words : 0u);
-  static int opted[kMaxDevices] = {};
-  cudaError_t e = opt_in_smem(reinterpret_cast<const void*>(gemm_kernel), smem, opted);
+  static int opted[2][kMaxDevices] = {};
+  auto kern = p.direct ? gemm_kernel<true> : gemm_kernel<false>;
+  cudaError_t e = opt_in_smem(reinterpret_cast<const void*>(kern), smem, opted[p.direct ? 1 : 0]);
   if (e != cudaSuccess) return e;
-  gemm_kernel<<<grid, kGemmThreads, smem, s>>>(p);
+  kern<<<grid, kGemmThreads, smem, s>>>(p);
   return cudaGetLastError();
 }
 

@@ -95,6 +95,8 @@ struct GemmParams {
   uint32_t cnt_words;    // shared-memory counter words (two 16-bit counters each), slice_g != 0
   uint32_t* overflow;    // set when a buffer would overflow
   uint32_t* err;
+  uint32_t direct;       // first round without a mask: every position is a candidate and
+                         // writes its key at slot (position - rt0 x 256); scnt counts them
 };
 
 struct SelectParams {

@@ -154,6 +154,23 @@ class CudaShardEngine:
                                           C.c_void_p(stream)))
         return keys
 
+    def search_topk(self, q, k: int, fetch: int, stream: int, mask=None):
+        """The whole answer of a single shard: the best k by exact score
+        (global rows), no candidate record (what one rank needs alone)."""
+        torch = self.torch
+        nq = q.shape[0]
+        rows = torch.empty((nq, k), dtype=torch.int32, device=self.device)
+        scores = torch.empty((nq, k), dtype=torch.float32, device=self.device)
+        counts = torch.empty(nq, dtype=torch.int32, device=self.device)
+        args = _lib.BvSearchArgs(queries=q.data_ptr(), nq=nq, k=k, fetch=fetch, rerank=1,
+                                 mask=None if mask is None else mask.data_ptr(),
+                                 mask_words=0 if mask is None else mask.numel(),
+                                 out_rows=rows.data_ptr(), out_scores=scores.data_ptr(),
+                                 out_counts=counts.data_ptr())
+        fn = self.L.bv_search_batch if self.batched else self.L.bv_search_async
+        _lib.check(fn(self.index._h, C.byref(args), C.c_void_p(stream)))
+        return rows, scores, counts
+
     def keys_threshold(self, gathered, world: int, nq: int, fetch: int, stream: int):
         thr = self.torch.empty(nq, dtype=self.torch.int64, device=self.device)
         _lib.check(self.L.bv_keys_threshold(C.c_void_p(gathered.data_ptr()), world, nq, fetch,
@@ -271,7 +288,11 @@ class ShardedIndex:
         ctx = torch.cuda.stream(self._stream) if self._stream is not None else nullcontext()
         with ctx:
             sid = self._stream.cuda_stream if self._stream is not None else 0
-            if self.world > 1 and getattr(self.engine, "two_phase", False):
+            if self.world == 1 and hasattr(self.engine, "search_topk"):
+                # one rank holds every row: its own best k is the answer (no
+                # candidate record, no merge)
+                out = self.engine.search_topk(q, k, fetch, sid, mask)
+            elif self.world > 1 and getattr(self.engine, "two_phase", False):
                 keys = self.engine.select_keys(q, k, fetch, sid, mask)
                 gk = torch.empty(self.world * keys.numel(), dtype=keys.dtype, device=keys.device)
                 self.dist.all_gather_into_tensor(gk, keys, group=self.group)

@@ -179,3 +179,44 @@ def test_two_phase_batched_shards_equal_single_index(bits, scoring, world, n, d,
             e.destroy()
         if single is not None:
             single.destroy()
+
+
+@pytest.mark.parametrize("bits,scoring,n,d,k,fetch,nq", [
+    (1, "int", 40000, 768, 100, 1000, 300),
+    (8, "asym", 20000, 384, 10, 40, 7),
+    (4, "int", 30000, 384, 10, 80, 300),
+])
+def test_one_rank_shortcut_equals_record_merge(bits, scoring, n, d, k, fetch, nq):
+    """A one-rank ShardedIndex answers with its shard's own best k (no record,
+    no merge): the same rows and score bits as the record + merge path."""
+    import socket
+
+    import torch
+    import torch.distributed as dist
+
+    from browservec_b200.sharded import ShardedIndex
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", world_size=1, rank=0)
+    try:
+        x = _rows(n, d, bits * 29 + 1)
+        qs = torch.from_numpy(_rows(nq, d, 5)).cuda()
+        idx = ShardedIndex(d, n, bits=bits, scoring=scoring, metric="cosine", device=0)
+        idx.load(torch.from_numpy(x).cuda())
+        got = [t.cpu().numpy() for t in idx.search(qs, k, fetch)]
+        eng, st = idx.engine, torch.cuda.Stream()
+        with torch.cuda.stream(st):
+            rec = eng.new_record(nq, fetch)
+            eng.search_record(qs, k, fetch, rec, st.cuda_stream)
+            want = [t.cpu().numpy() for t in eng.merge(rec, 1, nq, k, fetch, st.cuda_stream)]
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(got[2], want[2])
+        for q in range(nq):
+            m = int(want[2][q])
+            np.testing.assert_array_equal(got[0][q, :m], want[0][q, :m])
+            assert got[1][q, :m].view(np.uint32).tolist() == want[1][q, :m].view(np.uint32).tolist()
+        idx.destroy()
+    finally:
+        dist.destroy_process_group()
