@@ -478,6 +478,30 @@ def run_sharded(args, name, ds):
                 "recall_at_10": recall(r2), "recall_sample": ns}
         idx.set_scoring(scoring, batched=batched)
 
+    # 1-bit codes: the same batch scored as BASELINE words config 4's prefilter, the
+    # popc Hamming distance of the query's sign bits and the codes (+-1 x +-1 on the
+    # tensor cores: idot = P - 2 x hamming), timed like the headline
+    hamming = None
+    if cfg["bits"] == 1 and scoring == "int" and batched and not args.no_hamming:
+        idx.set_scoring("hamming", batched=True)
+        for _ in range(args.warmup):
+            search(qs)
+        dist.barrier()
+        h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        h0.record(cur)
+        for _ in range(args.steps):
+            rh, _, _ = search(qs)
+        h1.record(cur)
+        torch.cuda.synchronize()
+        t = torch.tensor([h0.elapsed_time(h1)], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        hms = float(t.item())
+        hamming = {"scoring": "hamming (popc of the query's sign bits against the 1-bit codes, as +-1 int8 "
+                              "on the tensor cores)",
+                   "value": args.steps * nq / (hms / 1e3), "unit": UNIT, "ms_per_step": hms / args.steps,
+                   "recall_at_10": recall(rh), "recall_sample": ns}
+        idx.set_scoring(scoring, batched=batched)
+
     # e2e: host queries (pinned) -> device, search, results back to the host, every step
     q_host = qs.cpu().pin_memory()
     e2e_steps = max(1, min(args.steps, 3))
@@ -513,6 +537,8 @@ def run_sharded(args, name, ds):
                 "recall_at_10": rec, "recall_sample": ns, "query_ms": query_ms,
                 "gpu_launches": args.steps * launches_per_step, "roofline": roofline, "cpu_baseline": cpu,
                 "e2e": e2e, "clocks": clk_res, "also": also, "step_breakdown_ms": breakdown}
+        if hamming is not None:
+            line["hamming"] = hamming
     idx.destroy()
     return line if rank == 0 else None
 
@@ -538,6 +564,8 @@ def main():
     ap.add_argument("--cpu-queries", type=int, default=0,
                     help="sharded configs: queries per CPU-baseline sample (default 16, reference arm 4 per step)")
     ap.add_argument("--no-asym", action="store_true", help="sharded configs: skip the asym recall figure")
+    ap.add_argument("--no-hamming", action="store_true",
+                    help="config 4: skip the Hamming (popc) scoring figure")
     ap.add_argument("--sharded-scoring", default=None, choices=["asym", "int", "hamming"],
                     help="scoring of a sharded config (default: the config's)")
     ap.add_argument("--rows", type=int, default=0, help="sharded configs: corpus rows (default: the config's)")
@@ -577,7 +605,7 @@ def main():
 def _summary(line):
     """The figures of one configuration's line kept under the headline's 'configs'."""
     keys = ("metric", "value", "unit", "ms_per_step", "dtype", "recall_at_10", "recall_sample", "gpu_launches",
-            "roofline", "cpu_baseline", "e2e", "also", "step_breakdown_ms", "clocks")
+            "roofline", "cpu_baseline", "e2e", "also", "hamming", "step_breakdown_ms", "clocks")
     out = {k: line[k] for k in keys if k in line}
     out["config"] = line.get("config")
     return out
