@@ -327,9 +327,12 @@ int plan_scan(bv_index* idx, uint32_t F, Plan* pl, bool fold = true, bool alone 
   pl->fold = fold && fp <= 256;
   // Folded scans run two CTAs per SM (consecutive queries): each CTA then
   // keeps to half of the SM's shared memory.
-  const bool two = pl->fold;
-  const uint32_t limit = two ? static_cast<uint32_t>(idx->smem_per_sm) / 2u - 1024u
-                             : static_cast<uint32_t>(idx->max_smem);
+  // A query alone runs one CTA per SM (below), so it may take an SM's whole
+  // shared memory: a deeper ring, and room for all of its re-rank rows in the
+  // finish.
+  const uint32_t half = static_cast<uint32_t>(idx->smem_per_sm) / 2u - 1024u;
+  const bool two = pl->fold && !alone;
+  const uint32_t limit = two ? half : static_cast<uint32_t>(idx->max_smem);
   pl->stages = 0;
   for (uint32_t lim : {limit, static_cast<uint32_t>(idx->max_smem)}) {  // two CTAs per SM, else one
     for (uint32_t st = 4; st >= 2 && !pl->stages; --st) {
@@ -353,7 +356,7 @@ int plan_scan(bv_index* idx, uint32_t F, Plan* pl, bool fold = true, bool alone 
   // epilogue are spread over more tiles.  Measured on B200 (100k x 768 int8,
   // back-to-back queries): 98 CTAs 47.1k q/s, 74 50.4k, 59 53.4k, 49 55.6k,
   // 42 53.6k.
-  const bool two_per_sm = pl->fold && pl->smem <= limit;
+  const bool two_per_sm = pl->fold && pl->smem <= half;
   const uint32_t nsm = static_cast<uint32_t>(idx->num_sms);
   const uint32_t all = two_per_sm ? 2u * nsm : pl->fold ? nsm : (nsm > 2 ? nsm - 2u : 1u);
   // One CTA per SM (wide F with the tail kernel): back to back, a query takes
