@@ -446,8 +446,8 @@ __device__ __forceinline__ float ld_row_f32(const float* p) {
   else return *p;
 }
 
-template <bool kGlobal>
-__device__ __noinline__ float dot_row_exact_warp(const float* x, const float* q, uint32_t dim, int lane) {
+template <bool kGlobal, typename QT = float>
+__device__ __noinline__ float dot_row_exact_warp(const float* x, const QT* q, uint32_t dim, int lane) {
   double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0, a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
   uint32_t i = static_cast<uint32_t>(lane);
   for (; i + 96u < dim; i += 128u) {
@@ -503,8 +503,8 @@ __device__ __noinline__ float dot_row_exact_warp(const float* x, const float* q,
 // fallback per row, with two partial sums per lane and row (lane l takes
 // i = l + 32t; at most dim / 64 + 8 additions per product, within the bound
 // dot_row_exact_warp uses).
-template <bool kGlobal>
-__device__ __forceinline__ float dot_row_check(double s, double a, const float* x, const float* q, uint32_t dim,
+template <bool kGlobal, typename QT = float>
+__device__ __forceinline__ float dot_row_check(double s, double a, const float* x, const QT* q, uint32_t dim,
                                                int lane) {
   const double K1 = static_cast<double>(dim / 4u + 13u);
   const double B = __dmul_ru(__dmul_ru(a, K1), 0x1p-51);
@@ -524,8 +524,10 @@ __device__ __forceinline__ float dot_row_check(double s, double a, const float* 
   return __double2float_rn(r);
 }
 
-template <bool kGlobal>
-__device__ __noinline__ void dot_rows2_exact_warp(const float* xa, const float* xb, const float* q, uint32_t dim,
+// QT: the query as float, or already widened to double (one conversion fewer
+// per product; the same values, since every float is a double exactly).
+template <bool kGlobal, typename QT = float>
+__device__ __noinline__ void dot_rows2_exact_warp(const float* xa, const float* xb, const QT* q, uint32_t dim,
                                                      int lane, float& ra, float& rb) {
   double sa0 = 0.0, sa1 = 0.0, aa0 = 0.0, aa1 = 0.0, sb0 = 0.0, sb1 = 0.0, ab0 = 0.0, ab1 = 0.0;
   uint32_t i = static_cast<uint32_t>(lane);
@@ -562,8 +564,8 @@ __device__ __noinline__ void dot_rows2_exact_warp(const float* xa, const float* 
     aa = __dadd_rn(aa, __shfl_xor_sync(0xffffffffu, aa, off));
     ab = __dadd_rn(ab, __shfl_xor_sync(0xffffffffu, ab, off));
   }
-  ra = dot_row_check<kGlobal>(sa, aa, xa, q, dim, lane);
-  rb = dot_row_check<kGlobal>(sb, ab, xb, q, dim, lane);
+  ra = dot_row_check<kGlobal, QT>(sa, aa, xa, q, dim, lane);
+  rb = dot_row_check<kGlobal, QT>(sb, ab, xb, q, dim, lane);
 }
 
 }  // namespace bv

@@ -39,6 +39,7 @@ __global__ void __launch_bounds__(kConsumerThreads, MINB) tail_kernel(const Tail
   uint32_t* hist = reinterpret_cast<uint32_t*>(smem + lay.hist_off);
   uint32_t* misc = reinterpret_cast<uint32_t*>(smem + lay.misc_off);
   float* q = reinterpret_cast<float*>(smem + lay.q_off);
+  double* qd = reinterpret_cast<double*>(smem + lay.qd_off);
   float* rows_s = reinterpret_cast<float*>(smem + lay.rows_off);
   uint64_t* gbar = reinterpret_cast<uint64_t*>(smem + lay.bar_off);
   uint64_t* pbar = gbar + 1;  // the CTA lists staged into shared memory
@@ -169,6 +170,13 @@ __global__ void __launch_bounds__(kConsumerThreads, MINB) tail_kernel(const Tail
                          p.dim * 4u);
     };
     named_bar_sync(kBarConsumers, kConsumerThreads);
+    // batches with wide F score with the warp form over the query widened
+    // once to double (the products then convert only the row's elements)
+    const bool wide = gridDim.x > 1 && p.F > 256u;
+    if (wide) {
+      for (uint32_t i = ctid; i < p.dim; i += kConsumerThreads) qd[i] = static_cast<double>(q[i]);
+      named_bar_sync(kBarConsumers, kConsumerThreads);
+    }
     if (bulk && warp == 1) prefetch(batch);
     for (uint32_t c0 = 0; c0 < nc; c0 += batch) {
       const uint32_t nb = nc - c0 < batch ? nc - c0 : batch;
@@ -230,14 +238,20 @@ __global__ void __launch_bounds__(kConsumerThreads, MINB) tail_kernel(const Tail
         const uint32_t c2 = c + kConsumerWarps;
         if (c2 < nb) {
           float sa, sb;
-          dot_rows2_exact_warp<false>(rows_s + static_cast<size_t>(c) * stride,
-                                      rows_s + static_cast<size_t>(c2) * stride, q, p.dim, lane, sa, sb);
+          if (wide)
+            dot_rows2_exact_warp<false, double>(rows_s + static_cast<size_t>(c) * stride,
+                                                rows_s + static_cast<size_t>(c2) * stride, qd, p.dim, lane, sa, sb);
+          else
+            dot_rows2_exact_warp<false>(rows_s + static_cast<size_t>(c) * stride,
+                                        rows_s + static_cast<size_t>(c2) * stride, q, p.dim, lane, sa, sb);
           if (lane == 0) {
             ex[c0 + c] = make_key(sa, key_row(cand[c0 + c]));
             ex[c0 + c2] = make_key(sb, key_row(cand[c0 + c2]));
           }
         } else {
-          const float sc = dot_row_exact_warp<false>(rows_s + static_cast<size_t>(c) * stride, q, p.dim, lane);
+          const float sc = wide ? dot_row_exact_warp<false, double>(rows_s + static_cast<size_t>(c) * stride, qd,
+                                                                    p.dim, lane)
+                                : dot_row_exact_warp<false>(rows_s + static_cast<size_t>(c) * stride, q, p.dim, lane);
           if (lane == 0) ex[c0 + c] = make_key(sc, key_row(cand[c0 + c]));
         }
       }

@@ -34,7 +34,7 @@ enum : int { kTrTailStart = 0, kTrTailMerged = 1, kTrTailDone = 2, kTrTailGather
              kTrTailDotted = 4, kTrTailEntry = 5, kTrTailStaged = 6 };
 
 struct TailSmem {
-  uint32_t cand_off, hist_off, misc_off, q_off, rows_off, bar_off, total;
+  uint32_t cand_off, hist_off, misc_off, q_off, qd_off, rows_off, bar_off, total;
 };
 
 __host__ __device__ inline TailSmem tail_smem_layout(uint32_t dim, uint32_t capc, uint32_t rows_bytes) {
@@ -51,6 +51,8 @@ __host__ __device__ inline TailSmem tail_smem_layout(uint32_t dim, uint32_t capc
   o = up(o + 128 * 4, 16);
   s.q_off = o;
   o = up(o + dim * 4 + 16, 16);
+  s.qd_off = o;  // the query widened to double (batches with wide F)
+  o = up(o + dim * 8, 16);
   s.bar_off = o;
   o = up(o + 16, 16);
   s.total = o;
