@@ -411,7 +411,10 @@ def run_sharded(args, name, ds):
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
     qps = args.steps * nq / (ms / 1e3)
-    launches_per_step = eng_index.last_launches() + (3 if world > 1 and batched else 1)
+    # the search's own launches, plus the exchange kernels: batched two-phase
+    # (keys threshold, finish's trim, merge), per-query (merge); one rank has
+    # no exchange
+    launches_per_step = eng_index.last_launches() + (0 if world == 1 else (3 if batched else 1))
 
     ns = min(nq, 100)
     keep = _unpack(torch, dc.mask(flt), hi - lo) if dc is not None else None
