@@ -89,6 +89,20 @@ class OracleShardEngine:
             v.exact[i * fetch:i * fetch + n] = exact.view(np.int32)
             v.counts[i] = n
 
+    def search_topk(self, q, k, fetch, stream, mask=None):
+        """A one-rank group's whole answer: the shard's own best k (global rows)."""
+        nq = q.shape[0]
+        rows = np.zeros((nq, k), np.int32)
+        scores = np.zeros((nq, k), np.float32)
+        counts = np.zeros(nq, np.int32)
+        self.topk_calls = getattr(self, "topk_calls", 0) + 1
+        for i in range(nq):
+            r, s, _, _ = self.corpus.query(q[i].numpy(), k, fetch, self.mode)
+            rows[i, :r.size] = (r + np.uint32(self.row_base)).view(np.int32)
+            scores[i, :r.size] = s
+            counts[i] = r.size
+        return torch.from_numpy(rows), torch.from_numpy(scores), torch.from_numpy(counts)
+
     # two-phase batched flow (select keys -> all-gather -> global threshold ->
     # re-rank only this shard's members of the global best F)
     two_phase = False
@@ -244,3 +258,29 @@ def test_gloo_three_ranks_two_phase_members_only(tmp_path):
             assert np.array_equal(got["rows"][i, :n].view(np.uint32), wr)
             assert np.array_equal(got["scores"][i, :n].view(np.uint32), ws.view(np.uint32))
     assert members == NQ * FETCH  # the shards' members partition the global best F
+
+
+def test_gloo_one_rank_answers_alone(tmp_path):
+    """A one-rank group takes the shortcut (its own best k, no record, no
+    merge) and returns the single-store answer."""
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(_free_port()))
+    dist.init_process_group("gloo", rank=0, world_size=1)
+    try:
+        x = _rows(N, D, 5)
+        eng = OracleShardEngine(D, BITS, MODE, 0)
+        idx = ShardedIndex(D, N, bits=BITS, engine=eng)
+        idx.load(x, global_rows=True)
+        qs = _rows(NQ, D, 6)
+        rows, scores, counts = idx.search(torch.from_numpy(qs), K, FETCH)
+        assert eng.topk_calls == 1
+        full = O.Corpus(x, D, BITS)
+        for i in range(NQ):
+            wr, ws, _, _ = full.query(qs[i], K, FETCH, MODE)
+            n = int(counts[i])
+            assert n == wr.size
+            assert np.array_equal(rows[i, :n].numpy().view(np.uint32), wr)
+            assert np.array_equal(scores[i, :n].numpy().view(np.uint32), ws.view(np.uint32))
+    finally:
+        dist.destroy_process_group()
